@@ -1,0 +1,199 @@
+/*
+ * h3b.h -- C ABI of the B200-native (sm_100a) DiT attention-block hot path.
+ *
+ * The hot path is Ulysses sequence-parallel self-attention wrapped in online-FP8 projections, as served by the
+ * h3_tp2 vLLM plugin.  Every entry point below replaces one kernel or op of that plugin; the comment above each names
+ * the reference interface it stands in for (paths inside the knapcio/MiniMax-H3-2x-DGX-Spark-TP2 project).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  Element types are fixed per argument and written in the comment:
+ *    bf16 = IEEE bfloat16, f16 = IEEE half, e4m3 = OCP FP8 E4M3 (torch.float8_e4m3fn), f32 = float.
+ *  - Sizes and strides are in ELEMENTS unless the name ends in _bytes.  Row-major unless stated.
+ *  - The caller owns and allocates every buffer (inputs, outputs, scratch).  No entry point allocates device memory
+ *    except the one-time per-device status word (h3b_device_status) and cached TMA descriptors (host memory).
+ *  - All work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).  Nothing synchronises.
+ *  - Return value: 0 (H3B_OK) or a negative h3b_status.  h3b_last_error() gives a one-line reason for the last
+ *    failure of the calling thread.  Argument errors are detected on the host before anything is enqueued.
+ *  - Device-side waits are bounded: a kernel whose pipeline stalls past H3B_WAIT_TIMEOUT_NS records
+ *    H3B_ETIMEOUT in the per-device status word and returns; h3b_device_status() reads and clears it.
+ */
+#ifndef H3B_H_
+#define H3B_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define H3B_API __attribute__((visibility("default")))
+#else
+#define H3B_API
+#endif
+
+typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
+
+enum h3b_status {
+  H3B_OK = 0,
+  H3B_EINVAL = -1,       /* bad shape, null pointer, negative size */
+  H3B_EALIGN = -2,       /* pointer or stride alignment not supported by the kernel */
+  H3B_EUNSUPPORTED = -3, /* valid request outside what the kernels implement (e.g. head_dim != 128) */
+  H3B_ECUDA = -4,        /* a CUDA runtime/driver call failed (launch, descriptor encode, ...) */
+  H3B_ETIMEOUT = -5,     /* a device-side bounded wait expired (pipeline stall, peer never signalled) */
+  H3B_ERANGE = -6        /* input values outside the range the requested fast path handles exactly */
+};
+
+enum h3b_div_mode {
+  H3B_DIV_IEEE = 0, /* correctly rounded fp32 division: the eager torch path (fp8_quant_fuse.quant_torch) */
+  H3B_DIV_FULL = 1  /* PTX div.full.f32: the instruction Triton emits for `/` in the Inductor QuantFP8 kernel */
+};
+
+enum h3b_out_dtype { H3B_OUT_BF16 = 0, H3B_OUT_F16 = 1 };
+
+/* FP8 GEMM epilogue kinds (h3b_fp8_gemm `epilogue`) */
+enum h3b_epilogue_kind {
+  H3B_EPI_PLAIN = 0,    /* y[m, n] = out(sa[m] * (sb[n] * acc)), bias by fma */
+  H3B_EPI_QKV_SEND = 1, /* plain epilogue, stored straight into three Ulysses send buffers [P, M, H/P, d] */
+  H3B_EPI_SWIGLU = 2    /* fc1: gate columns [0, F) and up columns [F, 2F) of W -> bf16 silu(gate) * up, y [M, F] */
+};
+
+/* Extra arguments of H3B_EPI_QKV_SEND.  Column n of the [M, 3*H*d] product is (which = n / (H*d), head
+ * h = (n % (H*d)) / d, c = n % d); it is written to send[which][p][m][j][c] with p = h / (H/P), j = h % (H/P).
+ * v_f16 != 0 stores the v slab as f16 (bf16-rounded first, then converted exactly) for the f16 P.V attention. */
+typedef struct h3b_qkv_send {
+  void* send[3]; /* q, k, v send buffers, each [P, M, H/P, d] contiguous, bf16 (v: f16 if v_f16) */
+  int32_t heads; /* H */
+  int32_t head_dim; /* d, must be 128 */
+  int32_t ws;    /* P (Ulysses degree), H % P == 0 */
+  int32_t v_f16;
+  int32_t* range_flag; /* device int or NULL: set to 1 when a finite v value overflows f16 (v_f16 only) */
+} h3b_qkv_send;
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * library information
+ * ------------------------------------------------------------------------------------------------------------- */
+H3B_API int h3b_abi_version(void);
+H3B_API const char* h3b_status_string(int status);
+H3B_API const char* h3b_last_error(void);
+/* Reads and clears the sticky device status word of the current device (0 or a negative h3b_status). Synchronises
+ * the current device first. */
+H3B_API int h3b_device_status(void);
+/* Sets the device-side wait bound (nanoseconds, default 4e9). */
+H3B_API int h3b_set_wait_timeout_ns(uint64_t ns);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * per-token dynamic FP8 quant (row kernels, HBM bound)
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Replaces ulysses_outq.quant_rows (h3_tp2/ulysses_outq.py:109) and its Triton kernel _quant_rows_kernel (:74-93);
+ * also serves fp8_quant_fuse.quant (h3_tp2/fp8_quant_fuse.py:318) with p = 1 and unpack_quant (:379) with the receive
+ * buffer's strides.  Row m (0 <= m < M) is the concatenation over s < p of the `seg` bf16 elements at
+ * base + s*stride_p + m*stride_m.  Writes q [M, p*seg] e4m3 contiguous and scale [M] f32:
+ *   amax = max |x| (NaN propagates), scale = max(amax / 448, 1/(448*512)), q = e4m3_rn(clamp(x * (1/scale), +-448)). */
+H3B_API int h3b_quant_rows_e4m3(const void* base, int64_t m, int32_t p, int64_t seg, int64_t stride_p, int64_t stride_m,
+                        void* q, float* scale, int32_t div_mode, h3b_stream_t stream);
+
+/* Replaces fp8_quant_fuse.rms_quant + _rms_norm_indexed_scale_shift_quant_kernel (h3_tp2/fp8_quant_fuse.py:144-188,
+ * :330): RMSNorm (fp32) * weight, then AdaLN modulation `* (1 + scale[idx]) + shift[idx]` when shift/scale are
+ * non-NULL (indices NULL = row i uses modulation row 0), rounded to bf16, then the per-token quant.  x [rows, hidden]
+ * bf16 (row stride stride_x), weight [hidden] bf16, shift/scale bf16 rows.  If ph != NULL the bf16 row is also
+ * stored there ([rows, hidden] contiguous). */
+H3B_API int h3b_rms_quant_e4m3(const void* x, int64_t rows, int64_t hidden, int64_t stride_x, const void* weight,
+                       const void* shift, int64_t stride_shift, const void* scale, int64_t stride_scale,
+                       const int64_t* indices, float eps, void* ph, void* q, float* s, int32_t div_mode,
+                       h3b_stream_t stream);
+
+/* Replaces fp8_quant_fuse.gate_rms_quant + _indexed_gate_rms_norm_scale_shift_quant_kernel
+ * (h3_tp2/fp8_quant_fuse.py:191-243, :350): residual_out = bf16(residual + gate[idx] * branch), then RMSNorm,
+ * modulation and the per-token quant of the result.  All row tensors bf16 with the given row strides;
+ * residual_out [rows, hidden] contiguous. */
+H3B_API int h3b_gate_rms_quant_e4m3(const void* residual, int64_t stride_residual, const void* gate, int64_t stride_gate,
+                            const void* branch, int64_t stride_branch, const void* weight, const void* shift,
+                            int64_t stride_shift, const void* scale, int64_t stride_scale, const int64_t* indices,
+                            int64_t rows, int64_t hidden, float eps, void* residual_out, void* q, float* s,
+                            int32_t div_mode, h3b_stream_t stream);
+
+/* Replaces fp8_quant_fuse.silu_mul_quant + _silu_mul_quant_kernel (h3_tp2/fp8_quant_fuse.py:263-278, :392):
+ * x [rows, 2d] bf16 (row stride stride_x) -> silu_and_mul (vLLM arithmetic: silu rounded to bf16, bf16 product)
+ * -> per-token quant: q [rows, d] e4m3, s [rows] f32. */
+H3B_API int h3b_silu_mul_quant_e4m3(const void* x, int64_t rows, int64_t d, int64_t stride_x, void* q, float* s,
+                            int32_t div_mode, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * scale passes over an fp32 GEMM product (the two-pass path's second pass)
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Replaces fp8_gemm._scale_bias_cast (h3_tp2/fp8_gemm.py:38-54): y[m,n] = out(sa[m] * (sb[n] * x[m,n])) or
+ * out(fma(sa[m], sb[n]*x[m,n], bias[n])).  x [M, N] f32, bias bf16 [N] or NULL, y [M, N] (out_dtype). */
+H3B_API int h3b_scale_bias_cast(const float* x, const float* sa, const float* sb, const void* bias, void* y, int64_t M,
+                        int64_t N, int32_t out_dtype, h3b_stream_t stream);
+
+/* Replaces fp8_swiglu._scale_swiglu (h3_tp2/fp8_swiglu.py:48-70): x [M, 2*half] f32 product of fc1 ->
+ * y [M, half] bf16 = bf16(bf16(g / (1 + exp(-g))) * u) with g, u the bf16-rounded epilogue of the gate/up halves. */
+H3B_API int h3b_scale_swiglu(const float* x, const float* sa, const float* sb, const void* bias, void* y, int64_t M,
+                     int64_t half, h3b_stream_t stream);
+
+/* Replaces fp8_swiglu._scale_swiglu_quant (h3_tp2/fp8_swiglu.py:73-103): as h3b_scale_swiglu, then the per-token
+ * quant of each SwiGLU row for fc2: q [M, half] e4m3, s [M] f32. */
+H3B_API int h3b_scale_swiglu_quant(const float* x, const float* sa, const float* sb, const void* bias, void* q, float* s,
+                           int64_t M, int64_t half, int32_t div_mode, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * FP8 GEMM (tcgen05 + TMEM + TMA), scaled epilogue fused
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Replaces ops.cutlass_scaled_mm as routed by fp8_gemm._mm / route (h3_tp2/fp8_gemm.py:328-386) for per-token x
+ * per-channel scales: scaled_mm_tensor32 (:149), the CuTe-DSL kernel fp8_cutlass.scaled_mm (h3_tp2/fp8_cutlass.py:115,
+ * h3_tp2/fp8_cutlass_kernel.py:52) and, with H3B_EPI_SWIGLU, fp8_swiglu.gemm_swiglu (h3_tp2/fp8_swiglu.py:230).
+ *   a [M, K] e4m3 (row stride lda), w [N, K] e4m3 (row stride ldw; the reference's b = w.t()),
+ *   sa [M] f32, sb [N] f32, bias [N] bf16 or NULL, y [M, N] (row stride ldy; H3B_EPI_SWIGLU: [M, N/2]).
+ * Epilogue arithmetic: t = sb[n] * acc; y = sa[m] * t (or fma(sa[m], t, bias[n])); one rounding to out_dtype.
+ * Requirements: K % 16 == 0, N % 16 == 0 (SWIGLU: (N/2) % 128 == 0), lda/ldw multiples of 16, ldy multiple of 8,
+ * a/w 16-byte aligned. */
+H3B_API int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, const float* sa, const float* sb,
+                 const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int32_t out_dtype,
+                 int32_t epilogue, const h3b_qkv_send* send, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * attention (tcgen05 flash attention, non-causal, head_dim 128)
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Replaces the local attention of the Ulysses forward (upstream Attention._run_local_attention -> cuDNN SDPA, called
+ * at h3_tp2/ulysses_exact.py:495-496).  o[t, h, :] = softmax(q[t, h, :] . k[:valid_kv, h, :]^T * scale) v[:valid_kv].
+ *   q [s_q, heads, 128] bf16, k [s_kv, heads, 128] bf16, v [s_kv, heads, 128] bf16 or f16 (v_f16 != 0), o [s_q, heads,
+ *   128] bf16; token strides q_tok/k_tok/v_tok/o_tok and head strides q_head/k_head/v_head/o_head (elements, multiples
+ *   of 8, innermost stride 1).  valid_kv <= s_kv (< 0: s_kv).
+ * With v_f16 the P.V product runs in f16 (P in [0, 256] after the online max, V exactly representable when |v| lies
+ * in f16's normal range); with bf16 V it runs in bf16.  range_flag (device int or NULL) is the flag that the f16
+ * conversion of v raised; when it holds 1 the kernel writes nothing and records H3B_ERANGE in the device status word
+ * (the caller then reruns with bf16 v). */
+H3B_API int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok, int64_t k_head,
+                       const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok, int64_t o_head,
+                       int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
+                       int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Ulysses layout kernels
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Replaces ulysses_exact.pack_into (h3_tp2/ulysses_exact.py:119, stock comm.py:44's pack copy): x [M, H, d] with
+ * strides (stride_m, stride_h, 1) -> send [P, M, H/P, d] contiguous.  elem_bytes 2 (bf16/f16); to_f16 != 0 converts
+ * bf16 -> f16 on the way (and sets *range_flag to 1 when a finite value overflows f16). */
+H3B_API int h3b_pack_by_dest(const void* x, int64_t m, int32_t heads, int32_t d, int64_t stride_m, int64_t stride_h,
+                     int32_t ws, void* send, int32_t to_f16, int32_t* range_flag, h3b_stream_t stream);
+
+/* Replaces ulysses_exact.exchange_back's unpack (copy 5, h3_tp2/ulysses_exact.py:181-183) and unpack
+ * (:124): recv [P, M, hl, d] contiguous -> out [M, P*hl, d] contiguous.  2-byte elements. */
+H3B_API int h3b_unpack_recv(const void* recv, int32_t ws, int64_t m, int32_t hl, int32_t d, void* out, h3b_stream_t stream);
+
+/* bf16 -> f16 conversion of n elements (exact for values in f16's normal range); *range_flag (device int, may be
+ * NULL) is set to 1 if any finite value overflows f16.  Used to feed the f16 P.V attention from a bf16 v. */
+H3B_API int h3b_bf16_to_f16(const void* x, void* y, int64_t n, int32_t* range_flag, h3b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H_ */

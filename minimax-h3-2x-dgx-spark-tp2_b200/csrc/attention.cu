@@ -1,0 +1,403 @@
+// Non-causal flash attention, head_dim 128, on the 5th-generation tensor cores (replaces the cuDNN SDPA local
+// attention of the Ulysses forward, upstream Attention._run_local_attention called at
+// h3_tp2/ulysses_exact.py:495-496).
+//
+// One CTA per (pair of 128-row query tiles, head).  TMEM (512 columns): S0 | S1 | O0 | O1, 128 f32 columns each.
+//   warps 0-3 : softmax for query tile 0 (thread = query row = TMEM lane), warps 4-7: query tile 1
+//   warp 8    : TMA producer (Q once; K and V tiles of 128 keys through 2-stage rings)
+//   warp 9    : TMEM allocator + single-thread MMA issuer
+// Per key tile j and query tile q:
+//   S_q = Q_q K_j^T            tcgen05.mma kind::f16 bf16 x bf16 -> f32, both operands K-major in shared memory
+//   softmax: one row per thread, exp2 on the MUFU, running max with lazy rescaling of O (only when the max grows by
+//            more than 2^8), P written back into TMEM (columns 0..63 of S_q as packed 16-bit pairs)
+//   O_q += P_q V_j             tcgen05.mma kind::f16 with A = P from TMEM, B = V (MN-major in shared memory)
+// The MMA for S_q(j+1) is issued after O_q += P_q V_j, so the in-order tensor pipe never overwrites P before it is
+// consumed, and the commit that publishes S_q(j+1) also covers that P.V (the softmax may rescale O right away).
+// P.V runs in f16 when V is given in f16 (P in [0, 256], V exact in f16's normal range): the P rounding error is 8x
+// below bf16's, which keeps the output within rel-L2 2e-3 of fp32 SDPA.  Every wait is bounded; no multicast.
+#include "common.cuh"
+
+namespace h3b {
+namespace attn {
+
+constexpr int BQ = 128, BKV = 128, D = 128;
+constexpr int TILE_BYTES = BQ * D * 2;  // 32 KB
+constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int KST = 2, VST = 2;
+constexpr int THREADS = 320;
+constexpr int SMEM_BYTES = (2 + KST + VST) * TILE_BYTES + 1024 + 256;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+struct Params {
+  int64_t s_q, s_kv, valid_kv;
+  int heads;
+  float scale_log2;  // softmax scale * log2(e)
+  uint16_t* o;
+  int64_t o_tok, o_head;
+  int nkv;
+  const int32_t* range_flag;
+  WaitCtl wc;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_p(float lo, float hi) {
+  if (F16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+template <bool F16>
+__global__ void __launch_bounds__(THREADS, 1)
+    flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, Params p) {
+  constexpr uint32_t IDESC_QK = idesc_make(FMT_BF16, FMT_BF16, 0, BQ, BKV);
+  constexpr uint32_t IDESC_PV = idesc_make(F16 ? FMT_F16 : FMT_BF16, F16 ? FMT_F16 : FMT_BF16, 1, BQ, D);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);                   // 2 tiles
+  const uint32_t sK = sQ + 2 * TILE_BYTES;              // KST tiles
+  const uint32_t sV = sK + KST * TILE_BYTES;            // VST tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (2 + KST + VST) * TILE_BYTES);
+  const uint32_t b0 = smem_u32(bars);
+  // q_full | k_full[2] | k_empty[2] | v_full[2] | v_empty[2] | s_full[2] | p_full[2] | o_full[2] | done
+  const uint32_t q_full = b0;
+  auto k_full = [&](int s) { return b0 + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return b0 + 8u * (3 + s); };
+  auto v_full = [&](int s) { return b0 + 8u * (5 + s); };
+  auto v_empty = [&](int s) { return b0 + 8u * (7 + s); };
+  auto s_full = [&](int q) { return b0 + 8u * (9 + q); };
+  auto p_full = [&](int q) { return b0 + 8u * (11 + q); };
+  auto o_full = [&](int q) { return b0 + 8u * (13 + q); };
+  const uint32_t done_bar = b0 + 8u * 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * BQ;
+  bool aborted_at_entry = status_bad(p.wc);
+  if (p.range_flag != nullptr && *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0) {
+    if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
+    aborted_at_entry = true;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+      mbar_init(s_full(s), 1);
+      mbar_init(p_full(s), 128);
+      mbar_init(o_full(s), 1);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nkv = p.nkv;
+
+  if (!aborted_at_entry) {
+    if (warp == 8) {
+      if (lane == 0) {
+        // ---------------- TMA producer ----------------
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+        for (int t = 0; t < 2; ++t)
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d(sQ + t * TILE_BYTES + hf * HALF_BYTES, &tmQ, q_full, hf * 64, static_cast<int32_t>(q0 + t * BQ),
+                        head);
+        int kn[KST] = {0, 0}, vn[VST] = {0, 0};
+        for (int j = 0; j < nkv; ++j) {
+          const int ks = j % KST, vs = j % VST;
+          const uint32_t kph = static_cast<uint32_t>(j / KST) & 1u, vph = static_cast<uint32_t>(j / VST) & 1u;
+          if (!mbar_wait(k_empty(ks), kph ^ 1u, p.wc)) break;
+          mbar_arrive_expect_tx(k_full(ks), TILE_BYTES);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d(sK + ks * TILE_BYTES + hf * HALF_BYTES, &tmK, k_full(ks), hf * 64, j * BKV, head);
+          kn[ks]++;
+          if (!mbar_wait(v_empty(vs), vph ^ 1u, p.wc)) break;
+          mbar_arrive_expect_tx(v_full(vs), TILE_BYTES);
+          for (int hf = 0; hf < 2; ++hf)
+            tma_load_3d(sV + vs * TILE_BYTES + hf * HALF_BYTES, &tmV, v_full(vs), hf * 64, j * BKV, head);
+          vn[vs]++;
+        }
+        // drain outstanding loads before the CTA can exit
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < p.wc.timeout) {
+        }
+        for (int s = 0; s < 2; ++s) {
+          if (kn[s] > 0)
+            while (!mbar_try_wait(k_full(s), static_cast<uint32_t>(kn[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
+            }
+          if (vn[s] > 0)
+            while (!mbar_try_wait(v_full(s), static_cast<uint32_t>(vn[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
+            }
+        }
+      }
+    } else if (warp == 9) {
+      if (lane == 0) {
+        // ---------------- MMA issuer ----------------
+        bool ok = mbar_wait(q_full, 0, p.wc);
+        tc_fence_after();
+        auto issue_qk = [&](int q, int ks) {
+          const uint32_t d_tmem = tmem + static_cast<uint32_t>(q * BKV);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+            umma_f16_ss(d_tmem, sdesc_sw128(sQ + q * TILE_BYTES + off, 16, 1024),
+                        sdesc_sw128(sK + ks * TILE_BYTES + off, 16, 1024), IDESC_QK, kk != 0);
+          }
+        };
+        auto issue_pv = [&](int q, int vs, bool accumulate) {
+          const uint32_t d_tmem = tmem + static_cast<uint32_t>(2 * BKV + q * D);
+          const uint32_t p_tmem = tmem + static_cast<uint32_t>(q * BKV);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_f16_ts(d_tmem, p_tmem + 8u * kk, sdesc_sw128(sV + vs * TILE_BYTES + kk * 2048, HALF_BYTES, 1024),
+                        IDESC_PV, accumulate || kk != 0);
+        };
+        for (int j = 0; j < nkv && ok; ++j) {
+          const int ks = j % KST;
+          if (!mbar_wait(k_full(ks), static_cast<uint32_t>(j / KST) & 1u, p.wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int vprev = (j - 1) % VST;
+          for (int q = 0; q < 2 && ok; ++q) {
+            if (j > 0) {
+              if (!mbar_wait(p_full(q), static_cast<uint32_t>(j - 1) & 1u, p.wc)) {
+                ok = false;
+                break;
+              }
+              if (q == 0 && !mbar_wait(v_full(vprev), static_cast<uint32_t>((j - 1) / VST) & 1u, p.wc)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(q, vprev, j > 1);
+              if (q == 1) umma_commit(v_empty(vprev));
+            }
+            issue_qk(q, ks);
+            umma_commit(s_full(q));
+          }
+          if (!ok) break;
+          umma_commit(k_empty(ks));
+        }
+        if (ok) {
+          const int j = nkv;
+          const int vprev = (j - 1) % VST;
+          for (int q = 0; q < 2; ++q) {
+            if (!mbar_wait(p_full(q), static_cast<uint32_t>(j - 1) & 1u, p.wc)) break;
+            if (q == 0 && !mbar_wait(v_full(vprev), static_cast<uint32_t>((j - 1) / VST) & 1u, p.wc)) break;
+            tc_fence_after();
+            issue_pv(q, vprev, j > 1);
+            umma_commit(o_full(q));
+          }
+        }
+        umma_commit(done_bar);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(done_bar, 0) && globaltimer() - t0 < p.wc.timeout) {
+        }
+      }
+    } else {
+      // ---------------- softmax + epilogue (warps 0-7) ----------------
+      const int q = warp >> 2;
+      const int sub = warp & 3;
+      const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
+      const uint32_t s_tmem = tmem + lane_addr + static_cast<uint32_t>(q * BKV);
+      const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(2 * BKV + q * D);
+      const float c = p.scale_log2;
+      float m_run = -INFINITY, l_run = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        if (!mbar_wait(s_full(q), static_cast<uint32_t>(j) & 1u, p.wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t s[128];
+        tmem_ld32_at<0>(s_tmem + 0, s);
+        tmem_ld32_at<32>(s_tmem + 32, s);
+        tmem_ld32_at<64>(s_tmem + 64, s);
+        tmem_ld32_at<96>(s_tmem + 96, s);
+        tmem_ld_wait();
+        const int64_t kv_left = p.valid_kv - static_cast<int64_t>(j) * BKV;
+        if (kv_left < BKV) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= kv_left) s[i] = __float_as_uint(-INFINITY);
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+        const float m_new = fmaxf(m_run, mx * c);
+        const bool need = j > 0 && (m_new - m_run > RESCALE_THRESHOLD);
+        if (j == 0) {
+          m_run = m_new;
+        } else if (__any_sync(0xffffffffu, need)) {
+          // rescale this warp's rows of O (warp-collective TMEM access; rows that need none use alpha = 1)
+          const float alpha = need ? ex2(m_run - m_new) : 1.0f;
+          if (need) {
+            l_run *= alpha;
+            m_run = m_new;
+          }
+#pragma unroll 1
+          for (int cc = 0; cc < D; cc += 8) {
+            uint32_t o[8];
+            tmem_ld8(o_tmem + cc, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st8(o_tmem + cc, o);
+          }
+          tmem_st_wait();
+        }
+        const float neg_m = -m_run;
+        float lsum = 0.0f;
+        // P (16-bit pairs) goes to columns [0, 64) of S_q: chunk cc covers keys [32cc, 32cc+32) -> columns
+        // [16cc, 16cc+16), all of which were read into registers above
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float e0 = ex2(fmaf(__uint_as_float(s[32 * cc + 2 * i]), c, neg_m));
+            const float e1 = ex2(fmaf(__uint_as_float(s[32 * cc + 2 * i + 1]), c, neg_m));
+            lsum += e0 + e1;
+            pk[i] = pack_p<F16>(e0, e1);
+          }
+          tmem_st16(s_tmem + 16 * cc, pk);
+        }
+        l_run += lsum;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full(q));
+      }
+      if (ok && mbar_wait(o_full(q), 0, p.wc)) {
+        tc_fence_after();
+        const int64_t row = q0 + q * BQ + sub * 32 + lane;
+        const float inv_l = 1.0f / l_run;
+        uint16_t* orow = p.o + row * p.o_tok + static_cast<int64_t>(head) * p.o_head;
+#pragma unroll
+        for (int cc = 0; cc < D; cc += 32) {
+          uint32_t o[32];
+          tmem_ld32(o_tmem + cc, o);
+          tmem_ld_wait();
+          if (row < p.s_q) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv_l,
+                                                         __uint_as_float(o[8 * v + 2 * e + 1]) * inv_l);
+                w[e] = *reinterpret_cast<uint32_t*>(&b);
+              }
+              *reinterpret_cast<uint4*>(orow + cc + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace attn
+}  // namespace h3b
+
+using namespace h3b;
+
+static int make_qkv_map(CUtensorMap* m, const void* base, int64_t tokens, int heads, int64_t tok_stride,
+                        int64_t head_stride) {
+  const uint64_t dims[3] = {128, static_cast<uint64_t>(tokens), static_cast<uint64_t>(heads)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(tok_stride) * 2, static_cast<uint64_t>(head_stride) * 2};
+  const uint32_t box[3] = {64, 128, 1};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                  int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok,
+                                  int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads,
+                                  int32_t head_dim, float scale, int32_t v_f16, const int32_t* range_flag,
+                                  h3b_stream_t stream) {
+  using namespace h3b::attn;
+  if (s_q < 0 || s_kv <= 0 || heads <= 0) return fail(H3B_EINVAL, "flash_attn: s_q %lld s_kv %lld heads %d", (long long)s_q, (long long)s_kv, heads);
+  if (head_dim != 128) return fail(H3B_EUNSUPPORTED, "flash_attn: head_dim %d (only 128)", head_dim);
+  if (valid_kv < 0) valid_kv = s_kv;
+  if (valid_kv == 0 || valid_kv > s_kv) return fail(H3B_EINVAL, "flash_attn: valid_kv %lld of %lld", (long long)valid_kv, (long long)s_kv);
+  if (s_q == 0) return H3B_OK;
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return fail(H3B_EINVAL, "flash_attn: null pointer");
+  if (heads > 65535 || s_q > (1ll << 31) - 1 || s_kv > (1ll << 31) - 1) return fail(H3B_EUNSUPPORTED, "flash_attn: size limits");
+  const int64_t strides[8] = {q_tok, q_head, k_tok, k_head, v_tok, v_head, o_tok, o_head};
+  for (int64_t s : strides)
+    if (s <= 0 || s % 8) return fail(H3B_EALIGN, "flash_attn: token/head strides must be positive multiples of 8");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(o)) & 15u)
+    return fail(H3B_EALIGN, "flash_attn: q, k, v, o must be 16-byte aligned");
+
+  CUtensorMap tq, tk, tv;
+  int rc = make_qkv_map(&tq, q, s_q, heads, q_tok, q_head);
+  if (!rc) rc = make_qkv_map(&tk, k, s_kv, heads, k_tok, k_head);
+  if (!rc) rc = make_qkv_map(&tv, v, s_kv, heads, v_tok, v_head);
+  if (rc) return rc;
+
+  Params p{};
+  p.s_q = s_q;
+  p.s_kv = s_kv;
+  p.valid_kv = valid_kv;
+  p.heads = heads;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = static_cast<uint16_t*>(o);
+  p.o_tok = o_tok;
+  p.o_head = o_head;
+  p.nkv = static_cast<int>((valid_kv + BKV - 1) / BKV);
+  p.range_flag = v_f16 ? range_flag : nullptr;
+  p.wc.status = device_status_word();
+  p.wc.timeout = wait_timeout_ns();
+  if (p.wc.status == nullptr) return fail(H3B_ECUDA, "flash_attn: device status word");
+
+  static bool attr_set[2][64] = {{false}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int vi = v_f16 ? 1 : 0;
+  if (dev >= 0 && dev < 64 && !attr_set[vi][dev]) {
+    cudaError_t e = v_f16 ? cudaFuncSetAttribute(flash_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES)
+                          : cudaFuncSetAttribute(flash_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "flash_attn: smem attribute");
+    attr_set[vi][dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(heads));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (v_f16)
+    flash_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else
+    flash_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  H3B_CHECK_LAUNCH("flash_attn launch");
+  return H3B_OK;
+}

@@ -1,0 +1,105 @@
+"""The DiT attention block of the hot path, built from the h3b kernels (one rank of a Ulysses group).
+
+    x [M, C] bf16 (this rank's sequence rows)
+      -> per-token e4m3 quant                                  (ops.quant; fp8_quant_fuse qkv site)
+      -> qkv FP8 GEMM, epilogue writes q, k, v straight into the send buffers [P, M, H/P, d]
+         (v as f16, exactly converted from its bf16 value, for the f16 P.V product)
+      -> seq->head all-to-all x3 (NCCL over NVLink; skipped at P = 1)
+      -> flash attention over all P*M tokens for H/P heads     (tcgen05, non-causal, d = 128)
+      -> head->seq all-to-all of the output as is (skipped at P = 1)
+      -> per-token quant straight from the receive buffer      (ulysses_outq: no unpack copy)
+      -> out FP8 GEMM -> y [M, C] bf16
+This is the reference's ``ULYSSES_EXACT=2`` + ``FP8_GEMM`` + quant-fuse data flow (h3_tp2/ulysses_exact.py:187-220,
+h3_tp2/ulysses_outq.py:138, h3_tp2/fp8_gemm.py:149) with the pack copies moved into the GEMM epilogue.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+FP8_MAX = 448.0
+MIN_SCALE = 1.0 / (FP8_MAX * 512.0)
+
+
+def quant_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Online per-output-channel e4m3 weight quant (load time, not the hot path): sb = max(absmax/448, 1/229376)."""
+    wf = w.float()
+    sb = torch.clamp(wf.abs().amax(dim=1) / FP8_MAX, min=MIN_SCALE)
+    w8 = torch.clamp(wf / sb[:, None], -FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return w8.contiguous(), sb.contiguous()
+
+
+def block_flops(tokens: int, hidden: int, heads: int, head_dim: int = 128) -> dict:
+    hd = heads * head_dim
+    return {"attention": 4.0 * tokens * tokens * head_dim * heads,
+            "qkv": 2.0 * tokens * hidden * 3 * hd,
+            "out": 2.0 * tokens * hd * hidden}
+
+
+class AttentionBlock:
+    def __init__(self, hidden: int, heads: int, *, device, head_dim: int = 128, seed: int = 1, ws: int = 1, pg=None,
+                 weights: tuple | None = None, init_device=None, a2a=None):
+        if head_dim != 128:
+            raise ValueError("head_dim 128 only")
+        if heads % ws:
+            raise ValueError(f"heads {heads} not divisible by the Ulysses degree {ws}")
+        self.hidden, self.heads, self.head_dim, self.ws, self.pg = hidden, heads, head_dim, ws, pg
+        self.device = torch.device(device)
+        if weights is None:
+            gdev = torch.device(init_device) if init_device is not None else torch.device("cpu")
+            g = torch.Generator(device=gdev).manual_seed(seed)
+            wqkv = torch.randn(3 * heads * head_dim, hidden, generator=g, device=gdev) * 0.02
+            wo = torch.randn(hidden, heads * head_dim, generator=g, device=gdev) * 0.02
+            weights = (*quant_weight(wqkv), *quant_weight(wo))
+        self.wqkv8, self.sqkv, self.wo8, self.so = (t.to(self.device) for t in weights)
+        self.range_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.a2a = a2a   # injected collective a2a(out, inp, group=None); default: NCCL all_to_all_single
+
+    def exchange(self, send: torch.Tensor) -> torch.Tensor:
+        if self.ws == 1:
+            return send
+        recv = torch.empty_like(send)
+        if self.a2a is not None:
+            self.a2a(recv, send, group=self.pg)
+        else:
+            dist.all_to_all_single(recv, send, group=self.pg)
+        return recv
+
+    STAGES = ("quant_x", "qkv_gemm", "a2a_fwd", "attention", "a2a_back", "quant_out", "out_gemm")
+
+    def forward(self, x: torch.Tensor, marks: list | None = None) -> torch.Tensor:
+        """x [M, C] bf16 -> y [M, C] bf16.  ``marks``: if a list, a CUDA event is recorded on the current stream
+        after each stage (``STAGES``), preceded by one at the start, for per-stage device timing."""
+        def mark():
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append(ev)
+
+        m = x.shape[0]
+        hl, d = self.heads // self.ws, self.head_dim
+        mark()
+        q8, sx = ops.quant(x)
+        mark()
+        sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+                                      range_flag=self.range_flag)
+        mark()
+        q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
+        mark()
+        o = ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d), range_flag=self.range_flag)
+        mark()
+        back = self.exchange(o.view(self.ws, m, hl, d))
+        mark()
+        o8, so = ops.quant_from_recv(back)
+        mark()
+        y = ops.fp8_gemm(o8, self.wo8, so, self.so)
+        mark()
+        return y
+
+    KERNELS_PER_FORWARD = 5   # h3b launches per forward: quant, qkv GEMM, attention, quant, out GEMM
+
+    __call__ = forward

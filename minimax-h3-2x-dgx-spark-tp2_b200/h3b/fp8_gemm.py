@@ -1,0 +1,95 @@
+"""Drop-in for ``ops.cutlass_scaled_mm`` on per-token x per-channel scaled FP8 linears.
+
+Mirrors ``h3_tp2/fp8_gemm.py``: ``scaled_mm_tensor32(a, b, scale_a, scale_b, out_dtype, bias)`` (a [M, K] e4m3
+row-major, b [K, N] e4m3 with ``b.t()`` contiguous, scale_a [M, 1] or scalar fp32, scale_b [N] or scalar fp32) ->
+[M, N] in bf16/fp16, with the epilogue ``y = out(sa[m] * (sb[n] * acc))`` (bias by fma).  On B200 every level runs
+the one tcgen05 kernel with the epilogue fused (no fp32 product, no second pass); routers and stash hooks keep the
+reference's dispatch order (``route``).
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+
+from . import ops
+
+logger = logging.getLogger("h3b.fp8_gemm")
+
+_state = {"level": "tcgen05", "installed": False}
+_stash_hooks: list = []
+_routers: list = []
+
+
+def eligible(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, out_dtype,  # noqa: ANN001
+             bias: torch.Tensor | None) -> bool:
+    """The dispatcher's guards (h3_tp2/fp8_gemm.py:364-372)."""
+    M, N = a.shape[0], b.shape[-1]
+    return not (a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]
+                or (scale_a.numel() == 1 and scale_b.numel() == 1)
+                or scale_a.numel() not in (1, M) or scale_b.numel() not in (1, N)
+                or scale_a.dtype != torch.float32 or scale_b.dtype != torch.float32
+                or a.dtype != torch.float8_e4m3fn or b.dtype != torch.float8_e4m3fn
+                or a.device != b.device or out_dtype not in (torch.bfloat16, torch.float16)
+                or (bias is not None and (bias.dim() != 1 or bias.numel() != N))
+                or not a.is_contiguous() or not b.t().is_contiguous() or a.shape[1] % 16 or N % 16)
+
+
+def scaled_mm(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, out_dtype: torch.dtype,
+              bias: torch.Tensor | None = None) -> torch.Tensor:
+    """One tcgen05 FP8 GEMM with the scaled epilogue (the reference's ``scaled_mm_tensor32`` / ``scaled_mm_fused`` /
+    ``fp8_cutlass.scaled_mm`` arithmetic)."""
+    return ops.fp8_gemm(a, b.t(), scale_a, scale_b, bias, out_dtype)
+
+
+scaled_mm_tensor32 = scaled_mm     # h3_tp2/fp8_gemm.py:149
+scaled_mm_fused = scaled_mm        # h3_tp2/fp8_gemm.py:240
+
+
+def epilogue_reference_order() -> str:
+    return "t = scale_b * acc; y = scale_a * t (bias: fma(scale_a, t, bias)); one rounding"
+
+
+def set_stash_hook(fn) -> None:  # noqa: ANN001
+    if fn not in _stash_hooks:
+        _stash_hooks.append(fn)
+
+
+def set_router(fn) -> None:  # noqa: ANN001
+    if fn not in _routers:
+        _routers.append(fn)
+
+
+def route(a, b, scale_a, scale_b, out_dtype, bias=None, two_pass=None):  # noqa: ANN001,ANN201
+    """Routers, then stash hooks, then the GEMM (h3_tp2/fp8_gemm.py:328)."""
+    for router in _routers:
+        y = router(a, b, scale_a, scale_b, out_dtype, bias)
+        if y is not None:
+            return y
+    for hook in _stash_hooks:
+        ph = hook(a, b, scale_a, scale_b, out_dtype, bias)
+        if ph is not None:
+            return ph
+    return (two_pass or scaled_mm)(a, b, scale_a, scale_b, out_dtype, bias)
+
+
+def install(level: str = "tensor32") -> None:
+    """Replace vLLM's ``_custom_ops.cutlass_scaled_mm`` for eligible calls (h3_tp2/fp8_gemm.py:344).  ``level`` is
+    accepted for compatibility ("tensor32", "fused", "cutlass"): all run the same fused tcgen05 kernel here."""
+    if level not in ("tensor32", "fused", "cutlass"):
+        raise ValueError(f"unknown FP8 GEMM level {level!r}")
+    from vllm import _custom_ops as vops  # noqa: PLC0415
+
+    orig = vops.cutlass_scaled_mm
+    if getattr(orig, "_h3b", False):
+        return
+
+    def _mm(a, b, scale_a, scale_b, out_dtype, bias=None):  # noqa: ANN001
+        if not (a.is_cuda and eligible(a, b, scale_a, scale_b, out_dtype, bias)):
+            return orig(a, b, scale_a, scale_b, out_dtype, bias)
+        return route(a, b, scale_a, scale_b, out_dtype, bias)
+
+    _mm._h3b = True
+    vops.cutlass_scaled_mm = _mm
+    _state.update(level=level, installed=True)
+    logger.info("h3b: FP8 GEMM (tcgen05, fused scaled epilogue) installed for level %s", level)

@@ -1,0 +1,371 @@
+"""Tensor-level entry points over the C ABI (``include/h3b.h``), and their ``torch.ops.h3b.*`` registrations.
+
+Every function takes CUDA tensors, allocates its outputs with torch on the tensor's device (the caching allocator of
+the current stream, as the reference does with ``torch.empty``) and enqueues one kernel on the current stream.
+CPU tensors raise: there is no CPU fallback in the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import DIV_FULL, DIV_IEEE, EPI_PLAIN, EPI_QKV_SEND, EPI_SWIGLU, OUT_BF16, OUT_F16  # noqa: F401
+
+E4M3 = torch.float8_e4m3fn
+FP8_MAX = 448.0
+MIN_SCALE = 1.0 / (FP8_MAX * 512.0)
+
+
+def _need_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("h3b kernels run on CUDA tensors only (no CPU fallback)")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _dt(t: torch.Tensor, *dtypes: torch.dtype, what: str) -> None:
+    if t.dtype not in dtypes:
+        raise TypeError(f"{what}: dtype {t.dtype}, expected one of {dtypes}")
+
+
+def vec_scales(scale_a: torch.Tensor, scale_b: torch.Tensor, M: int, N: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row / per-column fp32 scale vectors (a scalar scale is broadcast), as fp8_gemm._vec_scales
+    (h3_tp2/fp8_gemm.py:228-236)."""
+    sa = scale_a.reshape(-1).float()
+    sb = scale_b.reshape(-1).float()
+    if sa.numel() == 1:
+        sa = sa.expand(M)
+    if sb.numel() == 1:
+        sb = sb.expand(N)
+    return sa.contiguous(), sb.contiguous()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# per-token quant family
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def quant_rows(base: torch.Tensor, m: int, p: int, seg: int, stride_p: int, stride_m: int, *,
+               div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
+    """``ulysses_outq.quant_rows`` (h3_tp2/ulysses_outq.py:109): row m = concat_p base[p*stride_p + m*stride_m :][:seg]
+    (element offsets from ``base``'s data pointer).  Returns (q [m, p*seg] e4m3, scale [m, 1] fp32)."""
+    _need_cuda(base)
+    _dt(base, torch.bfloat16, what="quant_rows")
+    q = torch.empty((m, p * seg), dtype=E4M3, device=base.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=base.device)
+    if m:
+        _lib.call("h3b_quant_rows_e4m3", base.data_ptr(), m, p, seg, stride_p, stride_m, q.data_ptr(), s.data_ptr(),
+                  div_mode, _stream(base))
+    return q, s
+
+
+def quant(h: torch.Tensor, *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token dynamic e4m3 quant of a bf16 [M, K] tensor (``fp8_quant_fuse.quant``, h3_tp2/fp8_quant_fuse.py:318)."""
+    if h.dim() != 2 or h.stride(1) != 1:
+        raise ValueError("quant: h must be [M, K] with unit column stride")
+    M, K = h.shape
+    return quant_rows(h, M, 1, K, 0, h.stride(0), div_mode=div_mode)
+
+
+def quant_from_recv(recv: torch.Tensor, *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
+    """recv [P, M, hl, d] contiguous -> quant of the [M, P*hl*d] rows stock's unpack would make
+    (``ulysses_outq.quant_from_recv``, h3_tp2/ulysses_outq.py:138)."""
+    if not recv.is_contiguous():
+        raise ValueError("quant_from_recv: recv must be contiguous")
+    p, m, hl, d = recv.shape
+    seg = hl * d
+    return quant_rows(recv, m, p, seg, m * seg, seg, div_mode=div_mode)
+
+
+def rms_quant(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor | None = None,
+              scale: torch.Tensor | None = None, indices: torch.Tensor | None = None, eps: float = 1e-6,
+              ph: torch.Tensor | None = None, *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm (+ AdaLN modulation) + per-token quant (``fp8_quant_fuse.rms_quant``, h3_tp2/fp8_quant_fuse.py:330)."""
+    _need_cuda(x, weight, shift, scale, indices, ph)
+    rows, hidden = x.shape
+    q = torch.empty((rows, hidden), dtype=E4M3, device=x.device)
+    s = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
+    if indices is not None:
+        indices = indices.to(torch.int64).contiguous()
+    _lib.call("h3b_rms_quant_e4m3", x.data_ptr(), rows, hidden, x.stride(0), weight.contiguous().data_ptr(),
+              _ptr(shift), shift.stride(0) if shift is not None else 0, _ptr(scale),
+              scale.stride(0) if scale is not None else 0, _ptr(indices), float(eps), _ptr(ph), q.data_ptr(),
+              s.data_ptr(), div_mode, _stream(x))
+    return q, s
+
+
+def gate_rms_quant(residual: torch.Tensor, gate: torch.Tensor, branch: torch.Tensor, weight: torch.Tensor,
+                   shift: torch.Tensor | None, scale: torch.Tensor | None, indices: torch.Tensor | None, eps: float,
+                   *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gated residual + RMSNorm + modulation + quant (``fp8_quant_fuse.gate_rms_quant``,
+    h3_tp2/fp8_quant_fuse.py:350).  Returns (residual_out bf16, q e4m3, scale [M, 1])."""
+    _need_cuda(residual, gate, branch, weight, shift, scale, indices)
+    rows, hidden = residual.shape
+    res_out = torch.empty((rows, hidden), dtype=torch.bfloat16, device=residual.device)
+    q = torch.empty((rows, hidden), dtype=E4M3, device=residual.device)
+    s = torch.empty((rows, 1), dtype=torch.float32, device=residual.device)
+    if indices is not None:
+        indices = indices.to(torch.int64).contiguous()
+    _lib.call("h3b_gate_rms_quant_e4m3", residual.data_ptr(), residual.stride(0), gate.data_ptr(), gate.stride(0),
+              branch.data_ptr(), branch.stride(0), weight.contiguous().data_ptr(), _ptr(shift),
+              shift.stride(0) if shift is not None else 0, _ptr(scale), scale.stride(0) if scale is not None else 0,
+              _ptr(indices), rows, hidden, float(eps), res_out.data_ptr(), q.data_ptr(), s.data_ptr(), div_mode,
+              _stream(residual))
+    return res_out, q, s
+
+
+def silu_mul_quant(x: torch.Tensor, *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
+    """silu_and_mul on bf16 [M, 2d] + per-token quant (``fp8_quant_fuse.silu_mul_quant``, :392)."""
+    _need_cuda(x)
+    rows, width = x.shape
+    d = width // 2
+    q = torch.empty((rows, d), dtype=E4M3, device=x.device)
+    s = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
+    _lib.call("h3b_silu_mul_quant_e4m3", x.data_ptr(), rows, d, x.stride(0), q.data_ptr(), s.data_ptr(), div_mode,
+              _stream(x))
+    return q, s
+
+
+def scale_bias_cast(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None,
+                    out_dtype: torch.dtype) -> torch.Tensor:
+    """The two-pass path's scale pass (``fp8_gemm._scale_bias_cast``, h3_tp2/fp8_gemm.py:38)."""
+    _need_cuda(x32, sa, sb, bias)
+    M, N = x32.shape
+    sa, sb = vec_scales(sa, sb, M, N)
+    y = torch.empty((M, N), dtype=out_dtype, device=x32.device)
+    _lib.call("h3b_scale_bias_cast", x32.contiguous().data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
+              y.data_ptr(), M, N, OUT_BF16 if out_dtype == torch.bfloat16 else OUT_F16, _stream(x32))
+    return y
+
+
+def scale_swiglu(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """``fp8_swiglu.scale_swiglu`` (h3_tp2/fp8_swiglu.py:180): fp32 fc1 product -> bf16 SwiGLU [M, half]."""
+    _need_cuda(x32, sa, sb, bias)
+    M, width = x32.shape
+    half = width // 2
+    sa, sb = vec_scales(sa, sb, M, width)
+    y = torch.empty((M, half), dtype=torch.bfloat16, device=x32.device)
+    _lib.call("h3b_scale_swiglu", x32.contiguous().data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
+              y.data_ptr(), M, half, _stream(x32))
+    return y
+
+
+def scale_swiglu_quant(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None, *,
+                       div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
+    """``fp8_swiglu.scale_swiglu_quant`` (h3_tp2/fp8_swiglu.py:191): SwiGLU + per-token quant for fc2."""
+    _need_cuda(x32, sa, sb, bias)
+    M, width = x32.shape
+    half = width // 2
+    sa, sb = vec_scales(sa, sb, M, width)
+    q = torch.empty((M, half), dtype=E4M3, device=x32.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x32.device)
+    _lib.call("h3b_scale_swiglu_quant", x32.contiguous().data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
+              q.data_ptr(), s.data_ptr(), M, half, div_mode, _stream(x32))
+    return q, s
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# FP8 GEMM
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def _gemm_operands(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, N: int):
+    _need_cuda(a, w, sa, sb)
+    _dt(a, E4M3, what="fp8_gemm a")
+    _dt(w, E4M3, what="fp8_gemm w")
+    if a.dim() != 2 or w.dim() != 2 or a.stride(1) != 1 or w.stride(1) != 1 or a.shape[1] != w.shape[1]:
+        raise ValueError("fp8_gemm: a [M, K] and w [N, K] with unit column strides")
+    M = a.shape[0]
+    return vec_scales(sa, sb, M, N)
+
+
+def fp8_gemm(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None = None,
+             out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [M, N] = out_dtype(sa[m] * (sb[n] * (a @ w.T))) (bias by fma): the fused tcgen05 FP8 GEMM.  ``w`` is the
+    weight [N, K] (the reference's ``b`` is ``w.t()``)."""
+    N = w.shape[0]
+    sa, sb = _gemm_operands(a, w, sa, sb, N)
+    M, K = a.shape
+    y = out if out is not None else torch.empty((M, N), dtype=out_dtype, device=a.device)
+    _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
+              _ptr(bias), y.data_ptr(), y.stride(0), M, N, K, OUT_BF16 if y.dtype == torch.bfloat16 else OUT_F16,
+              EPI_PLAIN, None, _stream(a))
+    return y
+
+
+def fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor,
+                    bias: torch.Tensor | None = None) -> torch.Tensor:
+    """fc1 + SwiGLU in one kernel (``fp8_swiglu.gemm_swiglu``, h3_tp2/fp8_swiglu.py:230): w [2F, K] holds the gate
+    rows then the up rows; returns bf16 [M, F]."""
+    N = w.shape[0]
+    sa, sb = _gemm_operands(a, w, sa, sb, N)
+    M, K = a.shape
+    y = torch.empty((M, N // 2), dtype=torch.bfloat16, device=a.device)
+    _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
+              _ptr(bias), y.data_ptr(), y.stride(0), M, N, K, OUT_BF16, EPI_SWIGLU, None, _stream(a))
+    return y
+
+
+def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, heads: int, ws: int, *,
+                      bias: torch.Tensor | None = None, v_f16: bool = False, sends=None,
+                      range_flag: torch.Tensor | None = None):
+    """qkv projection whose epilogue writes q, k, v straight into the Ulysses send buffers [P, M, H/P, d] (the
+    producer redirection of ulysses_exact.fused_into_send, h3_tp2/ulysses_exact.py:278, moved into the GEMM)."""
+    N = w.shape[0]
+    sa, sb = _gemm_operands(a, w, sa, sb, N)
+    M, K = a.shape
+    if N != 3 * heads * 128 or heads % ws:
+        raise ValueError(f"fp8_gemm_qkv_send: N {N} != 3 * {heads} * 128 or heads % ws")
+    shape = (ws, M, heads // ws, 128)
+    if sends is None:
+        sends = [torch.empty(shape, dtype=torch.bfloat16, device=a.device) for _ in range(2)]
+        sends.append(torch.empty(shape, dtype=torch.float16 if v_f16 else torch.bfloat16, device=a.device))
+    desc = _lib.QkvSend()
+    for i in range(3):
+        if tuple(sends[i].shape) != shape or not sends[i].is_contiguous():
+            raise ValueError("fp8_gemm_qkv_send: send buffers must be contiguous [P, M, H/P, d]")
+        desc.send[i] = sends[i].data_ptr()
+    desc.heads, desc.head_dim, desc.ws, desc.v_f16 = heads, 128, ws, int(bool(v_f16))
+    desc.range_flag = _ptr(range_flag)
+    _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
+              _ptr(bias), None, 0, M, N, K, OUT_BF16, EPI_QKV_SEND, ctypes.byref(desc), _stream(a))
+    return sends
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def _as3(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise ValueError("flash_attn: batch 1 only (strict Ulysses at batch 1)")
+        t = t[0]
+    if t.dim() != 3 or t.stride(2) != 1:
+        raise ValueError("flash_attn: [S, H, d] (or [1, S, H, d]) with unit innermost stride")
+    return t
+
+
+def bf16_to_f16(x: torch.Tensor, range_flag: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(x)
+    y = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    _lib.call("h3b_bf16_to_f16", x.contiguous().data_ptr(), y.data_ptr(), x.numel(), _ptr(range_flag), _stream(x))
+    return y
+
+
+def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
+               valid_kv: int | None = None, out: torch.Tensor | None = None, pv_f16: bool = True,
+               range_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale) v, non-causal, head_dim 128, batch 1: q/k/v [S, H, d] or [1, S, H, d] (any token/head
+    strides that are multiples of 8).  bf16 v is converted exactly to f16 for the f16 P.V product unless
+    ``pv_f16=False``; an f16 v is used as is.  Returns o with q's shape (bf16, contiguous)."""
+    _need_cuda(q, k, v)
+    q3, k3, v3 = _as3(q), _as3(k), _as3(v)
+    _dt(q3, torch.bfloat16, what="flash_attn q")
+    _dt(k3, torch.bfloat16, what="flash_attn k")
+    s_q, heads, d = q3.shape
+    s_kv = k3.shape[0]
+    if v3.dtype == torch.bfloat16 and pv_f16:
+        if range_flag is None:
+            range_flag = torch.zeros(1, dtype=torch.int32, device=q.device)
+        v3 = bf16_to_f16(v3.contiguous(), range_flag)
+    _dt(v3, torch.bfloat16, torch.float16, what="flash_attn v")
+    o = out if out is not None else torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    o3 = _as3(o)
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(d)
+    _lib.call("h3b_flash_attn_fwd", q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0),
+              k3.stride(1), v3.data_ptr(), v3.stride(0), v3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1),
+              s_q, s_kv, -1 if valid_kv is None else int(valid_kv), heads, d, sc, int(v3.dtype == torch.float16),
+              _ptr(range_flag) if v3.dtype == torch.float16 else None, _stream(q))
+    return o
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Ulysses layout kernels
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def pack_by_dest(x: torch.Tensor, ws: int, out: torch.Tensor | None = None, *, to_f16: bool = False,
+                 range_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """x [M, H, d] (strided) -> send [P, M, H/P, d] contiguous (``ulysses_exact.pack_into``, :119)."""
+    _need_cuda(x)
+    m, h, d = x.shape
+    if x.stride(2) != 1:
+        raise ValueError("pack_by_dest: unit innermost stride needed")
+    dt = torch.float16 if to_f16 else x.dtype
+    send = out if out is not None else torch.empty((ws, m, h // ws, d), dtype=dt, device=x.device)
+    _lib.call("h3b_pack_by_dest", x.data_ptr(), m, h, d, x.stride(0), x.stride(1), ws, send.data_ptr(),
+              int(bool(to_f16)), _ptr(range_flag), _stream(x))
+    return send
+
+
+def unpack_recv(recv: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """recv [P, M, hl, d] -> [M, P*hl, d] contiguous (copy 5 of the reverse exchange, :181-183)."""
+    _need_cuda(recv)
+    p, m, hl, d = recv.shape
+    o = out if out is not None else torch.empty((m, p * hl, d), dtype=recv.dtype, device=recv.device)
+    _lib.call("h3b_unpack_recv", recv.contiguous().data_ptr(), p, m, hl, d, o.data_ptr(), _stream(recv))
+    return o
+
+
+def device_status() -> int:
+    """Read and clear the library's sticky device status word (0 = no device-side failure since the last read)."""
+    return _lib.device_status()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# torch.ops.h3b registrations (the op signatures the drop-in shims call)
+# ---------------------------------------------------------------------------------------------------------------
+
+_REGISTERED = False
+
+
+def register_torch_ops() -> None:
+    global _REGISTERED
+    if _REGISTERED:
+        return
+    from torch.library import custom_op
+
+    @custom_op("h3b::quant_rows", mutates_args=())
+    def _quant_rows(base: torch.Tensor, m: int, p: int, seg: int, stride_p: int, stride_m: int,
+                    div_mode: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return quant_rows(base, m, p, seg, stride_p, stride_m, div_mode=div_mode)
+
+    @custom_op("h3b::fp8_gemm", mutates_args=())
+    def _fp8_gemm(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor,
+                  bias: torch.Tensor | None, out_f16: bool) -> torch.Tensor:
+        return fp8_gemm(a, w, sa, sb, bias, torch.float16 if out_f16 else torch.bfloat16)
+
+    @custom_op("h3b::fp8_gemm_swiglu", mutates_args=())
+    def _fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor,
+                         bias: torch.Tensor | None) -> torch.Tensor:
+        return fp8_gemm_swiglu(a, w, sa, sb, bias)
+
+    @custom_op("h3b::flash_attn", mutates_args=())
+    def _flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, valid_kv: int) -> torch.Tensor:
+        return flash_attn(q, k, v, scale=scale, valid_kv=None if valid_kv < 0 else valid_kv)
+
+    @custom_op("h3b::rms_quant", mutates_args=())
+    def _rms_quant(x: torch.Tensor, weight: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+        return rms_quant(x, weight, eps=eps)
+
+    @custom_op("h3b::silu_mul_quant", mutates_args=())
+    def _silu_mul_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        return silu_mul_quant(x)
+
+    @custom_op("h3b::pack_by_dest", mutates_args=())
+    def _pack_by_dest(x: torch.Tensor, ws: int) -> torch.Tensor:
+        return pack_by_dest(x, ws)
+
+    _REGISTERED = True

@@ -1,0 +1,81 @@
+"""Plugin entry point with the reference's environment switches (mirrors the hot-path parts of ``h3_tp2/plugin.py``:
+``register`` :74, the Ulysses block :272-308 and the FP8 block :429-505).
+
+``register()`` is a no-op unless ``H3_TP2_ROLE`` is set; a required patch that fails exits the process with code 70,
+as the reference does.  The patches themselves need vLLM / vLLM-Omni in the serving environment.
+"""
+from __future__ import annotations
+
+import logging
+import os
+
+logger = logging.getLogger("h3b.plugin")
+
+
+def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
+    """(pg, ws) when vLLM-Omni would run strict Ulysses for ``layer`` with nothing this path does not handle
+    (no ring, no joint tensors, no masks), else None (h3_tp2/ulysses_nocopy.py:336-362)."""
+    from vllm_omni.diffusion.attention.parallel.ulysses import UlyssesParallelAttention  # noqa: PLC0415
+    from vllm_omni.diffusion.forward_context import get_ulysses_mode  # noqa: PLC0415
+    import torch.distributed as dist  # noqa: PLC0415
+
+    strategy = layer._get_active_parallel_strategy()
+    if not isinstance(strategy, UlyssesParallelAttention) or getattr(layer, "use_ring", False):
+        return None
+    if get_ulysses_mode(default="strict") != "strict":
+        return None
+    if attn_metadata is not None and any(getattr(attn_metadata, n, None) is not None for n in
+                                         ("attn_mask", "joint_query", "joint_key", "joint_value", "joint_attn_mask")):
+        return None
+    if (strategy._scatter_idx, strategy._gather_idx) != (2, 1):
+        return None
+    pg = strategy._ulysses_pg
+    return pg, dist.get_world_size(pg)
+
+
+def plan(env: dict | None = None) -> dict:
+    """The patches ``_apply`` would install for an environment (pure; used by tests)."""
+    env = os.environ if env is None else env
+    out = {"ulysses": None, "fp8_gemm": None, "quant_fuse": None, "overlap": None, "a2a_timing": False}
+    overlap = env.get("H3_TP2_A2A_OVERLAP", "0").strip()
+    exact = env.get("H3_TP2_ULYSSES_EXACT", "2").strip().lower()
+    if overlap not in ("", "0"):
+        out["overlap"] = int(overlap)
+    elif exact not in ("", "0"):
+        out["ulysses"] = exact
+    level = env.get("H3_TP2_FP8_GEMM", "cutlass").strip().lower()
+    if level not in ("", "0", "off"):
+        out["fp8_gemm"] = level
+    fuse = env.get("H3_TP2_FP8_QUANT_FUSE", "1").strip().lower()
+    if fuse not in ("", "0", "off"):
+        out["quant_fuse"] = fuse
+    out["a2a_timing"] = env.get("H3_TP2_A2A_TIMING", "0").strip() == "1"
+    return out
+
+
+def _apply(role: str) -> None:
+    p = plan()
+    logger.warning("h3b plugin (%s): %s", role, p)
+    if p["a2a_timing"]:
+        from . import a2a_timing  # noqa: PLC0415
+        a2a_timing.install()
+    if p["overlap"]:
+        from . import ulysses_overlap  # noqa: PLC0415
+        ulysses_overlap.install(p["overlap"])
+    elif p["ulysses"]:
+        from . import ulysses_exact  # noqa: PLC0415
+        ulysses_exact.install(p["ulysses"])
+    if p["fp8_gemm"]:
+        from . import fp8_gemm  # noqa: PLC0415
+        fp8_gemm.install(p["fp8_gemm"])
+
+
+def register() -> None:
+    role = os.environ.get("H3_TP2_ROLE", "").strip()
+    if not role:
+        return
+    try:
+        _apply(role)
+    except Exception:  # noqa: BLE001
+        logger.exception("h3b plugin: a required patch failed; exiting (70)")
+        os._exit(70)

@@ -1,0 +1,97 @@
+"""Ulysses sequence<->head exchange layouts, restated from the reference's stock oracle and exact path.
+
+Reference: the stock ``all_to_all_4D`` (vLLM-Omni ``comm.py:36-98``) as the reference reproduces it in
+``tests/test_ulysses_exact.py:74-99`` (``stock_all_to_all_4d``), the exact path's send layout
+``h3_tp2/ulysses_exact.py:108-127`` (``send_shape`` / ``by_dest`` / ``pack_into`` / ``unpack``), the forward
+exchange ``:130-135`` and the reverse exchange + unpack ``:156-184``.  ``FakeA2A`` emulates
+``all_to_all_single`` over threads with equal dim-0 splits, as ``tests/test_ulysses_exact.py:25-50`` does.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+
+def send_shape(m: int, heads: int, d: int, ws: int) -> tuple[int, int, int, int]:
+    return (ws, m, heads // ws, d)
+
+
+def pack(x: torch.Tensor, ws: int) -> torch.Tensor:
+    """[M, H, d] -> contiguous [P, M, H/P, d]; head h = p*(H/P) + j goes to rank p."""
+    m, h, d = x.shape
+    return x.reshape(m, ws, h // ws, d).permute(1, 0, 2, 3).contiguous()
+
+
+def unpack(send: torch.Tensor) -> torch.Tensor:
+    """[P, M, hl, d] -> contiguous [M, P*hl, d]."""
+    p, m, hl, d = send.shape
+    return send.permute(1, 0, 2, 3).reshape(m, p * hl, d).contiguous()
+
+
+def a2a_reference(sends: list[torch.Tensor]) -> list[torch.Tensor]:
+    """all_to_all_single with equal dim-0 splits over ranks given all ranks' send buffers: rank r receives the r-th
+    dim-0 chunk of every source, in source order."""
+    ws = len(sends)
+    return [torch.cat([sends[s].reshape(-1).chunk(ws)[r] for s in range(ws)]).view(sends[r].shape) for r in range(ws)]
+
+
+def stock_all_to_all_4d(x: torch.Tensor, scatter_idx: int, gather_idx: int, ws: int, a2a) -> torch.Tensor:
+    """Stock strict Ulysses exchange at any batch; ``a2a(out, inp)`` is the collective."""
+    if scatter_idx == 2 and gather_idx == 1:
+        bs, s_loc, hc, hs = x.shape
+        inp = x.reshape(bs, s_loc, ws, hc // ws, hs).permute(2, 1, 0, 3, 4).contiguous()   # [P, S/P, B, hc/P, hs]
+        out = torch.empty_like(inp)
+        a2a(out, inp)
+        return out.reshape(s_loc * ws, bs, hc // ws, hs).permute(1, 0, 2, 3).contiguous()
+    bs, seq, shc, hs = x.shape
+    s_loc = seq // ws
+    inp = x.reshape(bs, ws, s_loc, shc, hs).permute(1, 3, 2, 0, 4).contiguous()           # [P, shc, S/P, B, hs]
+    out = torch.empty_like(inp)
+    a2a(out, inp)
+    return out.reshape(shc * ws, s_loc, bs, hs).permute(2, 1, 0, 3).contiguous()
+
+
+class FakeA2A:
+    """``all_to_all_single`` over ``ws`` threads (one per rank), equal dim-0 splits, contiguous buffers."""
+
+    def __init__(self, ws: int):
+        self.ws = ws
+        self.barrier = threading.Barrier(ws, timeout=60)
+        self.slots: list = [None] * ws
+
+    def bind(self, rank: int):
+        def a2a(out, inp, group=None):  # noqa: ARG001
+            assert out.is_contiguous() and inp.is_contiguous() and out.numel() == inp.numel()
+            assert inp.shape[0] % self.ws == 0
+            self.slots[rank] = inp
+            self.barrier.wait()
+            out.view(-1).copy_(torch.cat([self.slots[s].reshape(-1).chunk(self.ws)[rank] for s in range(self.ws)]))
+            self.barrier.wait()
+        return a2a
+
+
+def run_ranks(fn, ws: int):
+    """Run ``fn(rank, a2a)`` on ``ws`` threads sharing one FakeA2A; returns the per-rank results."""
+    fake = FakeA2A(ws)
+    res, err = [None] * ws, [None] * ws
+
+    def body(r):
+        try:
+            res[r] = fn(r, fake.bind(r))
+        except BaseException as e:  # noqa: BLE001
+            err[r] = e
+            fake.barrier.abort()
+
+    ts = [threading.Thread(target=body, args=(r,)) for r in range(ws)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for e in err:
+        if e is not None and not isinstance(e, threading.BrokenBarrierError):
+            raise e
+    for e in err:
+        if e is not None:
+            raise e
+    return res

@@ -1,0 +1,78 @@
+"""The C-ABI library loads without a GPU and exports exactly what include/h3b.h declares; argument errors are
+reported on the host before any CUDA call."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from h3b import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "h3b.h"
+
+
+def declared():
+    text = HEADER.read_text()
+    return set(re.findall(r"^H3B_API\s+[^(]*?\b(h3b_\w+)\s*\(", text, flags=re.M))
+
+
+def exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T h3b_" in line}
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared()
+    assert len(names) >= 17
+    for n in names:
+        assert hasattr(lib, n), n
+    assert exported() == names
+
+
+def test_binding_signatures_cover_the_header():
+    assert set(_lib.SIGNATURES) == declared()
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.h3b_abi_version() == 1
+    assert lib.h3b_status_string(0) == b"ok"
+    assert lib.h3b_status_string(_lib.H3B_ETIMEOUT) == b"device wait timed out"
+
+
+@pytest.mark.parametrize("call,status", [
+    (lambda L: L.h3b_quant_rows_e4m3(None, -1, 1, 8, 0, 8, None, None, 0, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_quant_rows_e4m3(None, 4, 1, 8, 0, 8, None, None, 7, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_quant_rows_e4m3(None, 0, 1, 8, 0, 8, None, None, 0, None), _lib.H3B_OK),
+    (lambda L: L.h3b_fp8_gemm(1, 16, 1, 16, 1, 1, None, 1, 16, 4, 24, 16, 0, 0, None, None), _lib.H3B_EUNSUPPORTED),
+    (lambda L: L.h3b_fp8_gemm(1, 16, 1, 16, 1, 1, None, 1, 16, 4, 32, 16, 0, 9, None, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_fp8_gemm(None, 16, 1, 16, 1, 1, None, 1, 16, 4, 32, 16, 0, 0, None, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_flash_attn_fwd(1, 8, 8, 1, 8, 8, 1, 8, 8, 1, 8, 8, 4, 4, -1, 1, 64, 1.0, 0, None, None),
+     _lib.H3B_EUNSUPPORTED),
+    (lambda L: L.h3b_flash_attn_fwd(1, 8, 8, 1, 8, 8, 1, 8, 8, 1, 8, 8, 4, 4, 9, 1, 128, 1.0, 0, None, None),
+     _lib.H3B_EINVAL),
+    (lambda L: L.h3b_flash_attn_fwd(1, 8, 8, 1, 12, 8, 1, 8, 8, 1, 8, 8, 4, 4, -1, 1, 128, 1.0, 0, None, None),
+     _lib.H3B_EALIGN),
+    (lambda L: L.h3b_pack_by_dest(1, 4, 6, 128, 768, 128, 4, 1, 0, None, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_rms_quant_e4m3(1, 4, 64, 64, 1, 1, 64, None, 0, None, 1e-6, None, 1, 1, 0, None),
+     _lib.H3B_EINVAL),
+])
+def test_host_side_argument_errors(call, status):
+    lib = _lib.load()
+    assert call(lib) == status
+    if status != _lib.H3B_OK:
+        assert lib.h3b_last_error()
+
+
+def test_check_raises_with_the_reason():
+    lib = _lib.load()
+    rc = lib.h3b_quant_rows_e4m3(None, -1, 1, 8, 0, 8, None, None, 0, None)
+    with pytest.raises(_lib.H3BError, match="quant_rows"):
+        _lib.check(rc, "h3b_quant_rows_e4m3")
+
+
+def test_qkv_send_struct_layout():
+    assert ctypes.sizeof(_lib.QkvSend) == 3 * 8 + 4 * 4 + 8

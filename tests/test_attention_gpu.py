@@ -1,0 +1,82 @@
+"""tcgen05 flash attention against an fp32 SDPA on the same bf16 inputs: rel-L2 <= 2e-3 and max-abs <= 2e-2."""
+import pytest
+import torch
+
+from _util import BF16, rel_l2
+from h3b import ops
+from oracle import attention as oa
+
+pytestmark = pytest.mark.gpu
+
+
+def _qkv(s_q, s_kv, h, seed, vscale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(s_q, h, 128, generator=g).to(BF16)
+    k = torch.randn(s_kv, h, 128, generator=g).to(BF16)
+    v = (torch.randn(s_kv, h, 128, generator=g) * vscale).to(BF16)
+    return q, k, v
+
+
+def _check(o, ref, tol_rel=2e-3, tol_abs=2e-2):
+    o = o.float().cpu()
+    assert rel_l2(o, ref) <= tol_rel, rel_l2(o, ref)
+    assert (o - ref).abs().max().item() <= tol_abs
+
+
+@pytest.mark.parametrize("s,h", [(128, 1), (256, 2), (300, 2), (1000, 3), (4096, 2)])
+def test_self_attention_shapes(dev, s, h):
+    q, k, v = _qkv(s, s, h, seed=s + h)
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev))
+    _check(o, oa.sdpa(q, k, v))
+    assert ops.device_status() == 0
+
+
+def test_cross_lengths_and_valid_kv(dev):
+    q, k, v = _qkv(200, 777, 2, seed=1)
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev))
+    _check(o, oa.sdpa(q, k, v))
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), valid_kv=517)
+    _check(o, oa.sdpa(q, k, v, valid_kv=517))
+
+
+def test_peaked_scores_rescale_path(dev):
+    # large q scale: the running max jumps by many binades between key tiles (exercises the O rescale)
+    g = torch.Generator().manual_seed(3)
+    q = (torch.randn(512, 2, 128, generator=g) * 4).to(BF16)
+    k = (torch.randn(2048, 2, 128, generator=g)).to(BF16)
+    k[1500:1510] *= 3
+    v = torch.randn(2048, 2, 128, generator=g).to(BF16)
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev))
+    _check(o, oa.sdpa(q, k, v))
+
+
+def test_bf16_pv_variant(dev):
+    q, k, v = _qkv(1024, 1024, 2, seed=7)
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), pv_f16=False)
+    _check(o, oa.sdpa(q, k, v), tol_rel=4e-3)
+
+
+def test_ulysses_receive_views_and_head_independence(dev):
+    # q/k/v as the [1, P*M, hl, d] receive views; heads computed alone equal heads computed together (bitwise)
+    s, h = 640, 4
+    q, k, v = _qkv(s, s, h, seed=11)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    o_all = ops.flash_attn(qd.unsqueeze(0), kd.unsqueeze(0), vd.unsqueeze(0))
+    for h0 in range(0, h, 2):
+        o_part = ops.flash_attn(qd[:, h0:h0 + 2].contiguous(), kd[:, h0:h0 + 2].contiguous(),
+                                vd[:, h0:h0 + 2].contiguous())
+        assert torch.equal(o_part.view(torch.int16), o_all[0, :, h0:h0 + 2].contiguous().view(torch.int16))
+    _check(o_all[0], oa.sdpa(q, k, v))
+    # strided (non-contiguous head slice) inputs
+    o_str = ops.flash_attn(qd[:, 1:3], kd[:, 1:3], vd[:, 1:3])
+    assert torch.equal(o_str.view(torch.int16), o_all[0, :, 1:3].contiguous().view(torch.int16))
+
+
+def test_f16_range_flag_refuses(dev):
+    q, k, v = _qkv(128, 128, 1, seed=2)
+    v[5, 0, 3] = 80000.0
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), range_flag=flag)
+    assert ops.device_status() == ops._lib.H3B_ERANGE
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), pv_f16=False)
+    assert torch.isfinite(o.float()).all()

@@ -1,0 +1,133 @@
+"""The tcgen05 FP8 GEMM against the reference's golden vectors (integer inputs: exact in any summation order) and the
+reference's two-pass arithmetic (torch._scaled_mm fp32 product + the eager scale pass) on DiT shapes."""
+import pytest
+import torch
+
+from _util import BF16, E4M3, F16, rel_l2, same_bits, t8, t16, tf, ulp_diff_bf16
+from h3b import fp8_gemm, ops
+from oracle import gemm as og
+from oracle import ulysses as ou
+
+pytestmark = pytest.mark.gpu
+
+# BASELINE shapes (N, K): qkv, out, fc1 (gate|up), fc2
+SHAPES = {"qkv": (15360, 5120), "out": (5120, 5120), "fc1": (27648, 5120), "fc2": (5120, 13824)}
+
+
+def _quant_rows(rows, cols, std, g, dev):
+    x = (torch.randn(rows, cols, generator=g, device=dev) * std).to(BF16).float()
+    s = torch.clamp(x.abs().amax(dim=1) / 448.0, min=1.0 / (448.0 * 512.0))
+    return torch.clamp(x / s[:, None], -448.0, 448.0).to(E4M3), s
+
+
+def _serving_like(M, N, K, seed, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    a, sa = _quant_rows(M, K, torch.exp(torch.randn(M, 1, device=dev, generator=g) * 1.5), g, dev)
+    w, sb = _quant_rows(N, K, 0.02, g, dev)
+    return a, w, sa, sb
+
+
+def _two_pass(a, w, sa, sb, out_dtype=BF16):
+    one = torch.ones((), device=a.device)
+    acc = torch._scaled_mm(a, w.t(), scale_a=one, scale_b=one, out_dtype=torch.float32)
+    return ((sb.view(1, -1) * acc) * sa.view(-1, 1)).to(out_dtype)
+
+
+def test_integer_inputs_golden_exact_with_guards(dev, golden):
+    g = golden("gemm")
+    a, w = t8(g["int_a"]).to(dev), t8(g["int_w"]).to(dev)
+    sa, sb = tf(g["int_sa"]).to(dev), tf(g["int_sb"]).to(dev)
+    M, N = a.shape[0], w.shape[0]
+    guard = 4096
+    buf = torch.full((M * N + 2 * guard,), float("nan"), device=dev, dtype=BF16)
+    buf[:guard] = 7.0
+    buf[-guard:] = 7.0
+    y = buf[guard:guard + M * N].view(M, N)
+    ops.fp8_gemm(a, w, sa, sb, out=y)
+    assert same_bits(y.cpu(), t16(g["int_y"]))
+    assert bool((buf[:guard] == 7.0).all()) and bool((buf[-guard:] == 7.0).all())
+    yb = ops.fp8_gemm(a, w, sa, sb, t16(g["int_bias"]).to(dev))
+    assert (yb.cpu().view(torch.int16) != t16(g["int_ybias"]).view(torch.int16)).sum().item() <= 2
+    y16 = ops.fp8_gemm(a, w, sa, sb, out_dtype=F16)
+    assert same_bits(y16.cpu(), t16(g["int_yf16"], F16))
+    assert ops.device_status() == 0
+
+
+def test_random_golden_close(dev, golden):
+    g = golden("gemm")
+    y = ops.fp8_gemm(t8(g["rnd_a"]).to(dev), t8(g["rnd_w"]).to(dev), tf(g["rnd_sa"]).to(dev), tf(g["rnd_sb"]).to(dev))
+    assert int(ulp_diff_bf16(y.cpu(), t16(g["rnd_y"])).max()) <= 1
+
+
+@pytest.mark.parametrize("M", [1, 200, 1000, 4100])
+@pytest.mark.parametrize("shape", list(SHAPES))
+def test_dit_shapes_against_two_pass(dev, shape, M):
+    N, K = SHAPES[shape]
+    a, w, sa, sb = _serving_like(M, N, K, seed=M * 7 + N, dev=dev)
+    y = fp8_gemm.scaled_mm(a, w.t(), sa.view(M, 1), sb, BF16)
+    ref = _two_pass(a, w, sa, sb)
+    assert rel_l2(y.float(), ref.float()) <= 1e-3          # the contract is 1e-2; the epilogue is the reference's
+    ud = ulp_diff_bf16(y.cpu(), ref.cpu())
+    assert int(ud.max()) <= 2 and (ud == 0).float().mean().item() > 0.95
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (200, 400, 512), (333, 272, 1024), (129, 5376, 7168),
+                                   (8200, 144, 320)])
+def test_integer_partial_tiles_exact(dev, M, N, K):
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    a = torch.randint(-4, 5, (M, K), device=dev, generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), device=dev, generator=g).to(E4M3)
+    sa = torch.exp(torch.empty(M, device=dev).uniform_(-9.0, -2.0, generator=g))
+    sb = torch.exp(torch.empty(N, device=dev).uniform_(-9.5, -7.5, generator=g))
+    y = ops.fp8_gemm(a, w, sa, sb)
+    ref = og.scaled_mm(a.cpu(), w.cpu(), sa.cpu(), sb.cpu())
+    assert same_bits(y.cpu(), ref)
+
+
+def test_swiglu_epilogue_integer_inputs(dev):
+    M, F, K = 300, 384, 512
+    g = torch.Generator(device=dev).manual_seed(3)
+    a = torch.randint(-4, 5, (M, K), device=dev, generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (2 * F, K), device=dev, generator=g).to(E4M3)
+    sa = torch.rand(M, device=dev, generator=g) * 0.05 + 0.01
+    sb = torch.rand(2 * F, device=dev, generator=g) * 0.05 + 0.01
+    y = ops.fp8_gemm_swiglu(a, w, sa, sb).cpu()
+    ref = og.swiglu_epilogue(og.accumulate(a.cpu(), w.cpu()), sa.cpu(), sb.cpu(), None)
+    ud = ulp_diff_bf16(y, ref)
+    assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.99
+
+
+@pytest.mark.parametrize("ws", [1, 2, 4, 8])
+def test_qkv_send_epilogue_layout(dev, ws):
+    M, heads, K = 150, 8, 256
+    N = 3 * heads * 128
+    g = torch.Generator(device=dev).manual_seed(ws)
+    a = torch.randint(-4, 5, (M, K), device=dev, generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), device=dev, generator=g).to(E4M3)
+    sa = torch.rand(M, device=dev, generator=g) * 0.05
+    sb = torch.rand(N, device=dev, generator=g) * 0.05
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    sq, sk, sv = ops.fp8_gemm_qkv_send(a, w, sa, sb, heads, ws, v_f16=True, range_flag=flag)
+    y = ops.fp8_gemm(a, w, sa, sb).cpu()
+    q, k, v = (t.reshape(M, heads, 128) for t in y.split(heads * 128, dim=1))
+    assert same_bits(sq.cpu(), ou.pack(q, ws)) and same_bits(sk.cpu(), ou.pack(k, ws))
+    assert sv.dtype == F16 and torch.equal(sv.cpu().float(), ou.pack(v, ws).float())
+    assert int(flag.item()) == 0
+
+
+def test_side_stream(dev):
+    a, w, sa, sb = _serving_like(1000, 5120, 5120, seed=5, dev=dev)
+    ref = ops.fp8_gemm(a, w, sa, sb)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        y = ops.fp8_gemm(a, w, sa, sb)
+    torch.cuda.current_stream().wait_stream(s)
+    assert same_bits(y.cpu(), ref.cpu())
+
+
+def test_deterministic_repeat(dev):
+    a, w, sa, sb = _serving_like(4100, 15360, 5120, seed=9, dev=dev)
+    y0 = ops.fp8_gemm(a, w, sa, sb)
+    for _ in range(3):
+        assert torch.equal(ops.fp8_gemm(a, w, sa, sb).view(torch.int16), y0.view(torch.int16))

@@ -1,0 +1,100 @@
+"""Host-side logic of the drop-in modules on the CPU: the Ulysses orchestration with injected layout functions and a
+threaded collective, the plugin's switch plan, and the no-CPU-fallback rule."""
+import pytest
+import torch
+
+from _util import same_bits, t16
+from h3b import fp8_gemm, ops, plugin, ulysses_exact, ulysses_outq
+from oracle import ulysses as ou
+
+
+def _layout_attn(q, k, v):
+    return (q.float() + 2.0 * k.float() - 0.5 * v.float()).to(q.dtype)
+
+
+@pytest.mark.parametrize("ws", [2, 4])
+def test_exact_forward_matches_reference_outputs(golden, ws):
+    g = golden("ulysses")
+    m, heads, d = (int(v) for v in g[f"ws{ws}_shape"])
+    qs, ks, vs = ([t16(g[f"ws{ws}_{n}{r}"]) for r in range(ws)] for n in ("q", "k", "v"))
+
+    def body(r, a2a):
+        return ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a, pack=ou.pack,
+                                           unpack_fn=ou.unpack)
+
+    res = ou.run_ranks(body, ws)
+    for r in range(ws):
+        assert same_bits(res[r], t16(g[f"ws{ws}_out{r}"]))
+
+
+def test_exact_forward_with_presupplied_sends_and_defer():
+    ws, m, heads, d = 2, 4, 4, 8
+    qs = [torch.randn(1, m, heads, d) for _ in range(ws)]
+    ks = [torch.randn(1, m, heads, d) for _ in range(ws)]
+    vs = [torch.randn(1, m, heads, d) for _ in range(ws)]
+
+    def body(r, a2a):
+        sends = [ou.pack(t[r][0], ws) for t in (qs, ks, vs)]
+        res = ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a, sends=sends,
+                                          back="defer")
+        assert sends == []
+        return res
+
+    res = ou.run_ranks(body, ws)
+    ref = ou.run_ranks(lambda r, a2a: ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a,
+                                                                  pack=ou.pack, unpack_fn=ou.unpack), ws)
+    for r in range(ws):
+        assert isinstance(res[r], ulysses_outq.Deferred)
+        assert res[r].shape == (1, m, heads, d)
+        assert torch.equal(ou.unpack(res[r].recv).view(1, m, heads, d), ref[r])
+
+
+def test_send_shape_and_by_dest_views():
+    x = torch.arange(6 * 8 * 4).float().view(6, 8, 4)
+    assert ulysses_exact.send_shape(6, 8, 4, 2) == (2, 6, 4, 4)
+    assert torch.equal(ulysses_exact.by_dest(x, 2).contiguous(), ou.pack(x, 2))
+
+
+def test_eligibility():
+    q = torch.zeros(1, 4, 8, 16)
+    assert ulysses_exact.eligible_shape(q, q, q, 2)
+    assert not ulysses_exact.eligible_shape(q, q, q, 1)
+    assert not ulysses_exact.eligible_shape(q, q, q, 3)
+    assert not ulysses_exact.eligible_shape(torch.zeros(2, 4, 8, 16), q, q, 2)
+
+
+def test_plugin_plan_defaults_and_switches():
+    p = plugin.plan({})
+    assert p["ulysses"] == "2" and p["fp8_gemm"] == "cutlass" and p["overlap"] is None
+    p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_FP8_GEMM": "0", "H3_TP2_A2A_TIMING": "1"})
+    assert p["overlap"] == 2 and p["ulysses"] is None and p["fp8_gemm"] is None and p["a2a_timing"]
+    plugin.register()  # no H3_TP2_ROLE: a no-op
+
+
+def test_gemm_dispatch_guards():
+    a = torch.zeros(8, 32, dtype=torch.float8_e4m3fn)
+    b = torch.zeros(16, 32, dtype=torch.float8_e4m3fn).t()
+    sa, sb = torch.ones(8, 1), torch.ones(16)
+    assert fp8_gemm.eligible(a, b, sa, sb, torch.bfloat16, None)
+    assert not fp8_gemm.eligible(a, b, torch.ones(1), torch.ones(1), torch.bfloat16, None)   # per-tensor: stock
+    assert not fp8_gemm.eligible(a, b.contiguous(), sa, sb, torch.bfloat16, None)            # b.t() not contiguous
+    assert not fp8_gemm.eligible(a, b, sa, sb, torch.float32, None)
+
+
+def test_route_order_routers_then_hooks():
+    calls = []
+    fp8_gemm._routers.clear(), fp8_gemm._stash_hooks.clear()
+    fp8_gemm.set_router(lambda *a: calls.append("router"))
+    fp8_gemm.set_stash_hook(lambda *a: (calls.append("hook"), "ph")[1])
+    assert fp8_gemm.route(None, None, None, None, None) == "ph"
+    assert calls == ["router", "hook"]
+    fp8_gemm._routers.clear(), fp8_gemm._stash_hooks.clear()
+
+
+def test_kernels_refuse_cpu_tensors():
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.quant(x)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.flash_attn(torch.zeros(8, 1, 128, dtype=torch.bfloat16), torch.zeros(8, 1, 128, dtype=torch.bfloat16),
+                       torch.zeros(8, 1, 128, dtype=torch.bfloat16))
