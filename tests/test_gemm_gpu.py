@@ -111,7 +111,8 @@ def test_qkv_send_epilogue_layout(dev, ws):
     y = ops.fp8_gemm(a, w, sa, sb).cpu()
     q, k, v = (t.reshape(M, heads, 128) for t in y.split(heads * 128, dim=1))
     assert same_bits(sq.cpu(), ou.pack(q, ws)) and same_bits(sk.cpu(), ou.pack(k, ws))
-    assert sv.dtype == F16 and torch.equal(sv.cpu().float(), ou.pack(v, ws).float())
+    # v: the bf16 value converted to f16 (round to nearest even; tiny values become f16 subnormals)
+    assert sv.dtype == F16 and same_bits(sv.cpu(), ou.pack(v, ws).to(F16))
     assert int(flag.item()) == 0
 
 

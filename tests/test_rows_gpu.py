@@ -79,7 +79,8 @@ def test_div_full_mode_close_to_ieee(dev):
     q1, s1 = ops.quant(x, div_mode=ops.DIV_FULL)
     d = (s0.view(torch.int32) - s1.view(torch.int32)).abs().max().item()
     assert d <= 2
-    assert (q0.view(torch.uint8) != q1.view(torch.uint8)).float().mean().item() < 1e-3
+    # div.full differs from IEEE division by at most 2 ulp: a scale one ulp off moves a few e4m3 roundings
+    assert (q0.view(torch.uint8) != q1.view(torch.uint8)).float().mean().item() < 1e-2
 
 
 def test_rms_quant_golden(dev, golden):
