@@ -174,6 +174,24 @@ H3B_API int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, con
                        int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
                        int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream);
 
+/* No counterpart in the reference: an attention entry point for callers that cannot allocate device memory (code
+ * running inside a CUDA graph capture, where cudaMalloc is not allowed; plugins whose host framework owns all device
+ * memory; hosts that forbid device allocation after start-up).  Same arguments and result as h3b_flash_attn_fwd with
+ * a bf16 v (v_f16 = 0 there means bf16 P.V; here v is bf16 and the P.V product runs in f16 whenever v fits, bf16
+ * otherwise), but it allocates nothing: the f16 copy of v and its control words live in a fixed file-scope device
+ * array of H3B_NOALLOC_SCRATCH_BYTES (32 MiB + 256 B) that every GPU loading the library holds until exit.
+ * Limit: s_kv * heads * 128 <= H3B_NOALLOC_MAX_V_ELEMS (s_kv * heads <= 131072), else H3B_EUNSUPPORTED.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and sets the kernels'
+ * shared-memory limit; make that first call before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU (other streams, other threads) race and must be serialised by the caller.  Device-side wait
+ * failures are recorded in the array's own status word, not in h3b_device_status(). */
+#define H3B_NOALLOC_MAX_V_ELEMS (16ll << 20)
+#define H3B_NOALLOC_SCRATCH_BYTES (256ll + 2ll * H3B_NOALLOC_MAX_V_ELEMS)
+H3B_API int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                       int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o,
+                                       int64_t o_tok, int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv,
+                                       int32_t heads, int32_t head_dim, float scale, h3b_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * Ulysses layout kernels
  * ------------------------------------------------------------------------------------------------------------- */

@@ -37,7 +37,7 @@ def nvcc() -> str:
 def _deps_hash(src: Path, extra: list[str]) -> str:
     h = hashlib.sha256()
     h.update(" ".join(ARCH + FLAGS + extra).encode())
-    for p in sorted(CSRC.glob("*.cuh")) + [REPO / "include" / "h3b.h", src]:
+    for p in sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.cu")) + [REPO / "include" / "h3b.h", src]:
         h.update(p.read_bytes())
     return h.hexdigest()[:16]
 

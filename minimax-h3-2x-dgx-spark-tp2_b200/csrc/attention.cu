@@ -36,6 +36,7 @@ struct Params {
   int64_t o_tok, o_head;
   int nkv;
   const int32_t* range_flag;
+  int range_mode;  // 0: flag set -> record H3B_ERANGE, skip; 1: flag set -> skip; 2: run only when the flag is set
   WaitCtl wc;
 };
 
@@ -85,9 +86,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int head = blockIdx.y;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * BQ;
   bool aborted_at_entry = status_bad(p.wc);
-  if (p.range_flag != nullptr && *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0) {
-    if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
-    aborted_at_entry = true;
+  if (p.range_flag != nullptr) {
+    const bool raised = *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0;
+    if (p.range_mode == 0 && raised) {
+      if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
+      aborted_at_entry = true;
+    } else if ((p.range_mode == 1 && raised) || (p.range_mode == 2 && !raised)) {
+      aborted_at_entry = true;
+    }
   }
 
   if (threadIdx.x == 0) {
@@ -341,6 +347,8 @@ static int make_qkv_map(CUtensorMap* m, const void* base, int64_t tokens, int he
   return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+#ifndef H3B_ATTENTION_KERNEL_ONLY
+
 extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
                                   int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok,
                                   int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads,
@@ -401,3 +409,5 @@ extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, 
   H3B_CHECK_LAUNCH("flash_attn launch");
   return H3B_OK;
 }
+
+#endif  // H3B_ATTENTION_KERNEL_ONLY

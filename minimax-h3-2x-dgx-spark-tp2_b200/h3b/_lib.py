@@ -44,6 +44,8 @@ SIGNATURES = {
                                     ctypes.POINTER(QkvSend), _p]),
     "h3b_flash_attn_fwd": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
                                           _i64, _i32, _i32, _f32, _i32, _p, _p]),
+    "h3b_flash_attn_fwd_noalloc": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64,
+                                                  _i64, _i64, _i64, _i32, _i32, _f32, _p]),
     "h3b_pack_by_dest": (ctypes.c_int, [_p, _i64, _i32, _i32, _i64, _i64, _i32, _p, _i32, _p, _p]),
     "h3b_unpack_recv": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _p]),
     "h3b_bf16_to_f16": (ctypes.c_int, [_p, _p, _i64, _p, _p]),
