@@ -174,9 +174,9 @@ H3B_API int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, con
                        int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
                        int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream);
 
-/* No counterpart in the reference: an attention entry point for callers that cannot allocate device memory (code
- * running inside a CUDA graph capture, where cudaMalloc is not allowed; plugins whose host framework owns all device
- * memory; hosts that forbid device allocation after start-up).  Same arguments and result as h3b_flash_attn_fwd with
+/* No counterpart in the reference: an attention entry point for callers that cannot allocate device memory (plugins
+ * whose host framework owns all device memory and exposes no allocator to them; processes that must not allocate
+ * after start-up, such as real-time services with a fixed memory plan).  Same arguments and result as h3b_flash_attn_fwd with
  * a bf16 v (v_f16 = 0 there means bf16 P.V; here v is bf16 and the P.V product runs in f16 whenever v fits, bf16
  * otherwise), but it allocates nothing: the f16 copy of v and its control words live in a fixed file-scope device
  * array of H3B_NOALLOC_SCRATCH_BYTES (32 MiB + 256 B) that every GPU loading the library holds until exit.

@@ -1,8 +1,8 @@
 // Flash attention with a bf16 v for callers that cannot allocate device memory.
 //
-// Some callers of this library cannot call cudaMalloc: code that runs while a CUDA graph is being captured (an
-// allocation there is not allowed), plugins whose host framework owns every byte of device memory and exposes no
-// allocator, and hosts that forbid device allocation after start-up.  The regular entry point h3b_flash_attn_fwd
+// Some callers of this library cannot call cudaMalloc: plugins whose host framework owns every byte of device memory
+// and exposes no allocator to them, and processes that must not allocate after start-up (real-time services with a
+// fixed memory plan).  The regular entry point h3b_flash_attn_fwd
 // needs, for a bf16 v, an f16 copy of v that its caller allocates, and a device status word that the library
 // allocates on first use.  h3b_flash_attn_fwd_noalloc needs neither: the f16 copy of v, the overflow flag and the
 // status word live in one file-scope device array, g_scratch, of fixed size (H3B_NOALLOC_SCRATCH_BYTES).  Every

@@ -1,8 +1,8 @@
 """The allocation-free attention entry point (h3b_flash_attn_fwd_noalloc), called through the C ABI.
 
-Some callers cannot allocate device memory (a CUDA graph capture in progress, a host framework that owns every byte
-of device memory, a host that forbids allocation after start-up); this entry point serves them from a fixed device
-array inside the library.  Its output must match the regular entry point's (h3b_flash_attn_fwd on the f16 copy of v)
+Some callers cannot allocate device memory (a host framework that owns every byte of device memory and exposes no
+allocator, a process that must not allocate after start-up); this entry point serves them from a fixed device array
+inside the library.  Its output must match the regular entry point's (h3b_flash_attn_fwd on the f16 copy of v)
 within the attention tolerance, on two calls in a row (the second reuses the array the first one left behind), and
 must fall back to bf16 P.V when v does not fit f16.  This file is collected last so a stop-at-first-failure run has
 already run every other test; it also passes alone in a fresh process."""
