@@ -21,6 +21,23 @@ __device__ __forceinline__ float qdiv(float a, float b, int mode) {
   return mode == H3B_DIV_FULL ? div_full(a, b) : __fdiv_rn(a, b);
 }
 
+// abs-max of non-negative bf16 bit patterns as unsigned integers: for |x| the bit order is the value order, and every
+// NaN pattern (0x7F81..0x7FFF) sorts above +inf (0x7F80), so the integer max propagates NaN like the reference's max
+template <int THREADS>
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, uint32_t* red) {
+  v = __reduce_max_sync(0xffffffffu, v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < THREADS / 32 ? red[lane] : 0u;
+    w = __reduce_max_sync(0xffffffffu, w);
+    if (lane == 0) red[32] = w;
+  }
+  __syncthreads();
+  return red[32];
+}
+
 template <int THREADS>
 __device__ __forceinline__ float block_max_nan(float v, float* red) {
 #pragma unroll
@@ -58,27 +75,25 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-__device__ __forceinline__ float absmax8(const uint4& v, float m) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m = nan_max(m, fabsf(lo_bf16(w[i])));
-    m = nan_max(m, fabsf(hi_bf16(w[i])));
-  }
-  return m;
+// running abs-max of 8 bf16 values, kept as two packed 16-bit unsigned maxima
+__device__ __forceinline__ uint32_t absmax8(const uint4& v, uint32_t m2) {
+  m2 = __vmaxu2(m2, v.x & 0x7FFF7FFFu);
+  m2 = __vmaxu2(m2, v.y & 0x7FFF7FFFu);
+  m2 = __vmaxu2(m2, v.z & 0x7FFF7FFFu);
+  m2 = __vmaxu2(m2, v.w & 0x7FFF7FFFu);
+  return m2;
 }
+__device__ __forceinline__ uint32_t fold16(uint32_t m2) { return max(m2 & 0xFFFFu, m2 >> 16); }
 
-__device__ __forceinline__ float clamp448(float y) { return nan_min(nan_max(y, -kFp8Max), kFp8Max); }
-
-// 8 bf16 -> 8 e4m3 (one 8-byte word), x * inv then clamp then RNE
+// 8 bf16 -> 8 e4m3 (one 8-byte word): x * inv, round to nearest even; satfinite clamps to +-448 exactly as the
+// reference's clamp does for every finite or infinite product, and keeps NaN
 __device__ __forceinline__ uint2 quant8(const uint4& v, float inv) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t o[2];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const uint16_t a = f32x2_to_e4m3x2(clamp448(lo_bf16(w[2 * i]) * inv), clamp448(hi_bf16(w[2 * i]) * inv));
-    const uint16_t b =
-        f32x2_to_e4m3x2(clamp448(lo_bf16(w[2 * i + 1]) * inv), clamp448(hi_bf16(w[2 * i + 1]) * inv));
+    const uint16_t a = f32x2_to_e4m3x2(lo_bf16(w[2 * i]) * inv, hi_bf16(w[2 * i]) * inv);
+    const uint16_t b = f32x2_to_e4m3x2(lo_bf16(w[2 * i + 1]) * inv, hi_bf16(w[2 * i + 1]) * inv);
     o[i] = static_cast<uint32_t>(a) | (static_cast<uint32_t>(b) << 16);
   }
   return make_uint2(o[0], o[1]);
@@ -89,11 +104,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// the quant tail shared by every row kernel: row held as VPT x 8 bf16 per thread (vector i = tid + k*THREADS)
+// the quant tail shared by every row kernel: row held as VPT x 8 bf16 per thread (vector i = tid + k*THREADS),
+// m2 = this thread's packed abs-max bits
 template <int THREADS, int VPT>
-__device__ __forceinline__ void quant_tail(const uint4 (&h)[VPT], float amax, int64_t nvec, uint8_t* qrow,
-                                           float* srow, int div_mode, float* red) {
-  amax = block_max_nan<THREADS>(amax, red);
+__device__ __forceinline__ void quant_tail(const uint4 (&h)[VPT], uint32_t m2, int64_t nvec, uint8_t* qrow,
+                                           float* srow, int div_mode, uint32_t* red) {
+  const float amax = __uint_as_float(block_max_u32<THREADS>(fold16(m2), red) << 16);
   const float scale = nan_max(qdiv(amax, kFp8Max, div_mode), kMinScale);
   const float inv = qdiv(1.0f, scale, div_mode);
 #pragma unroll
@@ -107,28 +123,34 @@ __device__ __forceinline__ void quant_tail(const uint4 (&h)[VPT], float amax, in
 // ---------------------------------------------------------------------------------------------------------------
 // K6 / K10: quant of segmented rows (ulysses_outq._quant_rows_kernel, fp8_quant_fuse._quant_kernel/_unpack_quant)
 // ---------------------------------------------------------------------------------------------------------------
-template <int THREADS, int VPT>
+template <int THREADS, int VPT, bool SEGMENTED>
 __global__ void __launch_bounds__(THREADS) quant_rows_vec_kernel(const __nv_bfloat16* __restrict__ base, int64_t m,
                                                                  int64_t segv, int64_t stride_p, int64_t stride_m,
                                                                  int64_t nvec, uint8_t* __restrict__ q,
                                                                  float* __restrict__ s, int div_mode) {
-  __shared__ float red[33];
+  __shared__ uint32_t red[33];
   for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
     uint4 h[VPT];
-    float amax = 0.0f;
+    uint32_t m2 = 0;
+    const __nv_bfloat16* rbase = base + row * stride_m;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-      const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
+      const uint32_t i = threadIdx.x + static_cast<uint32_t>(k) * THREADS;
       if (i < nvec) {
-        const int64_t sg = i / segv;
-        const int64_t c = (i - sg * segv) * 8;
-        h[k] = __ldg(reinterpret_cast<const uint4*>(base + sg * stride_p + row * stride_m + c));
-        amax = absmax8(h[k], amax);
+        const __nv_bfloat16* src;
+        if (SEGMENTED) {
+          const uint32_t sg = i / static_cast<uint32_t>(segv);
+          src = rbase + sg * stride_p + static_cast<int64_t>(i - sg * static_cast<uint32_t>(segv)) * 8;
+        } else {
+          src = rbase + static_cast<int64_t>(i) * 8;
+        }
+        h[k] = __ldg(reinterpret_cast<const uint4*>(src));
+        m2 = absmax8(h[k], m2);
       } else {
         h[k] = make_uint4(0, 0, 0, 0);
       }
     }
-    quant_tail<THREADS, VPT>(h, amax, nvec, q + row * nvec * 8, s + row, div_mode, red);
+    quant_tail<THREADS, VPT>(h, m2, nvec, q + row * nvec * 8, s + row, div_mode, red);
   }
 }
 
@@ -150,7 +172,7 @@ __global__ void __launch_bounds__(256) quant_rows_scalar_kernel(const __nv_bfloa
     const float inv = qdiv(1.0f, scale, div_mode);
     for (int64_t j = threadIdx.x; j < K; j += 256) {
       const int64_t sg = j / seg, c = j - sg * seg;
-      const float y = clamp448(__bfloat162float(base[sg * stride_p + row * stride_m + c]) * inv);
+      const float y = __bfloat162float(base[sg * stride_p + row * stride_m + c]) * inv;
       q[row * K + j] = static_cast<uint8_t>(f32x2_to_e4m3x2(y, 0.0f) & 0xFF);
     }
     if (threadIdx.x == 0) s[row] = scale;
@@ -200,6 +222,7 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 template <int THREADS, int VPT, bool GATED>
 __global__ void __launch_bounds__(THREADS) rms_quant_kernel(RmsArgs a) {
   __shared__ float red[33];
+  __shared__ uint32_t redu[33];
   const int64_t nvec = a.hidden / 8;
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const int64_t idx = a.indices != nullptr ? a.indices[row] : 0;
@@ -230,7 +253,7 @@ __global__ void __launch_bounds__(THREADS) rms_quant_kernel(RmsArgs a) {
     }
     const float var = __fdiv_rn(block_sum<THREADS>(ss, red), static_cast<float>(a.hidden));
     const float rstd = rsqrtf(var + a.eps);
-    float amax = 0.0f;
+    uint32_t m2 = 0;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
@@ -249,10 +272,10 @@ __global__ void __launch_bounds__(THREADS) rms_quant_kernel(RmsArgs a) {
         }
         xv[k] = pack8(x);
         if (a.ph != nullptr) *reinterpret_cast<uint4*>(a.ph + row * a.hidden + i * 8) = xv[k];
-        amax = absmax8(xv[k], amax);
+        m2 = absmax8(xv[k], m2);
       }
     }
-    quant_tail<THREADS, VPT>(xv, amax, nvec, a.q + row * a.hidden, a.s + row, a.div_mode, red);
+    quant_tail<THREADS, VPT>(xv, m2, nvec, a.q + row * a.hidden, a.s + row, a.div_mode, redu);
   }
 }
 
@@ -273,11 +296,11 @@ template <int THREADS, int VPT>
 __global__ void __launch_bounds__(THREADS) silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
                                                                  int64_t d, int64_t stride_x, uint8_t* __restrict__ q,
                                                                  float* __restrict__ s, int div_mode) {
-  __shared__ float red[33];
+  __shared__ uint32_t red[33];
   const int64_t nvec = d / 8;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     uint4 h[VPT];
-    float amax = 0.0f;
+    uint32_t m2 = 0;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
@@ -289,10 +312,10 @@ __global__ void __launch_bounds__(THREADS) silu_mul_quant_kernel(const __nv_bflo
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] = silu_mul(g[e], u[e]);
         h[k] = pack8(y);
-        amax = absmax8(h[k], amax);
+        m2 = absmax8(h[k], m2);
       }
     }
-    quant_tail<THREADS, VPT>(h, amax, nvec, q + row * d, s + row, div_mode, red);
+    quant_tail<THREADS, VPT>(h, m2, nvec, q + row * d, s + row, div_mode, red);
   }
 }
 
@@ -327,12 +350,12 @@ __global__ void __launch_bounds__(THREADS) scale_swiglu_quant_kernel(const float
                                                                      const __nv_bfloat16* __restrict__ bias, int64_t M,
                                                                      int64_t half, uint8_t* __restrict__ q,
                                                                      float* __restrict__ s, int div_mode) {
-  __shared__ float red[33];
+  __shared__ uint32_t red[33];
   const int64_t nvec = half / 8;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const float sar = sa[row];
     uint4 h[VPT];
-    float amax = 0.0f;
+    uint32_t m2 = 0;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
@@ -341,10 +364,10 @@ __global__ void __launch_bounds__(THREADS) scale_swiglu_quant_kernel(const float
         float y[8];
         swiglu8(x + row * 2 * half, half, i * 8, sar, sb, bias, y);
         h[k] = pack8(y);
-        amax = absmax8(h[k], amax);
+        m2 = absmax8(h[k], m2);
       }
     }
-    quant_tail<THREADS, VPT>(h, amax, nvec, q + row * half, s + row, div_mode, red);
+    quant_tail<THREADS, VPT>(h, m2, nvec, q + row * half, s + row, div_mode, red);
   }
 }
 
@@ -490,9 +513,15 @@ int h3b_quant_rows_e4m3(const void* base, int64_t m, int32_t p, int64_t seg, int
                    K <= 256 * 8 * 16;
   if (vec) {
     const int64_t nvec = K / 8, segv = seg / 8;
-#define L(V) quant_rows_vec_kernel<256, V><<<grid_rows(m), 256, 0, st>>>(b, m, segv, stride_p, stride_m, nvec, qq, scale, div_mode)
-    H3B_VPT_DISPATCH(nvec, L);
+    if (p == 1) {
+#define L(V) quant_rows_vec_kernel<256, V, false><<<grid_rows(m), 256, 0, st>>>(b, m, segv, stride_p, stride_m, nvec, qq, scale, div_mode)
+      H3B_VPT_DISPATCH(nvec, L);
 #undef L
+    } else {
+#define L(V) quant_rows_vec_kernel<256, V, true><<<grid_rows(m), 256, 0, st>>>(b, m, segv, stride_p, stride_m, nvec, qq, scale, div_mode)
+      H3B_VPT_DISPATCH(nvec, L);
+#undef L
+    }
   } else {
     quant_rows_scalar_kernel<<<grid_rows(m), 256, 0, st>>>(b, m, seg, p, stride_p, stride_m, qq, scale, div_mode);
   }

@@ -1,0 +1,49 @@
+"""Worker for tests/test_multigpu_gpu.py (launched by torchrun, one process per GPU, NCCL): every rank runs its rows
+of the cfg-like attention block with the Ulysses exchange over NCCL; rank 0 also runs the single-GPU block.  Results
+are written to --out for the test to compare."""
+import argparse
+import datetime
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path[:0] = [str(ROOT / "minimax-h3-2x-dgx-spark-tp2_b200"), str(ROOT)]
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--hidden", type=int, default=1024)
+    ap.add_argument("--heads", type=int, default=8)
+    args = ap.parse_args()
+    rank, ws, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        from h3b import ops
+        from h3b.block import AttentionBlock
+
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(args.tokens, args.hidden, generator=g).to(torch.bfloat16)
+        m = args.tokens // ws
+        blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=ws, pg=dist.group.WORLD, seed=1)
+        y = blk(x[rank * m:(rank + 1) * m].contiguous().to(dev))
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        torch.save(y.cpu(), Path(args.out) / f"rank{rank}.pt")
+        if rank == 0:
+            full = AttentionBlock(args.hidden, args.heads, device=dev, ws=1, seed=1)(x.to(dev))
+            torch.save(full.cpu(), Path(args.out) / "full.pt")
+        dist.barrier(device_ids=[local])
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -80,3 +80,29 @@ def test_f16_range_flag_refuses(dev):
     assert ops.device_status() == ops._lib.H3B_ERANGE
     o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), pv_f16=False)
     assert torch.isfinite(o.float()).all()
+
+
+def test_poly_exp2_variant_in_a_fresh_process(dev, tmp_path):
+    """H3B_ATTN_EXP2_POLY=1 (a quarter of the exponentials on the FMA pipe) stays within the attention tolerance."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys, torch\n"
+        f"sys.path[:0] = [{str(root / 'minimax-h3-2x-dgx-spark-tp2_b200')!r}, {str(root)!r}, {str(root / 'tests')!r}]\n"
+        "from h3b import ops\n"
+        "from oracle import attention as oa\n"
+        "from _util import rel_l2\n"
+        "g = torch.Generator().manual_seed(5)\n"
+        "q, k, v = (torch.randn(1000, 2, 128, generator=g).to(torch.bfloat16) for _ in range(3))\n"
+        "o = ops.flash_attn(q.cuda(), k.cuda(), v.cuda()).float().cpu()\n"
+        "ref = oa.sdpa(q, k, v)\n"
+        "print(rel_l2(o, ref), (o - ref).abs().max().item(), ops.device_status())\n")
+    env = dict(os.environ, H3B_ATTN_EXP2_POLY="1")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    rel, mabs, status = out.stdout.split()
+    assert float(rel) <= 2e-3 and float(mabs) <= 2e-2 and int(status) == 0

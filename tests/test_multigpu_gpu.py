@@ -1,0 +1,34 @@
+"""Ulysses over NCCL on 2 (and, when visible, 4 or 8) GPUs, one process per GPU: the ranks' rows of the attention
+block are bit-identical to the single-GPU block (each head's attention sees the same keys in the same order)."""
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_ulysses_nccl_ranks_equal_single_gpu(dev, tmp_path, n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs, {torch.cuda.device_count()} visible")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
+           "--nproc-per-node", str(n), "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           str(ROOT / "tests" / "mgpu_worker.py"), "--out", str(tmp_path)]
+    res = subprocess.run(cmd, capture_output=True, text=True, env={**__import__("os").environ, "NCCL_NVLS_ENABLE": "0"})
+    assert res.returncode == 0, res.stderr[-4000:]
+    full = torch.load(tmp_path / "full.pt")
+    parts = torch.cat([torch.load(tmp_path / f"rank{r}.pt") for r in range(n)])
+    assert torch.equal(parts.view(torch.int16), full.view(torch.int16))
