@@ -29,6 +29,7 @@ constexpr int KST = 2, VST = 2;
 constexpr int THREADS = 320;
 constexpr int SMEM_BYTES = (2 + KST + VST) * TILE_BYTES + 1024 + 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr int kDefaultPoly = 0;             // FMA-pipe exponential pairs per 8 (see poly_pairs)
 
 struct Params {
   int64_t s_q, s_kv, valid_kv;
@@ -63,6 +64,41 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
 }
 
+// packed fp32 pair arithmetic (one instruction for two lanes of work on sm_100a)
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// ex2_poly on a pair with the packed instructions
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& e0, float& e1) {
+  constexpr float kRound = 12582912.0f;
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  float j0, j1, n0, n1, f0, f1, p0, p1;
+  fadd2(j0, j1, x0, x1, kRound, kRound);
+  fadd2(n0, n1, j0, j1, -kRound, -kRound);
+  ffma2(f0, f1, n0, n1, -1.0f, -1.0f, x0, x1);
+  ffma2(p0, p1, 0.055170949548482895f, 0.055170949548482895f, f0, f1, 0.2426096349954605f, 0.2426096349954605f);
+  ffma2(p0, p1, p0, p1, f0, f1, 0.6932609677314758f, 0.6932609677314758f);
+  ffma2(p0, p1, p0, p1, f0, f1, 0.9999281764030457f, 0.9999281764030457f);
+  e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23));
+  e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23));
+}
+
 template <bool F16>
 __device__ __forceinline__ uint32_t pack_p(float lo, float hi) {
   if (F16) {
@@ -73,7 +109,8 @@ __device__ __forceinline__ uint32_t pack_p(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-template <bool F16, bool POLY = false>
+// POLY = how many of every 8 exponential pairs run on the FMA pipe (ex2_poly2) instead of the MUFU
+template <bool F16, int POLY = 0>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, Params p) {
@@ -271,14 +308,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < 128; ++i)
             if (i >= kv_left) s[i] = __float_as_uint(-INFINITY);
         }
-        // row max with 8 independent chains (the softmax warps have no other warps to hide latency behind)
+        // row max: 8 independent chains of 3-input max (the softmax warps have no other warps to hide latency)
         float m8[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(s[i]);
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
 #pragma unroll
-        for (int i = 8; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(s[i]));
-        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = 16; i < 128; i += 2)
+          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         const float m_new = fmaxf(m_run, mx * c);
         const bool need = j > 0 && (m_new - m_run > RESCALE_THRESHOLD);
         if (j == 0) {
@@ -310,18 +347,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float x0 = fmaf(__uint_as_float(s[32 * cc + 2 * i]), c, neg_m);
-            const float x1 = fmaf(__uint_as_float(s[32 * cc + 2 * i + 1]), c, neg_m);
-            float e0, e1;
-            if (POLY && (i & 3) == 3) {  // a quarter of the exponentials on the FMA pipe
-              e0 = ex2_poly(x0);
-              e1 = ex2_poly(x1);
+            float x0, x1, e0, e1;
+            ffma2(x0, x1, __uint_as_float(s[32 * cc + 2 * i]), __uint_as_float(s[32 * cc + 2 * i + 1]), c, c, neg_m,
+                  neg_m);
+            if ((i & 7) >= 8 - POLY) {
+              ex2_poly2(x0, x1, e0, e1);
             } else {
               e0 = ex2(x0);
               e1 = ex2(x1);
             }
-            l8[(2 * i) & 7] += e0;
-            l8[(2 * i + 1) & 7] += e1;
+            const int a = (2 * i) & 7;
+            fadd2(l8[a], l8[a + 1], l8[a], l8[a + 1], e0, e1);
             pk[i] = pack_p<F16>(e0, e1);
           }
           tmem_st16(s_tmem + 16 * cc, pk);
@@ -381,13 +417,16 @@ static int make_qkv_map(CUtensorMap* m, const void* base, int64_t tokens, int he
 
 #ifndef H3B_ATTENTION_KERNEL_ONLY
 
-// H3B_ATTN_EXP2_POLY=1 evaluates a quarter of the softmax exponentials with ex2_poly (FMA pipe) instead of the MUFU
-static bool poly_exp2() {
-  static const bool on = [] {
+// How many of every 8 softmax exponential pairs run on the FMA pipe: kDefaultPoly, or H3B_ATTN_EXP2_POLY in
+// {0, 2, 3, 4} (a tuning switch; every setting computes the same softmax within the kernel's tolerance)
+static int poly_pairs() {
+  static const int n = [] {
     const char* v = getenv("H3B_ATTN_EXP2_POLY");
-    return v != nullptr && v[0] == '1';
+    if (v == nullptr || v[0] == '\0') return h3b::attn::kDefaultPoly;
+    const int x = atoi(v);
+    return (x == 0 || x == 2 || x == 3 || x == 4) ? x : h3b::attn::kDefaultPoly;
   }();
-  return on;
+  return n;
 }
 
 extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
@@ -435,22 +474,31 @@ extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_kernel<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(flash_attn_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      e = cudaFuncSetAttribute(flash_attn_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(flash_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      e = cudaFuncSetAttribute(flash_attn_kernel<true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(flash_attn_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(flash_attn_kernel<false, kDefaultPoly>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return cuda_fail(e, "flash_attn: smem attribute");
     attr_set[dev] = true;
   }
   dim3 grid(static_cast<unsigned>((s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(heads));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (v_f16 && poly_exp2())
-    flash_attn_kernel<true, true><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-  else if (v_f16)
-    flash_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  const int poly = poly_pairs();
+  if (!v_f16)
+    flash_attn_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else if (poly == 0)
+    flash_attn_kernel<true, 0><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else if (poly == 2)
+    flash_attn_kernel<true, 2><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else if (poly == 3)
+    flash_attn_kernel<true, 3><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
   else
-    flash_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+    flash_attn_kernel<true, 4><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
   H3B_CHECK_LAUNCH("flash_attn launch");
   return H3B_OK;
 }

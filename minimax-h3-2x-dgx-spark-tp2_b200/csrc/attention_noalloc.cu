@@ -42,10 +42,10 @@ static int setup(int dev, unsigned char** base) {
     void* ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "flash_attn_noalloc: cudaGetSymbolAddress(g_scratch)");
-    e = cudaFuncSetAttribute(attn::flash_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(attn::flash_attn_kernel<true, attn::kDefaultPoly>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              attn::SMEM_BYTES);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn::flash_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(attn::flash_attn_kernel<false, attn::kDefaultPoly>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                attn::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_fail(e, "flash_attn_noalloc: smem attribute");
     st.base = static_cast<unsigned char*>(ptr);
@@ -152,10 +152,10 @@ extern "C" int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t 
   p.wc.timeout = wait_timeout_ns();
   dim3 grid(static_cast<unsigned>((s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(heads));
   p.range_mode = 1;  // f16 P.V unless v overflowed f16
-  flash_attn_kernel<true><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv16, p);
+  flash_attn_kernel<true, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv16, p);
   H3B_CHECK_LAUNCH("flash_attn_noalloc: f16 launch");
   p.range_mode = 2;  // bf16 P.V only if it did
-  flash_attn_kernel<false><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  flash_attn_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
   H3B_CHECK_LAUNCH("flash_attn_noalloc: bf16 launch");
   return H3B_OK;
 }

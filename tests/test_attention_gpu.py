@@ -82,8 +82,9 @@ def test_f16_range_flag_refuses(dev):
     assert torch.isfinite(o.float()).all()
 
 
-def test_poly_exp2_variant_in_a_fresh_process(dev, tmp_path):
-    """H3B_ATTN_EXP2_POLY=1 (a quarter of the exponentials on the FMA pipe) stays within the attention tolerance."""
+@pytest.mark.parametrize("poly", ["0", "2", "3", "4"])
+def test_poly_exp2_variants_in_a_fresh_process(dev, poly):
+    """H3B_ATTN_EXP2_POLY=n (n of every 8 exponential pairs on the FMA pipe) stays within the attention tolerance."""
     import os
     import subprocess
     import sys
@@ -101,7 +102,7 @@ def test_poly_exp2_variant_in_a_fresh_process(dev, tmp_path):
         "o = ops.flash_attn(q.cuda(), k.cuda(), v.cuda()).float().cpu()\n"
         "ref = oa.sdpa(q, k, v)\n"
         "print(rel_l2(o, ref), (o - ref).abs().max().item(), ops.device_status())\n")
-    env = dict(os.environ, H3B_ATTN_EXP2_POLY="1")
+    env = dict(os.environ, H3B_ATTN_EXP2_POLY=poly)
     out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stderr
     rel, mabs, status = out.stdout.split()
