@@ -29,7 +29,7 @@ constexpr int KST = 2, VST = 2;
 constexpr int THREADS = 320;
 constexpr int SMEM_BYTES = (2 + KST + VST) * TILE_BYTES + 1024 + 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
-constexpr int kDefaultPoly = 0;             // FMA-pipe exponential pairs per 8 (see poly_pairs)
+constexpr int kDefaultPoly = 2;             // FMA-pipe exponential pairs per 8 (see poly_pairs)
 
 struct Params {
   int64_t s_q, s_kv, valid_kv;
@@ -302,6 +302,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32_at<64>(s_tmem + 64, s);
         tmem_ld32_at<96>(s_tmem + 96, s);
         tmem_ld_wait();
+        reg_fence(s);
         const int64_t kv_left = p.valid_kv - static_cast<int64_t>(j) * BKV;
         if (kv_left < BKV) {
 #pragma unroll
@@ -332,6 +333,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t o[8];
             tmem_ld8(o_tmem + cc, o);
             tmem_ld_wait();
+            asm volatile("" : "+r"(o[0]), "+r"(o[1]), "+r"(o[2]), "+r"(o[3]), "+r"(o[4]), "+r"(o[5]), "+r"(o[6]), "+r"(o[7]));
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st8(o_tmem + cc, o);
@@ -378,6 +380,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t o[32];
           tmem_ld32(o_tmem + cc, o);
           tmem_ld_wait();
+          reg_fence(o);
           if (row < p.s_q) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {

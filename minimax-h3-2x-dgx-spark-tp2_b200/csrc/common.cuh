@@ -209,6 +209,28 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
+// Register dependency fence: makes the compiler treat r[OFF..OFF+16) as redefined here, so no use of a tcgen05.ld
+// destination can be scheduled above the tcgen05.wait::ld that precedes this fence (the load writes its registers
+// asynchronously; only the wait makes them valid).
+#define H3B_RF4(i) "+r"(r[OFF + i]), "+r"(r[OFF + i + 1]), "+r"(r[OFF + i + 2]), "+r"(r[OFF + i + 3])
+template <int OFF, int N>
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[N]) {
+  static_assert(OFF + 16 <= N, "reg_fence16 out of range");
+  asm volatile("" : H3B_RF4(0), H3B_RF4(4), H3B_RF4(8), H3B_RF4(12));
+}
+#undef H3B_RF4
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+  static_assert(N % 16 == 0, "reg_fence needs a multiple of 16 registers");
+  if constexpr (N >= 16) reg_fence16<0>(r);
+  if constexpr (N >= 32) reg_fence16<16>(r);
+  if constexpr (N >= 48) reg_fence16<32>(r);
+  if constexpr (N >= 64) reg_fence16<48>(r);
+  if constexpr (N >= 80) reg_fence16<64>(r);
+  if constexpr (N >= 96) reg_fence16<80>(r);
+  if constexpr (N >= 112) reg_fence16<96>(r);
+  if constexpr (N >= 128) reg_fence16<112>(r);
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -227,6 +227,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_ld32(tacc + c0, g);
             tmem_ld32(tacc + 128 + c0, u);
             tmem_ld_wait();
+            reg_fence(g);
+            reg_fence(u);
             const int64_t ng = static_cast<int64_t>(nb) * 128 + c0;  // output / gate column
             const int64_t nu = p.half + ng;                           // up column of W
             uint32_t o[16];
@@ -260,6 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t r[32];
             tmem_ld32(tacc + c0, r);
             tmem_ld_wait();
+            reg_fence(r);
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
