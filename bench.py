@@ -187,7 +187,8 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
     if tokens % world:
         raise SystemExit(f"tokens {tokens} not divisible by {world} ranks")
     m = tokens // world
-    blk = AttentionBlock(HIDDEN, HEADS, device=dev, ws=world, pg=pg, init_device=dev, seed=1)
+    blk = AttentionBlock(HIDDEN, HEADS, device=dev, ws=world, pg=pg, init_device=dev, seed=1,
+                         groups=args.groups or None)
     g = torch.Generator(device=dev).manual_seed(rank)
     x = torch.randn(m, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
 
@@ -266,7 +267,7 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
         "config": {"workload": f"cfg2 DiT attention block: {tokens} tokens (31x48x84), hidden {HIDDEN}, "
                                f"{HEADS} heads x {HEAD_DIM}, Ulysses SP={world}", "tokens": tokens,
                    "rows_per_rank": m, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM, "sp": world,
-                   "l2": "inputs larger than L2 (no flush)"},
+                   "head_groups": blk.groups, "l2": "inputs larger than L2 (no flush)"},
         "ms_per_stage": stage_ms,
         "roofline": {"bound": "tensor", "kernel": "flash_attn", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
@@ -294,6 +295,8 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0, help="override the token count (tests / small runs)")
     ap.add_argument("--ref-rows", type=int, default=1024, help="query rows of the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--groups", type=int, default=0,
+                    help="Ulysses head groups overlapped with attention (0: about 5 local heads per group)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

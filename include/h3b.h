@@ -60,7 +60,10 @@ enum h3b_epilogue_kind {
 };
 
 /* Extra arguments of H3B_EPI_QKV_SEND.  Column n of the [M, 3*H*d] product is (which = n / (H*d), head
- * h = (n % (H*d)) / d, c = n % d); it is written to send[which][p][m][j][c] with p = h / (H/P), j = h % (H/P).
+ * h = (n % (H*d)) / d, c = n % d).  With G head groups (groups <= 1: one group) of hg = H/G heads and
+ * hgl = hg/P heads per rank and group, head h = g*hg + p*hgl + j is written to send[which][g][p][m][j][c]
+ * (each send buffer [G, P, M, hgl, d]; G = 1 is stock's input_t [P, M, H/P, d]), so each group's all-to-all is one
+ * contiguous equal-split exchange (the reference's head-group overlap, h3_tp2/ulysses_overlap.py:116-159).
  * v_f16 != 0 stores the v slab as f16 (bf16-rounded first, then converted exactly) for the f16 P.V attention. */
 typedef struct h3b_qkv_send {
   void* send[3]; /* q, k, v send buffers, each [P, M, H/P, d] contiguous, bf16 (v: f16 if v_f16) */
@@ -69,6 +72,7 @@ typedef struct h3b_qkv_send {
   int32_t ws;    /* P (Ulysses degree), H % P == 0 */
   int32_t v_f16;
   int32_t* range_flag; /* device int or NULL: set to 1 when a finite v value overflows f16 (v_f16 only) */
+  int32_t groups;      /* head groups G (0 or 1: none); H % (G * P) == 0 */
 } h3b_qkv_send;
 
 /* ---------------------------------------------------------------------------------------------------------------

@@ -39,7 +39,9 @@ struct Params {
   int64_t half;  // SWIGLU: N / 2
   void* send[3];
   int hd;        // QKV_SEND: heads * 128
-  int hl;        // heads per rank
+  int hl;        // heads per rank and group (hgl)
+  int hg;        // heads per group
+  int ws;        // Ulysses degree P
   int v_f16;
   int32_t* range_flag;
   WaitCtl wc;
@@ -284,8 +286,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int which = static_cast<int>(n0 / p.hd);
               const int hcol = static_cast<int>(n0 - static_cast<int64_t>(which) * p.hd);
               const int h = hcol >> 7, c = hcol & 127;
-              const int dst_rank = h / p.hl, j = h - dst_rank * p.hl;
-              const int64_t off = ((static_cast<int64_t>(dst_rank) * p.M + m) * p.hl + j) * 128 + c;
+              const int g = h / p.hg, hh = h - g * p.hg;
+              const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
+              const int64_t seg = static_cast<int64_t>(g) * p.ws + dst_rank;  // (group, destination) slab
+              const int64_t off = ((seg * p.M + m) * p.hl + j) * 128 + c;
               const bool as_f16 = which == 2 && p.v_f16;
               if (as_f16 && p.range_flag != nullptr) {
                 bool bad = false;
@@ -382,8 +386,12 @@ extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t l
       if (reinterpret_cast<uintptr_t>(send->send[i]) & 15u) return fail(H3B_EALIGN, "fp8_gemm qkv_send: send alignment");
       p.send[i] = send->send[i];
     }
+    const int groups = send->groups > 1 ? send->groups : 1;
+    if (send->heads % (groups * send->ws)) return fail(H3B_EINVAL, "fp8_gemm qkv_send: heads %% (groups * ws) != 0");
     p.hd = send->heads * 128;
-    p.hl = send->heads / send->ws;
+    p.hg = send->heads / groups;
+    p.hl = p.hg / send->ws;
+    p.ws = send->ws;
     p.v_f16 = send->v_f16 != 0;
     p.range_flag = send->range_flag;
     p.num_nb = static_cast<int>((N + BN - 1) / BN);

@@ -21,7 +21,7 @@ _p, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ct
 
 class QkvSend(ctypes.Structure):
     _fields_ = [("send", _p * 3), ("heads", _i32), ("head_dim", _i32), ("ws", _i32), ("v_f16", _i32),
-                ("range_flag", _p)]
+                ("range_flag", _p), ("groups", _i32)]
 
 
 # name -> (restype, argtypes): exactly the declarations of include/h3b.h

@@ -42,7 +42,7 @@ def block_flops(tokens: int, hidden: int, heads: int, head_dim: int = 128) -> di
 
 class AttentionBlock:
     def __init__(self, hidden: int, heads: int, *, device, head_dim: int = 128, seed: int = 1, ws: int = 1, pg=None,
-                 weights: tuple | None = None, init_device=None, a2a=None):
+                 weights: tuple | None = None, init_device=None, a2a=None, groups: int | None = None):
         if head_dim != 128:
             raise ValueError("head_dim 128 only")
         if heads % ws:
@@ -58,6 +58,10 @@ class AttentionBlock:
         self.wqkv8, self.sqkv, self.wo8, self.so = (t.to(self.device) for t in weights)
         self.range_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.a2a = a2a   # injected collective a2a(out, inp, group=None); default: NCCL all_to_all_single
+        from .ulysses_overlap import default_groups
+        self.groups = default_groups(heads, ws) if groups is None else int(groups)
+        if heads % (self.groups * ws):
+            raise ValueError(f"heads {heads} not divisible by groups {self.groups} x ws {ws}")
 
     def exchange(self, send: torch.Tensor) -> torch.Tensor:
         if self.ws == 1:
@@ -85,16 +89,30 @@ class AttentionBlock:
         mark()
         q8, sx = ops.quant(x)
         mark()
-        sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
-                                      range_flag=self.range_flag)
-        mark()
-        q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
-        mark()
-        o = ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d), range_flag=self.range_flag)
-        mark()
-        back = self.exchange(o.view(self.ws, m, hl, d))
-        mark()
-        o8, so = ops.quant_from_recv(back)
+        if self.ws > 1 and self.groups > 1:
+            from .ulysses_overlap import grouped_attention, quant_grouped_back
+            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+                                          range_flag=self.range_flag, groups=self.groups)
+            mark()
+            mark()      # with head groups the exchanges overlap the attention: the attention stage holds all three
+            back = grouped_attention(sends, self.ws, self.groups,
+                                     lambda q, k, v: ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d),
+                                                                    range_flag=self.range_flag),
+                                     pg=self.pg, a2a=self.a2a)
+            mark()
+            mark()
+            o8, so = quant_grouped_back(back)
+        else:
+            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+                                          range_flag=self.range_flag)
+            mark()
+            q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
+            mark()
+            o = ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d), range_flag=self.range_flag)
+            mark()
+            back = self.exchange(o.view(self.ws, m, hl, d))
+            mark()
+            o8, so = ops.quant_from_recv(back)
         mark()
         y = ops.fp8_gemm(o8, self.wo8, so, self.so)
         mark()

@@ -218,24 +218,27 @@ def fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torc
 
 def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, heads: int, ws: int, *,
                       bias: torch.Tensor | None = None, v_f16: bool = False, sends=None,
-                      range_flag: torch.Tensor | None = None):
-    """qkv projection whose epilogue writes q, k, v straight into the Ulysses send buffers [P, M, H/P, d] (the
-    producer redirection of ulysses_exact.fused_into_send, h3_tp2/ulysses_exact.py:278, moved into the GEMM)."""
+                      range_flag: torch.Tensor | None = None, groups: int = 1):
+    """qkv projection whose epilogue writes q, k, v straight into the Ulysses send buffers (the producer redirection
+    of ulysses_exact.fused_into_send, h3_tp2/ulysses_exact.py:278, moved into the GEMM).  groups = 1: each buffer is
+    stock's [P, M, H/P, d]; groups = G > 1: [G, P, M, H/(G*P), d], head h = g*(H/G) + p*(H/(G*P)) + j, one
+    contiguous all-to-all per group (the head-group overlap layout)."""
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
-    if N != 3 * heads * 128 or heads % ws:
-        raise ValueError(f"fp8_gemm_qkv_send: N {N} != 3 * {heads} * 128 or heads % ws")
-    shape = (ws, M, heads // ws, 128)
+    if N != 3 * heads * 128 or heads % (ws * groups):
+        raise ValueError(f"fp8_gemm_qkv_send: N {N} != 3 * {heads} * 128 or heads % (ws * groups)")
+    shape = (ws, M, heads // ws, 128) if groups == 1 else (groups, ws, M, heads // (ws * groups), 128)
     if sends is None:
         sends = [torch.empty(shape, dtype=torch.bfloat16, device=a.device) for _ in range(2)]
         sends.append(torch.empty(shape, dtype=torch.float16 if v_f16 else torch.bfloat16, device=a.device))
     desc = _lib.QkvSend()
     for i in range(3):
         if tuple(sends[i].shape) != shape or not sends[i].is_contiguous():
-            raise ValueError("fp8_gemm_qkv_send: send buffers must be contiguous [P, M, H/P, d]")
+            raise ValueError(f"fp8_gemm_qkv_send: send buffers must be contiguous {shape}")
         desc.send[i] = sends[i].data_ptr()
     desc.heads, desc.head_dim, desc.ws, desc.v_f16 = heads, 128, ws, int(bool(v_f16))
+    desc.groups = int(groups)
     desc.range_flag = _ptr(range_flag)
     _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
               _ptr(bias), None, 0, M, N, K, OUT_BF16, EPI_QKV_SEND, ctypes.byref(desc), _stream(a))

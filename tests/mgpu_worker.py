@@ -20,6 +20,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--hidden", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=8)
+    ap.add_argument("--groups", type=int, default=0)
     args = ap.parse_args()
     rank, ws, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -32,7 +33,8 @@ def main():
         g = torch.Generator().manual_seed(0)
         x = torch.randn(args.tokens, args.hidden, generator=g).to(torch.bfloat16)
         m = args.tokens // ws
-        blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=ws, pg=dist.group.WORLD, seed=1)
+        blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=ws, pg=dist.group.WORLD, seed=1,
+                             groups=args.groups or None)
         y = blk(x[rank * m:(rank + 1) * m].contiguous().to(dev))
         torch.cuda.synchronize()
         assert ops.device_status() == 0

@@ -44,3 +44,48 @@ def test_ulysses_ranks_equal_single_rank_bitwise(dev, ws):
     outs = ou.run_ranks(body, ws)
     y = torch.cat(outs, dim=0)
     assert torch.equal(y.view(torch.int16), full.view(torch.int16))
+
+
+@pytest.mark.parametrize("ws,groups", [(2, 2), (2, 4), (4, 2)])
+def test_head_group_overlap_bitwise(dev, ws, groups):
+    """The head-group overlap (grouped send layout, per-group exchanges on the communication stream, quant from the
+    grouped reverse buffer) gives the same bytes as the single-rank block."""
+    n, hidden, heads = 1024, 512, 8
+    weights = ob.make_weights(hidden, heads, seed=3)
+    x = torch.randn(n, hidden, generator=torch.Generator().manual_seed(4)).to(BF16).to(dev)
+    full = AttentionBlock(hidden, heads, device=dev, weights=weights)(x)
+    m = n // ws
+    torch.cuda.synchronize()
+
+    def body(r, a2a):
+        blk = AttentionBlock(hidden, heads, device=dev, weights=weights, ws=ws, a2a=a2a, groups=groups)
+        out = blk(x[r * m:(r + 1) * m].contiguous())
+        torch.cuda.synchronize()
+        return out
+
+    y = torch.cat(ou.run_ranks(body, ws), dim=0)
+    assert torch.equal(y.view(torch.int16), full.view(torch.int16))
+
+
+def test_grouped_forward_stock_layout_matches_exact_forward(dev):
+    from h3b import ulysses_exact, ulysses_overlap
+
+    ws, m, heads = 2, 256, 8
+    g = torch.Generator().manual_seed(8)
+    qs, ks, vs = ([torch.randn(1, m, heads, 128, generator=g).to(BF16).to(dev) for _ in range(ws)] for _ in range(3))
+    attn = ulysses_exact.local_attention
+    torch.cuda.synchronize()
+
+    def ref(r, a2a):
+        out = ulysses_exact.exact_forward(qs[r], ks[r], vs[r], attn, ws=ws, a2a=a2a)
+        torch.cuda.synchronize()
+        return out
+
+    def grouped(r, a2a):
+        out = ulysses_overlap.grouped_forward(qs[r], ks[r], vs[r], attn, ws=ws, groups=2, a2a=a2a)
+        torch.cuda.synchronize()
+        return out
+
+    a, b = ou.run_ranks(ref, ws), ou.run_ranks(grouped, ws)
+    for r in range(ws):
+        assert torch.equal(a[r].view(torch.int16), b[r].view(torch.int16))

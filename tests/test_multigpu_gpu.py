@@ -20,13 +20,13 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("n", [2, 4, 8])
-def test_ulysses_nccl_ranks_equal_single_gpu(dev, tmp_path, n):
+@pytest.mark.parametrize("n,groups", [(2, 1), (2, 2), (4, 1), (4, 2), (8, 1)])
+def test_ulysses_nccl_ranks_equal_single_gpu(dev, tmp_path, n, groups):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs, {torch.cuda.device_count()} visible")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(n), "--master-addr", "127.0.0.1", "--master-port", str(_port()),
-           str(ROOT / "tests" / "mgpu_worker.py"), "--out", str(tmp_path)]
+           str(ROOT / "tests" / "mgpu_worker.py"), "--out", str(tmp_path), "--heads", "16", "--groups", str(groups)]
     res = subprocess.run(cmd, capture_output=True, text=True, env={**__import__("os").environ, "NCCL_NVLS_ENABLE": "0"})
     assert res.returncode == 0, res.stderr[-4000:]
     full = torch.load(tmp_path / "full.pt")
