@@ -33,8 +33,7 @@ struct DeviceState {
 static DeviceState g_state[64];
 static std::mutex g_mu;
 
-// Once per device, with that device current: the array's device address (host code may not use the symbol itself)
-// and the kernels' shared-memory opt-in.
+// Once per device, with that device current: the array's device address (host code may not use the symbol itself).
 static int setup(int dev, unsigned char** base) {
   std::lock_guard<std::mutex> lock(g_mu);
   DeviceState& st = g_state[dev];
@@ -42,12 +41,6 @@ static int setup(int dev, unsigned char** base) {
     void* ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "flash_attn_noalloc: cudaGetSymbolAddress(g_scratch)");
-    e = cudaFuncSetAttribute(attn::flash_attn_kernel<true, attn::kDefaultPoly>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             attn::SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn::flash_attn_kernel<false, attn::kDefaultPoly>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               attn::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "flash_attn_noalloc: smem attribute");
     st.base = static_cast<unsigned char*>(ptr);
   }
   *base = st.base;
@@ -118,13 +111,6 @@ extern "C" int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t 
   int* status = reinterpret_cast<int*>(base + 4);
   uint16_t* v16 = reinterpret_cast<uint16_t*>(base + kControlBytes);
 
-  CUtensorMap tq, tk, tv16, tv;
-  rc = make_qkv_map(&tq, q, s_q, heads, q_tok, q_head);
-  if (!rc) rc = make_qkv_map(&tk, k, s_kv, heads, k_tok, k_head);
-  if (!rc) rc = make_qkv_map(&tv16, v16, s_kv, heads, static_cast<int64_t>(heads) * 128, 128);
-  if (!rc) rc = make_qkv_map(&tv, v, s_kv, heads, v_tok, v_head);
-  if (rc) return rc;
-
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // the array keeps the previous call's contents: the flag and the status word must start at zero
   e = cudaMemsetAsync(base, 0, 8, st);
@@ -146,16 +132,14 @@ extern "C" int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t 
   p.o = static_cast<uint16_t*>(o);
   p.o_tok = o_tok;
   p.o_head = o_head;
-  p.nkv = static_cast<int>((valid_kv + BKV - 1) / BKV);
   p.range_flag = flag;
   p.wc.status = status;
   p.wc.timeout = wait_timeout_ns();
-  dim3 grid(static_cast<unsigned>((s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(heads));
   p.range_mode = 1;  // f16 P.V unless v overflowed f16
-  flash_attn_kernel<true, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv16, p);
-  H3B_CHECK_LAUNCH("flash_attn_noalloc: f16 launch");
+  rc = launch_attention(q, q_tok, q_head, k, k_tok, k_head, v16, static_cast<int64_t>(heads) * 128, 128, true, p, st);
+  if (rc) return rc;
   p.range_mode = 2;  // bf16 P.V only if it did
-  flash_attn_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-  H3B_CHECK_LAUNCH("flash_attn_noalloc: bf16 launch");
+  rc = launch_attention(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, false, p, st);
+  if (rc) return rc;
   return H3B_OK;
 }
