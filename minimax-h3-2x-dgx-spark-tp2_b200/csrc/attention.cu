@@ -406,651 +406,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 
-// ---------------------------------------------------------------------------------------------------------------
-// Second schedule: 64-key tiles with S double-buffered per query tile.
-// TMEM: S[q][b] at column q*128 + b*64 (64 f32 columns each), O[q] at 256 + q*128.  The MMA issuer computes
-// S_q(j+1) into the other buffer before it waits for P_q(j), so the tensor core works on the next key tile while
-// the softmax warps turn the current one into P; the softmax of a query tile runs back to back over key tiles.
-// QK^T is M=128 x N=64 x K=128 (SS), P.V is M=128 x N=128 x K=64 (TS).  P_q(j) overwrites columns [0, 32) of its
-// S buffer; the next S MMA into that buffer is issued only after the P.V that reads it (in-order tensor pipe).
-// O rescaling waits for the previous P.V of the same tile (o_done), which the next P.V cannot overtake (it needs the
-// P this warp has not yet written).
-// ---------------------------------------------------------------------------------------------------------------
-constexpr int BKV2 = 64;
-constexpr int KV2_TILE = BKV2 * D * 2;  // 16 KB
-constexpr int KV2_HALF = KV2_TILE / 2;  // one 64-element half of d
-constexpr int ST2 = 4;                  // K and V ring stages
-constexpr int SMEM2_BYTES = 2 * TILE_BYTES + 2 * ST2 * KV2_TILE + 1024 + 256;
-
-template <bool F16, int POLY = 0>
-__global__ void __launch_bounds__(THREADS, 1)
-    flash_attn_db_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, Params p) {
-  constexpr uint32_t IDESC_QK = idesc_make(FMT_BF16, FMT_BF16, 0, BQ, BKV2);
-  constexpr uint32_t IDESC_PV = idesc_make(F16 ? FMT_F16 : FMT_BF16, F16 ? FMT_F16 : FMT_BF16, 1, BQ, D);
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + 2 * TILE_BYTES;
-  const uint32_t sV = sK + ST2 * KV2_TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TILE_BYTES + 2 * ST2 * KV2_TILE);
-  const uint32_t b0 = smem_u32(bars);
-  // q_full | k_full[4] | k_empty[4] | v_full[4] | v_empty[4] | s_full[2][2] | p_full[2][2] | o_done[2] | done
-  const uint32_t q_full = b0;
-  auto k_full = [&](int s) { return b0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return b0 + 8u * (5 + s); };
-  auto v_full = [&](int s) { return b0 + 8u * (9 + s); };
-  auto v_empty = [&](int s) { return b0 + 8u * (13 + s); };
-  auto s_full = [&](int q, int b) { return b0 + 8u * (17 + 2 * q + b); };
-  auto p_full = [&](int q, int b) { return b0 + 8u * (21 + 2 * q + b); };
-  auto o_done = [&](int q) { return b0 + 8u * (25 + q); };
-  const uint32_t done_bar = b0 + 8u * 27;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * BQ;
-  bool aborted_at_entry = status_bad(p.wc);
-  if (p.range_flag != nullptr) {
-    const bool raised = *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0;
-    if (p.range_mode == 0 && raised) {
-      if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
-      aborted_at_entry = true;
-    } else if ((p.range_mode == 1 && raised) || (p.range_mode == 2 && !raised)) {
-      aborted_at_entry = true;
-    }
-  }
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < ST2; ++s) {
-      mbar_init(k_full(s), 1);
-      mbar_init(k_empty(s), 1);
-      mbar_init(v_full(s), 1);
-      mbar_init(v_empty(s), 1);
-    }
-    for (int q = 0; q < 2; ++q) {
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(s_full(q, b), 1);
-        mbar_init(p_full(q, b), 128);
-      }
-      mbar_init(o_done(q), 1);
-    }
-    mbar_init(done_bar, 1);
-    fence_mbar_init();
-  }
-  if (warp == 9) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int nkv = p.nkv;
-
-  if (!aborted_at_entry) {
-    if (warp == 8) {
-      if (lane == 0) {
-        // ---------------- TMA producer ----------------
-        tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-        for (int t = 0; t < 2; ++t)
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_3d(sQ + t * TILE_BYTES + hf * HALF_BYTES, &tmQ, q_full, hf * 64, static_cast<int32_t>(q0 + t * BQ),
-                        head);
-        int kn[ST2] = {0, 0, 0, 0}, vn[ST2] = {0, 0, 0, 0};
-        for (int j = 0; j < nkv; ++j) {
-          const int st = j % ST2;
-          const uint32_t ph = static_cast<uint32_t>(j / ST2) & 1u;
-          if (!mbar_wait(k_empty(st), ph ^ 1u, p.wc)) break;
-          mbar_arrive_expect_tx(k_full(st), KV2_TILE);
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_3d(sK + st * KV2_TILE + hf * KV2_HALF, &tmK, k_full(st), hf * 64, j * BKV2, head);
-          kn[st]++;
-          if (!mbar_wait(v_empty(st), ph ^ 1u, p.wc)) break;
-          mbar_arrive_expect_tx(v_full(st), KV2_TILE);
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_3d(sV + st * KV2_TILE + hf * KV2_HALF, &tmV, v_full(st), hf * 64, j * BKV2, head);
-          vn[st]++;
-        }
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < p.wc.timeout) {
-        }
-        for (int s = 0; s < ST2; ++s) {
-          if (kn[s] > 0)
-            while (!mbar_try_wait(k_full(s), static_cast<uint32_t>(kn[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
-            }
-          if (vn[s] > 0)
-            while (!mbar_try_wait(v_full(s), static_cast<uint32_t>(vn[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
-            }
-        }
-      }
-    } else if (warp == 9) {
-      if (lane == 0) {
-        // ---------------- MMA issuer ----------------
-        bool ok = mbar_wait(q_full, 0, p.wc);
-        tc_fence_after();
-        auto issue_qk = [&](int q, int b, int st) {
-          const uint32_t d_tmem = tmem + static_cast<uint32_t>(q * 128 + b * BKV2);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t qoff = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-            const uint32_t koff = (kk >> 2) * KV2_HALF + (kk & 3) * 32;
-            umma_f16_ss(d_tmem, sdesc_sw128(sQ + q * TILE_BYTES + qoff, 16, 1024),
-                        sdesc_sw128(sK + st * KV2_TILE + koff, 16, 1024), IDESC_QK, kk != 0);
-          }
-        };
-        auto issue_pv = [&](int q, int b, int st, bool accumulate) {
-          const uint32_t d_tmem = tmem + static_cast<uint32_t>(256 + q * D);
-          const uint32_t p_tmem = tmem + static_cast<uint32_t>(q * 128 + b * BKV2);
-#pragma unroll
-          for (int kk = 0; kk < BKV2 / 16; ++kk)
-            umma_f16_ts(d_tmem, p_tmem + 8u * kk, sdesc_sw128(sV + st * KV2_TILE + kk * 2048, KV2_HALF, 1024),
-                        IDESC_PV, accumulate || kk != 0);
-        };
-        if (ok && nkv > 0) {
-          ok = mbar_wait(k_full(0), 0, p.wc);
-          if (ok) {
-            tc_fence_after();
-            issue_qk(0, 0, 0);
-            umma_commit(s_full(0, 0));
-            issue_qk(1, 0, 0);
-            umma_commit(s_full(1, 0));
-            umma_commit(k_empty(0));
-          }
-        }
-        for (int j = 0; j < nkv && ok; ++j) {
-          if (j + 1 < nkv) {
-            const int st1 = (j + 1) % ST2, b1 = (j + 1) & 1;
-            if (!mbar_wait(k_full(st1), static_cast<uint32_t>((j + 1) / ST2) & 1u, p.wc)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_qk(0, b1, st1);
-            umma_commit(s_full(0, b1));
-            issue_qk(1, b1, st1);
-            umma_commit(s_full(1, b1));
-            umma_commit(k_empty(st1));
-          }
-          const int st = j % ST2, b = j & 1;
-          if (!mbar_wait(v_full(st), static_cast<uint32_t>(j / ST2) & 1u, p.wc)) {
-            ok = false;
-            break;
-          }
-          for (int q = 0; q < 2; ++q) {
-            if (!mbar_wait(p_full(q, b), static_cast<uint32_t>(j >> 1) & 1u, p.wc)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_pv(q, b, st, j > 0);
-            umma_commit(o_done(q));
-          }
-          if (!ok) break;
-          umma_commit(v_empty(st));
-        }
-        umma_commit(done_bar);
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(done_bar, 0) && globaltimer() - t0 < p.wc.timeout) {
-        }
-      }
-    } else {
-      // ---------------- softmax + epilogue (warps 0-7) ----------------
-      const int q = warp >> 2;
-      const int sub = warp & 3;
-      const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-      const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(256 + q * D);
-      const float c = p.scale_log2;
-      float m_run = -INFINITY, l_run = 0.0f;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        const int b = j & 1;
-        const uint32_t s_tmem = tmem + lane_addr + static_cast<uint32_t>(q * 128 + b * BKV2);
-        if (!mbar_wait(s_full(q, b), static_cast<uint32_t>(j >> 1) & 1u, p.wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t s[64];
-        tmem_ld32_at<0>(s_tmem + 0, s);
-        tmem_ld32_at<32>(s_tmem + 32, s);
-        tmem_ld_wait();
-        reg_fence(s);
-        const int64_t kv_left = p.valid_kv - static_cast<int64_t>(j) * BKV2;
-        if (kv_left < BKV2) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i >= kv_left) s[i] = __float_as_uint(-INFINITY);
-        }
-        float m8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
-#pragma unroll
-        for (int i = 16; i < 64; i += 2)
-          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
-        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-        const float m_new = fmaxf(m_run, mx * c);
-        const bool need = j > 0 && (m_new - m_run > RESCALE_THRESHOLD);
-        if (j == 0) {
-          m_run = m_new;
-        } else if (__any_sync(0xffffffffu, need)) {
-          // O_q is final up to P.V(j-1): wait for that product, then rescale this warp's rows
-          if (!mbar_wait(o_done(q), static_cast<uint32_t>(j - 1) & 1u, p.wc)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float alpha = need ? ex2(m_run - m_new) : 1.0f;
-          if (need) {
-            l_run *= alpha;
-            m_run = m_new;
-          }
-#pragma unroll 1
-          for (int cc = 0; cc < D; cc += 8) {
-            uint32_t o[8];
-            tmem_ld8(o_tmem + cc, o);
-            tmem_ld_wait();
-            asm volatile("" : "+r"(o[0]), "+r"(o[1]), "+r"(o[2]), "+r"(o[3]), "+r"(o[4]), "+r"(o[5]), "+r"(o[6]), "+r"(o[7]));
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st8(o_tmem + cc, o);
-          }
-          tmem_st_wait();
-        }
-        const float neg_m = -m_run;
-        float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float x0, x1, e0, e1;
-            ffma2(x0, x1, __uint_as_float(s[32 * cc + 2 * i]), __uint_as_float(s[32 * cc + 2 * i + 1]), c, c, neg_m,
-                  neg_m);
-            if ((i & 7) >= 8 - POLY) {
-              ex2_poly2(x0, x1, e0, e1);
-            } else {
-              e0 = ex2(x0);
-              e1 = ex2(x1);
-            }
-            const int a = (2 * i) & 7;
-            fadd2(l8[a], l8[a + 1], l8[a], l8[a + 1], e0, e1);
-            pk[i] = pack_p<F16>(e0, e1);
-          }
-          tmem_st16(s_tmem + 16 * cc, pk);
-        }
-        l_run += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(p_full(q, b));
-      }
-      // the last P.V of this tile is completion nkv of o_done; the barrier may still be two phases behind (P.V(nkv-2)
-      // pending), where a parity wait cannot tell the phases apart: wait for completion nkv-1 first
-      if (ok && nkv > 1) ok = mbar_wait(o_done(q), static_cast<uint32_t>(nkv - 2) & 1u, p.wc);
-      if (ok && nkv > 0 && mbar_wait(o_done(q), static_cast<uint32_t>(nkv - 1) & 1u, p.wc)) {
-        tc_fence_after();
-        const int64_t row = q0 + q * BQ + sub * 32 + lane;
-        const float inv_l = 1.0f / l_run;
-        uint16_t* orow = p.o + row * p.o_tok + static_cast<int64_t>(head) * p.o_head;
-#pragma unroll
-        for (int cc = 0; cc < D; cc += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_tmem + cc, o);
-          tmem_ld_wait();
-          reg_fence(o);
-          if (row < p.s_q) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint32_t w[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                __nv_bfloat162 bv = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv_l,
-                                                          __uint_as_float(o[8 * v + 2 * e + 1]) * inv_l);
-                w[e] = *reinterpret_cast<uint32_t*>(&bv);
-              }
-              *reinterpret_cast<uint4*>(orow + cc + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          }
-        }
-      }
-    }
-  }
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 9) tmem_dealloc(tmem, 512);
-}
-
-
-// ---------------------------------------------------------------------------------------------------------------
-// Third schedule: the ping-pong of the first (two 128-row query tiles, 128-key tiles, S/P/O in TMEM) with each query
-// tile's softmax split by columns over two warpgroups: warpgroup h of tile q owns key columns [64h, 64h+64) of every
-// S row (and output columns [64h, 64h+64) of O).  The two halves exchange their partial row maxima through shared
-// memory behind a named barrier, so both apply the same running max; each keeps a partial row sum, added at the end.
-// 16 softmax warps (4 per SMSP) halve the per-tile softmax latency, which then fits in the other tile's tensor-core
-// window (P.V + S of 128x128x128 each).  The exchanges use mbarriers with bounded waits (no named barrier, so a
-// warpgroup that gives up on a wait cannot leave its partner blocked).
-// warps 0-15: softmax (tile q = warp / 8, half h = (warp / 4) % 2, TMEM subpartition warp % 4), 16: TMA, 17: MMA.
-// ---------------------------------------------------------------------------------------------------------------
-constexpr int THREADS3 = 18 * 32;
-constexpr int SMEM3_BYTES = (2 + KST + VST) * TILE_BYTES + 1024 + 256 + 2 * 2 * 2 * 128 * 4 + 2 * 2 * 128 * 4;
-
-template <bool F16, int POLY = 0>
-__global__ void __launch_bounds__(THREADS3, 1)
-    flash_attn_cs_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, Params p) {
-  constexpr uint32_t IDESC_QK = idesc_make(FMT_BF16, FMT_BF16, 0, BQ, BKV);
-  constexpr uint32_t IDESC_PV = idesc_make(F16 ? FMT_F16 : FMT_BF16, F16 ? FMT_F16 : FMT_BF16, 1, BQ, D);
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + 2 * TILE_BYTES;
-  const uint32_t sV = sK + KST * TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (2 + KST + VST) * TILE_BYTES);
-  // partial row maxima [step parity][tile][half][row] and partial row sums [tile][half][row]
-  float* xmax = reinterpret_cast<float*>(smem + (2 + KST + VST) * TILE_BYTES + 256);
-  float* xsum = xmax + 2 * 2 * 2 * 128;
-  const uint32_t b0 = smem_u32(bars);
-  const uint32_t q_full = b0;
-  auto k_full = [&](int s) { return b0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return b0 + 8u * (3 + s); };
-  auto v_full = [&](int s) { return b0 + 8u * (5 + s); };
-  auto v_empty = [&](int s) { return b0 + 8u * (7 + s); };
-  auto s_full = [&](int q) { return b0 + 8u * (9 + q); };
-  auto p_full = [&](int q) { return b0 + 8u * (11 + q); };
-  auto o_full = [&](int q) { return b0 + 8u * (13 + q); };
-  const uint32_t done_bar = b0 + 8u * 15;
-  // exchange barriers of a tile's two softmax warpgroups (256 arrivals): per-step maxima, final sums
-  auto x_bar = [&](int q) { return b0 + 8u * (16 + q); };
-  auto f_bar = [&](int q) { return b0 + 8u * (18 + q); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * BQ;
-  bool aborted_at_entry = status_bad(p.wc);
-  if (p.range_flag != nullptr) {
-    const bool raised = *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0;
-    if (p.range_mode == 0 && raised) {
-      if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
-      aborted_at_entry = true;
-    } else if ((p.range_mode == 1 && raised) || (p.range_mode == 2 && !raised)) {
-      aborted_at_entry = true;
-    }
-  }
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full(s), 1);
-      mbar_init(k_empty(s), 1);
-      mbar_init(v_full(s), 1);
-      mbar_init(v_empty(s), 1);
-      mbar_init(s_full(s), 1);
-      mbar_init(p_full(s), 256);
-      mbar_init(o_full(s), 1);
-      mbar_init(x_bar(s), 256);
-      mbar_init(f_bar(s), 256);
-    }
-    mbar_init(done_bar, 1);
-    fence_mbar_init();
-  }
-  if (warp == 17) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int nkv = p.nkv;
-
-  if (!aborted_at_entry) {
-    if (warp == 16) {
-      if (lane == 0) {
-        // ---------------- TMA producer (as in the first schedule) ----------------
-        tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-        for (int t = 0; t < 2; ++t)
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_3d(sQ + t * TILE_BYTES + hf * HALF_BYTES, &tmQ, q_full, hf * 64, static_cast<int32_t>(q0 + t * BQ),
-                        head);
-        int kn[KST] = {0, 0}, vn[VST] = {0, 0};
-        for (int j = 0; j < nkv; ++j) {
-          const int ks = j % KST, vs = j % VST;
-          const uint32_t kph = static_cast<uint32_t>(j / KST) & 1u, vph = static_cast<uint32_t>(j / VST) & 1u;
-          if (!mbar_wait(k_empty(ks), kph ^ 1u, p.wc)) break;
-          mbar_arrive_expect_tx(k_full(ks), TILE_BYTES);
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_3d(sK + ks * TILE_BYTES + hf * HALF_BYTES, &tmK, k_full(ks), hf * 64, j * BKV, head);
-          kn[ks]++;
-          if (!mbar_wait(v_empty(vs), vph ^ 1u, p.wc)) break;
-          mbar_arrive_expect_tx(v_full(vs), TILE_BYTES);
-          for (int hf = 0; hf < 2; ++hf)
-            tma_load_3d(sV + vs * TILE_BYTES + hf * HALF_BYTES, &tmV, v_full(vs), hf * 64, j * BKV, head);
-          vn[vs]++;
-        }
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < p.wc.timeout) {
-        }
-        for (int s = 0; s < 2; ++s) {
-          if (kn[s] > 0)
-            while (!mbar_try_wait(k_full(s), static_cast<uint32_t>(kn[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
-            }
-          if (vn[s] > 0)
-            while (!mbar_try_wait(v_full(s), static_cast<uint32_t>(vn[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
-            }
-        }
-      }
-    } else if (warp == 17) {
-      if (lane == 0) {
-        // ---------------- MMA issuer (as in the first schedule) ----------------
-        bool ok = mbar_wait(q_full, 0, p.wc);
-        tc_fence_after();
-        auto issue_qk = [&](int q, int ks) {
-          const uint32_t d_tmem = tmem + static_cast<uint32_t>(q * BKV);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-            umma_f16_ss(d_tmem, sdesc_sw128(sQ + q * TILE_BYTES + off, 16, 1024),
-                        sdesc_sw128(sK + ks * TILE_BYTES + off, 16, 1024), IDESC_QK, kk != 0);
-          }
-        };
-        auto issue_pv = [&](int q, int vs, bool accumulate) {
-          const uint32_t d_tmem = tmem + static_cast<uint32_t>(2 * BKV + q * D);
-          const uint32_t p_tmem = tmem + static_cast<uint32_t>(q * BKV);
-#pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)
-            umma_f16_ts(d_tmem, p_tmem + 8u * kk, sdesc_sw128(sV + vs * TILE_BYTES + kk * 2048, HALF_BYTES, 1024),
-                        IDESC_PV, accumulate || kk != 0);
-        };
-        for (int j = 0; j < nkv && ok; ++j) {
-          const int ks = j % KST;
-          if (!mbar_wait(k_full(ks), static_cast<uint32_t>(j / KST) & 1u, p.wc)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int vprev = (j - 1) % VST;
-          for (int q = 0; q < 2 && ok; ++q) {
-            if (j > 0) {
-              if (!mbar_wait(p_full(q), static_cast<uint32_t>(j - 1) & 1u, p.wc)) {
-                ok = false;
-                break;
-              }
-              if (q == 0 && !mbar_wait(v_full(vprev), static_cast<uint32_t>((j - 1) / VST) & 1u, p.wc)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_pv(q, vprev, j > 1);
-              if (q == 1) umma_commit(v_empty(vprev));
-            }
-            issue_qk(q, ks);
-            umma_commit(s_full(q));
-          }
-          if (!ok) break;
-          umma_commit(k_empty(ks));
-        }
-        if (ok) {
-          const int j = nkv;
-          const int vprev = (j - 1) % VST;
-          for (int q = 0; q < 2; ++q) {
-            if (!mbar_wait(p_full(q), static_cast<uint32_t>(j - 1) & 1u, p.wc)) break;
-            if (q == 0 && !mbar_wait(v_full(vprev), static_cast<uint32_t>((j - 1) / VST) & 1u, p.wc)) break;
-            tc_fence_after();
-            issue_pv(q, vprev, j > 1);
-            umma_commit(o_full(q));
-          }
-        }
-        umma_commit(done_bar);
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(done_bar, 0) && globaltimer() - t0 < p.wc.timeout) {
-        }
-      }
-    } else {
-      // ---------------- softmax (warps 0-15): tile q, column half h ----------------
-      const int q = warp >> 3;
-      const int h = (warp >> 2) & 1;
-      const int sub = warp & 3;
-      const int row = sub * 32 + lane;
-      const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-      const uint32_t s_tmem = tmem + lane_addr + static_cast<uint32_t>(q * BKV + 64 * h);   // my 64 key columns
-      const uint32_t p_tmem = tmem + lane_addr + static_cast<uint32_t>(q * BKV + 32 * h);   // my 32 P columns
-      const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(2 * BKV + q * D + 64 * h);
-      const float c = p.scale_log2;
-      float m_run = -INFINITY, l_run = 0.0f;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        if (!mbar_wait(s_full(q), static_cast<uint32_t>(j) & 1u, p.wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t s[64];
-        tmem_ld32_at<0>(s_tmem + 0, s);
-        tmem_ld32_at<32>(s_tmem + 32, s);
-        tmem_ld_wait();
-        reg_fence(s);
-        const int64_t kv_left = p.valid_kv - static_cast<int64_t>(j) * BKV - 64 * h;
-        if (kv_left < 64) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i >= kv_left) s[i] = __float_as_uint(-INFINITY);
-        }
-        float m8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
-#pragma unroll
-        for (int i = 16; i < 64; i += 2)
-          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
-        const float my_mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-        float* slot = xmax + ((j & 1) * 2 + q) * 2 * 128;
-        slot[h * 128 + row] = my_mx;
-        mbar_arrive(x_bar(q));
-        if (!mbar_wait(x_bar(q), static_cast<uint32_t>(j) & 1u, p.wc)) {
-          ok = false;
-          break;
-        }
-        const float mx = fmaxf(my_mx, slot[(1 - h) * 128 + row]);
-        const float m_new = fmaxf(m_run, mx * c);
-        const bool need = j > 0 && (m_new - m_run > RESCALE_THRESHOLD);
-        if (j == 0) {
-          m_run = m_new;
-        } else if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2(m_run - m_new) : 1.0f;
-          if (need) {
-            l_run *= alpha;
-            m_run = m_new;
-          }
-#pragma unroll 1
-          for (int cc = 0; cc < 64; cc += 8) {
-            uint32_t o[8];
-            tmem_ld8(o_tmem + cc, o);
-            tmem_ld_wait();
-            asm volatile("" : "+r"(o[0]), "+r"(o[1]), "+r"(o[2]), "+r"(o[3]), "+r"(o[4]), "+r"(o[5]), "+r"(o[6]), "+r"(o[7]));
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st8(o_tmem + cc, o);
-          }
-          tmem_st_wait();
-        }
-        const float neg_m = -m_run;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float x0, x1, e0, e1;
-            ffma2(x0, x1, __uint_as_float(s[32 * cc + 2 * i]), __uint_as_float(s[32 * cc + 2 * i + 1]), c, c, neg_m,
-                  neg_m);
-            if ((i & 7) >= 8 - POLY) {
-              ex2_poly2(x0, x1, e0, e1);
-            } else {
-              e0 = ex2(x0);
-              e1 = ex2(x1);
-            }
-            const int a = (2 * i) & 3;
-            fadd2(l4[a], l4[a + 1], l4[a], l4[a + 1], e0, e1);
-            pk[i] = pack_p<F16>(e0, e1);
-          }
-          tmem_st16(p_tmem + 16 * cc, pk);
-        }
-        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(p_full(q));
-      }
-      // the row sum is the two halves' partial sums; both halves apply the same running max
-      xsum[(q * 2 + h) * 128 + row] = l_run;
-      mbar_arrive(f_bar(q));
-      if (ok) ok = mbar_wait(f_bar(q), 0, p.wc);
-      const float l_tot = l_run + xsum[(q * 2 + (1 - h)) * 128 + row];
-      if (ok && mbar_wait(o_full(q), 0, p.wc)) {
-        tc_fence_after();
-        const int64_t grow = q0 + q * BQ + row;
-        const float inv_l = 1.0f / l_tot;
-        uint16_t* orow = p.o + grow * p.o_tok + static_cast<int64_t>(head) * p.o_head + 64 * h;
-#pragma unroll
-        for (int cc = 0; cc < 64; cc += 32) {
-          uint32_t o[32];
-          tmem_ld32(o_tmem + cc, o);
-          tmem_ld_wait();
-          reg_fence(o);
-          if (grow < p.s_q) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint32_t w[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                __nv_bfloat162 bv = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv_l,
-                                                          __uint_as_float(o[8 * v + 2 * e + 1]) * inv_l);
-                w[e] = *reinterpret_cast<uint32_t*>(&bv);
-              }
-              *reinterpret_cast<uint4*>(orow + cc + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          }
-        }
-      }
-    }
-  }
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 17) tmem_dealloc(tmem, 512);
-}
-
 }  // namespace attn
 }  // namespace h3b
 
@@ -1076,18 +431,6 @@ static int poly_pairs() {
   return n;
 }
 
-// Kernel schedule: 1 = 128-key ping-pong (default), 2 = 64-key tiles with double-buffered S (H3B_ATTN_SCHEDULE=db),
-// 3 = ping-pong with each tile's softmax split by columns over two warpgroups (H3B_ATTN_SCHEDULE=cs)
-static int attn_schedule() {
-  static const int n = [] {
-    const char* v = getenv("H3B_ATTN_SCHEDULE");
-    if (v != nullptr && v[0] == 'd') return 2;
-    if (v != nullptr && v[0] == 'c') return 3;
-    return 1;
-  }();
-  return n;
-}
-
 template <typename K>
 static cudaError_t set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -1107,72 +450,36 @@ static int attn_attrs() {
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<true, 3>, SMEM_BYTES);
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<true, 4>, SMEM_BYTES);
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<false, kDefaultPoly>, SMEM_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_db_kernel<true, 0>, SMEM2_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_db_kernel<true, 2>, SMEM2_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_db_kernel<true, 3>, SMEM2_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_db_kernel<true, 4>, SMEM2_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_db_kernel<false, kDefaultPoly>, SMEM2_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_cs_kernel<true, 0>, SMEM3_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_cs_kernel<true, 2>, SMEM3_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_cs_kernel<true, 3>, SMEM3_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_cs_kernel<true, 4>, SMEM3_BYTES);
-  if (e == cudaSuccess) e = set_smem(flash_attn_cs_kernel<false, kDefaultPoly>, SMEM3_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "flash_attn: smem attribute");
   done[dev] = true;
   return H3B_OK;
 }
 
-// Builds the tensor maps for the chosen schedule and launches one attention kernel.  p carries everything but nkv.
+// Builds the tensor maps and launches one attention kernel.  p carries everything but nkv.
 static int launch_attention(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
                             int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, bool v_f16,
                             h3b::attn::Params p, cudaStream_t st) {
   using namespace h3b::attn;
   int rc = attn_attrs();
   if (rc) return rc;
-  const int sched = attn_schedule();
-  const uint32_t kv_rows = sched == 2 ? BKV2 : BKV;
   CUtensorMap tq, tk, tv;
   rc = make_qkv_map(&tq, q, p.s_q, p.heads, q_tok, q_head, BQ);
-  if (!rc) rc = make_qkv_map(&tk, k, p.s_kv, p.heads, k_tok, k_head, kv_rows);
-  if (!rc) rc = make_qkv_map(&tv, v, p.s_kv, p.heads, v_tok, v_head, kv_rows);
+  if (!rc) rc = make_qkv_map(&tk, k, p.s_kv, p.heads, k_tok, k_head, BKV);
+  if (!rc) rc = make_qkv_map(&tv, v, p.s_kv, p.heads, v_tok, v_head, BKV);
   if (rc) return rc;
-  p.nkv = static_cast<int>((p.valid_kv + kv_rows - 1) / kv_rows);
+  p.nkv = static_cast<int>((p.valid_kv + BKV - 1) / BKV);
   dim3 grid(static_cast<unsigned>((p.s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(p.heads));
   const int poly = poly_pairs();
-  if (sched == 3) {
-    if (!v_f16)
-      flash_attn_cs_kernel<false, kDefaultPoly><<<grid, THREADS3, SMEM3_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 0)
-      flash_attn_cs_kernel<true, 0><<<grid, THREADS3, SMEM3_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 2)
-      flash_attn_cs_kernel<true, 2><<<grid, THREADS3, SMEM3_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 3)
-      flash_attn_cs_kernel<true, 3><<<grid, THREADS3, SMEM3_BYTES, st>>>(tq, tk, tv, p);
-    else
-      flash_attn_cs_kernel<true, 4><<<grid, THREADS3, SMEM3_BYTES, st>>>(tq, tk, tv, p);
-  } else if (sched == 2) {
-    if (!v_f16)
-      flash_attn_db_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM2_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 0)
-      flash_attn_db_kernel<true, 0><<<grid, THREADS, SMEM2_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 2)
-      flash_attn_db_kernel<true, 2><<<grid, THREADS, SMEM2_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 3)
-      flash_attn_db_kernel<true, 3><<<grid, THREADS, SMEM2_BYTES, st>>>(tq, tk, tv, p);
-    else
-      flash_attn_db_kernel<true, 4><<<grid, THREADS, SMEM2_BYTES, st>>>(tq, tk, tv, p);
-  } else {
-    if (!v_f16)
-      flash_attn_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 0)
-      flash_attn_kernel<true, 0><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 2)
-      flash_attn_kernel<true, 2><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-    else if (poly == 3)
-      flash_attn_kernel<true, 3><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-    else
-      flash_attn_kernel<true, 4><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
-  }
+  if (!v_f16)
+    flash_attn_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else if (poly == 0)
+    flash_attn_kernel<true, 0><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else if (poly == 2)
+    flash_attn_kernel<true, 2><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else if (poly == 3)
+    flash_attn_kernel<true, 3><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  else
+    flash_attn_kernel<true, 4><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
   H3B_CHECK_LAUNCH("flash_attn launch");
   return H3B_OK;
 }
