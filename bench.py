@@ -57,52 +57,85 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons of this rank's GPU, sampled every 10 ms through NVML while the timed region runs
+    (read-only queries; falls back to `nvidia-smi -lms 50` when NVML is unavailable)."""
 
-    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
-              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
-              "clocks_event_reasons.sw_power_cap")
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._proc = None
 
-    def __init__(self, gpu_index: int):
-        self.proc = None
-        self.gpu = gpu_index
+    def _nvml_handle(self):
+        import pynvml  # noqa: PLC0415 (nvidia-ml-py)
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
 
     def __enter__(self):
+        import threading  # noqa: PLC0415
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, ValueError):
-            self.proc = None
+            nv, h = self._nvml_handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._stop = threading.Event()
+            masks = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+                     "sw_power_cap": 0x4}
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        r = reasons_fn(h)
+                        self.samples.append((mhz, {k for k, m in masks.items() if r & m}))
+                    except Exception:  # noqa: BLE001
+                        pass
+                    self._stop.wait(0.01)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                     "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                     "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "50",
+                     "-i", str(self.device.index or 0)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except (OSError, ValueError):
+                self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                out, _ = self._proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                self._proc.kill()
+                out, _ = self._proc.communicate()
+            names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+            for line in (out or "").splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    mhz, self.max_mhz = float(parts[0]), float(parts[1])
+                except (ValueError, IndexError):
+                    continue
+                self.samples.append((mhz, {n for n, v in zip(names, parts[2:]) if v.lower() in ("active", "1")}))
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in (getattr(self, "out", "") or "").splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) != len(self.FIELDS):
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[3:]):
-                if v.lower() in ("active", "1"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [m for m, _ in self.samples]
+        reasons = set().union(*[r for _, r in self.samples]) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -213,7 +246,7 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
 
     # ---- device-timed region: K steps, inputs resident in HBM ----
     marks_all = []
-    with ClockSampler(local_rank) as clocks:
+    with ClockSampler(dev) as clocks:
         barrier()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
