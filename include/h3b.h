@@ -73,6 +73,15 @@ typedef struct h3b_qkv_send {
   int32_t v_f16;
   int32_t* range_flag; /* device int or NULL: set to 1 when a finite v value overflows f16 (v_f16 only) */
   int32_t groups;      /* head groups G (0 or 1: none); H % (G * P) == 0 */
+  /* optional qk RMSNorm + partial RoPE on q and k before the store (the upstream norm+RoPE producer fused, see
+   * h3b_norm_rope_send): per (token, head) n = bf16(y * rsqrt(mean(y^2) + eps) * w) of the bf16 GEMM output y, then
+   * the first `rot` dims rotate with rope_table[m] = cos | sin.  NULL weights: no norm (v is never normed). */
+  const void* q_norm_weight; /* bf16 [128] */
+  const void* k_norm_weight; /* bf16 [128] */
+  const float* rope_table;   /* [M, rot] f32, row stride rope_stride */
+  int64_t rope_stride;
+  int32_t rot;               /* 0, 32, 64, 96 or 128 */
+  float eps;
 } h3b_qkv_send;
 
 /* ---------------------------------------------------------------------------------------------------------------
@@ -205,6 +214,16 @@ H3B_API int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t q_h
  * bf16 -> f16 on the way (and sets *range_flag to 1 when a finite value overflows f16). */
 H3B_API int h3b_pack_by_dest(const void* x, int64_t m, int32_t heads, int32_t d, int64_t stride_m, int64_t stride_h,
                      int32_t ws, void* send, int32_t to_f16, int32_t* range_flag, h3b_stream_t stream);
+
+/* Replaces the upstream norm+RoPE producer launched per destination by ulysses_exact.rope_into_send
+ * (h3_tp2/ulysses_exact.py:264-271; arithmetic of the reference's eager stand-in, tests/test_ulysses_exact.py:107-116):
+ * x [M, H, 128] bf16 (strides stride_m, stride_h, 1), per (token, head) row n = bf16(x * rsqrt(mean(x^2) + eps) * w),
+ * then the first `rot` dims rotate in half-split pairs with table[m] = cos[rot/2] | sin[rot/2] (f32, row stride
+ * table_stride): (a, b) = (n[i], n[i + rot/2]) -> (a cos_i - b sin_i, b cos_i + a sin_i); written as bf16 into
+ * send [P, M, H/P, 128] (head h -> rank h / (H/P)).  rot % 8 == 0, rot <= 128. */
+H3B_API int h3b_norm_rope_send(const void* x, int64_t m, int32_t heads, int64_t stride_m, int64_t stride_h,
+                               const void* weight, const float* table, int64_t table_stride, int32_t rot, float eps,
+                               int32_t ws, void* send, h3b_stream_t stream);
 
 /* Replaces ulysses_exact.exchange_back's unpack (copy 5, h3_tp2/ulysses_exact.py:181-183) and unpack
  * (:124): recv [P, M, hl, d] contiguous -> out [M, P*hl, d] contiguous.  2-byte elements. */

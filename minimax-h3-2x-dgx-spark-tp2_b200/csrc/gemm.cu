@@ -44,8 +44,15 @@ struct Params {
   int ws;        // Ulysses degree P
   int v_f16;
   int32_t* range_flag;
+  const __nv_bfloat16* norm_w[2];  // q, k RMSNorm weights (nullptr: no norm + RoPE)
+  const float* rope;
+  int64_t rope_stride;
+  int rot;
+  float eps;
   WaitCtl wc;
 };
+
+__device__ __forceinline__ float rbf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
   const int in_group = GROUP_M * p.num_nb;
@@ -261,6 +268,88 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c0 = 0; c0 < BN; c0 += 32) {
             const int64_t n0 = static_cast<int64_t>(nb) * BN + c0;
             if (n0 >= p.N) break;  // warp-uniform
+            if (p.epi == H3B_EPI_QKV_SEND && p.norm_w[0] != nullptr && n0 < 2ll * p.hd) {
+              // q or k head with RMSNorm + partial RoPE: handled a whole head (128 columns) at a time
+              if ((c0 & 127) == 0) {
+                const int which = static_cast<int>(n0 / p.hd);
+                const int hcol = static_cast<int>(n0 - static_cast<int64_t>(which) * p.hd);
+                const int h = hcol >> 7;
+                const int g = h / p.hg, hh = h - g * p.hg;
+                const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
+                const int64_t seg = static_cast<int64_t>(g) * p.ws + dst_rank;
+                uint16_t* dst = static_cast<uint16_t*>(p.send[which]) + ((seg * p.M + m) * p.hl + j) * 128;
+                const __nv_bfloat16* wn = p.norm_w[which];
+                const uint32_t hbase = tacc + c0;
+                // pass 1: the bf16 head values (the GEMM output the reference normalises) and their sum of squares
+                float ss = 0.0f;
+#pragma unroll 1
+                for (int cc = 0; cc < 128; cc += 32) {
+                  uint32_t r[32];
+                  tmem_ld32(hbase + cc, r);
+                  tmem_ld_wait();
+                  reg_fence(r);
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) {
+                    const float y = rbf16(sam * (__ldg(p.sb + n0 + cc + i) * __uint_as_float(r[i])));
+                    ss = __fadd_rn(ss, __fmul_rn(y, y));
+                  }
+                }
+                const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), p.eps));
+                const int half = p.rot >> 1;
+                const float* trow = p.rope + m * p.rope_stride;
+                // pass 2: 16-column blocks; block b < half/16 rotates with block b + half/16
+#pragma unroll 1
+                for (int b = 0; b < 8; ++b) {
+                  const int e0 = 16 * b;
+                  if (e0 >= half && e0 < p.rot) continue;  // written with its partner below
+                  uint32_t ra[16], rb[16];
+                  tmem_ld16(hbase + e0, ra);
+                  const bool rotate = e0 < half;
+                  if (rotate) tmem_ld16(hbase + e0 + half, rb);
+                  tmem_ld_wait();
+                  reg_fence16<0>(ra);
+                  reg_fence16<0>(rb);
+                  float na[16], nb2[16];
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                    const float y = rbf16(sam * (__ldg(p.sb + n0 + e0 + i) * __uint_as_float(ra[i])));
+                    na[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), __bfloat162float(wn[e0 + i])));
+                  }
+                  if (rotate) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                      const float y = rbf16(sam * (__ldg(p.sb + n0 + e0 + half + i) * __uint_as_float(rb[i])));
+                      nb2[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), __bfloat162float(wn[e0 + half + i])));
+                    }
+                    float oa[16], ob[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                      const float cs = __ldg(trow + e0 + i), sn = __ldg(trow + half + e0 + i);
+                      oa[i] = __fsub_rn(__fmul_rn(na[i], cs), __fmul_rn(nb2[i], sn));
+                      ob[i] = __fadd_rn(__fmul_rn(nb2[i], cs), __fmul_rn(na[i], sn));
+                    }
+                    if (row_ok) {
+                      uint4* da = reinterpret_cast<uint4*>(dst + e0);
+                      uint4* db = reinterpret_cast<uint4*>(dst + e0 + half);
+#pragma unroll
+                      for (int q = 0; q < 2; ++q) {
+                        da[q] = make_uint4(pack2(oa[8 * q], oa[8 * q + 1], 0), pack2(oa[8 * q + 2], oa[8 * q + 3], 0),
+                                           pack2(oa[8 * q + 4], oa[8 * q + 5], 0), pack2(oa[8 * q + 6], oa[8 * q + 7], 0));
+                        db[q] = make_uint4(pack2(ob[8 * q], ob[8 * q + 1], 0), pack2(ob[8 * q + 2], ob[8 * q + 3], 0),
+                                           pack2(ob[8 * q + 4], ob[8 * q + 5], 0), pack2(ob[8 * q + 6], ob[8 * q + 7], 0));
+                      }
+                    }
+                  } else if (row_ok) {
+                    uint4* da = reinterpret_cast<uint4*>(dst + e0);
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+                      da[q] = make_uint4(pack2(na[8 * q], na[8 * q + 1], 0), pack2(na[8 * q + 2], na[8 * q + 3], 0),
+                                         pack2(na[8 * q + 4], na[8 * q + 5], 0), pack2(na[8 * q + 6], na[8 * q + 7], 0));
+                  }
+                }
+              }
+              continue;
+            }
             uint32_t r[32];
             tmem_ld32(tacc + c0, r);
             tmem_ld_wait();
@@ -388,6 +477,19 @@ extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t l
     }
     const int groups = send->groups > 1 ? send->groups : 1;
     if (send->heads % (groups * send->ws)) return fail(H3B_EINVAL, "fp8_gemm qkv_send: heads %% (groups * ws) != 0");
+    if ((send->q_norm_weight == nullptr) != (send->k_norm_weight == nullptr))
+      return fail(H3B_EINVAL, "fp8_gemm qkv_send: q and k norm weights go together");
+    if (send->q_norm_weight != nullptr) {
+      if (send->rot < 0 || send->rot > 128 || send->rot % 32)
+        return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: rot %d (0, 32, 64, 96 or 128)", send->rot);
+      if (send->rot > 0 && send->rope_table == nullptr) return fail(H3B_EINVAL, "fp8_gemm qkv_send: rope table");
+      p.norm_w[0] = static_cast<const __nv_bfloat16*>(send->q_norm_weight);
+      p.norm_w[1] = static_cast<const __nv_bfloat16*>(send->k_norm_weight);
+      p.rope = send->rope_table;
+      p.rope_stride = send->rope_stride;
+      p.rot = send->rot;
+      p.eps = send->eps;
+    }
     p.hd = send->heads * 128;
     p.hg = send->heads / groups;
     p.hl = p.hg / send->ws;

@@ -464,6 +464,64 @@ __global__ void bf16_to_f16_kernel(const uint4* __restrict__ x, uint4* __restric
     y[t] = bf16x8_to_f16x8(__ldg(x + t), range_flag);
 }
 
+
+// ---------------------------------------------------------------------------------------------------------------
+// qk RMSNorm + partial RoPE per (token, head) row, written into the Ulysses send layout (rope_into_send producer)
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void norm_rope_send_kernel(const uint16_t* __restrict__ x, int64_t m, int heads, int64_t stride_m,
+                                      int64_t stride_h, const __nv_bfloat16* __restrict__ w,
+                                      const float* __restrict__ table, int64_t tstride, int rot, float eps, int hl,
+                                      uint16_t* __restrict__ send) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int half = rot >> 1;
+  const int e0 = 4 * lane;  // this lane's 4 elements of the 128
+  float wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wv[i] = __bfloat162float(w[e0 + i]);
+  for (int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; row < m * heads;
+       row += warps) {
+    const int64_t mm = row / heads;
+    const int h = static_cast<int>(row - mm * heads);
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + mm * stride_m + h * stride_h + e0));
+    float f[4] = {lo_bf16(raw.x), hi_bf16(raw.x), lo_bf16(raw.y), hi_bf16(raw.y)};
+    float ss = __fmul_rn(f[0], f[0]);
+#pragma unroll
+    for (int i = 1; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(f[i], f[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), eps));
+    float n[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) n[i] = round_bf16(__fmul_rn(__fmul_rn(f[i], inv), wv[i]));
+    // rotation partner: element e pairs with e + half (first half) or e - half (second half of the rotated dims)
+    const bool first = e0 < half, second = e0 >= half && e0 < rot;
+    const int src = first ? lane + (half >> 2) : (second ? lane - (half >> 2) : lane);
+    float pn[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pn[i] = __shfl_sync(0xffffffffu, n[i], src);
+    float out[4];
+    const float* trow = table + mm * tstride;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (first) {
+        const float cs = __ldg(trow + e0 + i), sn = __ldg(trow + half + e0 + i);
+        out[i] = __fsub_rn(__fmul_rn(n[i], cs), __fmul_rn(pn[i], sn));       // a cos - b sin
+      } else if (second) {
+        const float cs = __ldg(trow + e0 - half + i), sn = __ldg(trow + e0 + i);
+        out[i] = __fadd_rn(__fmul_rn(n[i], cs), __fmul_rn(pn[i], sn));       // b cos + a sin
+      } else {
+        out[i] = n[i];
+      }
+    }
+    const int p = h / hl, j = h - p * hl;
+    uint2 o;
+    o.x = pack_bf16x2(out[0], out[1]);
+    o.y = pack_bf16x2(out[2], out[3]);
+    *reinterpret_cast<uint2*>(send + ((static_cast<int64_t>(p) * m + mm) * hl + j) * 128 + e0) = o;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------------------------------------------
@@ -688,6 +746,28 @@ int h3b_pack_by_dest(const void* x, int64_t m, int32_t heads, int32_t d, int64_t
                                                               stride_m, stride_h, ws, static_cast<uint16_t*>(send),
                                                               to_f16, range_flag);
   H3B_CHECK_LAUNCH("pack_by_dest launch");
+  return H3B_OK;
+}
+
+int h3b_norm_rope_send(const void* x, int64_t m, int32_t heads, int64_t stride_m, int64_t stride_h,
+                       const void* weight, const float* table, int64_t table_stride, int32_t rot, float eps,
+                       int32_t ws, void* send, h3b_stream_t stream) {
+  if (m < 0 || heads <= 0 || ws <= 0 || heads % ws) return fail(H3B_EINVAL, "norm_rope_send: bad shape");
+  if (rot < 0 || rot > 128 || rot % 8) return fail(H3B_EUNSUPPORTED, "norm_rope_send: rot %d (multiple of 8, <= 128)", rot);
+  if (m == 0) return H3B_OK;
+  if (x == nullptr || weight == nullptr || send == nullptr || (rot > 0 && table == nullptr))
+    return fail(H3B_EINVAL, "norm_rope_send: null pointer");
+  if (stride_m % 4 || stride_h % 4 || (reinterpret_cast<uintptr_t>(x) & 7u) || (reinterpret_cast<uintptr_t>(send) & 7u))
+    return fail(H3B_EALIGN, "norm_rope_send: 8-byte granules needed");
+  const int64_t warps = m * heads;
+  const int threads = 256;
+  int64_t blocks = (warps * 32 + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  norm_rope_send_kernel<<<static_cast<int>(blocks), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), m, heads, stride_m, stride_h, static_cast<const __nv_bfloat16*>(weight), table,
+      table_stride, rot, eps, heads / ws, static_cast<uint16_t*>(send));
+  H3B_CHECK_LAUNCH("norm_rope_send launch");
   return H3B_OK;
 }
 

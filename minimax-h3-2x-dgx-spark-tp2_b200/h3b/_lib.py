@@ -21,7 +21,8 @@ _p, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ct
 
 class QkvSend(ctypes.Structure):
     _fields_ = [("send", _p * 3), ("heads", _i32), ("head_dim", _i32), ("ws", _i32), ("v_f16", _i32),
-                ("range_flag", _p), ("groups", _i32)]
+                ("range_flag", _p), ("groups", _i32), ("q_norm_weight", _p), ("k_norm_weight", _p),
+                ("rope_table", _p), ("rope_stride", _i64), ("rot", _i32), ("eps", _f32)]
 
 
 # name -> (restype, argtypes): exactly the declarations of include/h3b.h
@@ -48,6 +49,7 @@ SIGNATURES = {
                                                   _i64, _i64, _i64, _i32, _i32, _f32, _p]),
     "h3b_pack_by_dest": (ctypes.c_int, [_p, _i64, _i32, _i32, _i64, _i64, _i32, _p, _i32, _p, _p]),
     "h3b_unpack_recv": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _p]),
+    "h3b_norm_rope_send": (ctypes.c_int, [_p, _i64, _i32, _i64, _i64, _p, _p, _i64, _i32, _f32, _i32, _p, _p]),
     "h3b_bf16_to_f16": (ctypes.c_int, [_p, _p, _i64, _p, _p]),
 }
 

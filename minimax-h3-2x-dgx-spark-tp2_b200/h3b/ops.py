@@ -218,11 +218,13 @@ def fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torc
 
 def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, heads: int, ws: int, *,
                       bias: torch.Tensor | None = None, v_f16: bool = False, sends=None,
-                      range_flag: torch.Tensor | None = None, groups: int = 1):
+                      range_flag: torch.Tensor | None = None, groups: int = 1, qk_norm=None):
     """qkv projection whose epilogue writes q, k, v straight into the Ulysses send buffers (the producer redirection
     of ulysses_exact.fused_into_send, h3_tp2/ulysses_exact.py:278, moved into the GEMM).  groups = 1: each buffer is
     stock's [P, M, H/P, d]; groups = G > 1: [G, P, M, H/(G*P), d], head h = g*(H/G) + p*(H/(G*P)) + j, one
-    contiguous all-to-all per group (the head-group overlap layout)."""
+    contiguous all-to-all per group (the head-group overlap layout).  ``qk_norm = (q_weight, k_weight, rope_table,
+    eps)`` applies the per-(token, head) RMSNorm + partial RoPE of the upstream producer to q and k in the epilogue
+    (rope_table [M, R] fp32, cos | sin, R in {0, 32, 64, 96, 128})."""
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
@@ -239,6 +241,17 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
         desc.send[i] = sends[i].data_ptr()
     desc.heads, desc.head_dim, desc.ws, desc.v_f16 = heads, 128, ws, int(bool(v_f16))
     desc.groups = int(groups)
+    if qk_norm is not None:
+        qw, kw, table, eps = qk_norm
+        _need_cuda(qw, kw, table)
+        qw, kw = qw.contiguous(), kw.contiguous()
+        table = table.float()
+        if table.stride(-1) != 1:
+            table = table.contiguous()
+        desc.q_norm_weight, desc.k_norm_weight = qw.data_ptr(), kw.data_ptr()
+        desc.rope_table, desc.rope_stride, desc.rot = table.data_ptr(), table.stride(0), table.shape[-1]
+        desc.eps = float(eps)
+        keep = (qw, kw, table)  # alive until the launch below returns
     desc.range_flag = _ptr(range_flag)
     _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
               _ptr(bias), None, 0, M, N, K, OUT_BF16, EPI_QKV_SEND, ctypes.byref(desc), _stream(a))
@@ -310,6 +323,24 @@ def pack_by_dest(x: torch.Tensor, ws: int, out: torch.Tensor | None = None, *, t
     send = out if out is not None else torch.empty((ws, m, h // ws, d), dtype=dt, device=x.device)
     _lib.call("h3b_pack_by_dest", x.data_ptr(), m, h, d, x.stride(0), x.stride(1), ws, send.data_ptr(),
               int(bool(to_f16)), _ptr(range_flag), _stream(x))
+    return send
+
+
+def norm_rope_send(x: torch.Tensor, weight: torch.Tensor, table: torch.Tensor, eps: float, ws: int,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """qk RMSNorm + partial RoPE of x [M, H, 128] (strided) written into send [P, M, H/P, 128] (the upstream
+    norm+RoPE producer as ``ulysses_exact.rope_into_send`` launches it per destination, h3_tp2/ulysses_exact.py:264).
+    table [M, R] fp32 holds cos[:R/2] | sin[R/2:] per token."""
+    _need_cuda(x, weight, table)
+    m, h, d = x.shape
+    if d != 128 or x.stride(2) != 1:
+        raise ValueError("norm_rope_send: x must be [M, H, 128] with unit innermost stride")
+    table = table.float()
+    if table.stride(-1) != 1:
+        table = table.contiguous()
+    send = out if out is not None else torch.empty((ws, m, h // ws, d), dtype=torch.bfloat16, device=x.device)
+    _lib.call("h3b_norm_rope_send", x.data_ptr(), m, h, x.stride(0), x.stride(1), weight.contiguous().data_ptr(),
+              table.data_ptr(), table.stride(0), table.shape[-1], float(eps), ws, send.data_ptr(), _stream(x))
     return send
 
 

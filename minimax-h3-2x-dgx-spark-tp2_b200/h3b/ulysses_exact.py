@@ -44,6 +44,16 @@ def unpack(send: torch.Tensor) -> torch.Tensor:
     return ops.unpack_recv(send.contiguous())
 
 
+def rope_into_send(send_q, send_k, q, k, q_weight, k_weight, rope_table, eps, launch=None) -> None:  # noqa: ANN001
+    """The norm+RoPE producer writing straight into the send buffers (h3_tp2/ulysses_exact.py:264): q/k [M, H, d]
+    views of the qkv output -> send_q / send_k [P, M, H/P, d].  ``launch`` (the reference's per-destination launcher
+    argument) is accepted for signature compatibility; one CUDA kernel covers all destinations."""
+    del launch
+    ws = send_q.shape[0]
+    ops.norm_rope_send(q, q_weight, rope_table, eps, ws, out=send_q)
+    ops.norm_rope_send(k, k_weight, rope_table, eps, ws, out=send_k)
+
+
 def exchange_fwd(send: torch.Tensor, a2a, pg=None) -> torch.Tensor:  # noqa: ANN001
     """One forward all-to-all; the receive buffer viewed [1, P*M, hl, d] (h3_tp2/ulysses_exact.py:130)."""
     recv = torch.empty_like(send)

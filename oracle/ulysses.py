@@ -95,3 +95,23 @@ def run_ranks(fn, ws: int):
         if e is not None:
             raise e
     return res
+
+
+def norm_rope(x: torch.Tensor, w: torch.Tensor, table: torch.Tensor, eps: float) -> torch.Tensor:
+    """Per-(token, head) RMSNorm over head_dim then partial RoPE, as the reference's eager stand-in for the upstream
+    ``_rms_norm_rope_kernel`` (``tests/test_ulysses_exact.py:107-116``): x [M, H, d] bf16, w [d], table [M, R] fp32
+    holding cos[:R/2] | sin[R/2:]; n = bf16(x * rsqrt(mean(x^2) + eps) * w); the first R dims rotate in half-split
+    pairs (a, b) = (n[i], n[i + R/2]) -> (a cos - b sin, b cos + a sin); the rest pass; result bf16."""
+    xf = x.float()
+    inv = torch.rsqrt((xf * xf).sum(-1, keepdim=True) / x.shape[-1] + eps)
+    n = (xf * inv * w.float()).to(torch.bfloat16).float()
+    half = table.shape[-1] // 2
+    cos, sin = table[:, None, :half].float(), table[:, None, half:].float()
+    a, b = n[..., :half], n[..., half:2 * half]
+    return torch.cat((a * cos - b * sin, b * cos + a * sin, n[..., 2 * half:]), dim=-1).to(x.dtype)
+
+
+def norm_rope_into_send(x: torch.Tensor, w: torch.Tensor, table: torch.Tensor, eps: float, ws: int) -> torch.Tensor:
+    """``ulysses_exact.rope_into_send`` (h3_tp2/ulysses_exact.py:264-271) with the eager producer: the normed and
+    rotated q (or k) of each destination's heads written into send [P, M, H/P, d]."""
+    return pack(norm_rope(x, w, table, eps), ws)

@@ -16,6 +16,7 @@ Reference functions exercised (paths inside the reference project):
   rms:      h3_tp2/fp8_quant_fuse.py:330 rms_quant, :350 gate_rms_quant (stock = tests/fake_h3_consumers.py mirrors)
   ulysses:  h3_tp2/ulysses_exact.py:187 exact_forward, :108 send_shape, :119 pack_into, :156 exchange_back, and the
             stock exchange tests/test_ulysses_exact.py:74 stock_all_to_all_4d, with FakeA2A (:25)
+  rope:     h3_tp2/ulysses_exact.py:264 rope_into_send with the eager norm+RoPE stand-in tests/test_ulysses_exact.py:107
 """
 from __future__ import annotations
 
@@ -222,6 +223,27 @@ def gen_ulysses(ux, tue) -> dict:
     return out
 
 
+def gen_rope(ux, tue) -> dict:
+    """The upstream norm+RoPE producer's eager stand-in (tests/test_ulysses_exact.py:107-116) written per destination
+    by ulysses_exact.rope_into_send (h3_tp2/ulysses_exact.py:264), on the reference's own input recipe
+    (tests/test_ulysses_exact.py:123-130: q/k from a random qkv, weights 1 + 0.1 N(0,1), table N(0,1) [M, 96])."""
+    out = {}
+    for ws, m, heads in ((2, 24, 8), (4, 16, 8)):
+        g = torch.Generator().manual_seed(20 + ws)
+        qkv = torch.randn(m, 3 * heads * 128, generator=g).to(BF16)
+        q, k, v = (t.view(m, heads, 128) for t in qkv.split([heads * 128] * 3, dim=-1))
+        w_q = (1 + 0.1 * torch.randn(128, generator=g)).to(BF16)
+        w_k = (1 + 0.1 * torch.randn(128, generator=g)).to(BF16)
+        table = torch.randn(m, 96, generator=g)
+        sq = torch.empty(ux.send_shape(m, heads, 128, ws), dtype=BF16)
+        sk = torch.empty_like(sq)
+        ux.rope_into_send(sq, sk, q, k, w_q, w_k, table, 1e-6, tue.eager_launch)
+        out.update({f"ws{ws}_qkv": bits16(qkv), f"ws{ws}_wq": bits16(w_q), f"ws{ws}_wk": bits16(w_k),
+                    f"ws{ws}_table": f32(table), f"ws{ws}_sendq": bits16(sq), f"ws{ws}_sendk": bits16(sk),
+                    f"ws{ws}_shape": np.array([m, heads])})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -239,6 +261,7 @@ def main() -> None:
     np.savez_compressed(HERE / "swiglu.npz", **gen_swiglu(fp8_swiglu, fp8_quant_fuse))
     np.savez_compressed(HERE / "rms.npz", **gen_rms(fp8_quant_fuse, fake_h3_consumers))
     np.savez_compressed(HERE / "ulysses.npz", **gen_ulysses(ulysses_exact, test_ulysses_exact))
+    np.savez_compressed(HERE / "rope.npz", **gen_rope(ulysses_exact, test_ulysses_exact))
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

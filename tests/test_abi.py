@@ -75,4 +75,4 @@ def test_check_raises_with_the_reason():
 
 
 def test_qkv_send_struct_layout():
-    assert ctypes.sizeof(_lib.QkvSend) == 3 * 8 + 4 * 4 + 8 + 8
+    assert ctypes.sizeof(_lib.QkvSend) == 96

@@ -132,3 +132,28 @@ def test_deterministic_repeat(dev):
     y0 = ops.fp8_gemm(a, w, sa, sb)
     for _ in range(3):
         assert torch.equal(ops.fp8_gemm(a, w, sa, sb).view(torch.int16), y0.view(torch.int16))
+
+
+@pytest.mark.parametrize("ws", [1, 2])
+def test_qkv_send_epilogue_with_qk_norm_rope(dev, ws):
+    """The norm+RoPE producer fused into the qkv epilogue equals the oracle producer applied to the GEMM's own bf16
+    output (a bf16 ulp at most: rsqrt and the sum order)."""
+    from oracle import ulysses as oul
+    M, heads, K = 200, 4, 256
+    N = 3 * heads * 128
+    g = torch.Generator(device=dev).manual_seed(7)
+    a = torch.randint(-4, 5, (M, K), device=dev, generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), device=dev, generator=g).to(E4M3)
+    sa = torch.rand(M, device=dev, generator=g) * 0.05
+    sb = torch.rand(N, device=dev, generator=g) * 0.05
+    qw = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(BF16)
+    kw = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(BF16)
+    table = torch.randn(M, 96, device=dev, generator=g)
+    sq, sk, sv = ops.fp8_gemm_qkv_send(a, w, sa, sb, heads, ws, qk_norm=(qw, kw, table, 1e-6))
+    y = ops.fp8_gemm(a, w, sa, sb).cpu()
+    q, k, v = (t.reshape(M, heads, 128) for t in y.split(heads * 128, dim=1))
+    for got, x, wt in ((sq, q, qw), (sk, k, kw)):
+        ref = oul.norm_rope_into_send(x, wt.cpu(), table.cpu(), 1e-6, ws)
+        ud = ulp_diff_bf16(got.cpu(), ref)
+        assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.98
+    assert same_bits(sv.cpu(), ou.pack(v, ws))

@@ -36,3 +36,36 @@ def test_bf16_to_f16(dev):
     flag = torch.zeros(1, dtype=torch.int32, device=dev)
     y = ops.bf16_to_f16(x.to(dev), flag)
     assert torch.equal(y.cpu().float(), x.float()) and int(flag.item()) == 0
+
+
+def test_norm_rope_send_against_reference_vectors(dev, golden):
+    from _util import t16, tf, ulp_diff_bf16
+    g = golden("rope")
+    for ws in (2, 4):
+        m, heads = (int(v) for v in g[f"ws{ws}_shape"])
+        qkv = t16(g[f"ws{ws}_qkv"]).to(dev)
+        q, k, _ = (t.view(m, heads, 128) for t in qkv.split([heads * 128] * 3, dim=-1))
+        table = tf(g[f"ws{ws}_table"]).to(dev)
+        sq = torch.empty((ws, m, heads // ws, 128), dtype=BF16, device=dev)
+        sk = torch.empty_like(sq)
+        ulysses_exact.rope_into_send(sq, sk, q, k, t16(g[f"ws{ws}_wq"]).to(dev), t16(g[f"ws{ws}_wk"]).to(dev), table,
+                                     1e-6)
+        for got, key in ((sq, "sendq"), (sk, "sendk")):
+            ud = ulp_diff_bf16(got.cpu(), t16(g[f"ws{ws}_{key}"]))
+            # rsqrt on the GPU vs the CPU's: a bf16 ulp at most, on few elements
+            assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.98
+
+
+def test_norm_rope_send_dit_shape(dev):
+    from oracle import ulysses as oul
+    from _util import ulp_diff_bf16
+    m, heads, ws = 300, 40, 4
+    gen = torch.Generator().manual_seed(2)
+    qkv = torch.randn(m, 3 * heads * 128, generator=gen).to(BF16)
+    q = qkv[:, :heads * 128].view(m, heads, 128)
+    w = (1 + 0.1 * torch.randn(128, generator=gen)).to(BF16)
+    table = torch.randn(m, 96, generator=gen)
+    got = ops.norm_rope_send(qkv.to(dev)[:, :heads * 128].view(m, heads, 128), w.to(dev), table.to(dev), 1e-6, ws)
+    ref = oul.norm_rope_into_send(q, w, table, 1e-6, ws)
+    ud = ulp_diff_bf16(got.cpu(), ref)
+    assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.98

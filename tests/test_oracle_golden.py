@@ -129,3 +129,14 @@ def test_a2a_reference_matches_fake_collective():
 def test_quant_dtype_contract():
     q, s = oq.quant(torch.randn(4, 64).to(BF16))
     assert q.dtype == E4M3 and s.shape == (4, 1) and s.dtype == torch.float32
+
+
+def test_norm_rope_into_send(golden):
+    g = golden("rope")
+    for ws in (2, 4):
+        m, heads = (int(v) for v in g[f"ws{ws}_shape"])
+        qkv = t16(g[f"ws{ws}_qkv"])
+        q, k, _ = (t.view(m, heads, 128) for t in qkv.split([heads * 128] * 3, dim=-1))
+        table = tf(g[f"ws{ws}_table"])
+        assert same_bits(ou.norm_rope_into_send(q, t16(g[f"ws{ws}_wq"]), table, 1e-6, ws), t16(g[f"ws{ws}_sendq"]))
+        assert same_bits(ou.norm_rope_into_send(k, t16(g[f"ws{ws}_wk"]), table, 1e-6, ws), t16(g[f"ws{ws}_sendk"]))
