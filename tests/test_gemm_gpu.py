@@ -155,5 +155,6 @@ def test_qkv_send_epilogue_with_qk_norm_rope(dev, ws):
     for got, x, wt in ((sq, q, qw), (sk, k, kw)):
         ref = oul.norm_rope_into_send(x, wt.cpu(), table.cpu(), 1e-6, ws)
         ud = ulp_diff_bf16(got.cpu(), ref)
-        assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.98
+        assert (ud == 0).float().mean().item() > 0.98 and int(ud.max()) <= 8
+        assert rel_l2(got.float().cpu(), ref.float()) <= 2e-3
     assert same_bits(sv.cpu(), ou.pack(v, ws))

@@ -2,7 +2,7 @@
 import pytest
 import torch
 
-from _util import BF16, same_bits
+from _util import BF16, rel_l2, same_bits
 from h3b import ops, ulysses_exact
 from oracle import ulysses as ou
 
@@ -52,8 +52,10 @@ def test_norm_rope_send_against_reference_vectors(dev, golden):
                                      1e-6)
         for got, key in ((sq, "sendq"), (sk, "sendk")):
             ud = ulp_diff_bf16(got.cpu(), t16(g[f"ws{ws}_{key}"]))
-            # rsqrt on the GPU vs the CPU's: a bf16 ulp at most, on few elements
-            assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.98
+            # rsqrt on the GPU vs the CPU's moves a normalised value by a bf16 ulp at most; the rotation
+            # a cos - b sin can cancel and turn that into a few ulps of a smaller result, on few elements
+            assert (ud == 0).float().mean().item() > 0.98 and int(ud.max()) <= 8
+            assert rel_l2(got.float().cpu(), t16(g[f"ws{ws}_{key}"]).float()) <= 2e-3
 
 
 def test_norm_rope_send_dit_shape(dev):
@@ -68,4 +70,5 @@ def test_norm_rope_send_dit_shape(dev):
     got = ops.norm_rope_send(qkv.to(dev)[:, :heads * 128].view(m, heads, 128), w.to(dev), table.to(dev), 1e-6, ws)
     ref = oul.norm_rope_into_send(q, w, table, 1e-6, ws)
     ud = ulp_diff_bf16(got.cpu(), ref)
-    assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.98
+    assert (ud == 0).float().mean().item() > 0.98 and int(ud.max()) <= 8
+    assert rel_l2(got.float().cpu(), ref.float()) <= 2e-3
