@@ -35,6 +35,8 @@ extern "C" {
 
 typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 
+#define H3B_MAX_RANKS 8 /* Ulysses ranks of one NVSwitch box */
+
 enum h3b_status {
   H3B_OK = 0,
   H3B_EINVAL = -1,       /* bad shape, null pointer, negative size */
@@ -82,12 +84,19 @@ typedef struct h3b_qkv_send {
   int64_t rope_stride;
   int32_t rot;               /* 0, 32, 64, 96 or 128 */
   float eps;
+  /* optional peer-memory exchange (p2p != 0; groups must be 1; send[] and range_flag unused): destination rank p's
+   * slab is stored straight into rank p's receive buffer peer_recv[p][which] ([P, M, H/P, d], slot `rank`), so the
+   * forward all-to-all (h3_tp2/ulysses_exact.py:94 dist.all_to_all_single) never runs.  No reference counterpart. */
+  int32_t p2p;
+  int32_t rank;
+  void* peer_recv[H3B_MAX_RANKS][3];
+  int32_t* peer_range_flag[H3B_MAX_RANKS]; /* v_f16 overflow flag of each destination rank (replaces range_flag) */
 } h3b_qkv_send;
 
 /* ---------------------------------------------------------------------------------------------------------------
  * library information
  * ------------------------------------------------------------------------------------------------------------- */
-H3B_API int h3b_abi_version(void);
+H3B_API int h3b_abi_version(void); /* 2: h3b_qkv_send gained the peer-memory fields */
 H3B_API const char* h3b_status_string(int status);
 H3B_API const char* h3b_last_error(void);
 /* Reads and clears the sticky device status word of the current device (0 or a negative h3b_status). Synchronises
@@ -204,6 +213,38 @@ H3B_API int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t q_h
                                        int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o,
                                        int64_t o_tok, int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv,
                                        int32_t heads, int32_t head_dim, float scale, h3b_stream_t stream);
+
+/* Peer-memory variant of h3b_flash_attn_fwd for the Ulysses reverse exchange (no reference counterpart: it replaces
+ * the head->seq dist.all_to_all_single of h3_tp2/ulysses_exact.py:94): instead of o, each output row t of this
+ * rank's heads goes to its owner rank t / m_rows, into that rank's reverse receive buffer peer_back[owner]
+ * ([P, m_rows, heads, 128] bf16, this rank's slot `rank`), so the head->seq all-to-all never runs.
+ * peer_back: host array of ws device pointers (this rank's own buffer at index rank). */
+H3B_API int h3b_flash_attn_fwd_p2p(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                   int64_t k_head, const void* v, int64_t v_tok, int64_t v_head,
+                                   void* const* peer_back, int32_t ws, int32_t rank, int64_t m_rows, int64_t s_q,
+                                   int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
+                                   int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * peer memory (CUDA IPC over NVLink; no multicast) for the Ulysses P2P exchange.  No reference counterpart: the
+ * reference exchanges through NCCL only (h3_tp2/ulysses_exact.py:94, h3_tp2/ulysses_overlap.py:34,45).
+ * ------------------------------------------------------------------------------------------------------------- */
+typedef struct h3b_ipc_handle {
+  unsigned char bytes[64];
+} h3b_ipc_handle;
+
+/* cudaMalloc + zero fill + IPC handle of `bytes` on the current device. */
+H3B_API int h3b_p2p_alloc(size_t bytes, void** ptr, h3b_ipc_handle* handle);
+/* Maps a peer's allocation into this process (peer access enabled lazily); *ptr is its device address here. */
+H3B_API int h3b_p2p_open(const h3b_ipc_handle* handle, void** ptr);
+H3B_API int h3b_p2p_close(void* peer_ptr);
+H3B_API int h3b_p2p_free(void* ptr);
+/* One kernel on `stream`: this rank stores `epoch` (system-scope release, after a system fence) into slot `rank` of every
+ * rank's flag array (peer_flags[p], an int32[ws] on rank p), then waits until its own flags (my_flags) hold at least
+ * `epoch` in every slot (acquire loads, bounded: H3B_ETIMEOUT in the device status word).  Work enqueued before it on
+ * this stream is visible to the peers' work enqueued after their matching call. */
+H3B_API int h3b_p2p_signal_wait(int32_t* const* peer_flags, int32_t* my_flags, int32_t ws, int32_t rank,
+                                int32_t epoch, h3b_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Ulysses layout kernels

@@ -40,6 +40,10 @@ struct Params {
   int nkv;
   const int32_t* range_flag;
   int range_mode;  // 0: flag set -> record H3B_ERANGE, skip; 1: flag set -> skip; 2: run only when the flag is set
+  // m_rows > 0: output row t goes to rank t / m_rows, row (rank * m_rows + t % m_rows) of peer_o[t / m_rows]
+  int64_t m_rows;
+  int rank;
+  uint16_t* peer_o[H3B_MAX_RANKS];
   WaitCtl wc;
 };
 
@@ -113,7 +117,7 @@ __device__ __forceinline__ uint32_t pack_p(float lo, float hi) {
 template <bool F16, int POLY = 0>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, Params p) {
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ Params p) {
   constexpr uint32_t IDESC_QK = idesc_make(FMT_BF16, FMT_BF16, 0, BQ, BKV);
   constexpr uint32_t IDESC_PV = idesc_make(F16 ? FMT_F16 : FMT_BF16, F16 ? FMT_F16 : FMT_BF16, 1, BQ, D);
 
@@ -374,7 +378,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const int64_t row = q0 + q * BQ + sub * 32 + lane;
         const float inv_l = 1.0f / l_run;
-        uint16_t* orow = p.o + row * p.o_tok + static_cast<int64_t>(head) * p.o_head;
+        uint16_t* orow;
+        if (p.m_rows > 0) {  // Ulysses reverse exchange through peer memory
+          const int64_t owner = row / p.m_rows;
+          orow = p.peer_o[owner < H3B_MAX_RANKS ? owner : 0] +
+                 (p.rank * p.m_rows + (row - owner * p.m_rows)) * p.o_tok + static_cast<int64_t>(head) * p.o_head;
+        } else {
+          orow = p.o + row * p.o_tok + static_cast<int64_t>(head) * p.o_head;
+        }
 #pragma unroll
         for (int cc = 0; cc < D; cc += 32) {
           uint32_t o[32];
@@ -519,6 +530,52 @@ extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, 
   p.wc.status = device_status_word();
   p.wc.timeout = wait_timeout_ns();
   if (p.wc.status == nullptr) return fail(H3B_ECUDA, "flash_attn: device status word");
+  return launch_attention(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v_f16 != 0, p,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_flash_attn_fwd_p2p(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                      int64_t k_head, const void* v, int64_t v_tok, int64_t v_head,
+                                      void* const* peer_back, int32_t ws, int32_t rank, int64_t m_rows, int64_t s_q,
+                                      int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
+                                      int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream) {
+  using namespace h3b::attn;
+  if (peer_back == nullptr || ws < 1 || ws > H3B_MAX_RANKS || rank < 0 || rank >= ws)
+    return fail(H3B_EINVAL, "flash_attn_p2p: ws %d rank %d", ws, rank);
+  if (s_q < 0 || s_kv <= 0 || heads <= 0) return fail(H3B_EINVAL, "flash_attn_p2p: s_q %lld s_kv %lld heads %d", (long long)s_q, (long long)s_kv, heads);
+  if (m_rows <= 0 || s_q != m_rows * ws)
+    return fail(H3B_EINVAL, "flash_attn_p2p: s_q %lld must be ws * m_rows (%d * %lld)", (long long)s_q, ws, (long long)m_rows);
+  if (head_dim != 128) return fail(H3B_EUNSUPPORTED, "flash_attn_p2p: head_dim %d (only 128)", head_dim);
+  if (valid_kv < 0) valid_kv = s_kv;
+  if (valid_kv == 0 || valid_kv > s_kv) return fail(H3B_EINVAL, "flash_attn_p2p: valid_kv %lld of %lld", (long long)valid_kv, (long long)s_kv);
+  if (q == nullptr || k == nullptr || v == nullptr) return fail(H3B_EINVAL, "flash_attn_p2p: null pointer");
+  if (heads > 65535 || s_q > (1ll << 31) - 1 || s_kv > (1ll << 31) - 1) return fail(H3B_EUNSUPPORTED, "flash_attn_p2p: size limits");
+  const int64_t strides[6] = {q_tok, q_head, k_tok, k_head, v_tok, v_head};
+  for (int64_t s : strides)
+    if (s <= 0 || s % 8) return fail(H3B_EALIGN, "flash_attn_p2p: token/head strides must be positive multiples of 8");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)
+    return fail(H3B_EALIGN, "flash_attn_p2p: q, k, v must be 16-byte aligned");
+
+  Params p{};
+  for (int r = 0; r < ws; ++r) {
+    if (peer_back[r] == nullptr || (reinterpret_cast<uintptr_t>(peer_back[r]) & 15u))
+      return fail(H3B_EALIGN, "flash_attn_p2p: peer buffer %d null or not 16-byte aligned", r);
+    p.peer_o[r] = static_cast<uint16_t*>(peer_back[r]);
+  }
+  p.s_q = s_q;
+  p.s_kv = s_kv;
+  p.valid_kv = valid_kv;
+  p.heads = heads;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = p.peer_o[rank];
+  p.o_tok = static_cast<int64_t>(heads) * 128;  // receive buffers [P, m_rows, heads, 128]
+  p.o_head = 128;
+  p.m_rows = m_rows;
+  p.rank = rank;
+  p.range_flag = v_f16 ? range_flag : nullptr;
+  p.wc.status = device_status_word();
+  p.wc.timeout = wait_timeout_ns();
+  if (p.wc.status == nullptr) return fail(H3B_ECUDA, "flash_attn_p2p: device status word");
   return launch_attention(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v_f16 != 0, p,
                           reinterpret_cast<cudaStream_t>(stream));
 }

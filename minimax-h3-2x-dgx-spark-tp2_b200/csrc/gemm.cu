@@ -49,8 +49,22 @@ struct Params {
   int64_t rope_stride;
   int rot;
   float eps;
+  int p2p;                               // QKV_SEND into the peers' receive buffers
+  int rank;
+  void* peer[H3B_MAX_RANKS][3];
+  int32_t* peer_rf[H3B_MAX_RANKS];
   WaitCtl wc;
 };
+
+// QKV_SEND destination of (which, group g, destination rank): the slab base and its slot index in that buffer
+__device__ __forceinline__ uint16_t* send_slab(const Params& p, int which, int g, int dst_rank, int64_t& slot) {
+  if (p.p2p) {
+    slot = p.rank;  // the peer's receive buffer [P, M, hl, d], indexed by the source rank
+    return static_cast<uint16_t*>(p.peer[dst_rank][which]);
+  }
+  slot = static_cast<int64_t>(g) * p.ws + dst_rank;  // (group, destination) slab of this rank's send buffer
+  return static_cast<uint16_t*>(p.send[which]);
+}
 
 __device__ __forceinline__ float rbf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -89,7 +103,8 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -276,8 +291,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int h = hcol >> 7;
                 const int g = h / p.hg, hh = h - g * p.hg;
                 const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
-                const int64_t seg = static_cast<int64_t>(g) * p.ws + dst_rank;
-                uint16_t* dst = static_cast<uint16_t*>(p.send[which]) + ((seg * p.M + m) * p.hl + j) * 128;
+                int64_t seg;
+                uint16_t* dst = send_slab(p, which, g, dst_rank, seg);
+                dst += ((seg * p.M + m) * p.hl + j) * 128;
                 const __nv_bfloat16* wn = p.norm_w[which];
                 const uint32_t hbase = tacc + c0;
                 // pass 1: the bf16 head values (the GEMM output the reference normalises) and their sum of squares
@@ -296,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), p.eps));
                 const int half = p.rot >> 1;
-                const float* trow = p.rope + m * p.rope_stride;
+                const float* trow = p.rope + (row_ok ? m : 0) * p.rope_stride;  // rows past M read row 0
                 // pass 2: 16-column blocks; block b < half/16 rotates with block b + half/16
 #pragma unroll 1
                 for (int b = 0; b < 8; ++b) {
@@ -377,16 +393,18 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int h = hcol >> 7, c = hcol & 127;
               const int g = h / p.hg, hh = h - g * p.hg;
               const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
-              const int64_t seg = static_cast<int64_t>(g) * p.ws + dst_rank;  // (group, destination) slab
+              int64_t seg;
+              uint16_t* slab = send_slab(p, which, g, dst_rank, seg);
               const int64_t off = ((seg * p.M + m) * p.hl + j) * 128 + c;
               const bool as_f16 = which == 2 && p.v_f16;
-              if (as_f16 && p.range_flag != nullptr) {
+              int32_t* rf = p.p2p ? p.peer_rf[dst_rank] : p.range_flag;
+              if (as_f16 && rf != nullptr) {
                 bool bad = false;
 #pragma unroll
                 for (int i = 0; i < 32; ++i) bad |= fabsf(v[i]) > 65504.0f && isfinite(v[i]);
-                if (bad) atomicExch(p.range_flag, 1);
+                if (bad) atomicExch(rf, 1);
               }
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.send[which]) + off);
+              uint4* dst = reinterpret_cast<uint4*>(slab + off);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 uint32_t w[4];
@@ -465,17 +483,33 @@ extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t l
     p.half = N / 2;
     p.num_nb = static_cast<int>(p.half / 128);
   } else if (epilogue == H3B_EPI_QKV_SEND) {
-    if (send == nullptr || send->send[0] == nullptr || send->send[1] == nullptr || send->send[2] == nullptr)
-      return fail(H3B_EINVAL, "fp8_gemm qkv_send: send buffers");
+    if (send == nullptr) return fail(H3B_EINVAL, "fp8_gemm qkv_send: send descriptor");
     if (send->head_dim != 128) return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: head_dim must be 128");
     if (send->heads <= 0 || send->ws <= 0 || send->heads % send->ws) return fail(H3B_EINVAL, "fp8_gemm qkv_send: heads % ws");
     if (N != 3ll * send->heads * 128) return fail(H3B_EINVAL, "fp8_gemm qkv_send: N must be 3 * heads * 128");
     if (out_dtype != H3B_OUT_BF16) return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: bf16 output only");
-    for (int i = 0; i < 3; ++i) {
-      if (reinterpret_cast<uintptr_t>(send->send[i]) & 15u) return fail(H3B_EALIGN, "fp8_gemm qkv_send: send alignment");
-      p.send[i] = send->send[i];
-    }
     const int groups = send->groups > 1 ? send->groups : 1;
+    if (send->p2p) {
+      if (groups != 1) return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: p2p with head groups");
+      if (send->ws > H3B_MAX_RANKS || send->rank < 0 || send->rank >= send->ws)
+        return fail(H3B_EINVAL, "fp8_gemm qkv_send: p2p ws %d rank %d", send->ws, send->rank);
+      p.p2p = 1;
+      p.rank = send->rank;
+      for (int r = 0; r < send->ws; ++r) {
+        for (int i = 0; i < 3; ++i) {
+          if (send->peer_recv[r][i] == nullptr || (reinterpret_cast<uintptr_t>(send->peer_recv[r][i]) & 15u))
+            return fail(H3B_EALIGN, "fp8_gemm qkv_send: peer buffer %d/%d null or not 16-byte aligned", r, i);
+          p.peer[r][i] = send->peer_recv[r][i];
+        }
+        p.peer_rf[r] = send->v_f16 ? send->peer_range_flag[r] : nullptr;
+      }
+    } else {
+      for (int i = 0; i < 3; ++i) {
+        if (send->send[i] == nullptr || (reinterpret_cast<uintptr_t>(send->send[i]) & 15u))
+          return fail(H3B_EALIGN, "fp8_gemm qkv_send: send buffer %d null or not 16-byte aligned", i);
+        p.send[i] = send->send[i];
+      }
+    }
     if (send->heads % (groups * send->ws)) return fail(H3B_EINVAL, "fp8_gemm qkv_send: heads %% (groups * ws) != 0");
     if ((send->q_norm_weight == nullptr) != (send->k_norm_weight == nullptr))
       return fail(H3B_EINVAL, "fp8_gemm qkv_send: q and k norm weights go together");

@@ -17,12 +17,19 @@ OUT_BF16, OUT_F16 = 0, 1
 EPI_PLAIN, EPI_QKV_SEND, EPI_SWIGLU = 0, 1, 2
 
 _p, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
+MAX_RANKS = 8   # H3B_MAX_RANKS
+ABI_VERSION = 2
 
 
 class QkvSend(ctypes.Structure):
     _fields_ = [("send", _p * 3), ("heads", _i32), ("head_dim", _i32), ("ws", _i32), ("v_f16", _i32),
                 ("range_flag", _p), ("groups", _i32), ("q_norm_weight", _p), ("k_norm_weight", _p),
-                ("rope_table", _p), ("rope_stride", _i64), ("rot", _i32), ("eps", _f32)]
+                ("rope_table", _p), ("rope_stride", _i64), ("rot", _i32), ("eps", _f32),
+                ("p2p", _i32), ("rank", _i32), ("peer_recv", (_p * 3) * MAX_RANKS), ("peer_range_flag", _p * MAX_RANKS)]
+
+
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 # name -> (restype, argtypes): exactly the declarations of include/h3b.h
@@ -51,6 +58,13 @@ SIGNATURES = {
     "h3b_unpack_recv": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _p]),
     "h3b_norm_rope_send": (ctypes.c_int, [_p, _i64, _i32, _i64, _i64, _p, _p, _i64, _i32, _f32, _i32, _p, _p]),
     "h3b_bf16_to_f16": (ctypes.c_int, [_p, _p, _i64, _p, _p]),
+    "h3b_flash_attn_fwd_p2p": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i32, _i32, _i64,
+                                              _i64, _i64, _i64, _i32, _i32, _f32, _i32, _p, _p]),
+    "h3b_p2p_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_p), ctypes.POINTER(IpcHandle)]),
+    "h3b_p2p_open": (ctypes.c_int, [ctypes.POINTER(IpcHandle), ctypes.POINTER(_p)]),
+    "h3b_p2p_close": (ctypes.c_int, [_p]),
+    "h3b_p2p_free": (ctypes.c_int, [_p]),
+    "h3b_p2p_signal_wait": (ctypes.c_int, [_p, _p, _i32, _i32, _i32, _p]),
 }
 
 _lib = None

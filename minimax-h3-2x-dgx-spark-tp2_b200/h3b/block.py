@@ -42,7 +42,8 @@ def block_flops(tokens: int, hidden: int, heads: int, head_dim: int = 128) -> di
 
 class AttentionBlock:
     def __init__(self, hidden: int, heads: int, *, device, head_dim: int = 128, seed: int = 1, ws: int = 1, pg=None,
-                 weights: tuple | None = None, init_device=None, a2a=None, groups: int | None = None):
+                 weights: tuple | None = None, init_device=None, a2a=None, groups: int | None = None,
+                 exchange: str = "nccl", rank: int | None = None):
         if head_dim != 128:
             raise ValueError("head_dim 128 only")
         if heads % ws:
@@ -62,6 +63,38 @@ class AttentionBlock:
         self.groups = default_groups(heads, ws) if groups is None else int(groups)
         if heads % (self.groups * ws):
             raise ValueError(f"heads {heads} not divisible by groups {self.groups} x ws {ws}")
+        # "nccl": the all-to-alls as collectives (stock's exchange); "p2p": stored by the kernels into the peers'
+        # receive buffers (h3b.ulysses_p2p), no collective on the data path
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange {exchange!r}: 'nccl' or 'p2p'")
+        if exchange == "p2p" and self.groups != 1:
+            raise ValueError("exchange 'p2p' has no head groups")
+        self.exchange_kind = exchange
+        self.rank = rank if rank is not None else (dist.get_rank(pg) if exchange == "p2p" and ws > 1 else 0)
+        self._peers = None
+
+    def _peer_exchange(self, m: int):
+        from .ulysses_p2p import PeerExchange
+        if self._peers is None or self._peers.m != m:
+            if self._peers is not None:
+                self.close()
+            self._peers = PeerExchange(m, self.heads, self.ws, self.rank, self.device, pg=self.pg)
+        return self._peers
+
+    def close(self) -> None:
+        """Releases the peer buffers of the p2p exchange (collective over the group)."""
+        if self._peers is not None:
+            pg = self.pg
+            self._peers.close(host_barrier=lambda: dist.barrier(group=pg))
+            self._peers = None
+
+    def share_range_flag(self) -> None:
+        """Max of the v-overflow flags of all ranks (a rank's flag covers only the v slabs it sent, while its attention
+        reads the slabs every rank sent), through the same all-to-all the exchange uses."""
+        if self.ws == 1:
+            return
+        recv = self.exchange(self.range_flag.repeat(self.ws))
+        torch.amax(recv, dim=0, keepdim=True, out=self.range_flag)
 
     def exchange(self, send: torch.Tensor) -> torch.Tensor:
         if self.ws == 1:
@@ -89,10 +122,22 @@ class AttentionBlock:
         mark()
         q8, sx = ops.quant(x)
         mark()
-        if self.ws > 1 and self.groups > 1:
+        if self.ws > 1 and self.exchange_kind == "p2p":
+            px = self._peer_exchange(m)
+            px.forward_qkv(q8, self.wqkv8, sx, self.sqkv)
+            mark()
+            px.barrier()
+            mark()
+            px.attention(1.0 / math.sqrt(d))
+            mark()
+            px.barrier()
+            mark()
+            o8, so = ops.quant_from_recv(px.back)
+        elif self.ws > 1 and self.groups > 1:
             from .ulysses_overlap import grouped_attention, quant_grouped_back
             sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
                                           range_flag=self.range_flag, groups=self.groups)
+            self.share_range_flag()
             mark()
             mark()      # with head groups the exchanges overlap the attention: the attention stage holds all three
             back = grouped_attention(sends, self.ws, self.groups,
@@ -105,6 +150,7 @@ class AttentionBlock:
         else:
             sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
                                           range_flag=self.range_flag)
+            self.share_range_flag()
             mark()
             q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
             mark()
@@ -119,5 +165,6 @@ class AttentionBlock:
         return y
 
     KERNELS_PER_FORWARD = 5   # h3b launches per forward: quant, qkv GEMM, attention, quant, out GEMM
+    P2P_BARRIERS = 2          # extra h3b launches per forward with exchange "p2p" (the two epoch barriers)
 
     __call__ = forward

@@ -33,6 +33,13 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+def _addr(x) -> int | None:
+    """Device address of a tensor, or an address given as an int (a peer's IPC mapping)."""
+    if x is None:
+        return None
+    return x.data_ptr() if isinstance(x, torch.Tensor) else int(x)
+
+
 def _dt(t: torch.Tensor, *dtypes: torch.dtype, what: str) -> None:
     if t.dtype not in dtypes:
         raise TypeError(f"{what}: dtype {t.dtype}, expected one of {dtypes}")
@@ -218,19 +225,37 @@ def fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torc
 
 def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, heads: int, ws: int, *,
                       bias: torch.Tensor | None = None, v_f16: bool = False, sends=None,
-                      range_flag: torch.Tensor | None = None, groups: int = 1, qk_norm=None):
+                      range_flag: torch.Tensor | None = None, groups: int = 1, qk_norm=None, p2p=None):
     """qkv projection whose epilogue writes q, k, v straight into the Ulysses send buffers (the producer redirection
     of ulysses_exact.fused_into_send, h3_tp2/ulysses_exact.py:278, moved into the GEMM).  groups = 1: each buffer is
     stock's [P, M, H/P, d]; groups = G > 1: [G, P, M, H/(G*P), d], head h = g*(H/G) + p*(H/(G*P)) + j, one
     contiguous all-to-all per group (the head-group overlap layout).  ``qk_norm = (q_weight, k_weight, rope_table,
     eps)`` applies the per-(token, head) RMSNorm + partial RoPE of the upstream producer to q and k in the epilogue
-    (rope_table [M, R] fp32, cos | sin, R in {0, 32, 64, 96, 128})."""
+    (rope_table [M, R] fp32, cos | sin, R in {0, 32, 64, 96, 128}).
+
+    ``p2p = (rank, peer_recv, peer_range_flag)``: no send buffers; the slab for rank p goes straight into
+    ``peer_recv[p] = (q, k, v)`` (device tensors or addresses of rank p's [P, M, H/P, d] receive buffers, slot
+    ``rank``) and a v overflow raises ``peer_range_flag[p]``.  Returns None then."""
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
     if N != 3 * heads * 128 or heads % (ws * groups):
         raise ValueError(f"fp8_gemm_qkv_send: N {N} != 3 * {heads} * 128 or heads % (ws * groups)")
     shape = (ws, M, heads // ws, 128) if groups == 1 else (groups, ws, M, heads // (ws * groups), 128)
+    if p2p is not None:
+        rank, peer_recv, peer_rf = p2p
+        if groups != 1 or len(peer_recv) != ws or ws > _lib.MAX_RANKS:
+            raise ValueError("fp8_gemm_qkv_send: p2p needs groups 1 and one (q, k, v) triple per rank")
+        desc = _lib.QkvSend()
+        desc.heads, desc.head_dim, desc.ws, desc.v_f16, desc.groups = heads, 128, ws, int(bool(v_f16)), 1
+        desc.p2p, desc.rank = 1, int(rank)
+        for r in range(ws):
+            for i in range(3):
+                desc.peer_recv[r][i] = _addr(peer_recv[r][i])
+            desc.peer_range_flag[r] = None if peer_rf is None else _addr(peer_rf[r])
+        _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(),
+                  sb.data_ptr(), _ptr(bias), None, 0, M, N, K, OUT_BF16, EPI_QKV_SEND, ctypes.byref(desc), _stream(a))
+        return None
     if sends is None:
         sends = [torch.empty(shape, dtype=torch.bfloat16, device=a.device) for _ in range(2)]
         sends.append(torch.empty(shape, dtype=torch.float16 if v_f16 else torch.bfloat16, device=a.device))
@@ -305,6 +330,39 @@ def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: floa
               s_q, s_kv, -1 if valid_kv is None else int(valid_kv), heads, d, sc, int(v3.dtype == torch.float16),
               _ptr(range_flag) if v3.dtype == torch.float16 else None, _stream(q))
     return o
+
+
+def flash_attn_p2p(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer_back, rank: int, *,
+                   scale: float | None = None, valid_kv: int | None = None,
+                   range_flag: torch.Tensor | None = None) -> None:
+    """Attention of this rank's heads over the gathered sequence (q/k/v [P*M, H/P, d], v f16 or bf16) whose output
+    row t is stored into rank t // M's reverse receive buffer ``peer_back[t // M]`` ([P, M, H/P, d] bf16, slot
+    ``rank``; tensors or device addresses): the head->seq all-to-all folded into the epilogue."""
+    _need_cuda(q, k, v)
+    q3, k3, v3 = _as3(q), _as3(k), _as3(v)
+    _dt(q3, torch.bfloat16, what="flash_attn_p2p q")
+    _dt(k3, torch.bfloat16, what="flash_attn_p2p k")
+    _dt(v3, torch.bfloat16, torch.float16, what="flash_attn_p2p v")
+    s_q, heads, d = q3.shape
+    ws = len(peer_back)
+    if ws < 1 or ws > _lib.MAX_RANKS or s_q % ws:
+        raise ValueError(f"flash_attn_p2p: {ws} peers for {s_q} query rows")
+    ptrs = (ctypes.c_void_p * ws)(*[_addr(b) for b in peer_back])
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(d)
+    f16 = v3.dtype == torch.float16
+    _lib.call("h3b_flash_attn_fwd_p2p", q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0),
+              k3.stride(1), v3.data_ptr(), v3.stride(0), v3.stride(1), ptrs, ws, int(rank), s_q // ws, s_q,
+              k3.shape[0], -1 if valid_kv is None else int(valid_kv), heads, d, sc, int(f16),
+              _ptr(range_flag) if f16 else None, _stream(q))
+
+
+def p2p_signal_wait(peer_flags, my_flags, rank: int, epoch: int, stream: int) -> None:
+    """Epoch barrier over peer memory (one kernel): publish ``epoch`` into slot ``rank`` of every rank's flags,
+    then wait (bounded) until this rank's flags all reach it."""
+    ws = len(peer_flags)
+    ptrs = (ctypes.c_void_p * ws)(*[_addr(f) for f in peer_flags])
+    e32 = ((int(epoch) + 2 ** 31) % 2 ** 32) - 2 ** 31
+    _lib.call("h3b_p2p_signal_wait", ptrs, _addr(my_flags), ws, int(rank), e32, stream)
 
 
 # ---------------------------------------------------------------------------------------------------------------

@@ -1,6 +1,6 @@
 """Worker for tests/test_multigpu_gpu.py (launched by torchrun, one process per GPU, NCCL): every rank runs its rows
-of the cfg-like attention block with the Ulysses exchange over NCCL; rank 0 also runs the single-GPU block.  Results
-are written to --out for the test to compare."""
+of the cfg-like attention block with the Ulysses exchange over NCCL (--exchange nccl) or through peer memory
+(--exchange p2p); rank 0 also runs the single-GPU block.  Results are written to --out for the test to compare."""
 import argparse
 import datetime
 import os
@@ -21,6 +21,8 @@ def main():
     ap.add_argument("--hidden", type=int, default=1024)
     ap.add_argument("--heads", type=int, default=8)
     ap.add_argument("--groups", type=int, default=0)
+    ap.add_argument("--exchange", default="nccl")
+    ap.add_argument("--iters", type=int, default=1)
     args = ap.parse_args()
     rank, ws, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -30,18 +32,20 @@ def main():
         from h3b import ops
         from h3b.block import AttentionBlock
 
-        g = torch.Generator().manual_seed(0)
-        x = torch.randn(args.tokens, args.hidden, generator=g).to(torch.bfloat16)
         m = args.tokens // ws
         blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=ws, pg=dist.group.WORLD, seed=1,
-                             groups=args.groups or None)
-        y = blk(x[rank * m:(rank + 1) * m].contiguous().to(dev))
+                             groups=args.groups or None, exchange=args.exchange)
+        full_blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=1, seed=1) if rank == 0 else None
+        for it in range(args.iters):   # several forwards back to back: buffer reuse across steps
+            g = torch.Generator().manual_seed(it)
+            x = torch.randn(args.tokens, args.hidden, generator=g).to(torch.bfloat16)
+            y = blk(x[rank * m:(rank + 1) * m].contiguous().to(dev))
+            torch.save(y.cpu(), Path(args.out) / f"rank{rank}_{it}.pt")
+            if rank == 0:
+                torch.save(full_blk(x.to(dev)).cpu(), Path(args.out) / f"full_{it}.pt")
         torch.cuda.synchronize()
         assert ops.device_status() == 0
-        torch.save(y.cpu(), Path(args.out) / f"rank{rank}.pt")
-        if rank == 0:
-            full = AttentionBlock(args.hidden, args.heads, device=dev, ws=1, seed=1)(x.to(dev))
-            torch.save(full.cpu(), Path(args.out) / "full.pt")
+        blk.close()
         dist.barrier(device_ids=[local])
     finally:
         dist.destroy_process_group()

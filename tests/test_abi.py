@@ -38,9 +38,22 @@ def test_binding_signatures_cover_the_header():
 
 def test_status_strings_and_version():
     lib = _lib.load()
-    assert lib.h3b_abi_version() == 1
+    assert lib.h3b_abi_version() == _lib.ABI_VERSION == 2
     assert lib.h3b_status_string(0) == b"ok"
     assert lib.h3b_status_string(_lib.H3B_ETIMEOUT) == b"device wait timed out"
+
+
+_PEERS2 = (ctypes.c_void_p * 2)(16, 32)
+_PEERS2_BAD = (ctypes.c_void_p * 2)(16, 33)
+
+
+def _qkv_p2p(rank=0, groups=1, null_peer=False):
+    d = _lib.QkvSend()
+    d.heads, d.head_dim, d.ws, d.groups, d.p2p, d.rank = 2, 128, 2, groups, 1, rank
+    for r in range(2):
+        for i in range(3):
+            d.peer_recv[r][i] = None if (null_peer and r == 1) else 4096 * (1 + 3 * r + i)
+    return d
 
 
 @pytest.mark.parametrize("call,status", [
@@ -59,6 +72,26 @@ def test_status_strings_and_version():
     (lambda L: L.h3b_pack_by_dest(1, 4, 6, 128, 768, 128, 4, 1, 0, None, None), _lib.H3B_EINVAL),
     (lambda L: L.h3b_rms_quant_e4m3(1, 4, 64, 64, 1, 1, 64, None, 0, None, 1e-6, None, 1, 1, 0, None),
      _lib.H3B_EINVAL),
+    # peer-memory exchange: bad rank / world, row split, sizes
+    (lambda L: L.h3b_p2p_signal_wait(None, None, 2, 0, 1, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_p2p_signal_wait(_PEERS2, 1, 9, 0, 1, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_p2p_signal_wait(_PEERS2, 1, 2, 2, 1, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_p2p_alloc(0, ctypes.byref(ctypes.c_void_p()), ctypes.byref(_lib.IpcHandle())), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_p2p_open(None, ctypes.byref(ctypes.c_void_p())), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_p2p_close(None), _lib.H3B_OK),
+    (lambda L: L.h3b_p2p_free(None), _lib.H3B_OK),
+    (lambda L: L.h3b_flash_attn_fwd_p2p(16, 8, 8, 16, 8, 8, 16, 8, 8, _PEERS2, 2, 0, 100, 256, 256, -1, 1, 128, 1.0,
+                                        0, None, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_flash_attn_fwd_p2p(16, 8, 8, 16, 8, 8, 16, 8, 8, _PEERS2, 2, 3, 128, 256, 256, -1, 1, 128, 1.0,
+                                        0, None, None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_flash_attn_fwd_p2p(16, 8, 8, 16, 8, 8, 16, 8, 8, _PEERS2_BAD, 2, 0, 128, 256, 256, -1, 1, 128,
+                                        1.0, 0, None, None), _lib.H3B_EALIGN),
+    (lambda L: L.h3b_fp8_gemm(16, 16, 16, 16, 16, 16, None, None, 0, 4, 3 * 2 * 128, 16, 0, 1,
+                              ctypes.byref(_qkv_p2p(rank=2)), None), _lib.H3B_EINVAL),
+    (lambda L: L.h3b_fp8_gemm(16, 16, 16, 16, 16, 16, None, None, 0, 4, 3 * 2 * 128, 16, 0, 1,
+                              ctypes.byref(_qkv_p2p(groups=2)), None), _lib.H3B_EUNSUPPORTED),
+    (lambda L: L.h3b_fp8_gemm(16, 16, 16, 16, 16, 16, None, None, 0, 4, 3 * 2 * 128, 16, 0, 1,
+                              ctypes.byref(_qkv_p2p(null_peer=True)), None), _lib.H3B_EALIGN),
 ])
 def test_host_side_argument_errors(call, status):
     lib = _lib.load()
@@ -74,5 +107,18 @@ def test_check_raises_with_the_reason():
         _lib.check(rc, "h3b_quant_rows_e4m3")
 
 
-def test_qkv_send_struct_layout():
-    assert ctypes.sizeof(_lib.QkvSend) == 96
+def test_qkv_send_struct_layout(tmp_path):
+    """The ctypes mirror matches the C compiler's layout of h3b_qkv_send field by field."""
+    fields = [f[0] for f in _lib.QkvSend._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "h3b.h"\nint main(void) {\n'
+                   '  printf("%zu\\n", sizeof(h3b_qkv_send));\n' +
+                   "".join(f'  printf("%zu\\n", offsetof(h3b_qkv_send, {f}));\n' for f in fields) +
+                   '  printf("%zu\\n", sizeof(h3b_ipc_handle));\n  return 0;\n}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [ctypes.sizeof(_lib.QkvSend)] + [getattr(_lib.QkvSend, f).offset for f in fields] + \
+        [ctypes.sizeof(_lib.IpcHandle)]
+    assert got == want
+    assert ctypes.sizeof(_lib.QkvSend) == 360
