@@ -210,7 +210,6 @@ def run_reference(args, rank: int, world: int) -> None:
 
 def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
     import h3b  # noqa: PLC0415
-    from h3b import ops  # noqa: PLC0415
     from h3b.block import AttentionBlock  # noqa: PLC0415
 
     h3b.load_library()
@@ -220,8 +219,18 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
     if tokens % world:
         raise SystemExit(f"tokens {tokens} not divisible by {world} ranks")
     m = tokens // world
+    p2p = args.exchange == "p2p" and world > 1
     blk = AttentionBlock(HIDDEN, HEADS, device=dev, ws=world, pg=pg, init_device=dev, seed=1,
-                         groups=args.groups or None)
+                         groups=1 if p2p else (args.groups or None), exchange="p2p" if p2p else "nccl")
+    try:
+        _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p)
+    finally:
+        blk.close()
+
+
+def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
+    from h3b import ops  # noqa: PLC0415
+
     g = torch.Generator(device=dev).manual_seed(rank)
     x = torch.randn(m, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
 
@@ -300,7 +309,9 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
         "config": {"workload": f"cfg2 DiT attention block: {tokens} tokens (31x48x84), hidden {HIDDEN}, "
                                f"{HEADS} heads x {HEAD_DIM}, Ulysses SP={world}", "tokens": tokens,
                    "rows_per_rank": m, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM, "sp": world,
-                   "head_groups": blk.groups, "l2": "inputs larger than L2 (no flush)"},
+                   "head_groups": blk.groups, "l2": "inputs larger than L2 (no flush)",
+                   "exchange": ("peer memory (epilogue stores over NVLink + epoch barriers)" if p2p else
+                                "NCCL all_to_all_single") if world > 1 else "none (SP=1)"},
         "ms_per_stage": stage_ms,
         "roofline": {"bound": "tensor", "kernel": "flash_attn", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
@@ -308,7 +319,7 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
                      "traffic": None},
         "e2e": {"value": total_fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": m * HIDDEN * 2, "d2h_bytes_per_step": m * HIDDEN * 2},
-        "gpu_launches": blk.KERNELS_PER_FORWARD * args.steps,
+        "gpu_launches": (blk.KERNELS_PER_FORWARD + (blk.P2P_BARRIERS if p2p else 0)) * args.steps,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -329,7 +340,9 @@ def main() -> None:
     ap.add_argument("--ref-rows", type=int, default=1024, help="query rows of the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--groups", type=int, default=0,
-                    help="Ulysses head groups overlapped with attention (0: about 5 local heads per group)")
+                    help="Ulysses head groups overlapped with attention (NCCL exchange; 0: the measured default)")
+    ap.add_argument("--exchange", choices=("nccl", "p2p"), default="nccl",
+                    help="Ulysses exchange at SP > 1: NCCL all-to-all, or the kernels' stores into peer memory")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
