@@ -378,21 +378,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const int64_t row = q0 + q * BQ + sub * 32 + lane;
         const float inv_l = 1.0f / l_run;
-        uint16_t* orow;
-        if (p.m_rows > 0) {  // Ulysses reverse exchange through peer memory
-          const int64_t owner = row / p.m_rows;
-          orow = p.peer_o[owner < H3B_MAX_RANKS ? owner : 0] +
-                 (p.rank * p.m_rows + (row - owner * p.m_rows)) * p.o_tok + static_cast<int64_t>(head) * p.o_head;
-        } else {
-          orow = p.o + row * p.o_tok + static_cast<int64_t>(head) * p.o_head;
-        }
+        uint16_t* orow = p.o + row * p.o_tok + static_cast<int64_t>(head) * p.o_head;
+        // peer stores: this warp's 32 output rows are staged in the (now idle) K tiles and leave as 2 rows x 256 B per
+        // store instruction; every QK^T MMA completed before o_full, so nothing reads K any more
+        uint4* srow = reinterpret_cast<uint4*>(smem + 2 * TILE_BYTES) + (warp * 32 + lane) * 16;
 #pragma unroll
         for (int cc = 0; cc < D; cc += 32) {
           uint32_t o[32];
           tmem_ld32(o_tmem + cc, o);
           tmem_ld_wait();
           reg_fence(o);
-          if (row < p.s_q) {
+          if (p.m_rows > 0) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv_l,
+                                                         __uint_as_float(o[8 * v + 2 * e + 1]) * inv_l);
+                w[e] = *reinterpret_cast<uint32_t*>(&b);
+              }
+              srow[((cc >> 3) + v) ^ (lane & 15)] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else if (row < p.s_q) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               uint32_t w[4];
@@ -403,6 +411,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                 w[e] = *reinterpret_cast<uint32_t*>(&b);
               }
               *reinterpret_cast<uint4*>(orow + cc + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        if (p.m_rows > 0) {  // Ulysses reverse exchange: row t goes to rank t / m_rows, slot `rank` there
+          __syncwarp();
+          const int64_t r0 = q0 + q * BQ + sub * 32;
+          const uint4* wst = reinterpret_cast<const uint4*>(smem + 2 * TILE_BYTES) + warp * 32 * 16;
+#pragma unroll 4
+          for (int it = 0; it < 16; ++it) {
+            const int idx = it * 32 + lane, r = idx >> 4, part = idx & 15;
+            const int64_t t = r0 + r;
+            if (t < p.s_q) {
+              const int64_t owner = t / p.m_rows;
+              uint16_t* dst = p.peer_o[owner < H3B_MAX_RANKS ? owner : 0] +
+                              (p.rank * p.m_rows + (t - owner * p.m_rows)) * p.o_tok +
+                              static_cast<int64_t>(head) * p.o_head + part * 8;
+              *reinterpret_cast<uint4*>(dst) = wst[r * 16 + (part ^ (r & 15))];
             }
           }
         }

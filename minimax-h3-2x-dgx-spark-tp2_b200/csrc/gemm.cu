@@ -23,7 +23,10 @@ constexpr int B_BYTES = BN * BK;   // 32 KB (two 128-row boxes)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+// peer-store staging: per epilogue warp 32 rows x 128 B (64 columns), so the stores to another GPU leave as whole
+// 128-byte lines instead of 16-byte pieces of 32 different rows
+constexpr int STAGING_BYTES = 4 * 32 * 128;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + STAGING_BYTES;
 constexpr uint32_t IDESC = idesc_make(FMT_E4M3, FMT_E4M3, 0, BM, BN);
 
 struct Params {
@@ -110,6 +113,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256);
   const uint32_t smem0 = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -384,6 +388,48 @@ __global__ void __launch_bounds__(THREADS, 1)
                 else
                   v[i + e] = sam * tv;
               }
+            }
+            if (p.epi == H3B_EPI_QKV_SEND && p.p2p) {
+              // peer stores (warp-uniform branch): the warp's 32 rows of this 64-column block go through shared
+              // memory and leave as 4 rows x 128 B per store instruction
+              const int which = static_cast<int>(n0 / p.hd);
+              const int hcol = static_cast<int>(n0 - static_cast<int64_t>(which) * p.hd);
+              const int h = hcol >> 7, c = hcol & 127;
+              const int dst_rank = h / p.hl, j = h - dst_rank * p.hl;
+              const bool as_f16 = which == 2 && p.v_f16;
+              int32_t* rf = p.peer_rf[dst_rank];
+              if (row_ok && as_f16 && rf != nullptr) {
+                bool bad = false;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) bad |= fabsf(v[i]) > 65504.0f && isfinite(v[i]);
+                if (bad) atomicExch(rf, 1);
+              }
+              uint4* srow = staging + (sub * 32 + lane) * 8;
+              const int hb = (c >> 5) & 1;  // which 32-column half of the 64-column block
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  w[e] = as_f16 ? pack2_bf16_as_f16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1])
+                                : pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], 0);
+                srow[(hb * 4 + q) ^ (lane & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+              if (hb == 1) {
+                __syncwarp();
+                const int64_t m0 = static_cast<int64_t>(mb) * BM + sub * 32;
+                uint16_t* base = static_cast<uint16_t*>(p.peer[dst_rank][which]) +
+                                 ((static_cast<int64_t>(p.rank) * p.M + m0) * p.hl + j) * 128 + (c & 64);
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                  const int idx = it * 32 + lane, r = idx >> 3, part = idx & 7;
+                  if (m0 + r < p.M)
+                    *reinterpret_cast<uint4*>(base + static_cast<int64_t>(r) * p.hl * 128 + part * 8) =
+                        staging[(sub * 32 + r) * 8 + (part ^ (r & 7))];
+                }
+                __syncwarp();
+              }
+              continue;
             }
             if (!row_ok) continue;
             if (p.epi == H3B_EPI_QKV_SEND) {
