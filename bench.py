@@ -276,20 +276,41 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
     if status != 0:
         raise RuntimeError(f"device status {status} in the timed region")
 
-    # ---- end to end through the public API: pinned host x -> device -> block -> host y, every step ----
+    # ---- end to end through the public API: every step copies its x from pinned host memory to the device and
+    # reads its y back to pinned host memory.  The copies run on a side stream: step i+1's input and step i-1's output
+    # cross PCIe while step i's block computes (two device input buffers, two host output buffers). ----
     hx = x.cpu().pin_memory()
-    hy = torch.empty((m, HIDDEN), dtype=torch.bfloat16).pin_memory()
-    for _ in range(1):
-        blk(hx.to(dev, non_blocking=True))
+    hy = [torch.empty((m, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(x) for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    blk(hx.to(dev, non_blocking=True))
     barrier()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        xd = hx.to(dev, non_blocking=True)
-        y = blk(xd)
-        hy.copy_(y, non_blocking=True)
-    e1.record()
+    e0.record(comp)
+    copy.wait_stream(comp)
+    with torch.cuda.stream(copy):
+        xd[0].copy_(hx, non_blocking=True)
+        ev_in[0].record(copy)
+    for i in range(args.steps):
+        if i + 1 < args.steps:
+            with torch.cuda.stream(copy):
+                if i >= 1:
+                    copy.wait_event(ev_used[(i + 1) % 2])   # step i-1 is done with that buffer
+                xd[(i + 1) % 2].copy_(hx, non_blocking=True)
+                ev_in[(i + 1) % 2].record(copy)
+        comp.wait_event(ev_in[i % 2])
+        y = blk(xd[i % 2])
+        ev_used[i % 2].record(comp)
+        copy.wait_stream(comp)
+        with torch.cuda.stream(copy):
+            y.record_stream(copy)
+            hy[i % 2].copy_(y, non_blocking=True)
+    comp.wait_stream(copy)
+    e1.record(comp)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
@@ -341,7 +362,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--groups", type=int, default=0,
                     help="Ulysses head groups overlapped with attention (NCCL exchange; 0: the measured default)")
-    ap.add_argument("--exchange", choices=("nccl", "p2p"), default="nccl",
+    ap.add_argument("--exchange", choices=("nccl", "p2p"), default="p2p",
                     help="Ulysses exchange at SP > 1: NCCL all-to-all, or the kernels' stores into peer memory")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -25,8 +25,10 @@ constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;
 // peer-store staging: per epilogue warp 32 rows x 128 B (64 columns), so the stores to another GPU leave as whole
 // 128-byte lines instead of 16-byte pieces of 32 different rows
+// (only the PEER instantiation of the kernel has it; the other keeps its registers and shared memory as without)
 constexpr int STAGING_BYTES = 4 * 32 * 128;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + STAGING_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES_PEER = SMEM_BYTES + STAGING_BYTES;
 constexpr uint32_t IDESC = idesc_make(FMT_E4M3, FMT_E4M3, 0, BM, BN);
 
 struct Params {
@@ -105,6 +107,8 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
   return s * u;
 }
 
+// PEER: the QKV_SEND epilogue stores into other GPUs' receive buffers (Params::p2p set)
+template <bool PEER>
 __global__ void __launch_bounds__(THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ Params p) {
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                   v[i + e] = sam * tv;
               }
             }
-            if (p.epi == H3B_EPI_QKV_SEND && p.p2p) {
+            if (PEER && p.epi == H3B_EPI_QKV_SEND) {
               // peer stores (warp-uniform branch): the warp's 32 rows of this 64-column block go through shared
               // memory and leave as 4 rows x 128 B per store instruction
               const int which = static_cast<int>(n0 / p.hd);
@@ -443,7 +447,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               uint16_t* slab = send_slab(p, which, g, dst_rank, seg);
               const int64_t off = ((seg * p.M + m) * p.hl + j) * 128 + c;
               const bool as_f16 = which == 2 && p.v_f16;
-              int32_t* rf = p.p2p ? p.peer_rf[dst_rank] : p.range_flag;
+              int32_t* rf = p.range_flag;
               if (as_f16 && rf != nullptr) {
                 bool bad = false;
 #pragma unroll
@@ -605,13 +609,18 @@ extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t l
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fp8_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_PEER);
     if (e != cudaSuccess) return cuda_fail(e, "fp8_gemm: smem attribute");
     attr_set[dev] = true;
   }
   const int tiles = p.num_mb * p.num_nb;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  fp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
+  if (p.p2p)
+    fp8_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_PEER, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
+  else
+    fp8_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
   H3B_CHECK_LAUNCH("fp8_gemm launch");
   return H3B_OK;
 }
