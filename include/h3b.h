@@ -178,6 +178,18 @@ H3B_API int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t ldw,
                  const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int32_t out_dtype,
                  int32_t epilogue, const h3b_qkv_send* send, h3b_stream_t stream);
 
+/* fc2 with the indexed gated residual in its epilogue.  Replaces the fc2 consumer pair the reference fuses at the
+ * tensor32 level: the scale pass + indexed_gate (h3_tp2/fp8_consumers.py:203-239 _scale_indexed_gate_kernel, its
+ * eager mirror _gate_torch :367-371): o = bf16(sa[m] * (sb[n] * acc)) (bias by fma), then
+ * y[m, n] = bf16(x[m, n] + gate[indices[m], n] * o) in fp32 with separate rounding of the product and the sum.
+ * x, gate, y: bf16 row-major with leading dimensions ldx, ld_gate, ldy (multiples of 8, 16-byte aligned);
+ * indices: int64 [M] (row of gate for each token, in [0, gate_rows); a row whose index is outside leaves y
+ * untouched and records H3B_EINVAL in the device status word). */
+H3B_API int h3b_fp8_gemm_gate(const void* a, int64_t lda, const void* w, int64_t ldw, const float* sa,
+                              const float* sb, const void* bias, const void* x, int64_t ldx, const void* gate,
+                              int64_t ld_gate, int64_t gate_rows, const int64_t* indices, void* y, int64_t ldy,
+                              int64_t M, int64_t N, int64_t K, h3b_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * attention (tcgen05 flash attention, non-causal, head_dim 128)
  * ------------------------------------------------------------------------------------------------------------- */

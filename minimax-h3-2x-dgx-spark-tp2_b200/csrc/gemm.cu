@@ -23,6 +23,7 @@ constexpr int B_BYTES = BN * BK;   // 32 KB (two 128-row boxes)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;
+constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
 // peer-store staging: per epilogue warp 32 rows x 128 B (64 columns), so the stores to another GPU leave as whole
 // 128-byte lines instead of 16-byte pieces of 32 different rows
 // (only the PEER instantiation of the kernel has it; the other keeps its registers and shared memory as without)
@@ -54,6 +55,11 @@ struct Params {
   int64_t rope_stride;
   int rot;
   float eps;
+  const uint16_t* gx;                    // GATE: residual x, gate rows, token -> gate row
+  int64_t ldx;
+  const uint16_t* gate;
+  int64_t ldg, gate_rows;
+  const int64_t* gidx;
   int p2p;                               // QKV_SEND into the peers' receive buffers
   int rank;
   void* peer[H3B_MAX_RANKS][3];
@@ -464,6 +470,35 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 : pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], 0);
                 dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
               }
+            } else if (p.epi == EPI_GATE) {
+              // y = x + gate[idx[m]] * bf16(o): fp32, product and sum rounded separately (the eager mirror's order)
+              const int64_t gi = __ldg(p.gidx + m);
+              if (gi < 0 || gi >= p.gate_rows) {
+                record_status(p.wc, H3B_EINVAL);
+                continue;
+              }
+              const uint4* xrow = reinterpret_cast<const uint4*>(p.gx + m * p.ldx + n0);
+              const uint4* grow = reinterpret_cast<const uint4*>(p.gate + gi * p.ldg + n0);
+              uint16_t* yrow = static_cast<uint16_t*>(p.y) + m * p.ldy;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (n0 + 8 * q >= p.N) break;
+                const uint4 xv = __ldg(xrow + q), gv = __ldg(grow + q);
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float r[2];
+#pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    const float xf = __uint_as_float(h ? (xw[e] & 0xFFFF0000u) : (xw[e] << 16));
+                    const float gf = __uint_as_float(h ? (gw[e] & 0xFFFF0000u) : (gw[e] << 16));
+                    r[h] = __fadd_rn(xf, __fmul_rn(gf, rbf16(v[8 * q + 2 * e + h])));
+                  }
+                  w[e] = pack2(r[0], r[1], 0);
+                }
+                *reinterpret_cast<uint4*>(yrow + n0 + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+              }
             } else {
               uint16_t* yrow = static_cast<uint16_t*>(p.y) + m * p.ldy;
 #pragma unroll
@@ -498,13 +533,22 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 using namespace h3b;
 
-extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, const float* sa, const float* sb,
-                            const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int32_t out_dtype,
-                            int32_t epilogue, const h3b_qkv_send* send, h3b_stream_t stream) {
+namespace {
+struct GateArgs {
+  const void* x;
+  int64_t ldx;
+  const void* gate;
+  int64_t ldg;
+  int64_t gate_rows;
+  const int64_t* indices;
+};
+
+int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const float* sa, const float* sb,
+                  const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int32_t out_dtype,
+                  int32_t epilogue, const h3b_qkv_send* send, const GateArgs* ga, h3b_stream_t stream) {
   using namespace h3b::gemm;
   if (M < 0 || N <= 0 || K <= 0) return fail(H3B_EINVAL, "fp8_gemm: M %lld N %lld K %lld", (long long)M, (long long)N, (long long)K);
   if (out_dtype != H3B_OUT_BF16 && out_dtype != H3B_OUT_F16) return fail(H3B_EINVAL, "fp8_gemm: out dtype %d", out_dtype);
-  if (epilogue < H3B_EPI_PLAIN || epilogue > H3B_EPI_SWIGLU) return fail(H3B_EINVAL, "fp8_gemm: epilogue %d", epilogue);
   if (M == 0) return H3B_OK;
   if (a == nullptr || w == nullptr || sa == nullptr || sb == nullptr) return fail(H3B_EINVAL, "fp8_gemm: null operand");
   if (K % 16 || N % 16) return fail(H3B_EUNSUPPORTED, "fp8_gemm: K and N must be multiples of 16");
@@ -584,6 +628,20 @@ extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t l
   } else {
     if (y == nullptr || ldy < N || ldy % 8 || (reinterpret_cast<uintptr_t>(y) & 15u))
       return fail(H3B_EALIGN, "fp8_gemm: y must be 16-byte aligned with ldy >= N, ldy % 8 == 0");
+    if (epilogue == EPI_GATE) {
+      if (ga == nullptr || ga->x == nullptr || ga->gate == nullptr || ga->indices == nullptr || ga->gate_rows <= 0)
+        return fail(H3B_EINVAL, "fp8_gemm_gate: x, gate (>= 1 row) and indices are required");
+      if (out_dtype != H3B_OUT_BF16) return fail(H3B_EUNSUPPORTED, "fp8_gemm_gate: bf16 output only");
+      if (ga->ldx < N || ga->ldx % 8 || ga->ldg < N || ga->ldg % 8 ||
+          ((reinterpret_cast<uintptr_t>(ga->x) | reinterpret_cast<uintptr_t>(ga->gate)) & 15u))
+        return fail(H3B_EALIGN, "fp8_gemm_gate: x and gate must be 16-byte aligned with leading dimensions >= N, % 8 == 0");
+      p.gx = static_cast<const uint16_t*>(ga->x);
+      p.ldx = ga->ldx;
+      p.gate = static_cast<const uint16_t*>(ga->gate);
+      p.ldg = ga->ldg;
+      p.gate_rows = ga->gate_rows;
+      p.gidx = ga->indices;
+    }
     p.num_nb = static_cast<int>((N + BN - 1) / BN);
   }
   p.wc.status = device_status_word();
@@ -623,4 +681,21 @@ extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t l
     fp8_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
   H3B_CHECK_LAUNCH("fp8_gemm launch");
   return H3B_OK;
+}
+}  // namespace
+
+extern "C" int h3b_fp8_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, const float* sa, const float* sb,
+                            const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int32_t out_dtype,
+                            int32_t epilogue, const h3b_qkv_send* send, h3b_stream_t stream) {
+  if (epilogue < H3B_EPI_PLAIN || epilogue > H3B_EPI_SWIGLU) return fail(H3B_EINVAL, "fp8_gemm: epilogue %d", epilogue);
+  return fp8_gemm_impl(a, lda, w, ldw, sa, sb, bias, y, ldy, M, N, K, out_dtype, epilogue, send, nullptr, stream);
+}
+
+extern "C" int h3b_fp8_gemm_gate(const void* a, int64_t lda, const void* w, int64_t ldw, const float* sa,
+                                 const float* sb, const void* bias, const void* x, int64_t ldx, const void* gate,
+                                 int64_t ld_gate, int64_t gate_rows, const int64_t* indices, void* y, int64_t ldy,
+                                 int64_t M, int64_t N, int64_t K, h3b_stream_t stream) {
+  const GateArgs ga{x, ldx, gate, ld_gate, gate_rows, indices};
+  return fp8_gemm_impl(a, lda, w, ldw, sa, sb, bias, y, ldy, M, N, K, H3B_OUT_BF16, h3b::gemm::EPI_GATE, nullptr, &ga,
+                       stream);
 }

@@ -58,6 +58,8 @@ SIGNATURES = {
     "h3b_unpack_recv": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _p]),
     "h3b_norm_rope_send": (ctypes.c_int, [_p, _i64, _i32, _i64, _i64, _p, _p, _i64, _i32, _f32, _i32, _p, _p]),
     "h3b_bf16_to_f16": (ctypes.c_int, [_p, _p, _i64, _p, _p]),
+    "h3b_fp8_gemm_gate": (ctypes.c_int, [_p, _i64, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _i64, _p, _p, _i64, _i64,
+                                         _i64, _i64, _p]),
     "h3b_flash_attn_fwd_p2p": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i32, _i32, _i64,
                                               _i64, _i64, _i64, _i32, _i32, _f32, _i32, _p, _p]),
     "h3b_p2p_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_p), ctypes.POINTER(IpcHandle)]),

@@ -223,6 +223,28 @@ def fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torc
     return y
 
 
+def fp8_gemm_gate(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, x: torch.Tensor,
+                  gate: torch.Tensor, indices: torch.Tensor, bias: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """fc2 with the indexed gated residual in the epilogue: ``x + gate[indices] * bf16(sa * (sb * (a @ w^T)))``
+    (``fp8_consumers.gate_fused`` / ``_scale_indexed_gate_kernel``, h3_tp2/fp8_consumers.py:203-239,468).  x, gate
+    bf16 with unit column stride (gate may be a row-strided view); indices [M] integer."""
+    N = w.shape[0]
+    sa, sb = _gemm_operands(a, w, sa, sb, N)
+    _need_cuda(x, gate, indices)
+    M, K = a.shape
+    _dt(x, torch.bfloat16, what="fp8_gemm_gate x")
+    _dt(gate, torch.bfloat16, what="fp8_gemm_gate gate")
+    if x.shape != (M, N) or x.stride(1) != 1 or gate.shape[-1] != N or gate.stride(-1) != 1:
+        raise ValueError(f"fp8_gemm_gate: x {tuple(x.shape)} / gate {tuple(gate.shape)} against [{M}, {N}]")
+    idx = indices.to(torch.int64).contiguous()
+    y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    _lib.call("h3b_fp8_gemm_gate", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
+              _ptr(bias), x.data_ptr(), x.stride(0), gate.data_ptr(), gate.stride(0), gate.shape[0], idx.data_ptr(),
+              y.data_ptr(), y.stride(0), M, N, K, _stream(a))
+    return y
+
+
 def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, heads: int, ws: int, *,
                       bias: torch.Tensor | None = None, v_f16: bool = False, sends=None,
                       range_flag: torch.Tensor | None = None, groups: int = 1, qk_norm=None, p2p=None):

@@ -59,3 +59,10 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     """silu_and_mul on bf16 [M, 2d] (h3_tp2/fp8_quant_fuse.py:263-278 arithmetic)."""
     d = x.shape[-1] // 2
     return silu_mul_bf16(x[..., :d].float(), x[..., d:].float())
+
+
+def indexed_gate(x: torch.Tensor, gate: torch.Tensor, other: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+    """x + gate[indices] * other in fp32 (product and sum rounded separately), to x's dtype: the eager mirror
+    ``_gate_torch`` of ``_scale_indexed_gate_kernel`` (h3_tp2/fp8_consumers.py:367-371); ``other`` is the bf16 fc2
+    output (the GEMM epilogue rounded to bf16)."""
+    return (x.float() + gate.index_select(0, indices).float() * other.float()).to(x.dtype)

@@ -17,6 +17,8 @@ Reference functions exercised (paths inside the reference project):
   ulysses:  h3_tp2/ulysses_exact.py:187 exact_forward, :108 send_shape, :119 pack_into, :156 exchange_back, and the
             stock exchange tests/test_ulysses_exact.py:74 stock_all_to_all_4d, with FakeA2A (:25)
   rope:     h3_tp2/ulysses_exact.py:264 rope_into_send with the eager norm+RoPE stand-in tests/test_ulysses_exact.py:107
+  gate:     h3_tp2/fp8_consumers.py:367 _gate_torch (the eager mirror of _scale_indexed_gate_kernel) on an exact
+            integer fp32 product, gate rows as a row-strided chunk view (recipe of tests/test_fp8_consumer_fuse.py:118)
 """
 from __future__ import annotations
 
@@ -244,6 +246,27 @@ def gen_rope(ux, tue) -> dict:
     return out
 
 
+def gen_gate(fc) -> dict:
+    g = torch.Generator().manual_seed(7)
+    M, N, K = 200, 272, 256        # partial row / column tiles
+    a = torch.randint(-4, 5, (M, K), generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), generator=g).to(E4M3)
+    sa = torch.exp(torch.empty(M).uniform_(-9.0, -2.0, generator=g))
+    sb = torch.exp(torch.empty(N).uniform_(-9.5, -7.5, generator=g))
+    bias = (torch.randn(N, generator=g) * 0.1).to(BF16)
+    x32 = a.float() @ w.float().t()                 # exact (integer products, |sum| < 2^24)
+    x = torch.randn(M, N, generator=g).to(BF16)
+    gate6 = torch.randn(3, 6 * N, generator=g).to(BF16)
+    gate = gate6.chunk(6, dim=-1)[5]                # [3, N] view with row stride 6N
+    idx = torch.randint(0, 3, (M,), generator=g)
+    y = torch.empty(M, N, dtype=BF16)
+    fc._gate_torch(x, gate, x32, sa, sb, None, idx, y)
+    yb = torch.empty(M, N, dtype=BF16)
+    fc._gate_torch(x, gate, x32, sa, sb, bias, idx, yb)
+    return dict(a=bits8(a), w=bits8(w), sa=f32(sa), sb=f32(sb), bias=bits16(bias), x=bits16(x), gate6=bits16(gate6),
+                idx=idx.numpy().copy(), y=bits16(y), ybias=bits16(yb))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -251,7 +274,7 @@ def main() -> None:
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
     sys.path.insert(0, str(ref / "tests"))
-    from h3_tp2 import fp8_gemm, fp8_quant_fuse, fp8_swiglu, ulysses_exact, ulysses_outq  # noqa: PLC0415
+    from h3_tp2 import fp8_consumers, fp8_gemm, fp8_quant_fuse, fp8_swiglu, ulysses_exact, ulysses_outq  # noqa: PLC0415
     import fake_h3_consumers  # noqa: PLC0415
     import test_ulysses_exact  # noqa: PLC0415
 
@@ -262,6 +285,7 @@ def main() -> None:
     np.savez_compressed(HERE / "rms.npz", **gen_rms(fp8_quant_fuse, fake_h3_consumers))
     np.savez_compressed(HERE / "ulysses.npz", **gen_ulysses(ulysses_exact, test_ulysses_exact))
     np.savez_compressed(HERE / "rope.npz", **gen_rope(ulysses_exact, test_ulysses_exact))
+    np.savez_compressed(HERE / "gate.npz", **gen_gate(fp8_consumers))
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -72,6 +72,12 @@ def _qkv_p2p(rank=0, groups=1, null_peer=False):
     (lambda L: L.h3b_pack_by_dest(1, 4, 6, 128, 768, 128, 4, 1, 0, None, None), _lib.H3B_EINVAL),
     (lambda L: L.h3b_rms_quant_e4m3(1, 4, 64, 64, 1, 1, 64, None, 0, None, 1e-6, None, 1, 1, 0, None),
      _lib.H3B_EINVAL),
+    (lambda L: L.h3b_fp8_gemm_gate(16, 16, 16, 16, 16, 16, None, None, 256, 16, 256, 2, 16, 16, 256, 4, 256, 16, None),
+     _lib.H3B_EINVAL),
+    (lambda L: L.h3b_fp8_gemm_gate(16, 16, 16, 16, 16, 16, None, 16, 250, 16, 256, 2, 16, 16, 256, 4, 256, 16, None),
+     _lib.H3B_EALIGN),
+    (lambda L: L.h3b_fp8_gemm_gate(16, 16, 16, 16, 16, 16, None, 16, 256, 16, 256, 0, 16, 16, 256, 4, 256, 16, None),
+     _lib.H3B_EINVAL),
     # peer-memory exchange: bad rank / world, row split, sizes
     (lambda L: L.h3b_p2p_signal_wait(None, None, 2, 0, 1, None), _lib.H3B_EINVAL),
     (lambda L: L.h3b_p2p_signal_wait(_PEERS2, 1, 9, 0, 1, None), _lib.H3B_EINVAL),

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from _util import BF16, E4M3, F16, rel_l2, same_bits, t8, t16, tf, ulp_diff_bf16
-from h3b import fp8_gemm, ops
+from h3b import fp8_consumers, fp8_gemm, ops
 from oracle import gemm as og
 from oracle import ulysses as ou
 
@@ -158,3 +158,79 @@ def test_qkv_send_epilogue_with_qk_norm_rope(dev, ws):
         assert (ud == 0).float().mean().item() > 0.98 and int(ud.max()) <= 8
         assert rel_l2(got.float().cpu(), ref.float()) <= 2e-3
     assert same_bits(sv.cpu(), ou.pack(v, ws))
+
+
+def test_gate_epilogue_golden_exact(dev, golden):
+    """fc2 + indexed gated residual in one kernel: bit-exact against the reference's eager mirror on exact integer
+    products, gate rows given as a row-strided view."""
+    g = golden("gate")
+    a, w = t8(g["a"]).to(dev), t8(g["w"]).to(dev)
+    sa, sb, bias = tf(g["sa"]).to(dev), tf(g["sb"]).to(dev), t16(g["bias"]).to(dev)
+    x, gate6 = t16(g["x"]).to(dev), t16(g["gate6"]).to(dev)
+    idx = torch.from_numpy(g["idx"]).to(dev)
+    gate = gate6.chunk(6, dim=-1)[5]
+    assert same_bits(ops.fp8_gemm_gate(a, w, sa, sb, x, gate, idx).cpu(), t16(g["y"]))
+    assert same_bits(ops.fp8_gemm_gate(a, w, sa, sb, x, gate, idx, bias).cpu(), t16(g["ybias"]))
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("M", [1, 333, 2000])
+def test_gate_epilogue_fc2_shape(dev, M):
+    """The fc2 shape (N = 5120, K = 13824) against the two-pass product + the oracle's indexed gate."""
+    N, K = SHAPES["fc2"]
+    a, w, sa, sb = _serving_like(M, N, K, seed=M + 11, dev=dev)
+    g = torch.Generator(device=dev).manual_seed(M)
+    x = torch.randn(M, N, device=dev, generator=g).to(BF16)
+    gate = torch.randn(4, N, device=dev, generator=g).to(BF16)
+    idx = torch.randint(0, 4, (M,), device=dev, generator=g)
+    y = ops.fp8_gemm_gate(a, w, sa, sb, x, gate, idx)
+    ref = og.indexed_gate(x.cpu(), gate.cpu(), _two_pass(a, w, sa, sb).cpu(), idx.cpu())
+    ud = ulp_diff_bf16(y.cpu(), ref)
+    assert int(ud.max()) <= 2 and (ud == 0).float().mean().item() > 0.95
+    assert ops.device_status() == 0
+
+
+def test_gate_index_out_of_range_is_reported(dev):
+    """A token whose gate row does not exist leaves its output row alone and records H3B_EINVAL."""
+    from h3b import _lib
+    M, N, K = 130, 256, 128
+    a = torch.randint(-2, 3, (M, K), device=dev).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), device=dev).to(E4M3)
+    sa, sb = torch.full((M,), 1e-3, device=dev), torch.full((N,), 1e-3, device=dev)
+    x = torch.zeros(M, N, device=dev, dtype=BF16)
+    gate = torch.ones(2, N, device=dev, dtype=BF16)
+    idx = torch.zeros(M, device=dev, dtype=torch.int64)
+    idx[7] = 2
+    y = torch.full((M, N), 5.0, device=dev, dtype=BF16)
+    ops.fp8_gemm_gate(a, w, sa, sb, x, gate, idx, out=y)
+    torch.cuda.synchronize()
+    assert ops.device_status() == _lib.H3B_EINVAL
+    assert bool((y[7] == 5.0).all())
+
+
+def test_consumers_mirror(dev):
+    """h3b.fp8_consumers (the reference's stash consumers): the qk norm + RoPE consumer is the qkv GEMM with the norm
+    epilogue (v = the plain scale pass), the fc2 gate consumer the gated GEMM, written into the placeholder."""
+    M, H, K = 300, 4, 512
+    a, w, sa, sb = _serving_like(M, 3 * H * 128, K, seed=5, dev=dev)
+    g = torch.Generator(device=dev).manual_seed(6)
+    qw = (1.0 + 0.1 * torch.randn(128, device=dev, generator=g)).to(BF16)
+    kw = (1.0 + 0.1 * torch.randn(128, device=dev, generator=g)).to(BF16)
+    pos = torch.arange(M, device=dev, dtype=torch.float32)[:, None] * torch.exp(-torch.arange(48, device=dev) / 8.0)
+    table = torch.cat((torch.cos(pos), torch.sin(pos)), dim=-1).to(BF16)
+    st = fp8_consumers.Stash(a, w, sa, sb, None)
+    q, k, v = fp8_consumers.qk_norm_rope_fused(st, H, H, 128, qw, kw, table, 1e-6)
+    sends = ops.fp8_gemm_qkv_send(a, w, sa, sb, H, 1, qk_norm=(qw, kw, table.float(), 1e-6))
+    assert same_bits(q.cpu(), sends[0].view(M, H, 128).cpu()) and same_bits(k.cpu(), sends[1].view(M, H, 128).cpu())
+    y = st.materialize()
+    assert same_bits(v.cpu(), y[:, 2 * H * 128:].reshape(M, H, 128).cpu())
+    N2, K2 = 512, 1024
+    a2, w2, sa2, sb2 = _serving_like(M, N2, K2, seed=7, dev=dev)
+    x = torch.randn(M, N2, device=dev, generator=g).to(BF16)
+    gate = torch.randn(3, N2, device=dev, generator=g).to(BF16)
+    idx = torch.randint(0, 3, (M,), device=dev, generator=g)
+    ph = torch.empty(M, N2, device=dev, dtype=BF16)
+    out = fp8_consumers.gate_fused(fp8_consumers.Stash(a2, w2, sa2, sb2, None, ph), x, gate, idx)
+    assert out.data_ptr() == ph.data_ptr()
+    assert same_bits(out.cpu(), ops.fp8_gemm_gate(a2, w2, sa2, sb2, x, gate, idx).cpu())
+    assert ops.device_status() == 0

@@ -43,6 +43,17 @@ def test_gemm_integer_inputs_exact(golden):
     assert same_bits(og.scaled_mm(a, w, sa, sb, None, torch.float16), t16(g["int_yf16"], torch.float16))
 
 
+def test_indexed_gate_fc2_epilogue(golden):
+    """x + gate[idx] * bf16(fc2 epilogue): the oracle equals the reference's eager mirror bit for bit."""
+    g = golden("gate")
+    a, w, sa, sb, bias = t8(g["a"]), t8(g["w"]), tf(g["sa"]), tf(g["sb"]), t16(g["bias"])
+    x, gate6, idx = t16(g["x"]), t16(g["gate6"]), torch.from_numpy(g["idx"])
+    gate = gate6.chunk(6, dim=-1)[5]
+    acc = og.accumulate(a, w)
+    assert same_bits(og.indexed_gate(x, gate, og.epilogue(acc, sa, sb, None, BF16), idx), t16(g["y"]))
+    assert same_bits(og.indexed_gate(x, gate, og.epilogue(acc, sa, sb, bias, BF16), idx), t16(g["ybias"]))
+
+
 def test_gemm_random_inputs_close(golden):
     g = golden("gemm")
     y = og.scaled_mm(t8(g["rnd_a"]), t8(g["rnd_w"]), tf(g["rnd_sa"]), tf(g["rnd_sb"]))
