@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(p_full(s), 128);
+      mbar_init(p_full(s), 4);  // one arrival per softmax warp (128 per-thread arrivals serialise on the word)
       mbar_init(o_full(s), 1);
     }
     mbar_init(done_bar, 1);
@@ -372,7 +372,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         l_run += lsum;
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(p_full(q));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(q));
       }
       if (ok && mbar_wait(o_full(q), 0, p.wc)) {
         tc_fence_after();
