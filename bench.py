@@ -342,8 +342,8 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
                      "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": f"{peaks['source']} bf16 dense, sustained (kernel timed inside a long step)",
                      "traffic": ATTN_TRAFFIC_BYTES if (world == 1 and tokens == TOKENS) else None,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch on this "
-                                       "workload (profiles/launches_cfg2_sp1.md)"},
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one attention launch "
+                                       "in the launch-list capture of this bench at cfg2 SP=1"},
         "e2e": {"value": total_fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": m * HIDDEN * 2, "d2h_bytes_per_step": m * HIDDEN * 2},
         "gpu_launches": (blk.KERNELS_PER_FORWARD + (blk.P2P_BARRIERS if p2p else 0)) * args.steps,
