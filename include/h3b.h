@@ -91,12 +91,15 @@ typedef struct h3b_qkv_send {
   int32_t rank;
   void* peer_recv[H3B_MAX_RANKS][3];
   int32_t* peer_range_flag[H3B_MAX_RANKS]; /* v_f16 overflow flag of each destination rank (replaces range_flag) */
+  /* qkv_interleaved != 0 (not with p2p): one send buffer send[0] = [G, P, M, 3, hgl, d] holding q, k, v of a token
+   * side by side (the combined-exchange layout of h3_tp2/ulysses_nocopy.py:74-90; send[1], send[2] unused) */
+  int32_t qkv_interleaved;
 } h3b_qkv_send;
 
 /* ---------------------------------------------------------------------------------------------------------------
  * library information
  * ------------------------------------------------------------------------------------------------------------- */
-H3B_API int h3b_abi_version(void); /* 2: h3b_qkv_send gained the peer-memory fields */
+H3B_API int h3b_abi_version(void); /* 3: h3b_qkv_send gained the peer-memory fields (2) and qkv_interleaved (3) */
 H3B_API const char* h3b_status_string(int status);
 H3B_API const char* h3b_last_error(void);
 /* Reads and clears the sticky device status word of the current device (0 or a negative h3b_status). Synchronises

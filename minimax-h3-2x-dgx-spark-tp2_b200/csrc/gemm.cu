@@ -46,6 +46,8 @@ struct Params {
   void* send[3];
   int hd;        // QKV_SEND: heads * 128
   int hl;        // heads per rank and group (hgl)
+  int rsh;       // QKV_SEND: heads per send row (hl, or 3 * hl when q, k, v are interleaved)
+  int64_t qkv_step;  // QKV_SEND interleaved: elements between the q, k and v slots of a row
   int hg;        // heads per group
   int ws;        // Ulysses degree P
   int v_f16;
@@ -74,6 +76,7 @@ __device__ __forceinline__ uint16_t* send_slab(const Params& p, int which, int g
     return static_cast<uint16_t*>(p.peer[dst_rank][which]);
   }
   slot = static_cast<int64_t>(g) * p.ws + dst_rank;  // (group, destination) slab of this rank's send buffer
+  if (p.qkv_step) return static_cast<uint16_t*>(p.send[0]) + which * p.qkv_step;
   return static_cast<uint16_t*>(p.send[which]);
 }
 
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
                 int64_t seg;
                 uint16_t* dst = send_slab(p, which, g, dst_rank, seg);
-                dst += ((seg * p.M + m) * p.hl + j) * 128;
+                dst += ((seg * p.M + m) * p.rsh + j) * 128;
                 const __nv_bfloat16* wn = p.norm_w[which];
                 const uint32_t hbase = tacc + c0;
                 // pass 1: the bf16 head values (the GEMM output the reference normalises) and their sum of squares
@@ -451,7 +454,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
               int64_t seg;
               uint16_t* slab = send_slab(p, which, g, dst_rank, seg);
-              const int64_t off = ((seg * p.M + m) * p.hl + j) * 128 + c;
+              const int64_t off = ((seg * p.M + m) * p.rsh + j) * 128 + c;
               const bool as_f16 = which == 2 && p.v_f16;
               int32_t* rf = p.range_flag;
               if (as_f16 && rf != nullptr) {
@@ -597,6 +600,10 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
         }
         p.peer_rf[r] = send->v_f16 ? send->peer_range_flag[r] : nullptr;
       }
+    } else if (send->qkv_interleaved) {
+      if (send->send[0] == nullptr || (reinterpret_cast<uintptr_t>(send->send[0]) & 15u))
+        return fail(H3B_EALIGN, "fp8_gemm qkv_send: send buffer null or not 16-byte aligned");
+      p.send[0] = send->send[0];
     } else {
       for (int i = 0; i < 3; ++i) {
         if (send->send[i] == nullptr || (reinterpret_cast<uintptr_t>(send->send[i]) & 15u))
@@ -621,6 +628,9 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
     p.hd = send->heads * 128;
     p.hg = send->heads / groups;
     p.hl = p.hg / send->ws;
+    if (send->qkv_interleaved && send->p2p) return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: interleaved with p2p");
+    p.rsh = send->qkv_interleaved ? 3 * p.hl : p.hl;
+    p.qkv_step = send->qkv_interleaved ? static_cast<int64_t>(p.hl) * 128 : 0;
     p.ws = send->ws;
     p.v_f16 = send->v_f16 != 0;
     p.range_flag = send->range_flag;

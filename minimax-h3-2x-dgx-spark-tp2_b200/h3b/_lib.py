@@ -18,14 +18,15 @@ EPI_PLAIN, EPI_QKV_SEND, EPI_SWIGLU = 0, 1, 2
 
 _p, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
 MAX_RANKS = 8   # H3B_MAX_RANKS
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class QkvSend(ctypes.Structure):
     _fields_ = [("send", _p * 3), ("heads", _i32), ("head_dim", _i32), ("ws", _i32), ("v_f16", _i32),
                 ("range_flag", _p), ("groups", _i32), ("q_norm_weight", _p), ("k_norm_weight", _p),
                 ("rope_table", _p), ("rope_stride", _i64), ("rot", _i32), ("eps", _f32),
-                ("p2p", _i32), ("rank", _i32), ("peer_recv", (_p * 3) * MAX_RANKS), ("peer_range_flag", _p * MAX_RANKS)]
+                ("p2p", _i32), ("rank", _i32), ("peer_recv", (_p * 3) * MAX_RANKS), ("peer_range_flag", _p * MAX_RANKS),
+                ("qkv_interleaved", _i32)]
 
 
 class IpcHandle(ctypes.Structure):

@@ -63,10 +63,11 @@ class AttentionBlock:
         self.groups = default_groups(heads, ws) if groups is None else int(groups)
         if heads % (self.groups * ws):
             raise ValueError(f"heads {heads} not divisible by groups {self.groups} x ws {ws}")
-        # "nccl": the all-to-alls as collectives (stock's exchange); "p2p": stored by the kernels into the peers'
-        # receive buffers (h3b.ulysses_p2p), no collective on the data path
-        if exchange not in ("nccl", "p2p"):
-            raise ValueError(f"exchange {exchange!r}: 'nccl' or 'p2p'")
+        # "nccl": the all-to-alls as collectives (stock's exchange); "nocopy": one combined q/k/v collective per head
+        # group on the interleaved layout (h3b.ulysses_nocopy); "p2p": stored by the kernels into the peers' receive
+        # buffers (h3b.ulysses_p2p), no collective on the data path
+        if exchange not in ("nccl", "nocopy", "p2p"):
+            raise ValueError(f"exchange {exchange!r}: 'nccl', 'nocopy' or 'p2p'")
         if exchange == "p2p" and self.groups != 1:
             raise ValueError("exchange 'p2p' has no head groups")
         self.exchange_kind = exchange
@@ -100,11 +101,14 @@ class AttentionBlock:
         if self.ws == 1:
             return send
         recv = torch.empty_like(send)
+        self.exchange_into(recv, send)
+        return recv
+
+    def exchange_into(self, recv: torch.Tensor, send: torch.Tensor) -> None:
         if self.a2a is not None:
             self.a2a(recv, send, group=self.pg)
         else:
             dist.all_to_all_single(recv, send, group=self.pg)
-        return recv
 
     STAGES = ("quant_x", "qkv_gemm", "a2a_fwd", "attention", "a2a_back", "quant_out", "out_gemm")
 
@@ -133,6 +137,27 @@ class AttentionBlock:
             px.barrier()
             mark()
             o8, so = ops.quant_from_recv(px.back)
+        elif self.ws > 1 and self.exchange_kind == "nocopy":
+            from .ulysses_nocopy import qkv_views
+            from .ulysses_overlap import quant_grouped_back
+            G = self.groups
+            send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+                                         range_flag=self.range_flag, groups=G, interleaved=True)
+            self.share_range_flag()
+            mark()
+            recv = torch.empty_like(send)
+            for g in range(G):
+                self.exchange_into(recv[g], send[g])
+            mark()
+            hgl = self.heads // (G * self.ws)
+            outs = [ops.flash_attn(*qkv_views(recv[g], v_f16=True), scale=1.0 / math.sqrt(d),
+                                   range_flag=self.range_flag) for g in range(G)]
+            mark()
+            back = torch.empty((G, self.ws, m, hgl, d), dtype=torch.bfloat16, device=self.device)
+            for g in range(G):
+                self.exchange_into(back[g], outs[g].view(self.ws, m, hgl, d))
+            mark()
+            o8, so = ops.quant_from_recv(back[0]) if G == 1 else quant_grouped_back(back)
         elif self.ws > 1 and self.groups > 1:
             from .ulysses_overlap import grouped_attention, quant_grouped_back
             sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,

@@ -46,6 +46,58 @@ scaled_mm_tensor32 = scaled_mm     # h3_tp2/fp8_gemm.py:149
 scaled_mm_fused = scaled_mm        # h3_tp2/fp8_gemm.py:240
 
 
+def launch_fused(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None,
+                 y: torch.Tensor) -> torch.Tensor:
+    """One fused launch into ``y`` (h3_tp2/fp8_gemm.py:213): sa [M], sb [N] fp32 vectors, b [K, N]."""
+    return ops.fp8_gemm(a, b.t(), sa, sb, bias, y.dtype, out=y)
+
+
+def fused_config() -> tuple[int, int, int, int, int]:
+    """(BLOCK_M, BLOCK_N, BLOCK_K, stages, GROUP_M) of the tcgen05 kernel (h3_tp2/fp8_gemm.py:202 returns the Triton
+    kernel's)."""
+    return 128, 256, 128, 4, 16
+
+
+def tile_coords(pid: int, M: int, N: int, block_m: int = 128, block_n: int = 256, group_m: int = 16) -> tuple[int, int]:
+    """Grouped raster of the persistent kernel: tile ``pid`` -> (row block, column block); GROUP_M row blocks share
+    each column block's W tile in L2 (h3_tp2/fp8_gemm.py:188 is the same raster)."""
+    num_mb, num_nb = -(-M // block_m), -(-N // block_n)
+    in_group = group_m * num_nb
+    group = pid // in_group
+    first = group * group_m
+    gsize = min(num_mb - first, group_m)
+    r = pid - group * in_group
+    return first + r % gsize, r // gsize
+
+
+def unit_scale(device) -> torch.Tensor:  # noqa: ANN001
+    """A cached fp32 scalar 1 (h3_tp2/fp8_gemm.py:132)."""
+    key = str(device)
+    t = _unit.get(key)
+    if t is None:
+        t = _unit[key] = torch.ones((), dtype=torch.float32, device=device)
+    return t
+
+
+_unit: dict = {}
+
+
+def probe_fused(device) -> bool:  # noqa: ANN001
+    """True when the tcgen05 kernel can serve on ``device``: an sm_100 GPU and the library loads; a small GEMM
+    against integer inputs (exact in any summation order) confirms it (h3_tp2/fp8_gemm.py:251)."""
+    dev = torch.device(device)
+    if dev.type != "cuda" or torch.cuda.get_device_capability(dev) != (10, 0):
+        return False
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randint(-3, 4, (130, 64), device=dev, generator=g).to(torch.float8_e4m3fn)
+    w = torch.randint(-3, 4, (272, 64), device=dev, generator=g).to(torch.float8_e4m3fn)
+    sa = torch.full((130,), 0.5, device=dev)
+    sb = torch.full((272,), 0.25, device=dev)
+    y = ops.fp8_gemm(a, w, sa, sb)
+    ref = ((a.float() @ w.float().t()) * 0.25 * 0.5).to(torch.bfloat16)
+    return bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
+
+
 def epilogue_reference_order() -> str:
     return "t = scale_b * acc; y = scale_a * t (bias: fma(scale_a, t, bias)); one rounding"
 

@@ -247,7 +247,8 @@ def fp8_gemm_gate(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.
 
 def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, heads: int, ws: int, *,
                       bias: torch.Tensor | None = None, v_f16: bool = False, sends=None,
-                      range_flag: torch.Tensor | None = None, groups: int = 1, qk_norm=None, p2p=None):
+                      range_flag: torch.Tensor | None = None, groups: int = 1, qk_norm=None, p2p=None,
+                      interleaved: bool = False):
     """qkv projection whose epilogue writes q, k, v straight into the Ulysses send buffers (the producer redirection
     of ulysses_exact.fused_into_send, h3_tp2/ulysses_exact.py:278, moved into the GEMM).  groups = 1: each buffer is
     stock's [P, M, H/P, d]; groups = G > 1: [G, P, M, H/(G*P), d], head h = g*(H/G) + p*(H/(G*P)) + j, one
@@ -257,7 +258,10 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
 
     ``p2p = (rank, peer_recv, peer_range_flag)``: no send buffers; the slab for rank p goes straight into
     ``peer_recv[p] = (q, k, v)`` (device tensors or addresses of rank p's [P, M, H/P, d] receive buffers, slot
-    ``rank``) and a v overflow raises ``peer_range_flag[p]``.  Returns None then."""
+    ``rank``) and a v overflow raises ``peer_range_flag[p]``.  Returns None then.
+
+    ``interleaved``: one send buffer [G, P, M, 3, H/(G*P), d] (q, k, v of a token side by side, the combined-exchange
+    layout of ulysses_nocopy) is returned instead of three; its v slots hold f16 bits when ``v_f16``."""
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
@@ -278,14 +282,24 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
         _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(),
                   sb.data_ptr(), _ptr(bias), None, 0, M, N, K, OUT_BF16, EPI_QKV_SEND, ctypes.byref(desc), _stream(a))
         return None
-    if sends is None:
-        sends = [torch.empty(shape, dtype=torch.bfloat16, device=a.device) for _ in range(2)]
-        sends.append(torch.empty(shape, dtype=torch.float16 if v_f16 else torch.bfloat16, device=a.device))
     desc = _lib.QkvSend()
-    for i in range(3):
-        if tuple(sends[i].shape) != shape or not sends[i].is_contiguous():
-            raise ValueError(f"fp8_gemm_qkv_send: send buffers must be contiguous {shape}")
-        desc.send[i] = sends[i].data_ptr()
+    if interleaved:
+        ishape = (groups, ws, M, 3, heads // (ws * groups), 128)
+        buf = sends if sends is not None else torch.empty(ishape, dtype=torch.bfloat16, device=a.device)
+        if tuple(buf.shape) != ishape or not buf.is_contiguous():
+            raise ValueError(f"fp8_gemm_qkv_send: interleaved send buffer must be contiguous {ishape}")
+        desc.send[0] = buf.data_ptr()
+        desc.qkv_interleaved = 1
+        result = buf
+    else:
+        if sends is None:
+            sends = [torch.empty(shape, dtype=torch.bfloat16, device=a.device) for _ in range(2)]
+            sends.append(torch.empty(shape, dtype=torch.float16 if v_f16 else torch.bfloat16, device=a.device))
+        for i in range(3):
+            if tuple(sends[i].shape) != shape or not sends[i].is_contiguous():
+                raise ValueError(f"fp8_gemm_qkv_send: send buffers must be contiguous {shape}")
+            desc.send[i] = sends[i].data_ptr()
+        result = sends
     desc.heads, desc.head_dim, desc.ws, desc.v_f16 = heads, 128, ws, int(bool(v_f16))
     desc.groups = int(groups)
     if qk_norm is not None:
@@ -302,7 +316,7 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
     desc.range_flag = _ptr(range_flag)
     _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
               _ptr(bias), None, 0, M, N, K, OUT_BF16, EPI_QKV_SEND, ctypes.byref(desc), _stream(a))
-    return sends
+    return result
 
 
 # ---------------------------------------------------------------------------------------------------------------

@@ -115,3 +115,46 @@ def norm_rope_into_send(x: torch.Tensor, w: torch.Tensor, table: torch.Tensor, e
     """``ulysses_exact.rope_into_send`` (h3_tp2/ulysses_exact.py:264-271) with the eager producer: the normed and
     rotated q (or k) of each destination's heads written into send [P, M, H/P, d]."""
     return pack(norm_rope(x, w, table, eps), ws)
+
+
+# ---- the combined q/k/v exchange (h3_tp2/ulysses_nocopy.py:74-189) -------------------------------------------------
+
+def nocopy_send_shape(m: int, heads: int, d: int, ws: int, groups: int) -> tuple[int, ...]:
+    """[G, P, M, 3, H/(G*P), d] (h3_tp2/ulysses_nocopy.py:74)."""
+    return (groups, ws, m, 3, heads // (groups * ws), d)
+
+
+def pack_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ws: int, groups: int) -> torch.Tensor:
+    """q, k, v [M, H, d] -> contiguous [G, P, M, 3, hl, d]; head h = g*(H/G) + p*hl + j (:78-87)."""
+    m, h, d = q.shape
+    hl = h // (groups * ws)
+
+    def by_dest(x):
+        return x.reshape(m, groups, ws, hl, d).permute(1, 2, 0, 3, 4)
+    return torch.stack((by_dest(q), by_dest(k), by_dest(v)), dim=3).contiguous()
+
+
+def qkv_views(recv_g: torch.Tensor):
+    """recv [P, M, 3, hl, d] of one group -> q, k, v views [1, P*M, hl, d] with row stride 3*hl*d (:105-109)."""
+    p, m, _, hl, d = recv_g.shape
+    flat = recv_g.reshape(p * m, 3, hl, d)
+    return flat[:, 0].unsqueeze(0), flat[:, 1].unsqueeze(0), flat[:, 2].unsqueeze(0)
+
+
+def nocopy_forward(q, k, v, attn, *, ws: int, groups: int, a2a) -> torch.Tensor:
+    """One rank of the combined exchange (:124-160, same stream): pack, one a2a per group, attention on the strided
+    views, the output's rows back with one a2a per group, unpacked into [1, M, H, d]."""
+    _, m, heads, d = q.shape
+    send = pack_qkv(q[0], k[0], v[0], ws, groups)
+    hl = send.shape[4]
+    hg = hl * ws
+    recv = torch.empty_like(send)
+    for g in range(groups):
+        a2a(recv[g], send[g])
+    result = torch.empty((1, m, heads, d), dtype=q.dtype)
+    for g in range(groups):
+        o = attn(*qkv_views(recv[g]))[0].contiguous()
+        recv_b = torch.empty((ws, m, hl, d), dtype=q.dtype)
+        a2a(recv_b, o)
+        result[0, :, g * hg:(g + 1) * hg] = recv_b.permute(1, 0, 2, 3).reshape(m, hg, d)
+    return result

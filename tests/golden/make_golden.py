@@ -17,6 +17,8 @@ Reference functions exercised (paths inside the reference project):
   ulysses:  h3_tp2/ulysses_exact.py:187 exact_forward, :108 send_shape, :119 pack_into, :156 exchange_back, and the
             stock exchange tests/test_ulysses_exact.py:74 stock_all_to_all_4d, with FakeA2A (:25)
   rope:     h3_tp2/ulysses_exact.py:264 rope_into_send with the eager norm+RoPE stand-in tests/test_ulysses_exact.py:107
+  nocopy:   h3_tp2/ulysses_nocopy.py:74 send_shape, :84 pack_qkv, :105 qkv_views, :112 back_into, :124 nocopy_forward
+            (one combined q/k/v exchange per head group) with FakeA2A, and the stock exchange for comparison
   gate:     h3_tp2/fp8_consumers.py:367 _gate_torch (the eager mirror of _scale_indexed_gate_kernel) on an exact
             integer fp32 product, gate rows as a row-strided chunk view (recipe of tests/test_fp8_consumer_fuse.py:118)
 """
@@ -246,6 +248,45 @@ def gen_rope(ux, tue) -> dict:
     return out
 
 
+def gen_nocopy(nc, tue) -> dict:
+    import threading
+    out = {}
+    heads, d = 8, 128
+    for ws, m, groups in ((2, 16, 1), (2, 16, 2), (4, 8, 1), (4, 8, 2)):
+        g = torch.Generator().manual_seed(100 + 10 * ws + groups)
+        qs = [(torch.randn(1, m, heads, d, generator=g)).to(BF16) for _ in range(ws)]
+        ks = [(torch.randn(1, m, heads, d, generator=g)).to(BF16) for _ in range(ws)]
+        vs = [(torch.randn(1, m, heads, d, generator=g)).to(BF16) for _ in range(ws)]
+
+        def attn(q, k, v):  # layout-revealing and elementwise; returns a dense [1, S, hl, d] like cuDNN
+            return (q.float() + 2.0 * k.float() - 0.5 * v.float()).to(q.dtype).contiguous()
+
+        def body(r, a2a):
+            res = nc.nocopy_forward(qs[r], ks[r], vs[r], attn, ws=ws, groups=groups, a2a=a2a)
+            send = torch.empty(nc.send_shape(m, heads, d, ws, groups), dtype=BF16)
+            nc.pack_qkv(send, qs[r][0], ks[r][0], vs[r][0], ws, groups)
+            return res, send
+
+        fake = tue.FakeA2A(ws)
+        results = [None] * ws
+
+        def run(r):
+            results[r] = body(r, fake.bind(r))
+        ts = [threading.Thread(target=run, args=(r,)) for r in range(ws)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        key = f"ws{ws}_g{groups}"
+        for r in range(ws):
+            res, send = results[r]
+            out[f"{key}_q{r}"], out[f"{key}_k{r}"], out[f"{key}_v{r}"] = bits16(qs[r]), bits16(ks[r]), bits16(vs[r])
+            out[f"{key}_out{r}"] = bits16(res)
+            out[f"{key}_send{r}"] = bits16(send)
+        out[f"{key}_shape"] = np.array([m, heads, d])
+    return out
+
+
 def gen_gate(fc) -> dict:
     g = torch.Generator().manual_seed(7)
     M, N, K = 200, 272, 256        # partial row / column tiles
@@ -274,7 +315,7 @@ def main() -> None:
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
     sys.path.insert(0, str(ref / "tests"))
-    from h3_tp2 import fp8_consumers, fp8_gemm, fp8_quant_fuse, fp8_swiglu, ulysses_exact, ulysses_outq  # noqa: PLC0415
+    from h3_tp2 import fp8_consumers, fp8_gemm, fp8_quant_fuse, fp8_swiglu, ulysses_exact, ulysses_nocopy, ulysses_outq  # noqa: PLC0415,E501
     import fake_h3_consumers  # noqa: PLC0415
     import test_ulysses_exact  # noqa: PLC0415
 
@@ -286,6 +327,7 @@ def main() -> None:
     np.savez_compressed(HERE / "ulysses.npz", **gen_ulysses(ulysses_exact, test_ulysses_exact))
     np.savez_compressed(HERE / "rope.npz", **gen_rope(ulysses_exact, test_ulysses_exact))
     np.savez_compressed(HERE / "gate.npz", **gen_gate(fp8_consumers))
+    np.savez_compressed(HERE / "nocopy.npz", **gen_nocopy(ulysses_nocopy, test_ulysses_exact))
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -151,3 +151,25 @@ def test_norm_rope_into_send(golden):
         table = tf(g[f"ws{ws}_table"])
         assert same_bits(ou.norm_rope_into_send(q, t16(g[f"ws{ws}_wq"]), table, 1e-6, ws), t16(g[f"ws{ws}_sendq"]))
         assert same_bits(ou.norm_rope_into_send(k, t16(g[f"ws{ws}_wk"]), table, 1e-6, ws), t16(g[f"ws{ws}_sendk"]))
+
+
+def test_nocopy_combined_exchange(golden):
+    """The combined q/k/v exchange (pack [G, P, M, 3, hl, d], one a2a per group, strided views, reverse a2a + unpack)
+    restated in the oracle equals the reference's nocopy_forward and pack_qkv bit for bit, over threads."""
+    g = golden("nocopy")
+
+    def attn(q, k, v):
+        return (q.float() + 2.0 * k.float() - 0.5 * v.float()).to(q.dtype).contiguous()
+
+    for ws, groups in ((2, 1), (2, 2), (4, 1), (4, 2)):
+        key = f"ws{ws}_g{groups}"
+        m, heads, d = (int(x) for x in g[f"{key}_shape"])
+        qs = [t16(g[f"{key}_q{r}"]) for r in range(ws)]
+        ks = [t16(g[f"{key}_k{r}"]) for r in range(ws)]
+        vs = [t16(g[f"{key}_v{r}"]) for r in range(ws)]
+        for r in range(ws):
+            assert same_bits(ou.pack_qkv(qs[r][0], ks[r][0], vs[r][0], ws, groups), t16(g[f"{key}_send{r}"]))
+        outs = ou.run_ranks(lambda r, a2a: ou.nocopy_forward(qs[r], ks[r], vs[r], attn, ws=ws, groups=groups,
+                                                              a2a=a2a), ws)
+        for r in range(ws):
+            assert same_bits(outs[r], t16(g[f"{key}_out{r}"])), (key, r)
