@@ -225,7 +225,7 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
     m = tokens // world
     p2p = args.exchange == "p2p" and world > 1
     blk = AttentionBlock(HIDDEN, HEADS, device=dev, ws=world, pg=pg, init_device=dev, seed=1,
-                         groups=1 if p2p else (args.groups or None), exchange="p2p" if p2p else "nccl")
+                         groups=1 if p2p else (args.groups or None), exchange=args.exchange if world > 1 else "nccl")
     try:
         _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p)
     finally:
@@ -335,8 +335,10 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
                                f"{HEADS} heads x {HEAD_DIM}, Ulysses SP={world}", "tokens": tokens,
                    "rows_per_rank": m, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM, "sp": world,
                    "head_groups": blk.groups, "l2": "inputs larger than L2 (no flush)",
-                   "exchange": ("peer memory (epilogue stores over NVLink + epoch barriers)" if p2p else
-                                "NCCL all_to_all_single") if world > 1 else "none (SP=1)"},
+                   "exchange": {"p2p": "peer memory (epilogue stores over NVLink + epoch barriers)",
+                                "nccl": "NCCL all_to_all_single (q, k, v, out)",
+                                "nocopy": "NCCL all_to_all_single (combined q/k/v per head group, out)"}[args.exchange]
+                               if world > 1 else "none (SP=1)"},
         "ms_per_stage": stage_ms,
         "roofline": {"bound": "tensor", "kernel": "flash_attn", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
@@ -368,8 +370,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--groups", type=int, default=0,
                     help="Ulysses head groups overlapped with attention (NCCL exchange; 0: the measured default)")
-    ap.add_argument("--exchange", choices=("nccl", "p2p"), default="p2p",
-                    help="Ulysses exchange at SP > 1: NCCL all-to-all, or the kernels' stores into peer memory")
+    ap.add_argument("--exchange", choices=("nccl", "nocopy", "p2p"), default="p2p",
+                    help="Ulysses exchange at SP > 1: NCCL all-to-alls (three per block, or one combined q/k/v "
+                         "exchange with nocopy), or the kernels' stores into peer memory")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

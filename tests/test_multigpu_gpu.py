@@ -22,7 +22,8 @@ def _port():
 
 
 @pytest.mark.parametrize("n,groups,exchange", [(2, 1, "nccl"), (2, 2, "nccl"), (4, 1, "nccl"), (4, 2, "nccl"),
-                                               (8, 1, "nccl"), (2, 1, "p2p"), (4, 1, "p2p"), (8, 1, "p2p")])
+                                               (8, 1, "nccl"), (2, 1, "p2p"), (4, 1, "p2p"), (8, 1, "p2p"),
+                                               (2, 1, "nocopy"), (4, 2, "nocopy")])
 def test_ulysses_ranks_equal_single_gpu(dev, tmp_path, n, groups, exchange):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs, {torch.cuda.device_count()} visible")
