@@ -98,3 +98,55 @@ def test_kernels_refuse_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         ops.flash_attn(torch.zeros(8, 1, 128, dtype=torch.bfloat16), torch.zeros(8, 1, 128, dtype=torch.bfloat16),
                        torch.zeros(8, 1, 128, dtype=torch.bfloat16))
+
+
+def test_new_entry_points_refuse_cpu_tensors():
+    z8 = torch.zeros(4, 64, dtype=torch.float8_e4m3fn)
+    s = torch.ones(4)
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.fp8_gemm_gate(z8, z8, s, s, x, x, torch.zeros(4, dtype=torch.int64))
+    q = torch.zeros(8, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.flash_attn_p2p(q, q, q, [q, q], 0)
+    from h3b import ulysses_nocopy
+    send = torch.zeros(ulysses_nocopy.send_shape(4, 4, 128, 2, 1), dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ulysses_nocopy.pack_qkv(send, torch.zeros(4, 4, 128), torch.zeros(4, 4, 128), torch.zeros(4, 4, 128), 2, 1)
+
+
+def test_nocopy_layout_helpers_match_the_oracle():
+    """send_shape / qkv_views of the mirror against the oracle's restatement (pure views, no kernel)."""
+    from h3b import ulysses_nocopy
+    assert ulysses_nocopy.send_shape(16, 8, 128, 2, 2) == ou.nocopy_send_shape(16, 8, 128, 2, 2) == (2, 2, 16, 3, 2, 128)
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(16, 8, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    send = ou.pack_qkv(q, k, v, 2, 1)
+    a = ulysses_nocopy.qkv_views(send[0])
+    b = ou.qkv_views(send[0])
+    for x, y in zip(a, b):
+        assert x.stride() == y.stride() and same_bits(x.contiguous(), y.contiguous())
+    v16 = ulysses_nocopy.qkv_views(send[0], v_f16=True)[2]
+    assert v16.dtype == torch.float16 and v16.data_ptr() == a[2].data_ptr()
+
+
+def test_p2p_epoch_is_passed_as_int32_serial_number(monkeypatch):
+    """Epochs grow without bound on the host; the barrier kernel compares them as 32-bit serial numbers."""
+    seen = []
+    monkeypatch.setattr(ops._lib, "call", lambda name, *args: seen.append(args[4]))
+    for e in (1, 2 ** 31 - 1, 2 ** 31, 2 ** 32 + 5):
+        ops.p2p_signal_wait([16, 32], 16, 0, e, 0)
+    assert seen == [1, 2 ** 31 - 1, -2 ** 31, 5]
+
+
+def test_block_exchange_options_are_validated():
+    from h3b.block import AttentionBlock
+    w = (torch.zeros(3 * 2 * 128, 64, dtype=torch.float8_e4m3fn), torch.ones(768),
+         torch.zeros(64, 256, dtype=torch.float8_e4m3fn), torch.ones(64))
+    with pytest.raises(ValueError, match="exchange"):
+        AttentionBlock(64, 2, device="cpu", ws=2, weights=w, exchange="rdma", groups=1)
+    with pytest.raises(ValueError, match="head groups"):
+        AttentionBlock(64, 4, device="cpu", ws=2, weights=(torch.zeros(3 * 4 * 128, 64, dtype=torch.float8_e4m3fn),
+                                                           torch.ones(1536), torch.zeros(64, 512,
+                                                                                        dtype=torch.float8_e4m3fn),
+                                                           torch.ones(64)), exchange="p2p", groups=2, rank=0)
