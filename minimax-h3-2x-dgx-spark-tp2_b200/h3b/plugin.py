@@ -36,13 +36,20 @@ def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
 def plan(env: dict | None = None) -> dict:
     """The patches ``_apply`` would install for an environment (pure; used by tests)."""
     env = os.environ if env is None else env
-    out = {"ulysses": None, "fp8_gemm": None, "quant_fuse": None, "overlap": None, "a2a_timing": False}
-    overlap = env.get("H3_TP2_A2A_OVERLAP", "0").strip()
+    out = {"ulysses": None, "fp8_gemm": None, "quant_fuse": None, "overlap": None, "nocopy": None,
+           "a2a_timing": False}
+    # the reference's precedence (h3_tp2/plugin.py:278-308): the combined exchange only when forced (it runs the
+    # overlap's head groups itself), else the exact exchange (default "2"; replaces the overlap when both are set),
+    # else the overlap
+    ov = env.get("H3_TP2_A2A_OVERLAP", "").strip()
+    ov_groups = int(ov) if ov and int(ov) > 1 else 1
     exact = env.get("H3_TP2_ULYSSES_EXACT", "2").strip().lower()
-    if overlap not in ("", "0"):
-        out["overlap"] = int(overlap)
+    if env.get("H3_TP2_ULYSSES_NOCOPY", "0") == "force":
+        out["nocopy"] = ov_groups
     elif exact not in ("", "0"):
         out["ulysses"] = exact
+    elif ov_groups > 1:
+        out["overlap"] = ov_groups
     level = env.get("H3_TP2_FP8_GEMM", "cutlass").strip().lower()
     if level not in ("", "0", "off"):
         out["fp8_gemm"] = level
@@ -59,12 +66,15 @@ def _apply(role: str) -> None:
     if p["a2a_timing"]:
         from . import a2a_timing  # noqa: PLC0415
         a2a_timing.install()
-    if p["overlap"]:
-        from . import ulysses_overlap  # noqa: PLC0415
-        ulysses_overlap.install(p["overlap"])
+    if p["nocopy"]:
+        from . import ulysses_nocopy  # noqa: PLC0415
+        ulysses_nocopy.install(p["nocopy"])
     elif p["ulysses"]:
         from . import ulysses_exact  # noqa: PLC0415
         ulysses_exact.install(p["ulysses"])
+    elif p["overlap"]:
+        from . import ulysses_overlap  # noqa: PLC0415
+        ulysses_overlap.install(p["overlap"])
     if p["fp8_gemm"]:
         from . import fp8_gemm  # noqa: PLC0415
         fp8_gemm.install(p["fp8_gemm"])

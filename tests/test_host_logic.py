@@ -67,7 +67,12 @@ def test_plugin_plan_defaults_and_switches():
     p = plugin.plan({})
     assert p["ulysses"] == "2" and p["fp8_gemm"] == "cutlass" and p["overlap"] is None
     p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_FP8_GEMM": "0", "H3_TP2_A2A_TIMING": "1"})
-    assert p["overlap"] == 2 and p["ulysses"] is None and p["fp8_gemm"] is None and p["a2a_timing"]
+    assert p["ulysses"] == "2" and p["overlap"] is None and p["fp8_gemm"] is None and p["a2a_timing"]  # exact wins
+    p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_ULYSSES_EXACT": "0"})
+    assert p["overlap"] == 2 and p["ulysses"] is None and p["nocopy"] is None
+    p = plugin.plan({"H3_TP2_A2A_OVERLAP": "4", "H3_TP2_ULYSSES_NOCOPY": "force"})
+    assert p["nocopy"] == 4 and p["ulysses"] is None and p["overlap"] is None
+    assert plugin.plan({"H3_TP2_ULYSSES_NOCOPY": "1"})["nocopy"] is None      # the reference requires "force"
     plugin.register()  # no H3_TP2_ROLE: a no-op
 
 
