@@ -224,8 +224,16 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
         raise SystemExit(f"tokens {tokens} not divisible by {world} ranks")
     m = tokens // world
     p2p = args.exchange == "p2p" and world > 1
+    exchange = args.exchange if world > 1 else "nccl"
+    if p2p:
+        from h3b.ulysses_p2p import probe  # noqa: PLC0415
+        ok, why = probe(pg, dev)
+        if not ok:   # every rank agreed: take the collective path instead, and say so in the JSON line
+            print(f"bench.py: peer memory unavailable ({why}); NCCL exchange instead", file=sys.stderr)
+            p2p, exchange = False, "nccl"
+            args.exchange = "nccl"
     blk = AttentionBlock(HIDDEN, HEADS, device=dev, ws=world, pg=pg, init_device=dev, seed=1,
-                         groups=1 if p2p else (args.groups or None), exchange=args.exchange if world > 1 else "nccl")
+                         groups=1 if p2p else (args.groups or None), exchange=exchange)
     try:
         _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p)
     finally:

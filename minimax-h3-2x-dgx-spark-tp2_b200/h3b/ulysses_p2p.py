@@ -64,6 +64,31 @@ def _default_allgather(pg):
     return allgather
 
 
+def probe(pg, device) -> tuple[bool, str]:
+    """Collective check that every rank of ``pg`` can map every other rank's memory (CUDA IPC over NVLink): a 4 KiB
+    exchange buffer per rank, all-gathered handles, every peer opened; the verdict is agreed by all ranks
+    (all-reduce MIN), so they all take the same exchange path.  Returns (ok, reason of this rank's failure)."""
+    ws, rank = dist.get_world_size(pg), dist.get_rank(pg)
+    dev = torch.device(device)
+    reason = ""
+    px = None
+    try:
+        px = PeerExchange(1, ws, ws, rank, dev, pg=pg)
+    except Exception as exc:  # noqa: BLE001  (the verdict is collective below)
+        reason = f"{type(exc).__name__}: {exc}"
+    flag = torch.tensor([0 if reason else 1], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=pg)
+    if px is not None:
+        px.close(host_barrier=lambda: dist.barrier(group=pg))
+    else:  # keep the two host barriers of the others' close() matched
+        dist.barrier(group=pg)
+        dist.barrier(group=pg)
+    ok = bool(flag.item())
+    if not ok and not reason:
+        reason = "another rank could not map peer memory"
+    return ok, reason
+
+
 class PeerExchange:
     """Receive buffers of one Ulysses group for a fixed per-rank sequence length ``m`` (tokens per rank).
 

@@ -33,6 +33,10 @@ def main():
         from h3b.block import AttentionBlock
 
         m = args.tokens // ws
+        if args.exchange == "p2p":
+            from h3b.ulysses_p2p import probe
+            ok, why = probe(dist.group.WORLD, dev)
+            assert ok, why
         blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=ws, pg=dist.group.WORLD, seed=1,
                              groups=args.groups or None, exchange=args.exchange)
         full_blk = AttentionBlock(args.hidden, args.heads, device=dev, ws=1, seed=1) if rank == 0 else None
