@@ -472,53 +472,72 @@ __global__ void norm_rope_send_kernel(const uint16_t* __restrict__ x, int64_t m,
                                       int64_t stride_h, const __nv_bfloat16* __restrict__ w,
                                       const float* __restrict__ table, int64_t tstride, int rot, float eps, int hl,
                                       uint16_t* __restrict__ send) {
+  // a warp per token: the RoPE factors of the lane's 4 elements are read once and reused for every head; the heads
+  // go 4 at a time so that their loads are in flight together
+  constexpr int HU = 4;
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int half = rot >> 1;
   const int e0 = 4 * lane;  // this lane's 4 elements of the 128
+  const bool first = e0 < half, second = e0 >= half && e0 < rot;
+  const int src = first ? lane + (half >> 2) : (second ? lane - (half >> 2) : lane);
   float wv[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) wv[i] = __bfloat162float(w[e0 + i]);
-  for (int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; row < m * heads;
-       row += warps) {
-    const int64_t mm = row / heads;
-    const int h = static_cast<int>(row - mm * heads);
-    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x + mm * stride_m + h * stride_h + e0));
-    float f[4] = {lo_bf16(raw.x), hi_bf16(raw.x), lo_bf16(raw.y), hi_bf16(raw.y)};
-    float ss = __fmul_rn(f[0], f[0]);
-#pragma unroll
-    for (int i = 1; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(f[i], f[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), eps));
-    float n[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) n[i] = round_bf16(__fmul_rn(__fmul_rn(f[i], inv), wv[i]));
-    // rotation partner: element e pairs with e + half (first half) or e - half (second half of the rotated dims)
-    const bool first = e0 < half, second = e0 >= half && e0 < rot;
-    const int src = first ? lane + (half >> 2) : (second ? lane - (half >> 2) : lane);
-    float pn[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) pn[i] = __shfl_sync(0xffffffffu, n[i], src);
-    float out[4];
+  for (int64_t mm = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; mm < m; mm += warps) {
+    float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
     const float* trow = table + mm * tstride;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       if (first) {
-        const float cs = __ldg(trow + e0 + i), sn = __ldg(trow + half + e0 + i);
-        out[i] = __fsub_rn(__fmul_rn(n[i], cs), __fmul_rn(pn[i], sn));       // a cos - b sin
+        cs[i] = __ldg(trow + e0 + i);
+        sn[i] = __ldg(trow + half + e0 + i);
       } else if (second) {
-        const float cs = __ldg(trow + e0 - half + i), sn = __ldg(trow + e0 + i);
-        out[i] = __fadd_rn(__fmul_rn(n[i], cs), __fmul_rn(pn[i], sn));       // b cos + a sin
-      } else {
-        out[i] = n[i];
+        cs[i] = __ldg(trow + e0 - half + i);
+        sn[i] = __ldg(trow + e0 + i);
       }
     }
-    const int p = h / hl, j = h - p * hl;
-    uint2 o;
-    o.x = pack_bf16x2(out[0], out[1]);
-    o.y = pack_bf16x2(out[2], out[3]);
-    *reinterpret_cast<uint2*>(send + ((static_cast<int64_t>(p) * m + mm) * hl + j) * 128 + e0) = o;
+    const uint16_t* xrow = x + mm * stride_m + e0;
+    for (int h0 = 0; h0 < heads; h0 += HU) {
+      uint2 raw[HU];
+#pragma unroll
+      for (int u = 0; u < HU; ++u)
+        raw[u] = (h0 + u < heads) ? __ldg(reinterpret_cast<const uint2*>(xrow + (h0 + u) * stride_h)) : make_uint2(0, 0);
+#pragma unroll
+      for (int u = 0; u < HU; ++u) {
+        const int h = h0 + u;
+        if (h >= heads) break;  // warp-uniform
+        float f[4] = {lo_bf16(raw[u].x), hi_bf16(raw[u].x), lo_bf16(raw[u].y), hi_bf16(raw[u].y)};
+        float ss = __fmul_rn(f[0], f[0]);
+#pragma unroll
+        for (int i = 1; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(f[i], f[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), eps));
+        float n[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) n[i] = round_bf16(__fmul_rn(__fmul_rn(f[i], inv), wv[i]));
+        // rotation partner: element e pairs with e + half (first half) or e - half (second half of the rotated dims)
+        float pn[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pn[i] = __shfl_sync(0xffffffffu, n[i], src);
+        float out[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (first)
+            out[i] = __fsub_rn(__fmul_rn(n[i], cs[i]), __fmul_rn(pn[i], sn[i]));  // a cos - b sin
+          else if (second)
+            out[i] = __fadd_rn(__fmul_rn(n[i], cs[i]), __fmul_rn(pn[i], sn[i]));  // b cos + a sin
+          else
+            out[i] = n[i];
+        }
+        const int p = h / hl, j = h - p * hl;
+        uint2 o;
+        o.x = pack_bf16x2(out[0], out[1]);
+        o.y = pack_bf16x2(out[2], out[3]);
+        *reinterpret_cast<uint2*>(send + ((static_cast<int64_t>(p) * m + mm) * hl + j) * 128 + e0) = o;
+      }
+    }
   }
 }
 
@@ -759,7 +778,7 @@ int h3b_norm_rope_send(const void* x, int64_t m, int32_t heads, int64_t stride_m
     return fail(H3B_EINVAL, "norm_rope_send: null pointer");
   if (stride_m % 4 || stride_h % 4 || (reinterpret_cast<uintptr_t>(x) & 7u) || (reinterpret_cast<uintptr_t>(send) & 7u))
     return fail(H3B_EALIGN, "norm_rope_send: 8-byte granules needed");
-  const int64_t warps = m * heads;
+  const int64_t warps = m;  // a warp per token
   const int threads = 256;
   int64_t blocks = (warps * 32 + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
