@@ -321,10 +321,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                   tmem_ld32(hbase + cc, r);
                   tmem_ld_wait();
                   reg_fence(r);
+                  const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0 + cc);
 #pragma unroll
-                  for (int i = 0; i < 32; ++i) {
-                    const float y = rbf16(sam * (__ldg(p.sb + n0 + cc + i) * __uint_as_float(r[i])));
-                    ss = __fadd_rn(ss, __fmul_rn(y, y));
+                  for (int i4 = 0; i4 < 8; ++i4) {
+                    const float4 sv = __ldg(sb4 + i4);
+                    const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                      const float y = rbf16(sam * (s4[e] * __uint_as_float(r[4 * i4 + e])));
+                      ss = __fadd_rn(ss, __fmul_rn(y, y));
+                    }
                   }
                 }
                 const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), p.eps));
@@ -342,24 +348,42 @@ __global__ void __launch_bounds__(THREADS, 1)
                   tmem_ld_wait();
                   reg_fence16<0>(ra);
                   reg_fence16<0>(rb);
-                  float na[16], nb2[16];
+                  // 16 normalised values of columns [c, c + 16): bf16 GEMM output, * rsqrt, * weight, rounded to bf16
+                  auto normed = [&](const uint32_t (&rr)[16], int c, float (&nn)[16]) {
+                    const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0 + c);
+                    const uint4* w8 = reinterpret_cast<const uint4*>(wn + c);
 #pragma unroll
-                  for (int i = 0; i < 16; ++i) {
-                    const float y = rbf16(sam * (__ldg(p.sb + n0 + e0 + i) * __uint_as_float(ra[i])));
-                    na[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), __bfloat162float(wn[e0 + i])));
-                  }
-                  if (rotate) {
+                    for (int h8 = 0; h8 < 2; ++h8) {
+                      const uint4 wq = __ldg(w8 + h8);
+                      const uint32_t ww[4] = {wq.x, wq.y, wq.z, wq.w};
+                      const float4 s0 = __ldg(sb4 + 2 * h8), s1 = __ldg(sb4 + 2 * h8 + 1);
+                      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                      const float y = rbf16(sam * (__ldg(p.sb + n0 + e0 + half + i) * __uint_as_float(rb[i])));
-                      nb2[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), __bfloat162float(wn[e0 + half + i])));
+                      for (int e = 0; e < 8; ++e) {
+                        const int i = 8 * h8 + e;
+                        const float wf = __uint_as_float((e & 1) ? (ww[e >> 1] & 0xFFFF0000u) : (ww[e >> 1] << 16));
+                        const float y = rbf16(sam * (sv[e] * __uint_as_float(rr[i])));
+                        nn[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), wf));
+                      }
                     }
+                  };
+                  float na[16], nb2[16];
+                  normed(ra, e0, na);
+                  if (rotate) {
+                    normed(rb, e0 + half, nb2);
                     float oa[16], ob[16];
+                    const float4* cs4 = reinterpret_cast<const float4*>(trow + e0);
+                    const float4* sn4 = reinterpret_cast<const float4*>(trow + half + e0);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                      const float cs = __ldg(trow + e0 + i), sn = __ldg(trow + half + e0 + i);
-                      oa[i] = __fsub_rn(__fmul_rn(na[i], cs), __fmul_rn(nb2[i], sn));
-                      ob[i] = __fadd_rn(__fmul_rn(nb2[i], cs), __fmul_rn(na[i], sn));
+                    for (int i4 = 0; i4 < 4; ++i4) {
+                      const float4 cv = __ldg(cs4 + i4), sv = __ldg(sn4 + i4);
+                      const float c4[4] = {cv.x, cv.y, cv.z, cv.w}, s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                      for (int e = 0; e < 4; ++e) {
+                        const int i = 4 * i4 + e;
+                        oa[i] = __fsub_rn(__fmul_rn(na[i], c4[e]), __fmul_rn(nb2[i], s4[e]));
+                        ob[i] = __fadd_rn(__fmul_rn(nb2[i], c4[e]), __fmul_rn(na[i], s4[e]));
+                      }
                     }
                     if (row_ok) {
                       uint4* da = reinterpret_cast<uint4*>(dst + e0);
@@ -618,6 +642,9 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
       if (send->rot < 0 || send->rot > 128 || send->rot % 32)
         return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: rot %d (0, 32, 64, 96 or 128)", send->rot);
       if (send->rot > 0 && send->rope_table == nullptr) return fail(H3B_EINVAL, "fp8_gemm qkv_send: rope table");
+      if (((reinterpret_cast<uintptr_t>(send->q_norm_weight) | reinterpret_cast<uintptr_t>(send->k_norm_weight) |
+            reinterpret_cast<uintptr_t>(send->rope_table)) & 15u) || (send->rot > 0 && send->rope_stride % 4))
+        return fail(H3B_EALIGN, "fp8_gemm qkv_send: norm weights and rope table 16-byte aligned, rope_stride % 4 == 0");
       p.norm_w[0] = static_cast<const __nv_bfloat16*>(send->q_norm_weight);
       p.norm_w[1] = static_cast<const __nv_bfloat16*>(send->k_norm_weight);
       p.rope = send->rope_table;
