@@ -452,6 +452,14 @@ def device_status() -> int:
     return _lib.device_status()
 
 
+def set_wait_timeout_ns(ns: int) -> None:
+    """Bound of every device-side wait in the library (nanoseconds; default 4e9); a wait that runs out records
+    H3B_ETIMEOUT in the device status word and its kernel returns.  Bounds below 1 ms are refused."""
+    if ns <= 0:
+        raise ValueError("set_wait_timeout_ns: the bound must be positive")
+    _lib.call("h3b_set_wait_timeout_ns", int(ns))
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # torch.ops.h3b registrations (the op signatures the drop-in shims call)
 # ---------------------------------------------------------------------------------------------------------------

@@ -113,6 +113,16 @@ def test_check_raises_with_the_reason():
         _lib.check(rc, "h3b_quant_rows_e4m3")
 
 
+def test_wait_timeout_bounds():
+    """The device-wait bound is a host-side setting: below 1 ms the library refuses it, and the default is restored."""
+    from h3b import ops
+    with pytest.raises(ValueError):
+        ops.set_wait_timeout_ns(0)
+    with pytest.raises(_lib.H3BError, match="below 1 ms"):
+        ops.set_wait_timeout_ns(999_999)
+    ops.set_wait_timeout_ns(4_000_000_000)
+
+
 def test_qkv_send_struct_layout(tmp_path):
     """The ctypes mirror matches the C compiler's layout of h3b_qkv_send field by field."""
     fields = [f[0] for f in _lib.QkvSend._fields_]
