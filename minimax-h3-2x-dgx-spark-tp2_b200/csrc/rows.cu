@@ -445,22 +445,52 @@ __global__ void __launch_bounds__(THREADS) silu_mul_quant_kernel(const __nv_bflo
   }
 }
 
-// fp32 product -> bf16 gate/up (fp8_gemm epilogue arithmetic, then bf16 rounding) -> silu * up
+// fp32 product -> bf16 gate/up (fp8_gemm epilogue arithmetic, then bf16 rounding) -> silu * up.  VEC: sb (and bias)
+// are 16-byte aligned and read as vectors; otherwise element by element (same values, same arithmetic)
+template <bool VEC>
 __device__ __forceinline__ void swiglu8(const float* xr, int64_t half, int64_t c, float sa, const float* sb,
                                         const __nv_bfloat16* bias, float (&y)[8]) {
-  const float4 g0 = __ldg(reinterpret_cast<const float4*>(xr + c));
-  const float4 g1 = __ldg(reinterpret_cast<const float4*>(xr + c + 4));
-  const float4 u0 = __ldg(reinterpret_cast<const float4*>(xr + half + c));
-  const float4 u1 = __ldg(reinterpret_cast<const float4*>(xr + half + c + 4));
+  const float4 g0 = __ldcs(reinterpret_cast<const float4*>(xr + c));
+  const float4 g1 = __ldcs(reinterpret_cast<const float4*>(xr + c + 4));
+  const float4 u0 = __ldcs(reinterpret_cast<const float4*>(xr + half + c));
+  const float4 u1 = __ldcs(reinterpret_cast<const float4*>(xr + half + c + 4));
   const float ga[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
   const float ua[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  float sg[8], su[8], bg[8], bu[8];
+  if (VEC) {
+    const float4 a0 = __ldg(reinterpret_cast<const float4*>(sb + c));
+    const float4 a1 = __ldg(reinterpret_cast<const float4*>(sb + c + 4));
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(sb + half + c));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(sb + half + c + 4));
+    const float sgv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float suv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sg[e] = sgv[e];
+      su[e] = suv[e];
+    }
+    if (bias != nullptr) {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(bias + c)), bg);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(bias + half + c)), bu);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sg[e] = __ldg(sb + c + e);
+      su[e] = __ldg(sb + half + c + e);
+      if (bias != nullptr) {
+        bg[e] = __bfloat162float(bias[c + e]);
+        bu[e] = __bfloat162float(bias[half + c + e]);
+      }
+    }
+  }
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    float g = __ldg(sb + c + e) * ga[e];
-    float u = __ldg(sb + half + c + e) * ua[e];
+    float g = sg[e] * ga[e];
+    float u = su[e] * ua[e];
     if (bias != nullptr) {
-      g = fmaf(sa, g, __bfloat162float(bias[c + e]));
-      u = fmaf(sa, u, __bfloat162float(bias[half + c + e]));
+      g = fmaf(sa, g, bg[e]);
+      u = fmaf(sa, u, bu[e]);
     } else {
       g = sa * g;
       u = sa * u;
@@ -469,7 +499,7 @@ __device__ __forceinline__ void swiglu8(const float* xr, int64_t half, int64_t c
   }
 }
 
-template <int THREADS, int VPT>
+template <int THREADS, int VPT, bool VEC>
 __global__ void __launch_bounds__(THREADS) scale_swiglu_quant_kernel(const float* __restrict__ x,
                                                                      const float* __restrict__ sa,
                                                                      const float* __restrict__ sb,
@@ -488,7 +518,7 @@ __global__ void __launch_bounds__(THREADS) scale_swiglu_quant_kernel(const float
       h[k] = make_uint4(0, 0, 0, 0);
       if (i < nvec) {
         float y[8];
-        swiglu8(x + row * 2 * half, half, i * 8, sar, sb, bias, y);
+        swiglu8<VEC>(x + row * 2 * half, half, i * 8, sar, sb, bias, y);
         h[k] = pack8(y);
         m2 = absmax8(h[k], m2);
       }
@@ -497,6 +527,7 @@ __global__ void __launch_bounds__(THREADS) scale_swiglu_quant_kernel(const float
   }
 }
 
+template <bool VEC>
 __global__ void scale_swiglu_kernel(const float* __restrict__ x, const float* __restrict__ sa,
                                     const float* __restrict__ sb, const __nv_bfloat16* __restrict__ bias, int64_t M,
                                     int64_t half, __nv_bfloat16* __restrict__ y) {
@@ -506,7 +537,7 @@ __global__ void scale_swiglu_kernel(const float* __restrict__ x, const float* __
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = t / nvec, i = t - row * nvec;
     float o[8];
-    swiglu8(x + row * 2 * half, half, i * 8, sa[row], sb, bias, o);
+    swiglu8<VEC>(x + row * 2 * half, half, i * 8, sa[row], sb, bias, o);
     *reinterpret_cast<uint4*>(y + row * half + i * 8) = pack8(o);
   }
 }
@@ -526,6 +557,45 @@ __global__ void scale_bias_cast_kernel(const float* __restrict__ x, const float*
       reinterpret_cast<__nv_bfloat16*>(y)[t] = __float2bfloat16_rn(v);
     else
       reinterpret_cast<__half*>(y)[t] = __float2half_rn(v);
+  }
+}
+
+// the same arithmetic 8 columns at a time: x read as two streaming 16-byte loads, sb and bias as 16-byte loads,
+// y written as one 16-byte store (N % 8 == 0, every pointer 16-byte aligned)
+template <bool BF16_OUT>
+__global__ void scale_bias_cast_vec_kernel(const float* __restrict__ x, const float* __restrict__ sa,
+                                           const float* __restrict__ sb, const __nv_bfloat16* __restrict__ bias,
+                                           void* __restrict__ y, int64_t M, int64_t nvec) {
+  const int64_t total = M * nvec;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = t / nvec, i = t - row * nvec;
+    const float4 x0 = __ldcs(reinterpret_cast<const float4*>(x) + 2 * t);
+    const float4 x1 = __ldcs(reinterpret_cast<const float4*>(x) + 2 * t + 1);
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(sb) + 2 * i);
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(sb) + 2 * i + 1);
+    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float sar = __ldg(sa + row);
+    float bb[8];
+    if (bias != nullptr) unpack8(__ldg(reinterpret_cast<const uint4*>(bias) + i), bb);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float tv = bv[e] * xv[e];
+      v[e] = bias != nullptr ? fmaf(sar, tv, bb[e]) : sar * tv;
+    }
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (BF16_OUT) {
+        w[k] = pack_bf16x2(v[2 * k], v[2 * k + 1]);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+        w[k] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    __stcs(reinterpret_cast<uint4*>(y) + t, make_uint4(w[0], w[1], w[2], w[3]));
   }
 }
 
@@ -865,7 +935,12 @@ int h3b_scale_bias_cast(const float* x, const float* sa, const float* sb, const 
   if (x == nullptr || sa == nullptr || sb == nullptr || y == nullptr) return fail(H3B_EINVAL, "scale_bias_cast: null pointer");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const auto* bb = static_cast<const __nv_bfloat16*>(bias);
-  if (out_dtype == H3B_OUT_BF16)
+  const bool vec = N % 8 == 0 && al16(x) && al16(sb) && al16(y) && (bias == nullptr || al16(bias));
+  if (vec && out_dtype == H3B_OUT_BF16)
+    scale_bias_cast_vec_kernel<true><<<grid_elems(M * (N / 8), 256), 256, 0, st>>>(x, sa, sb, bb, y, M, N / 8);
+  else if (vec)
+    scale_bias_cast_vec_kernel<false><<<grid_elems(M * (N / 8), 256), 256, 0, st>>>(x, sa, sb, bb, y, M, N / 8);
+  else if (out_dtype == H3B_OUT_BF16)
     scale_bias_cast_kernel<true><<<grid_elems(M * N, 256), 256, 0, st>>>(x, sa, sb, bb, y, M, N);
   else
     scale_bias_cast_kernel<false><<<grid_elems(M * N, 256), 256, 0, st>>>(x, sa, sb, bb, y, M, N);
@@ -880,8 +955,12 @@ int h3b_scale_swiglu(const float* x, const float* sa, const float* sb, const voi
   if (x == nullptr || sa == nullptr || sb == nullptr || y == nullptr) return fail(H3B_EINVAL, "scale_swiglu: null pointer");
   if (half % 8 || !al16(x) || !al16(y)) return fail(H3B_EALIGN, "scale_swiglu: half must be a multiple of 8, 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  scale_swiglu_kernel<<<grid_elems(M * (half / 8), 256), 256, 0, st>>>(
-      x, sa, sb, static_cast<const __nv_bfloat16*>(bias), M, half, static_cast<__nv_bfloat16*>(y));
+  const auto* bb = static_cast<const __nv_bfloat16*>(bias);
+  auto* yy = static_cast<__nv_bfloat16*>(y);
+  if (al16(sb) && (bias == nullptr || al16(bias)))
+    scale_swiglu_kernel<true><<<grid_elems(M * (half / 8), 256), 256, 0, st>>>(x, sa, sb, bb, M, half, yy);
+  else
+    scale_swiglu_kernel<false><<<grid_elems(M * (half / 8), 256), 256, 0, st>>>(x, sa, sb, bb, M, half, yy);
   H3B_CHECK_LAUNCH("scale_swiglu launch");
   return H3B_OK;
 }
@@ -899,9 +978,15 @@ int h3b_scale_swiglu_quant(const float* x, const float* sa, const float* sb, con
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const auto* bb = static_cast<const __nv_bfloat16*>(bias);
   auto* qq = static_cast<uint8_t*>(q);
-#define L(V) scale_swiglu_quant_kernel<256, V><<<grid_rows(M), 256, 0, st>>>(x, sa, sb, bb, M, half, qq, s, div_mode)
-  H3B_VPT_DISPATCH(nvec, L);
+  if (al16(sb) && (bias == nullptr || al16(bias))) {
+#define L(V) scale_swiglu_quant_kernel<256, V, true><<<grid_rows(M), 256, 0, st>>>(x, sa, sb, bb, M, half, qq, s, div_mode)
+    H3B_VPT_DISPATCH(nvec, L);
 #undef L
+  } else {
+#define L(V) scale_swiglu_quant_kernel<256, V, false><<<grid_rows(M), 256, 0, st>>>(x, sa, sb, bb, M, half, qq, s, div_mode)
+    H3B_VPT_DISPATCH(nvec, L);
+#undef L
+  }
   H3B_CHECK_LAUNCH("scale_swiglu_quant launch");
   return H3B_OK;
 }

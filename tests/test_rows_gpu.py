@@ -161,3 +161,35 @@ def test_scale_bias_cast(dev):
     y = ops.scale_bias_cast(x.to(dev), sa.to(dev), sb.to(dev), bias.to(dev), torch.float16).cpu()
     ref = og.epilogue(x, sa, sb, bias, torch.float16)
     assert (y.view(torch.int16) != ref.view(torch.int16)).float().mean().item() < 1e-3
+
+
+def test_scale_passes_vector_and_scalar_forms_agree(dev, golden):
+    """The launchers read sb / bias as 16-byte vectors when aligned and element by element otherwise; both forms give
+    the same bits (sb and bias passed at an odd element offset take the element-wise form)."""
+    g = golden("swiglu")
+    x32, sa, sb, bias = tf(g["x32"]).to(dev), tf(g["sa"]).to(dev), tf(g["sb"]).to(dev), t16(g["bias"]).to(dev)
+    sb_odd = torch.empty(sb.numel() + 1, device=dev)[1:]
+    sb_odd.copy_(sb)
+    b_odd = torch.empty(bias.numel() + 1, dtype=BF16, device=dev)[1:]
+    b_odd.copy_(bias)
+    assert sb_odd.data_ptr() % 16 and b_odd.data_ptr() % 16
+    for b, bo in ((None, None), (bias, b_odd)):
+        assert same_bits(ops.scale_swiglu(x32, sa, sb, b), ops.scale_swiglu(x32, sa, sb_odd, bo))
+    q1, s1 = ops.scale_swiglu_quant(x32, sa, sb, bias)
+    q2, s2 = ops.scale_swiglu_quant(x32, sa, sb_odd, b_odd)
+    assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2)
+
+
+@pytest.mark.parametrize("n", [403, 400])
+def test_scale_bias_cast_any_width(dev, n):
+    """N % 8 != 0 takes the element-wise kernel, N % 8 == 0 the vector one: both match the eager epilogue."""
+    g = torch.Generator().manual_seed(10)
+    x = torch.randn(65, n, generator=g) * 100
+    sa, sb = torch.rand(65, generator=g) * 1e-2, torch.rand(n, generator=g) * 1e-2
+    bias = (torch.randn(n, generator=g) * 0.1).to(BF16)
+    y = ops.scale_bias_cast(x.to(dev), sa.to(dev), sb.to(dev), None, BF16).cpu()
+    assert same_bits(y, og.epilogue(x, sa, sb, None, BF16))
+    # with a bias the oracle adds in double and rounds twice, the kernel rounds one fma: rare last-bit differences
+    y = ops.scale_bias_cast(x.to(dev), sa.to(dev), sb.to(dev), bias.to(dev), BF16).cpu()
+    ref = og.epilogue(x, sa, sb, bias, BF16)
+    assert (y.view(torch.int16) != ref.view(torch.int16)).float().mean().item() < 1e-3
