@@ -3,38 +3,43 @@
 // (h3_tp2/fp8_gemm.py:38-54) and of the CuTe-DSL kernel's epilogue (h3_tp2/fp8_cutlass_kernel.py), with no fp32
 // product in memory.
 //
-// Design (one CTA per SM, persistent over output tiles):
-//   tile 128 x 256 (M x N), K step 128 (one 128-byte swizzle row of e4m3), 4-stage TMA ring (48 KB per stage).
-//   warp 0      : TMA producer (one elected thread), A box 128x128 B and two B boxes 128x128 B per stage
-//   warp 1      : TMEM allocator + single-thread tcgen05.mma issuer (kind::f8f6f4, M=128 N=256 K=32)
-//   warps 2..5  : epilogue; thread t of the 128 owns accumulator row t (TMEM lane), reads 32-column slices with
-//                 tcgen05.ld, applies the scales and stores bf16/f16 (or scatters into the Ulysses send layout, or
-//                 applies SwiGLU to the gate/up halves).
+// Design (CTA pairs: clusters of two CTAs on two SMs, persistent over 256 x 256 output tiles):
+//   The pair computes a 256 x 256 tile with 2-SM MMAs (tcgen05.mma.cta_group::2, M = 256, N = 256, K = 32): CTA r
+//   of the pair holds rows [128 r, 128 r + 128) of the A tile and columns [128 r, 128 r + 128) of the B tile in its
+//   shared memory, and rows [128 r, 128 r + 128) x all 256 columns of the accumulator in its TMEM.  Each SM thus
+//   stages 32 KB per 128-deep K step instead of the 48 KB a one-CTA 128 x 256 tile needs for the same MMA work, and
+//   the 6-stage ring (192 KB) covers 1.5x the L2 latency of the one-CTA ring.
+//   warp 0      : TMA producer (one elected thread per CTA): A box 128x128 B and one B box 128x128 B per stage, both
+//                 counted on the even (leader) CTA's full barrier, which expects the pair's 64 KB
+//   warp 1      : TMEM allocator of the pair; in the leader, the single-thread tcgen05.mma issuer, whose commits
+//                 arrive on both CTAs' barriers
+//   warps 2..5  : epilogue; thread t of the 128 owns accumulator row t of its CTA (TMEM lane), reads 32-column
+//                 slices with tcgen05.ld, applies the scales and stores bf16/f16 (or scatters into the Ulysses send
+//                 layout, or applies SwiGLU to the gate/up halves); each warp then arrives on the leader's
+//                 accumulator-empty barrier (8 arrivals per tile, 4 of them from the other CTA).
 //   The accumulator is double buffered in TMEM (2 x 256 of the 512 columns) so the epilogue of tile i overlaps the
-//   main loop of tile i+1.  Every wait is bounded (common.cuh).  No TMA multicast, no clusters.
+//   main loop of tile i+1.  Every wait is bounded (common.cuh).  No TMA multicast.
 #include "common.cuh"
 
 namespace h3b {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 6;  // BM: rows per CTA (the pair's tile is 2 x BM rows)
 constexpr int A_BYTES = BM * BK;   // 16 KB
-constexpr int B_BYTES = BN * BK;   // 32 KB (two 128-row boxes)
+constexpr int B_BYTES = 128 * BK;  // 16 KB: this CTA's half of the 256 B rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
-constexpr int GROUP_M = 16;
+constexpr int GROUP_M = 8;   // pair row blocks (256 rows each) sharing one column block's W tile in L2
 constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
-// peer-store staging: per epilogue warp 32 rows x 128 B (64 columns), so the stores to another GPU leave as whole
-// 128-byte lines instead of 16-byte pieces of 32 different rows
-// (only the PEER instantiation of the kernel has it; the other keeps its registers and shared memory as without)
-constexpr int STAGING_BYTES = 4 * 32 * 128;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr int SMEM_BYTES_PEER = SMEM_BYTES + STAGING_BYTES;
-constexpr uint32_t IDESC = idesc_make(FMT_E4M3, FMT_E4M3, 0, BM, BN);
+// epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows)
+constexpr int STAGING_BYTES = 4 * 32 * 256;
+// ring, alignment slack, barriers, staging (230,656 B of the 232,448 a CTA may have)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + STAGING_BYTES;
+constexpr uint32_t IDESC = idesc_make(FMT_E4M3, FMT_E4M3, 0, 2 * BM, BN);
 
 struct Params {
   int64_t M, N, K;
-  int num_mb, num_nb, num_kb;
+  int num_mb, num_nb, num_kb;  // num_mb: 256-row blocks of the CTA pairs
   const float* sa;
   const float* sb;
   const __nv_bfloat16* bias;
@@ -82,6 +87,7 @@ __device__ __forceinline__ uint16_t* send_slab(const Params& p, int which, int g
 
 __device__ __forceinline__ float rbf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// pair tile t -> (256-row block, column block): GROUP_M row blocks in a row share each column block's W tile in L2
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& mb, int& nb) {
   const int in_group = GROUP_M * p.num_nb;
   const int group = t / in_group;
@@ -116,9 +122,8 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
   return s * u;
 }
 
-// PEER: the QKV_SEND epilogue stores into other GPUs' receive buffers (Params::p2p set)
-template <bool PEER>
-__global__ void __launch_bounds__(THREADS, 1)
+// With Params::p2p the QKV_SEND epilogue stores into the other GPUs' receive buffers (send_slab).
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -136,8 +141,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();  // 0: the pair's leader (issues the MMAs), 1: its partner
+  const uint32_t peer = crank ^ 1u;
   const bool aborted_at_entry = status_bad(p.wc);
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
@@ -145,7 +151,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 128);
+      mbar_init(tempty_bar(a), 8);  // one arrival per epilogue warp of both CTAs (counted on the leader's)
     }
     mbar_init(done_bar, 1);
     fence_mbar_init();
@@ -153,28 +159,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = p.num_mb * p.num_nb;
+  const int first_tile = static_cast<int>(cluster_id_x());
+  const int tile_step = static_cast<int>(cluster_count_x());
   if (!aborted_at_entry) {
     if (warp == 0) {
       if (lane == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (both CTAs; stage completion counted on the leader's full barrier) -------
+        const uint32_t lead_full0 = mapa_shared(full_bar(0), 0);
         int stage = 0;
         uint32_t phase = 0;
-        int issued[STAGES] = {0, 0, 0, 0};
+        int issued[STAGES];
+        for (int s = 0; s < STAGES; ++s) issued[s] = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        for (int t = first_tile; t < num_tiles && ok; t += tile_step) {
           int mb, nb;
           tile_coords(t, p, mb, nb);
-          const int n0 = p.epi == H3B_EPI_SWIGLU ? nb * 128 : nb * BN;
-          const int n1 = p.epi == H3B_EPI_SWIGLU ? static_cast<int>(p.half) + nb * 128 : nb * BN + 128;
+          const int arow = (2 * mb + static_cast<int>(crank)) * BM;
+          // this CTA's 128 B rows: SWIGLU gate rows (leader) / up rows (partner); else columns [256 nb + 128 r, +128)
+          const int brow = p.epi == H3B_EPI_SWIGLU ? (crank ? static_cast<int>(p.half) : 0) + nb * 128
+                                                   : nb * BN + 128 * static_cast<int>(crank);
           for (int kb = 0; kb < p.num_kb; ++kb) {
             if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.wc)) {
               ok = false;
@@ -182,10 +194,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             const uint32_t sA = smem0 + stage * STAGE_BYTES;
             const uint32_t sB = sA + A_BYTES;
-            mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
-            tma_load_2d(sA, &tmA, full_bar(stage), kb * BK, mb * BM);
-            tma_load_2d(sB, &tmB, full_bar(stage), kb * BK, n0);
-            tma_load_2d(sB + 16384, &tmB, full_bar(stage), kb * BK, n1);
+            const uint32_t fb = lead_full0 + 8u * stage;
+            if (crank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+            tma_load_2d_pair(sA, &tmA, fb, kb * BK, arow);
+            tma_load_2d_pair(sB, &tmB, fb, kb * BK, brow);
             issued[stage]++;
             if (++stage == STAGES) {
               stage = 0;
@@ -193,24 +205,28 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
-        // drain: never leave a TMA write in flight into shared memory the CTA is about to release
+        // drain: never leave a TMA write in flight into shared memory the CTA is about to release.  The leader
+        // sees both CTAs' bytes on its full barriers; the partner's last load of a stage has landed once the
+        // leader's MMAs consumed it (its empty barrier).
         for (int s = 0; s < STAGES; ++s)
           if (issued[s] > 0) {
             const uint32_t par = static_cast<uint32_t>(issued[s] - 1) & 1u;
+            const uint32_t bar = crank == 0 ? full_bar(s) : empty_bar(s);
             const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(full_bar(s), par) && globaltimer() - t0 < p.wc.timeout) {
+            while (!mbar_try_wait(bar, par) && globaltimer() - t0 < p.wc.timeout) {
             }
           }
       }
     } else if (warp == 1) {
-      if (lane == 0) {
-        // ---------------- MMA issuer ----------------
+      if (lane == 0 && crank == 0) {
+        // ---------------- MMA issuer (the leader only) ----------------
+        const uint32_t peer_bar0 = mapa_shared(bar0, peer);  // the partner's barrier array
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        for (int t = first_tile; t < num_tiles && ok; t += tile_step) {
           if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.wc)) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -226,39 +242,69 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t bdesc = sdesc_sw128(sB, 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < BK / 32; ++kk)
-              umma_f8_ss(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | kk) != 0);
-            umma_commit(empty_bar(stage));
+              umma_f8_ss_pair(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | kk) != 0);
+            umma_commit_pair(empty_bar(stage));
+            umma_commit_pair(peer_bar0 + 8u * (STAGES + stage));
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1u;
             }
           }
           if (!ok) break;
-          umma_commit(tfull_bar(acc));
+          umma_commit_pair(tfull_bar(acc));
+          umma_commit_pair(peer_bar0 + 8u * (2 * STAGES + acc));
           if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
           }
         }
         // all issued MMAs complete before TMEM is released
-        umma_commit(done_bar);
+        umma_commit_pair(done_bar);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(done_bar, 0) && globaltimer() - t0 < p.wc.timeout) {
         }
       }
     } else {
       // ---------------- epilogue (warps 2..5) ----------------
+      // Each warp turns its 32 accumulator rows into output 128 columns at a time: the values go through shared
+      // memory (32 rows x 256 B per warp; 16-byte granule g of row r at r * 16 + (g ^ (r & 15))), and every store
+      // instruction then writes two whole 256-byte rows (four full lines) instead of 16 bytes of 32 different rows,
+      // which keeps the load/store path free for the TMA fills of the main loop.
       const int sub = warp & 3;
       const int row_in_tile = sub * 32 + lane;
       const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
+      uint4* stg = staging + sub * 32 * 16;
+      auto stage = [&](int g, uint4 val) { stg[lane * 16 + (g ^ (lane & 15))] = val; };
+      // the warp's rows m0 + r (r < 32) of one 128-column block: row r to base + (m0 + r) * rstride, granules
+      // below `granules`
+      auto store_rows = [&](uint16_t* base, int64_t rstride, int64_t m0, int granules) {
+        __syncwarp();
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int r = 2 * it + (lane >> 4), g = lane & 15;
+          if (m0 + r < p.M && g < granules)
+            *reinterpret_cast<uint4*>(base + (m0 + r) * rstride + g * 8) = stg[r * 16 + (g ^ (r & 15))];
+        }
+        __syncwarp();
+      };
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const uint32_t lead_tempty0 = mapa_shared(tempty_bar(0), 0);
+      // one arrival per warp on the leader's accumulator-empty barrier once this warp's TMEM reads of the tile are
+      // complete (tcgen05.wait::ld is warp-wide); the stores of the last block follow it
+      auto release_acc = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_tempty0 + 8u * acc);
+      };
+      for (int t = first_tile; t < num_tiles; t += tile_step) {
         int mb, nb;
         tile_coords(t, p, mb, nb);
+        mb = 2 * mb + static_cast<int>(crank);  // this CTA's 128-row block
         if (!mbar_wait(tfull_bar(acc), acc_phase, p.wc)) break;
         tc_fence_after();
         const int64_t m = static_cast<int64_t>(mb) * BM + row_in_tile;
+        const int64_t m0 = static_cast<int64_t>(mb) * BM + sub * 32;  // the warp's first row
         const bool row_ok = m < p.M;
         const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
         const uint32_t tacc = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN);
@@ -276,10 +322,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
               float gv[2], uv[2];
+              // column scales of the gate and up halves, two at a time (ng and nu are multiples of 32)
+              const float2 sg = __ldg(reinterpret_cast<const float2*>(p.sb + ng + i));
+              const float2 su = __ldg(reinterpret_cast<const float2*>(p.sb + nu + i));
+              const float sgv[2] = {sg.x, sg.y}, suv[2] = {su.x, su.y};
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const float tg = __ldg(p.sb + ng + i + e) * __uint_as_float(g[i + e]);
-                const float tu = __ldg(p.sb + nu + i + e) * __uint_as_float(u[i + e]);
+                const float tg = sgv[e] * __uint_as_float(g[i + e]);
+                const float tu = suv[e] * __uint_as_float(u[i + e]);
                 if (p.bias != nullptr) {
                   gv[e] = fmaf(sam, tg, __bfloat162float(p.bias[ng + i + e]));
                   uv[e] = fmaf(sam, tu, __bfloat162float(p.bias[nu + i + e]));
@@ -290,257 +340,218 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
               o[i / 2] = pack2(silu_mul_bf16(gv[0], uv[0]), silu_mul_bf16(gv[1], uv[1]), 0);
             }
-            if (row_ok) {
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + ng);
 #pragma unroll
-              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
-            }
+            for (int v = 0; v < 4; ++v) stage(c0 / 8 + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
           }
+          release_acc();
+          store_rows(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(nb) * 128, p.ldy, m0, 16);
         } else {
-          for (int c0 = 0; c0 < BN; c0 += 32) {
-            const int64_t n0 = static_cast<int64_t>(nb) * BN + c0;
-            if (n0 >= p.N) break;  // warp-uniform
-            if (p.epi == H3B_EPI_QKV_SEND && p.norm_w[0] != nullptr && n0 < 2ll * p.hd) {
-              // q or k head with RMSNorm + partial RoPE: handled a whole head (128 columns) at a time
-              if ((c0 & 127) == 0) {
-                const int which = static_cast<int>(n0 / p.hd);
-                const int hcol = static_cast<int>(n0 - static_cast<int64_t>(which) * p.hd);
-                const int h = hcol >> 7;
-                const int g = h / p.hg, hh = h - g * p.hg;
-                const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
-                int64_t seg;
-                uint16_t* dst = send_slab(p, which, g, dst_rank, seg);
-                dst += ((seg * p.M + m) * p.rsh + j) * 128;
-                const __nv_bfloat16* wn = p.norm_w[which];
-                const uint32_t hbase = tacc + c0;
-                // pass 1: the bf16 head values (the GEMM output the reference normalises) and their sum of squares
-                float ss = 0.0f;
+          for (int b0 = 0; b0 < BN; b0 += 128) {
+            const int64_t nbk = static_cast<int64_t>(nb) * BN + b0;  // first column of the block
+            const bool last_block = b0 + 128 >= BN || nbk + 128 >= p.N;
+            if (nbk >= p.N) break;  // warp-uniform
+            // QKV_SEND: the block is one head of q, k or v; its destination rows are 256 B apart from the slab base
+            int which = 0, dst_rank = 0, j = 0;
+            uint16_t* qbase = nullptr;
+            int64_t qstride = 0;
+            if (p.epi == H3B_EPI_QKV_SEND) {
+              which = static_cast<int>(nbk / p.hd);
+              const int h = static_cast<int>(nbk - static_cast<int64_t>(which) * p.hd) >> 7;
+              const int g = h / p.hg, hh = h - g * p.hg;
+              dst_rank = hh / p.hl;
+              j = hh - dst_rank * p.hl;
+              int64_t seg;
+              uint16_t* slab = send_slab(p, which, g, dst_rank, seg);
+              qbase = slab + (seg * p.M * p.rsh + j) * 128;
+              qstride = static_cast<int64_t>(p.rsh) * 128;
+            }
+            if (p.epi == H3B_EPI_QKV_SEND && p.norm_w[0] != nullptr && which < 2) {
+              // q or k head with RMSNorm + partial RoPE, stored row by row: its arithmetic, not its stores, bounds
+              // this epilogue (staging measured 3 % slower here)
+              const __nv_bfloat16* wn = p.norm_w[which];
+              uint16_t* dst = qbase + m * qstride;
+              const uint32_t hbase = tacc + b0;
+              // pass 1: the bf16 head values (the GEMM output the reference normalises) and their sum of squares
+              float ss = 0.0f;
 #pragma unroll 1
-                for (int cc = 0; cc < 128; cc += 32) {
-                  uint32_t r[32];
-                  tmem_ld32(hbase + cc, r);
-                  tmem_ld_wait();
-                  reg_fence(r);
-                  const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0 + cc);
+              for (int cc = 0; cc < 128; cc += 32) {
+                uint32_t r[32];
+                tmem_ld32(hbase + cc, r);
+                tmem_ld_wait();
+                reg_fence(r);
+                const float4* sb4 = reinterpret_cast<const float4*>(p.sb + nbk + cc);
 #pragma unroll
-                  for (int i4 = 0; i4 < 8; ++i4) {
-                    const float4 sv = __ldg(sb4 + i4);
-                    const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+                for (int i4 = 0; i4 < 8; ++i4) {
+                  const float4 sv = __ldg(sb4 + i4);
+                  const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float y = rbf16(sam * (s4[e] * __uint_as_float(r[4 * i4 + e])));
+                    ss = __fadd_rn(ss, __fmul_rn(y, y));
+                  }
+                }
+              }
+              const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), p.eps));
+              const int half = p.rot >> 1;
+              const float* trow = p.rope + (row_ok ? m : 0) * p.rope_stride;  // rows past M read row 0
+              // pass 2: 16-column blocks; block b < half/16 rotates with block b + half/16
+#pragma unroll 1
+              for (int b = 0; b < 8; ++b) {
+                const int e0 = 16 * b;
+                if (e0 >= half && e0 < p.rot) continue;  // written with its partner below
+                uint32_t ra[16], rb[16];
+                tmem_ld16(hbase + e0, ra);
+                const bool rotate = e0 < half;
+                if (rotate) tmem_ld16(hbase + e0 + half, rb);
+                tmem_ld_wait();
+                reg_fence16<0>(ra);
+                reg_fence16<0>(rb);
+                // 16 normalised values of columns [c, c + 16): bf16 GEMM output, * rsqrt, * weight, rounded to bf16
+                auto normed = [&](const uint32_t (&rr)[16], int c, float (&nn)[16]) {
+                  const float4* sb4 = reinterpret_cast<const float4*>(p.sb + nbk + c);
+                  const uint4* w8 = reinterpret_cast<const uint4*>(wn + c);
+#pragma unroll
+                  for (int h8 = 0; h8 < 2; ++h8) {
+                    const uint4 wq = __ldg(w8 + h8);
+                    const uint32_t ww[4] = {wq.x, wq.y, wq.z, wq.w};
+                    const float4 s0 = __ldg(sb4 + 2 * h8), s1 = __ldg(sb4 + 2 * h8 + 1);
+                    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                      const int i = 8 * h8 + e;
+                      const float wf = __uint_as_float((e & 1) ? (ww[e >> 1] & 0xFFFF0000u) : (ww[e >> 1] << 16));
+                      const float y = rbf16(sam * (sv[e] * __uint_as_float(rr[i])));
+                      nn[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), wf));
+                    }
+                  }
+                };
+                float na[16], nb2[16];
+                normed(ra, e0, na);
+                if (rotate) {
+                  normed(rb, e0 + half, nb2);
+                  float oa[16], ob[16];
+                  const float4* cs4 = reinterpret_cast<const float4*>(trow + e0);
+                  const float4* sn4 = reinterpret_cast<const float4*>(trow + half + e0);
+#pragma unroll
+                  for (int i4 = 0; i4 < 4; ++i4) {
+                    const float4 cv = __ldg(cs4 + i4), sv = __ldg(sn4 + i4);
+                    const float c4[4] = {cv.x, cv.y, cv.z, cv.w}, s4[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                      const float y = rbf16(sam * (s4[e] * __uint_as_float(r[4 * i4 + e])));
-                      ss = __fadd_rn(ss, __fmul_rn(y, y));
+                      const int i = 4 * i4 + e;
+                      oa[i] = __fsub_rn(__fmul_rn(na[i], c4[e]), __fmul_rn(nb2[i], s4[e]));
+                      ob[i] = __fadd_rn(__fmul_rn(nb2[i], c4[e]), __fmul_rn(na[i], s4[e]));
                     }
                   }
-                }
-                const float inv = rsqrtf(__fadd_rn(ss * (1.0f / 128.0f), p.eps));
-                const int half = p.rot >> 1;
-                const float* trow = p.rope + (row_ok ? m : 0) * p.rope_stride;  // rows past M read row 0
-                // pass 2: 16-column blocks; block b < half/16 rotates with block b + half/16
-#pragma unroll 1
-                for (int b = 0; b < 8; ++b) {
-                  const int e0 = 16 * b;
-                  if (e0 >= half && e0 < p.rot) continue;  // written with its partner below
-                  uint32_t ra[16], rb[16];
-                  tmem_ld16(hbase + e0, ra);
-                  const bool rotate = e0 < half;
-                  if (rotate) tmem_ld16(hbase + e0 + half, rb);
-                  tmem_ld_wait();
-                  reg_fence16<0>(ra);
-                  reg_fence16<0>(rb);
-                  // 16 normalised values of columns [c, c + 16): bf16 GEMM output, * rsqrt, * weight, rounded to bf16
-                  auto normed = [&](const uint32_t (&rr)[16], int c, float (&nn)[16]) {
-                    const float4* sb4 = reinterpret_cast<const float4*>(p.sb + n0 + c);
-                    const uint4* w8 = reinterpret_cast<const uint4*>(wn + c);
-#pragma unroll
-                    for (int h8 = 0; h8 < 2; ++h8) {
-                      const uint4 wq = __ldg(w8 + h8);
-                      const uint32_t ww[4] = {wq.x, wq.y, wq.z, wq.w};
-                      const float4 s0 = __ldg(sb4 + 2 * h8), s1 = __ldg(sb4 + 2 * h8 + 1);
-                      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-                      for (int e = 0; e < 8; ++e) {
-                        const int i = 8 * h8 + e;
-                        const float wf = __uint_as_float((e & 1) ? (ww[e >> 1] & 0xFFFF0000u) : (ww[e >> 1] << 16));
-                        const float y = rbf16(sam * (sv[e] * __uint_as_float(rr[i])));
-                        nn[i] = rbf16(__fmul_rn(__fmul_rn(y, inv), wf));
-                      }
-                    }
-                  };
-                  float na[16], nb2[16];
-                  normed(ra, e0, na);
-                  if (rotate) {
-                    normed(rb, e0 + half, nb2);
-                    float oa[16], ob[16];
-                    const float4* cs4 = reinterpret_cast<const float4*>(trow + e0);
-                    const float4* sn4 = reinterpret_cast<const float4*>(trow + half + e0);
-#pragma unroll
-                    for (int i4 = 0; i4 < 4; ++i4) {
-                      const float4 cv = __ldg(cs4 + i4), sv = __ldg(sn4 + i4);
-                      const float c4[4] = {cv.x, cv.y, cv.z, cv.w}, s4[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-                      for (int e = 0; e < 4; ++e) {
-                        const int i = 4 * i4 + e;
-                        oa[i] = __fsub_rn(__fmul_rn(na[i], c4[e]), __fmul_rn(nb2[i], s4[e]));
-                        ob[i] = __fadd_rn(__fmul_rn(nb2[i], c4[e]), __fmul_rn(na[i], s4[e]));
-                      }
-                    }
-                    if (row_ok) {
-                      uint4* da = reinterpret_cast<uint4*>(dst + e0);
-                      uint4* db = reinterpret_cast<uint4*>(dst + e0 + half);
-#pragma unroll
-                      for (int q = 0; q < 2; ++q) {
-                        da[q] = make_uint4(pack2(oa[8 * q], oa[8 * q + 1], 0), pack2(oa[8 * q + 2], oa[8 * q + 3], 0),
-                                           pack2(oa[8 * q + 4], oa[8 * q + 5], 0), pack2(oa[8 * q + 6], oa[8 * q + 7], 0));
-                        db[q] = make_uint4(pack2(ob[8 * q], ob[8 * q + 1], 0), pack2(ob[8 * q + 2], ob[8 * q + 3], 0),
-                                           pack2(ob[8 * q + 4], ob[8 * q + 5], 0), pack2(ob[8 * q + 6], ob[8 * q + 7], 0));
-                      }
-                    }
-                  } else if (row_ok) {
+                  if (row_ok) {
                     uint4* da = reinterpret_cast<uint4*>(dst + e0);
+                    uint4* db = reinterpret_cast<uint4*>(dst + e0 + half);
 #pragma unroll
-                    for (int q = 0; q < 2; ++q)
-                      da[q] = make_uint4(pack2(na[8 * q], na[8 * q + 1], 0), pack2(na[8 * q + 2], na[8 * q + 3], 0),
-                                         pack2(na[8 * q + 4], na[8 * q + 5], 0), pack2(na[8 * q + 6], na[8 * q + 7], 0));
+                    for (int q = 0; q < 2; ++q) {
+                      da[q] = make_uint4(pack2(oa[8 * q], oa[8 * q + 1], 0), pack2(oa[8 * q + 2], oa[8 * q + 3], 0),
+                                         pack2(oa[8 * q + 4], oa[8 * q + 5], 0), pack2(oa[8 * q + 6], oa[8 * q + 7], 0));
+                      db[q] = make_uint4(pack2(ob[8 * q], ob[8 * q + 1], 0), pack2(ob[8 * q + 2], ob[8 * q + 3], 0),
+                                         pack2(ob[8 * q + 4], ob[8 * q + 5], 0), pack2(ob[8 * q + 6], ob[8 * q + 7], 0));
+                    }
                   }
+                } else if (row_ok) {
+                  uint4* da = reinterpret_cast<uint4*>(dst + e0);
+#pragma unroll
+                  for (int q = 0; q < 2; ++q)
+                    da[q] = make_uint4(pack2(na[8 * q], na[8 * q + 1], 0), pack2(na[8 * q + 2], na[8 * q + 3], 0),
+                                       pack2(na[8 * q + 4], na[8 * q + 5], 0), pack2(na[8 * q + 6], na[8 * q + 7], 0));
                 }
               }
+              if (last_block) release_acc();
               continue;
             }
-            uint32_t r[32];
-            tmem_ld32(tacc + c0, r);
-            tmem_ld_wait();
-            reg_fence(r);
-            float v[32];
+            // scaled accumulator of the block, 32 columns at a time, staged as the output's 16-bit values
+            const bool as_f16 = p.epi == H3B_EPI_QKV_SEND && which == 2 && p.v_f16;
+            int32_t* rf = p.epi == H3B_EPI_QKV_SEND ? (p.p2p ? p.peer_rf[dst_rank] : p.range_flag) : nullptr;
+            for (int c = 0; c < 128; c += 32) {
+              const int64_t n0 = nbk + c;
+              if (n0 >= p.N) break;  // warp-uniform
+              uint32_t r[32];
+              tmem_ld32(tacc + b0 + c, r);
+              tmem_ld_wait();
+              reg_fence(r);
+              float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              float4 sbv = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (n0 + i < p.N) sbv = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + i));
-              const float s4[4] = {sbv.x, sbv.y, sbv.z, sbv.w};
+              for (int i = 0; i < 32; i += 4) {
+                float4 sbv = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (n0 + i < p.N) sbv = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + i));
+                const float s4[4] = {sbv.x, sbv.y, sbv.z, sbv.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float tv = s4[e] * __uint_as_float(r[i + e]);
-                if (p.bias != nullptr && n0 + i + e < p.N)
-                  v[i + e] = fmaf(sam, tv, __bfloat162float(p.bias[n0 + i + e]));
-                else
-                  v[i + e] = sam * tv;
+                for (int e = 0; e < 4; ++e) {
+                  const float tv = s4[e] * __uint_as_float(r[i + e]);
+                  if (p.bias != nullptr && n0 + i + e < p.N)
+                    v[i + e] = fmaf(sam, tv, __bfloat162float(p.bias[n0 + i + e]));
+                  else
+                    v[i + e] = sam * tv;
+                }
               }
-            }
-            if (PEER && p.epi == H3B_EPI_QKV_SEND) {
-              // peer stores (warp-uniform branch): the warp's 32 rows of this 64-column block go through shared
-              // memory and leave as 4 rows x 128 B per store instruction
-              const int which = static_cast<int>(n0 / p.hd);
-              const int hcol = static_cast<int>(n0 - static_cast<int64_t>(which) * p.hd);
-              const int h = hcol >> 7, c = hcol & 127;
-              const int dst_rank = h / p.hl, j = h - dst_rank * p.hl;
-              const bool as_f16 = which == 2 && p.v_f16;
-              int32_t* rf = p.peer_rf[dst_rank];
               if (row_ok && as_f16 && rf != nullptr) {
                 bool bad = false;
 #pragma unroll
                 for (int i = 0; i < 32; ++i) bad |= fabsf(v[i]) > 65504.0f && isfinite(v[i]);
                 if (bad) atomicExch(rf, 1);
               }
-              uint4* srow = staging + (sub * 32 + lane) * 8;
-              const int hb = (c >> 5) & 1;  // which 32-column half of the 64-column block
+              const int f16 = p.epi == H3B_EPI_PLAIN ? p.out_f16 : 0;
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
                   w[e] = as_f16 ? pack2_bf16_as_f16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1])
-                                : pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], 0);
-                srow[(hb * 4 + q) ^ (lane & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
+                                : pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], f16);
+                stage(c / 8 + q, make_uint4(w[0], w[1], w[2], w[3]));
               }
-              if (hb == 1) {
-                __syncwarp();
-                const int64_t m0 = static_cast<int64_t>(mb) * BM + sub * 32;
-                uint16_t* base = static_cast<uint16_t*>(p.peer[dst_rank][which]) +
-                                 ((static_cast<int64_t>(p.rank) * p.M + m0) * p.hl + j) * 128 + (c & 64);
-#pragma unroll
-                for (int it = 0; it < 8; ++it) {
-                  const int idx = it * 32 + lane, r = idx >> 3, part = idx & 7;
-                  if (m0 + r < p.M)
-                    *reinterpret_cast<uint4*>(base + static_cast<int64_t>(r) * p.hl * 128 + part * 8) =
-                        staging[(sub * 32 + r) * 8 + (part ^ (r & 7))];
-                }
-                __syncwarp();
-              }
-              continue;
             }
-            if (!row_ok) continue;
+            if (last_block) release_acc();
+            const int granules = p.N - nbk >= 128 ? 16 : static_cast<int>((p.N - nbk) / 8);
             if (p.epi == H3B_EPI_QKV_SEND) {
-              // 32 columns inside one head: which tensor, which destination rank, which local head
-              const int which = static_cast<int>(n0 / p.hd);
-              const int hcol = static_cast<int>(n0 - static_cast<int64_t>(which) * p.hd);
-              const int h = hcol >> 7, c = hcol & 127;
-              const int g = h / p.hg, hh = h - g * p.hg;
-              const int dst_rank = hh / p.hl, j = hh - dst_rank * p.hl;
-              int64_t seg;
-              uint16_t* slab = send_slab(p, which, g, dst_rank, seg);
-              const int64_t off = ((seg * p.M + m) * p.rsh + j) * 128 + c;
-              const bool as_f16 = which == 2 && p.v_f16;
-              int32_t* rf = p.range_flag;
-              if (as_f16 && rf != nullptr) {
-                bool bad = false;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) bad |= fabsf(v[i]) > 65504.0f && isfinite(v[i]);
-                if (bad) atomicExch(rf, 1);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(slab + off);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  w[e] = as_f16 ? pack2_bf16_as_f16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1])
-                                : pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], 0);
-                dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
-              }
+              store_rows(qbase, qstride, m0, 16);  // with p2p: the destination rank's receive buffer
             } else if (p.epi == EPI_GATE) {
-              // y = x + gate[idx[m]] * bf16(o): fp32, product and sum rounded separately (the eager mirror's order)
-              const int64_t gi = __ldg(p.gidx + m);
-              if (gi < 0 || gi >= p.gate_rows) {
-                record_status(p.wc, H3B_EINVAL);
-                continue;
-              }
-              const uint4* xrow = reinterpret_cast<const uint4*>(p.gx + m * p.ldx + n0);
-              const uint4* grow = reinterpret_cast<const uint4*>(p.gate + gi * p.ldg + n0);
-              uint16_t* yrow = static_cast<uint16_t*>(p.y) + m * p.ldy;
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (n0 + 8 * q >= p.N) break;
-                const uint4 xv = __ldg(xrow + q), gv = __ldg(grow + q);
+              // y = x + gate[idx[m]] * o with o the staged bf16 output: fp32, product and sum rounded separately
+              // (the eager mirror's order); two rows per instruction, 16 bytes of x, gate and y per lane
+              __syncwarp();
+#pragma unroll 2
+              for (int it = 0; it < 16; ++it) {
+                const int r = 2 * it + (lane >> 4), g = lane & 15;
+                const int64_t mr = m0 + r;
+                if (mr >= p.M || g >= granules) continue;
+                const int64_t gi = __ldg(p.gidx + mr);
+                if (gi < 0 || gi >= p.gate_rows) {
+                  record_status(p.wc, H3B_EINVAL);
+                  continue;
+                }
+                const int64_t col = nbk + g * 8;
+                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(p.gx + mr * p.ldx + col));
+                const uint4 gv = __ldg(reinterpret_cast<const uint4*>(p.gate + gi * p.ldg + col));
+                const uint4 ov = stg[r * 16 + (g ^ (r & 15))];
                 const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+                const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                  float r[2];
+                  float rr[2];
 #pragma unroll
                   for (int h = 0; h < 2; ++h) {
                     const float xf = __uint_as_float(h ? (xw[e] & 0xFFFF0000u) : (xw[e] << 16));
                     const float gf = __uint_as_float(h ? (gw[e] & 0xFFFF0000u) : (gw[e] << 16));
-                    r[h] = __fadd_rn(xf, __fmul_rn(gf, rbf16(v[8 * q + 2 * e + h])));
+                    const float of = __uint_as_float(h ? (ow[e] & 0xFFFF0000u) : (ow[e] << 16));
+                    rr[h] = __fadd_rn(xf, __fmul_rn(gf, of));
                   }
-                  w[e] = pack2(r[0], r[1], 0);
+                  w[e] = pack2(rr[0], rr[1], 0);
                 }
-                *reinterpret_cast<uint4*>(yrow + n0 + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + mr * p.ldy + col) = make_uint4(w[0], w[1], w[2], w[3]);
               }
+              __syncwarp();
             } else {
-              uint16_t* yrow = static_cast<uint16_t*>(p.y) + m * p.ldy;
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (n0 + 8 * q >= p.N) break;
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) w[e] = pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], p.out_f16);
-                *reinterpret_cast<uint4*>(yrow + n0 + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
-              }
+              store_rows(static_cast<uint16_t*>(p.y) + nbk, p.ldy, m0, granules);
             }
           }
         }
-        tc_fence_before();
-        mbar_arrive(tempty_bar(acc));
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -550,9 +561,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // neither CTA leaves (or frees the pair's TMEM) while the other may still signal it
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 512);
+  if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
 }  // namespace gemm
@@ -595,7 +606,7 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
   p.ldy = ldy;
   p.out_f16 = out_dtype == H3B_OUT_F16;
   p.epi = epilogue;
-  p.num_mb = static_cast<int>((M + BM - 1) / BM);
+  p.num_mb = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
   p.num_kb = static_cast<int>((K + BK - 1) / BK);
   if (epilogue == H3B_EPI_SWIGLU) {
     if (N % 256) return fail(H3B_EUNSUPPORTED, "fp8_gemm swiglu: N/2 must be a multiple of 128");
@@ -700,22 +711,29 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
     int rc = encode_tmap(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  static bool attr_set[64] = {false};
+  // per device: the shared-memory limit and how many CTA pairs fit at once (a pair needs two SMs of one GPC; the
+  // grid is that many pairs, or fewer when there are fewer tiles)
+  static int pairs_fit[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(fp8_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_PEER);
-    if (e != cudaSuccess) return cuda_fail(e, "fp8_gemm: smem attribute");
-    attr_set[dev] = true;
+  if (dev < 0 || dev >= 64) return fail(H3B_EUNSUPPORTED, "fp8_gemm: device ordinal %d", dev);
+  if (pairs_fit[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    int fit = 0;
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(num_sms() & ~1), 1, 1);
+      cfg.blockDim = dim3(THREADS, 1, 1);
+      cfg.dynamicSmemBytes = SMEM_BYTES;
+      e = cudaOccupancyMaxActiveClusters(&fit, fp8_gemm_kernel, &cfg);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "fp8_gemm: smem attribute / cluster occupancy");
+    if (fit < 1) return fail(H3B_EUNSUPPORTED, "fp8_gemm: no CTA pair fits on this device");
+    pairs_fit[dev] = fit;
   }
   const int tiles = p.num_mb * p.num_nb;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  if (p.p2p)
-    fp8_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_PEER, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
-  else
-    fp8_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
+  const int grid = 2 * (tiles < pairs_fit[dev] ? tiles : pairs_fit[dev]);
+  fp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
   H3B_CHECK_LAUNCH("fp8_gemm launch");
   return H3B_OK;
 }

@@ -53,14 +53,14 @@ def launch_fused(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.T
 
 
 def fused_config() -> tuple[int, int, int, int, int]:
-    """(BLOCK_M, BLOCK_N, BLOCK_K, stages, GROUP_M) of the tcgen05 kernel (h3_tp2/fp8_gemm.py:202 returns the Triton
-    kernel's)."""
-    return 128, 256, 128, 4, 16
+    """(BLOCK_M, BLOCK_N, BLOCK_K, warps, stages) of the tcgen05 kernel, in the order of h3_tp2/fp8_gemm.py:202 (which
+    returns the Triton kernel's): a 256 x 256 tile per CTA pair (128 rows per CTA), 6 warps and 6 stages per CTA."""
+    return 256, 256, 128, 6, 6
 
 
-def tile_coords(pid: int, M: int, N: int, block_m: int = 128, block_n: int = 256, group_m: int = 16) -> tuple[int, int]:
-    """Grouped raster of the persistent kernel: tile ``pid`` -> (row block, column block); GROUP_M row blocks share
-    each column block's W tile in L2 (h3_tp2/fp8_gemm.py:188 is the same raster)."""
+def tile_coords(pid: int, M: int, N: int, block_m: int = 256, block_n: int = 256, group_m: int = 8) -> tuple[int, int]:
+    """Grouped raster of the persistent kernel: pair tile ``pid`` -> (row block, column block); GROUP_M row blocks
+    share each column block's W tile in L2 (h3_tp2/fp8_gemm.py:188 is the same raster)."""
     num_mb, num_nb = -(-M // block_m), -(-N // block_n)
     in_group = group_m * num_nb
     group = pid // in_group
