@@ -209,7 +209,7 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # DRAM bytes (read + write) of one attention launch at cfg2 SP=1, from the ncu launch list of this bench
-ATTN_TRAFFIC_BYTES = 35.41e9
+ATTN_TRAFFIC_BYTES = 33.82e9
 
 
 def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
