@@ -155,3 +155,16 @@ def test_block_exchange_options_are_validated():
                                                            torch.ones(1536), torch.zeros(64, 512,
                                                                                         dtype=torch.float8_e4m3fn),
                                                            torch.ones(64)), exchange="p2p", groups=2, rank=0)
+
+
+@pytest.mark.parametrize("M,N", [(1, 16), (255, 256), (257, 272), (62_496, 15_360), (15_624, 5_120), (3_000, 27_648)])
+def test_gemm_tile_raster_covers_every_tile_once(M, N):
+    """The pair-tile raster of the persistent GEMM (mirrored by fp8_gemm.tile_coords) visits each (256-row block,
+    256-column block) exactly once, GROUP_M row blocks at a time."""
+    bm, bn, _, _, _ = fp8_gemm.fused_config()
+    num_mb, num_nb = -(-M // bm), -(-N // bn)
+    seen = [fp8_gemm.tile_coords(t, M, N) for t in range(num_mb * num_nb)]
+    assert sorted(seen) == [(i, j) for i in range(num_mb) for j in range(num_nb)]
+    # within a group of 8 row blocks, consecutive tiles walk down the rows of one column block first
+    if num_mb >= 2 and num_nb >= 2:
+        assert seen[1] == (1, 0)
