@@ -1,11 +1,11 @@
 """Generate the golden vectors that pin the oracle (and, on the GPU, the kernels) to the reference itself.
 
 Runs IN THIS CONTAINER ONLY: it imports the reference package ``h3_tp2`` (and its CPU test fakes) from the read-only
-reference checkout given by ``--reference`` (default ``/root/reference``), executes the reference's own CPU/eager
-functions on seeded inputs built from the recipes of the reference's tests, and writes small ``.npz`` fixtures next to
-this script.  The GPU box never needs the reference: the fixtures are committed.
+reference checkout given by ``--reference`` (or the ``H3_TP2_REFERENCE`` environment variable), executes the reference's
+own CPU/eager functions on seeded inputs built from the recipes of the reference's tests, and writes small ``.npz``
+fixtures next to this script.  The GPU box never needs the reference: the fixtures are committed.
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
 
 Reference functions exercised (paths inside the reference project):
   quant:    h3_tp2/fp8_quant_fuse.py:302 quant_torch, h3_tp2/ulysses_outq.py:109 quant_rows (CPU path),
@@ -25,6 +25,7 @@ Reference functions exercised (paths inside the reference project):
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -310,8 +311,11 @@ def gen_gate(fc) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("H3_TP2_REFERENCE"),
+                    help="checkout of the reference project (the directory holding h3_tp2/ and tests/)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or H3_TP2_REFERENCE) is required")
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
     sys.path.insert(0, str(ref / "tests"))
