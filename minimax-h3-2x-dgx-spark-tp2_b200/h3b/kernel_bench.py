@@ -2,8 +2,11 @@
 algorithmic bytes (HBM-bound kernels) or FLOPs (tensor kernels) against the measured peaks.
 
     python -m h3b.kernel_bench [--rows M] [--iters N] [--once] [--only NAME,...]
+    python -m h3b.kernel_bench --ffn [--iters N]
 
 ``--once`` launches each kernel exactly once after its inputs are built (the form an ncu launch capture wants).
+``--ffn`` times the FFN of the DiT block (RMSNorm + quant -> fc1 with the SwiGLU epilogue -> quant -> fc2) at the token
+counts of the FFN sweep config, M = 124,992 / P for P = 8, 4, 2, 1, stage by stage.
 Inputs of the HBM-bound kernels exceed the 126 MB L2 at the default sizes, so no flush is needed between iterations.
 """
 from __future__ import annotations
@@ -183,15 +186,65 @@ def cases(M: int, dev):
     return out
 
 
+def ffn_sweep(dev, iters: int) -> None:
+    """FFN sweep: hidden 5120 -> gate/up 2 x 13,824 -> 5120, bf16 x ~ N(0,1), weights N(0, 0.02) quantised per output
+    channel to e4m3, RMSNorm eps 1e-6; one line per M with each stage's CUDA-event time."""
+    from .block import quant_weight  # noqa: PLC0415
+    g = torch.Generator(device=dev).manual_seed(1)
+    w1, s1 = quant_weight(torch.randn(2 * FFN, HIDDEN, device=dev, generator=g) * 0.02)
+    w2, s2 = quant_weight(torch.randn(HIDDEN, FFN, device=dev, generator=g) * 0.02)
+    nw = (1 + 0.1 * torch.randn(HIDDEN, device=dev, generator=g)).to(BF16)
+    for M in (15_624, 31_248, 62_496, 124_992):
+        x = torch.randn(M, HIDDEN, device=dev, generator=g).to(BF16)
+
+        def stages():
+            q, sq = ops.rms_quant(x, nw, eps=1e-6)
+            yield
+            h = ops.fp8_gemm_swiglu(q, w1, sq, s1)
+            yield
+            hq, sh = ops.quant(h)
+            yield
+            ops.fp8_gemm(hq, w2, sh, s2)
+            yield
+
+        for _ in range(3):
+            for _ in stages():
+                pass
+        torch.cuda.synchronize()
+        tot = [0.0] * 4
+        for _ in range(iters):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            ev[0].record()
+            for i, _ in enumerate(stages()):
+                ev[i + 1].record()
+            torch.cuda.synchronize()
+            for i in range(4):
+                tot[i] += ev[i].elapsed_time(ev[i + 1]) / iters
+        fl1, fl2 = 2.0 * M * HIDDEN * 2 * FFN, 2.0 * M * FFN * HIDDEN
+        print(json.dumps({"ffn_rows": M, "ms": round(sum(tot), 3), "rms_quant_ms": round(tot[0], 4),
+                          "fc1_swiglu_ms": round(tot[1], 4), "quant_ms": round(tot[2], 4), "fc2_ms": round(tot[3], 4),
+                          "fc1_tflops": round(fl1 / tot[1] / 1e9, 1), "fc2_tflops": round(fl2 / tot[3] / 1e9, 1),
+                          "ffn_tflops": round((fl1 + fl2) / sum(tot) / 1e9, 1)}), flush=True)
+        del x
+        torch.cuda.empty_cache()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--rows", type=int, default=62496, help="token rows M (default: cfg2 at SP=2)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--once", action="store_true", help="launch each kernel once (for an ncu launch capture)")
     ap.add_argument("--only", default="", help="comma-separated substrings of kernel names")
+    ap.add_argument("--ffn", action="store_true", help="time the FFN sweep instead of the single kernels")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.ffn:
+        ffn_sweep(dev, args.iters)
+        status = ops.device_status()
+        if status != 0:
+            raise SystemExit(f"device status {status}")
+        return
     peaks = _peaks()
     only = [s.strip() for s in args.only.split(",") if s.strip()]
     for name, bound, work, setup in cases(args.rows, dev):
