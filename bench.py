@@ -370,7 +370,9 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    # 10 steps: the end-to-end loop's first input copy and last output copy (no block to overlap them with) weigh
+    # 1/10 of a step each instead of 1/5
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("h3b", "reference"), default="h3b")
     ap.add_argument("--tokens", type=int, default=0, help="override the token count (tests / small runs)")
