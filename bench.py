@@ -392,6 +392,9 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: the h3b arm needs a CUDA GPU (there is no CPU fallback); --impl reference times "
+                         "the CPU path")
     pg = None
     if world > 1:
         import datetime  # noqa: PLC0415
