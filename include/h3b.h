@@ -90,7 +90,8 @@ typedef struct h3b_qkv_send {
   int32_t p2p;
   int32_t rank;
   void* peer_recv[H3B_MAX_RANKS][3];
-  int32_t* peer_range_flag[H3B_MAX_RANKS]; /* v_f16 overflow flag of each destination rank (replaces range_flag) */
+  int32_t* peer_range_flag[H3B_MAX_RANKS]; /* v_f16 overflow flag of each rank (replaces range_flag); an overflow
+                                            * in any slab raises all of them, so every rank sees the same flag */
   /* qkv_interleaved != 0 (not with p2p): one send buffer send[0] = [G, P, M, 3, hgl, d] holding q, k, v of a token
    * side by side (the combined-exchange layout of h3_tp2/ulysses_nocopy.py:74-90; send[1], send[2] unused) */
   int32_t qkv_interleaved;

@@ -494,7 +494,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 bool bad = false;
 #pragma unroll
                 for (int i = 0; i < 32; ++i) bad |= fabsf(v[i]) > 65504.0f && isfinite(v[i]);
-                if (bad) atomicExch(rf, 1);
+                if (bad && p.p2p) {
+                  // every rank's flag, not only the destination's: after the epoch barrier that follows this GEMM
+                  // all ranks then see the same flag and take the same decision
+                  for (int r = 0; r < p.ws; ++r)
+                    if (p.peer_rf[r] != nullptr) atomicExch(p.peer_rf[r], 1);
+                } else if (bad) {
+                  atomicExch(rf, 1);
+                }
               }
               const int f16 = p.epi == H3B_EPI_PLAIN ? p.out_f16 : 0;
 #pragma unroll

@@ -43,7 +43,7 @@ def block_flops(tokens: int, hidden: int, heads: int, head_dim: int = 128) -> di
 class AttentionBlock:
     def __init__(self, hidden: int, heads: int, *, device, head_dim: int = 128, seed: int = 1, ws: int = 1, pg=None,
                  weights: tuple | None = None, init_device=None, a2a=None, groups: int | None = None,
-                 exchange: str = "nccl", rank: int | None = None):
+                 exchange: str = "nccl", rank: int | None = None, range_check: bool = True):
         if head_dim != 128:
             raise ValueError("head_dim 128 only")
         if heads % ws:
@@ -73,14 +73,30 @@ class AttentionBlock:
         self.exchange_kind = exchange
         self.rank = rank if rank is not None else (dist.get_rank(pg) if exchange == "p2p" and ws > 1 else 0)
         self._peers = None
+        # v travels as f16 for the f16 P.V product; a v outside f16's range (|v| > 65504) is caught after the qkv
+        # projection (``range_check``: one host read of the group-wide flag per forward), and the block then switches
+        # to bf16 v and bf16 P.V for good and recomputes the projection.  Without the check the attention refuses f16
+        # P.V (H3B_ERANGE in the device status word) and leaves its output unwritten.
+        self.range_check = range_check
+        self.v_f16 = True
 
     def _peer_exchange(self, m: int):
         from .ulysses_p2p import PeerExchange
-        if self._peers is None or self._peers.m != m:
+        if self._peers is None or self._peers.m != m or self._peers.v_f16 != self.v_f16:
             if self._peers is not None:
                 self.close()
-            self._peers = PeerExchange(m, self.heads, self.ws, self.rank, self.device, pg=self.pg)
+            self._peers = PeerExchange(m, self.heads, self.ws, self.rank, self.device, pg=self.pg,
+                                       v_f16=self.v_f16)
         return self._peers
+
+    def _v_overflowed(self, flag: torch.Tensor) -> bool:
+        """True when the qkv projection just written left f16's range in some v (``flag``: the group-wide flag).  The
+        block then switches to bf16 v for good; the caller recomputes the projection."""
+        if not (self.v_f16 and self.range_check) or not bool(flag.item()):
+            return False
+        self.v_f16 = False
+        flag.zero_()
+        return True
 
     def close(self) -> None:
         """Releases the peer buffers of the p2p exchange (collective over the group)."""
@@ -131,6 +147,10 @@ class AttentionBlock:
             px.forward_qkv(q8, self.wqkv8, sx, self.sqkv)
             mark()
             px.barrier()
+            if self._v_overflowed(px.range_flag):  # every rank saw the same flag (raised on all ranks)
+                px = self._peer_exchange(m)         # rebuilt with bf16 v (collective)
+                px.forward_qkv(q8, self.wqkv8, sx, self.sqkv)
+                px.barrier()
             mark()
             px.attention(1.0 / math.sqrt(d))
             mark()
@@ -141,17 +161,20 @@ class AttentionBlock:
             from .ulysses_nocopy import qkv_views
             from .ulysses_overlap import quant_grouped_back
             G = self.groups
-            send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+            send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=self.v_f16,
                                          range_flag=self.range_flag, groups=G, interleaved=True)
             self.share_range_flag()
+            if self._v_overflowed(self.range_flag):
+                send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=False,
+                                             groups=G, interleaved=True)
             mark()
             recv = torch.empty_like(send)
             for g in range(G):
                 self.exchange_into(recv[g], send[g])
             mark()
             hgl = self.heads // (G * self.ws)
-            outs = [ops.flash_attn(*qkv_views(recv[g], v_f16=True), scale=1.0 / math.sqrt(d),
-                                   range_flag=self.range_flag) for g in range(G)]
+            outs = [ops.flash_attn(*qkv_views(recv[g], v_f16=self.v_f16), scale=1.0 / math.sqrt(d),
+                                   range_flag=self.range_flag, pv_f16=self.v_f16) for g in range(G)]
             mark()
             back = torch.empty((G, self.ws, m, hgl, d), dtype=torch.bfloat16, device=self.device)
             for g in range(G):
@@ -160,26 +183,32 @@ class AttentionBlock:
             o8, so = ops.quant_from_recv(back[0]) if G == 1 else quant_grouped_back(back)
         elif self.ws > 1 and self.groups > 1:
             from .ulysses_overlap import grouped_attention, quant_grouped_back
-            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=self.v_f16,
                                           range_flag=self.range_flag, groups=self.groups)
             self.share_range_flag()
+            if self._v_overflowed(self.range_flag):
+                sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=False,
+                                              groups=self.groups)
             mark()
             mark()      # with head groups the exchanges overlap the attention: the attention stage holds all three
+            pv_f16 = self.v_f16
             back = grouped_attention(sends, self.ws, self.groups,
                                      lambda q, k, v: ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d),
-                                                                    range_flag=self.range_flag),
+                                                                    range_flag=self.range_flag, pv_f16=pv_f16),
                                      pg=self.pg, a2a=self.a2a)
             mark()
             mark()
             o8, so = quant_grouped_back(back)
         else:
-            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=True,
+            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=self.v_f16,
                                           range_flag=self.range_flag)
             self.share_range_flag()
+            if self._v_overflowed(self.range_flag):
+                sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=False)
             mark()
             q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
             mark()
-            o = ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d), range_flag=self.range_flag)
+            o = ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d), range_flag=self.range_flag, pv_f16=self.v_f16)
             mark()
             back = self.exchange(o.view(self.ws, m, hl, d))
             mark()

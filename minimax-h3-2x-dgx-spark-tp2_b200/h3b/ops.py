@@ -258,7 +258,8 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
 
     ``p2p = (rank, peer_recv, peer_range_flag)``: no send buffers; the slab for rank p goes straight into
     ``peer_recv[p] = (q, k, v)`` (device tensors or addresses of rank p's [P, M, H/P, d] receive buffers, slot
-    ``rank``) and a v overflow raises ``peer_range_flag[p]``.  Returns None then.
+    ``rank``) and a v overflow raises every rank's ``peer_range_flag[p]`` (so all ranks agree once the stores are
+    ordered by the exchange's barrier).  Returns None then.
 
     ``interleaved``: one send buffer [G, P, M, 3, H/(G*P), d] (q, k, v of a token side by side, the combined-exchange
     layout of ulysses_nocopy) is returned instead of three; its v slots hold f16 bits when ``v_f16``."""
