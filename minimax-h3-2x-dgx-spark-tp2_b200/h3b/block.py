@@ -43,7 +43,7 @@ def block_flops(tokens: int, hidden: int, heads: int, head_dim: int = 128) -> di
 class AttentionBlock:
     def __init__(self, hidden: int, heads: int, *, device, head_dim: int = 128, seed: int = 1, ws: int = 1, pg=None,
                  weights: tuple | None = None, init_device=None, a2a=None, groups: int | None = None,
-                 exchange: str = "nccl", rank: int | None = None, range_check: bool = True):
+                 exchange: str = "nccl", rank: int | None = None, range_check: bool = False):
         if head_dim != 128:
             raise ValueError("head_dim 128 only")
         if heads % ws:
@@ -73,10 +73,12 @@ class AttentionBlock:
         self.exchange_kind = exchange
         self.rank = rank if rank is not None else (dist.get_rank(pg) if exchange == "p2p" and ws > 1 else 0)
         self._peers = None
-        # v travels as f16 for the f16 P.V product; a v outside f16's range (|v| > 65504) is caught after the qkv
-        # projection (``range_check``: one host read of the group-wide flag per forward), and the block then switches
-        # to bf16 v and bf16 P.V for good and recomputes the projection.  Without the check the attention refuses f16
-        # P.V (H3B_ERANGE in the device status word) and leaves its output unwritten.
+        # v travels as f16 for the f16 P.V product.  With ``range_check`` a v outside f16's range (|v| > 65504) is
+        # caught after the qkv projection (one host read of the group-wide flag per forward), and the block then
+        # switches to bf16 v and bf16 P.V for good and recomputes the projection.  The read waits for the copy
+        # engine, so a large device-to-host copy in flight on another stream delays the rest of the forward (11 ms
+        # per block measured with the bench's overlapped output copies): it is off by default, and without it the
+        # attention refuses f16 P.V on such a v (H3B_ERANGE in the device status word, output unwritten).
         self.range_check = range_check
         self.v_f16 = True
 

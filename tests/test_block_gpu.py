@@ -102,12 +102,12 @@ def _weights_with_large_v(hidden, heads, seed):
 
 
 def test_block_recovers_from_v_outside_f16(dev):
-    """A v outside f16's range is caught after the qkv projection: the block switches to bf16 v and bf16 P.V for good,
-    recomputes the projection, and the f16 attention never runs on it (no H3B_ERANGE)."""
+    """With range_check, a v outside f16's range is caught after the qkv projection: the block switches to bf16 v and
+    bf16 P.V for good, recomputes the projection, and the f16 attention never runs on it (no H3B_ERANGE)."""
     n, hidden, heads = 1024, 512, 4
     weights = _weights_with_large_v(hidden, heads, seed=5)
     x = torch.randn(n, hidden, generator=torch.Generator().manual_seed(6)).to(BF16)
-    blk = AttentionBlock(hidden, heads, device=dev, weights=weights)
+    blk = AttentionBlock(hidden, heads, device=dev, weights=weights, range_check=True)
     y = blk(x.to(dev))
     assert not blk.v_f16
     assert ops.device_status() == 0
@@ -130,14 +130,15 @@ def test_ulysses_ranks_recover_together(dev, ws, groups):
     x = torch.randn(n, hidden, generator=torch.Generator().manual_seed(8)).to(BF16)
     x[: n // 2] *= 1e-3   # rank 0's rows keep their v inside f16's range
     x = x.to(dev)
-    full_blk = AttentionBlock(hidden, heads, device=dev, weights=weights)
+    full_blk = AttentionBlock(hidden, heads, device=dev, weights=weights, range_check=True)
     full = full_blk(x)
     assert not full_blk.v_f16
     m = n // ws
     torch.cuda.synchronize()
 
     def body(r, a2a):
-        blk = AttentionBlock(hidden, heads, device=dev, weights=weights, ws=ws, a2a=a2a, groups=groups)
+        blk = AttentionBlock(hidden, heads, device=dev, weights=weights, ws=ws, a2a=a2a, groups=groups,
+                             range_check=True)
         out = blk(x[r * m:(r + 1) * m].contiguous())
         torch.cuda.synchronize()
         return out, blk.v_f16
