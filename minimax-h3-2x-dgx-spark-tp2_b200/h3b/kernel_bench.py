@@ -3,10 +3,13 @@ algorithmic bytes (HBM-bound kernels) or FLOPs (tensor kernels) against the meas
 
     python -m h3b.kernel_bench [--rows M] [--iters N] [--once] [--only NAME,...]
     python -m h3b.kernel_bench --ffn [--iters N]
+    python -m h3b.kernel_bench --cublas [--rows M] [--iters N]
 
 ``--once`` launches each kernel exactly once after its inputs are built (the form an ncu launch capture wants).
 ``--ffn`` times the FFN of the DiT block (RMSNorm + quant -> fc1 with the SwiGLU epilogue -> quant -> fc2) at the token
-counts of the FFN sweep config, M = 124,992 / P for P = 8, 4, 2, 1, stage by stage.
+counts of the FFN sweep config, M = 124,992 / P for P = 8, 4, 2, 1, stage by stage.  ``--cublas`` times cuBLASLt's FP8
+GEMM (``torch._scaled_mm``, tensor-wise and row-wise scales, bf16 out) at the qkv and fc1 shapes as a library
+reference point for the tcgen05 GEMM; it is not on the product path.
 Inputs of the HBM-bound kernels exceed the 126 MB L2 at the default sizes, so no flush is needed between iterations.
 """
 from __future__ import annotations
@@ -229,6 +232,35 @@ def ffn_sweep(dev, iters: int) -> None:
         torch.cuda.empty_cache()
 
 
+def cublas_reference(rows: int, dev, iters: int) -> None:
+    """cuBLASLt FP8 at the qkv (rows x 15,360 x 5,120) and fc1 (rows/4 x 27,648 x 5,120) shapes: the device's library
+    FP8 GEMM with tensor-wise scales (its fastest form) and with the row-wise scales this path needs."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    for name, (M, N, K) in {"qkv": (rows, 3 * HEADS * D, HIDDEN), "fc1": (max(rows // 4, 1), 2 * FFN, HIDDEN)}.items():
+        a = (torch.randn(M, K, device=dev, generator=g) * 0.5).to(E4M3)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.5).to(E4M3)
+        one = torch.ones((), device=dev)
+        sa = torch.rand(M, 1, device=dev, generator=g) + 0.5
+        sb = torch.rand(1, N, device=dev, generator=g) + 0.5
+        for mode, (s_a, s_b) in {"tensorwise": (one, one), "rowwise": (sa, sb)}.items():
+            def run():
+                return torch._scaled_mm(a, w.t(), scale_a=s_a, scale_b=s_b, out_dtype=BF16)
+            try:
+                for _ in range(2):
+                    run()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    run()
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / iters
+                print(json.dumps({"library_gemm": f"cuBLASLt FP8 {name}", "scales": mode, "ms": round(ms, 4),
+                                  "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)}), flush=True)
+            except RuntimeError as exc:  # a scaling mode this torch build does not offer
+                print(json.dumps({"library_gemm": f"cuBLASLt FP8 {name}", "scales": mode, "error": str(exc)[:200]}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--rows", type=int, default=62496, help="token rows M (default: cfg2 at SP=2)")
@@ -236,9 +268,13 @@ def main() -> None:
     ap.add_argument("--once", action="store_true", help="launch each kernel once (for an ncu launch capture)")
     ap.add_argument("--only", default="", help="comma-separated substrings of kernel names")
     ap.add_argument("--ffn", action="store_true", help="time the FFN sweep instead of the single kernels")
+    ap.add_argument("--cublas", action="store_true", help="time cuBLASLt's FP8 GEMM at the qkv / fc1 shapes")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.cublas:
+        cublas_reference(args.rows, dev, args.iters)
+        return
     if args.ffn:
         ffn_sweep(dev, args.iters)
         status = ops.device_status()
