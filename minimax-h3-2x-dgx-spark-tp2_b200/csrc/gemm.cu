@@ -14,9 +14,11 @@
 //   warp 1      : TMEM allocator of the pair; in the leader, the single-thread tcgen05.mma issuer, whose commits
 //                 arrive on both CTAs' barriers
 //   warps 2..5  : epilogue; thread t of the 128 owns accumulator row t of its CTA (TMEM lane), reads 32-column
-//                 slices with tcgen05.ld, applies the scales and stores bf16/f16 (or scatters into the Ulysses send
-//                 layout, or applies SwiGLU to the gate/up halves); each warp then arrives on the leader's
-//                 accumulator-empty barrier (8 arrivals per tile, 4 of them from the other CTA).
+//                 slices with tcgen05.ld, applies the scales (and SwiGLU to the gate/up halves, or the gated
+//                 residual), stages each 128-column block of its warp's 32 rows in shared memory and stores it as two
+//                 whole rows per instruction (into y, or scattered into the Ulysses send layout); each warp arrives on
+//                 the leader's accumulator-empty barrier once its TMEM reads of a tile are done (8 arrivals per tile,
+//                 4 of them from the other CTA).
 //   The accumulator is double buffered in TMEM (2 x 256 of the 512 columns) so the epilogue of tile i overlaps the
 //   main loop of tile i+1.  Every wait is bounded (common.cuh).  No TMA multicast.
 #include "common.cuh"
