@@ -2,8 +2,9 @@
 
 The reference compiles a CuTe-DSL sm_120 kernel (``DslGemm``) and routes the running block's GEMMs to it, returning
 None whenever the kernel cannot take a call (fp16 output, bias, misalignment, M = 0) so the dispatcher falls through.
-Here the same entry points run the library's tcgen05 kernel, which also takes bias and fp16 output; None is returned
-only where the kernel's own guards refuse (M = 0, K or N not a multiple of 16, unaligned operands).
+Here the same entry points run the library's tcgen05 kernel, which also takes a (bf16) bias and fp16 output; None is
+returned only where the kernel's own guards refuse (M = 0, K or N not a multiple of 16, unaligned operands, a bias
+that is not bf16).
 """
 from __future__ import annotations
 

@@ -23,7 +23,8 @@ _routers: list = []
 
 def eligible(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, out_dtype,  # noqa: ANN001
              bias: torch.Tensor | None) -> bool:
-    """The dispatcher's guards (h3_tp2/fp8_gemm.py:364-372)."""
+    """The dispatcher's guards (h3_tp2/fp8_gemm.py:364-372), plus: a bias must be bf16 (the kernels read it as bf16;
+    any other bias falls through to the stock dispatch)."""
     M, N = a.shape[0], b.shape[-1]
     return not (a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]
                 or (scale_a.numel() == 1 and scale_b.numel() == 1)
@@ -31,7 +32,7 @@ def eligible(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: t
                 or scale_a.dtype != torch.float32 or scale_b.dtype != torch.float32
                 or a.dtype != torch.float8_e4m3fn or b.dtype != torch.float8_e4m3fn
                 or a.device != b.device or out_dtype not in (torch.bfloat16, torch.float16)
-                or (bias is not None and (bias.dim() != 1 or bias.numel() != N))
+                or (bias is not None and (bias.dim() != 1 or bias.numel() != N or bias.dtype != torch.bfloat16))
                 or not a.is_contiguous() or not b.t().is_contiguous() or a.shape[1] % 16 or N % 16)
 
 
@@ -47,8 +48,15 @@ scaled_mm_fused = scaled_mm        # h3_tp2/fp8_gemm.py:240
 
 
 def launch_fused(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None,
-                 y: torch.Tensor) -> torch.Tensor:
-    """One fused launch into ``y`` (h3_tp2/fp8_gemm.py:213): sa [M], sb [N] fp32 vectors, b [K, N]."""
+                 y: torch.Tensor, cfg=None) -> torch.Tensor:  # noqa: ANN001
+    """One fused launch into ``y`` (h3_tp2/fp8_gemm.py:213): sa [M], sb [N] fp32 vectors, b [K, N], y bf16 or f16.
+    ``cfg`` (the Triton kernel's tile choice) is accepted and has no effect: the tcgen05 kernel has one tile shape.
+    The Triton kernel's raw-accumulator form (fp32 ``y``) is not provided: the epilogue always writes the scaled
+    output."""
+    del cfg
+    if y.dtype == torch.float32:
+        raise NotImplementedError("launch_fused: fp32 y (the raw accumulator) is not provided by the fused tcgen05 "
+                                  "kernel; it writes the scaled bf16 / f16 output")
     return ops.fp8_gemm(a, b.t(), sa, sb, bias, y.dtype, out=y)
 
 

@@ -45,6 +45,17 @@ def _dt(t: torch.Tensor, *dtypes: torch.dtype, what: str) -> None:
         raise TypeError(f"{what}: dtype {t.dtype}, expected one of {dtypes}")
 
 
+def _bias(bias: torch.Tensor | None, n: int, what: str) -> torch.Tensor | None:
+    """A bias the kernels can read: None, or n bf16 values, contiguous (the kernels read it as bf16; an f16 bias
+    would be misread, so it is refused rather than converted, which would round it)."""
+    if bias is None:
+        return None
+    _dt(bias, torch.bfloat16, what=f"{what} bias")
+    if bias.numel() != n:
+        raise ValueError(f"{what}: bias has {bias.numel()} values, expected {n}")
+    return bias.reshape(-1).contiguous()
+
+
 def vec_scales(scale_a: torch.Tensor, scale_b: torch.Tensor, M: int, N: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row / per-column fp32 scale vectors (a scalar scale is broadcast), as fp8_gemm._vec_scales
     (h3_tp2/fp8_gemm.py:228-236)."""
@@ -149,6 +160,9 @@ def scale_bias_cast(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias:
     _need_cuda(x32, sa, sb, bias)
     M, N = x32.shape
     sa, sb = vec_scales(sa, sb, M, N)
+    bias = _bias(bias, N, "scale_bias_cast")
+    if out_dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"scale_bias_cast: out_dtype {out_dtype}, expected bf16 or f16")
     y = torch.empty((M, N), dtype=out_dtype, device=x32.device)
     _lib.call("h3b_scale_bias_cast", x32.contiguous().data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
               y.data_ptr(), M, N, OUT_BF16 if out_dtype == torch.bfloat16 else OUT_F16, _stream(x32))
@@ -161,6 +175,7 @@ def scale_swiglu(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: to
     M, width = x32.shape
     half = width // 2
     sa, sb = vec_scales(sa, sb, M, width)
+    bias = _bias(bias, width, "scale_swiglu")
     y = torch.empty((M, half), dtype=torch.bfloat16, device=x32.device)
     _lib.call("h3b_scale_swiglu", x32.contiguous().data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
               y.data_ptr(), M, half, _stream(x32))
@@ -174,6 +189,7 @@ def scale_swiglu_quant(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bi
     M, width = x32.shape
     half = width // 2
     sa, sb = vec_scales(sa, sb, M, width)
+    bias = _bias(bias, width, "scale_swiglu")
     q = torch.empty((M, half), dtype=E4M3, device=x32.device)
     s = torch.empty((M, 1), dtype=torch.float32, device=x32.device)
     _lib.call("h3b_scale_swiglu_quant", x32.contiguous().data_ptr(), sa.data_ptr(), sb.data_ptr(), _ptr(bias),
@@ -203,6 +219,14 @@ def fp8_gemm(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tenso
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
+    bias = _bias(bias, N, "fp8_gemm")
+    if out is not None:
+        _need_cuda(out)
+        _dt(out, torch.bfloat16, torch.float16, what="fp8_gemm out")
+        if out.shape != (M, N) or out.stride(1) != 1:
+            raise ValueError(f"fp8_gemm: out must be [{M}, {N}] with unit column stride, got {tuple(out.shape)}")
+    elif out_dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"fp8_gemm: out_dtype {out_dtype}, expected bf16 or f16 (the epilogue writes the scaled output)")
     y = out if out is not None else torch.empty((M, N), dtype=out_dtype, device=a.device)
     _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
               _ptr(bias), y.data_ptr(), y.stride(0), M, N, K, OUT_BF16 if y.dtype == torch.bfloat16 else OUT_F16,
@@ -217,6 +241,7 @@ def fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torc
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
+    bias = _bias(bias, N, "fp8_gemm_swiglu")
     y = torch.empty((M, N // 2), dtype=torch.bfloat16, device=a.device)
     _lib.call("h3b_fp8_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
               _ptr(bias), y.data_ptr(), y.stride(0), M, N, K, OUT_BF16, EPI_SWIGLU, None, _stream(a))
@@ -237,6 +262,12 @@ def fp8_gemm_gate(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.
     _dt(gate, torch.bfloat16, what="fp8_gemm_gate gate")
     if x.shape != (M, N) or x.stride(1) != 1 or gate.shape[-1] != N or gate.stride(-1) != 1:
         raise ValueError(f"fp8_gemm_gate: x {tuple(x.shape)} / gate {tuple(gate.shape)} against [{M}, {N}]")
+    bias = _bias(bias, N, "fp8_gemm_gate")
+    if out is not None:
+        _need_cuda(out)
+        _dt(out, torch.bfloat16, what="fp8_gemm_gate out")
+        if out.shape != (M, N) or out.stride(1) != 1:
+            raise ValueError(f"fp8_gemm_gate: out must be [{M}, {N}] with unit column stride, got {tuple(out.shape)}")
     idx = indices.to(torch.int64).contiguous()
     y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     _lib.call("h3b_fp8_gemm_gate", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), sa.data_ptr(), sb.data_ptr(),
@@ -266,6 +297,7 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
     N = w.shape[0]
     sa, sb = _gemm_operands(a, w, sa, sb, N)
     M, K = a.shape
+    bias = _bias(bias, N, "fp8_gemm_qkv_send")
     if N != 3 * heads * 128 or heads % (ws * groups):
         raise ValueError(f"fp8_gemm_qkv_send: N {N} != 3 * {heads} * 128 or heads % (ws * groups)")
     shape = (ws, M, heads // ws, 128) if groups == 1 else (groups, ws, M, heads // (ws * groups), 128)

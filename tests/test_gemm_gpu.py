@@ -234,3 +234,19 @@ def test_consumers_mirror(dev):
     assert out.data_ptr() == ph.data_ptr()
     assert same_bits(out.cpu(), ops.fp8_gemm_gate(a2, w2, sa2, sb2, x, gate, idx).cpu())
     assert ops.device_status() == 0
+
+
+def test_wrappers_refuse_what_the_kernels_would_misread(dev):
+    """An f16 bias (the kernels read bf16) and an fp32 output are refused before any launch."""
+    a = torch.zeros(4, 64, dtype=E4M3, device=dev)
+    w = torch.zeros(32, 64, dtype=E4M3, device=dev)
+    sa, sb = torch.ones(4, device=dev), torch.ones(32, device=dev)
+    with pytest.raises(TypeError, match="bias"):
+        ops.fp8_gemm(a, w, sa, sb, torch.zeros(32, dtype=torch.float16, device=dev))
+    with pytest.raises(TypeError, match="out_dtype"):
+        ops.fp8_gemm(a, w, sa, sb, None, torch.float32)
+    with pytest.raises(TypeError, match="out"):
+        ops.fp8_gemm(a, w, sa, sb, None, out=torch.empty(4, 32, device=dev))
+    with pytest.raises(ValueError, match="unit column stride"):
+        ops.fp8_gemm(a, w, sa, sb, None, out=torch.empty(32, 4, dtype=torch.bfloat16, device=dev).t())
+    assert ops.device_status() == 0

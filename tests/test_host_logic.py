@@ -84,6 +84,18 @@ def test_gemm_dispatch_guards():
     assert not fp8_gemm.eligible(a, b, torch.ones(1), torch.ones(1), torch.bfloat16, None)   # per-tensor: stock
     assert not fp8_gemm.eligible(a, b.contiguous(), sa, sb, torch.bfloat16, None)            # b.t() not contiguous
     assert not fp8_gemm.eligible(a, b, sa, sb, torch.float32, None)
+    # a bias is read as bf16 by the kernels: bf16 is taken, an f16 bias falls through to the stock dispatch
+    assert fp8_gemm.eligible(a, b, sa, sb, torch.float16, torch.zeros(16, dtype=torch.bfloat16))
+    assert not fp8_gemm.eligible(a, b, sa, sb, torch.float16, torch.zeros(16, dtype=torch.float16))
+
+
+def test_launch_fused_signature_and_raw_accumulator_refusal():
+    """launch_fused takes the reference's cfg argument; the raw fp32 accumulator form is refused, not faked."""
+    a = torch.zeros(8, 32, dtype=torch.float8_e4m3fn)
+    b = torch.zeros(16, 32, dtype=torch.float8_e4m3fn).t()
+    y = torch.empty(8, 16)
+    with pytest.raises(NotImplementedError, match="raw accumulator"):
+        fp8_gemm.launch_fused(a, b, torch.ones(8), torch.ones(16), None, y, (128, 128, 64, 8, 3))
 
 
 def test_route_order_routers_then_hooks():
