@@ -10,14 +10,16 @@ the fp32 product reaches HBM: a ``Stash`` here holds the GEMM's operands, and ea
 * ``gate_fused`` (:468): ``x + gate[indices] * fc2`` — the fc2 GEMM with the indexed-gate epilogue
   (``h3b_fp8_gemm_gate``).
 * ``gate_rms_fused`` (:445) has no one-kernel form (the RMS needs whole rows of the out projection, the GEMM works
-  on 256-column tiles): ``materialize`` the out projection and use ``h3b.fp8_quant_fuse.gate_rms_quant``, which also
-  quantises the modulated output for fc1.
+  on 256-column tiles): it materialises the out projection, runs the gated residual + RMSNorm + modulation row kernel
+  for ``residual_out`` and the RMSNorm + modulation row kernel on that for the bf16 modulated rows.
 """
 from __future__ import annotations
 
 import torch
 
 from . import ops
+
+SITES = ("qkv", "out", "fc2")
 
 
 class Stash:
@@ -58,3 +60,50 @@ def gate_fused(st: Stash, x: torch.Tensor, gate: torch.Tensor, indices: torch.Te
     if x.shape[0] == 0:
         return out if out is not None else torch.empty_like(x)
     return ops.fp8_gemm_gate(st.a, st.w, st.sa, st.sb, x, gate, indices, st.bias, out=out)
+
+
+def gate_rms_fused(st: Stash, residual: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor,
+                   scale: torch.Tensor, indices: torch.Tensor, eps: float, reuse_placeholder: bool = True):
+    """``indexed_gate_rms_norm_scale_shift(residual, gate, branch, ...)`` with branch = the out projection of ``st``
+    (h3_tp2/fp8_consumers.py:445): returns (residual_out = bf16(residual + gate[indices] * branch), modulated_out =
+    bf16 RMSNorm(residual_out) * weight * (1 + scale[indices]) + shift[indices]); ``residual_out`` goes into the
+    placeholder when ``reuse_placeholder`` and the stash has one."""
+    rows = residual.shape[0]
+    residual_out = st.ph if (reuse_placeholder and st.ph is not None) else torch.empty_like(residual)
+    modulated_out = torch.empty_like(residual)
+    if rows == 0:
+        return residual_out, modulated_out
+    branch = ops.fp8_gemm(st.a, st.w, st.sa, st.sb, st.bias)
+    r_out, _, _ = ops.gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, eps)
+    ops.rms_quant(r_out, weight, shift, scale, indices, eps, modulated_out)
+    if residual_out is not r_out:
+        residual_out.copy_(r_out)
+    return residual_out, modulated_out
+
+
+def epilogue_bf16_torch(acc: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """The bf16 epilogue in eager torch on broadcastable fp32 tensors (h3_tp2/fp8_consumers.py:305): column scale,
+    row scale (bias by an fma carried out in float64), rounded to bf16 and returned as fp32."""
+    t = sb * acc
+    y = sa * t if bias is None else (sa.double() * t.double() + bias.double()).float()
+    return y.to(torch.bfloat16).float()
+
+
+def scale_pass_into(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None,
+                    y: torch.Tensor) -> torch.Tensor:
+    """The ordinary two-pass scale pass into ``y`` (h3_tp2/fp8_consumers.py:373): the scale-pass kernel on the GPU.
+    CPU tensors raise (the reference's eager CPU branch is ``fp8_gemm.epilogue_torch``, called explicitly)."""
+    y.copy_(ops.scale_bias_cast(x32, sa, sb, bias, y.dtype))
+    return y
+
+
+def parse_sites(value: str | None) -> tuple[str, ...]:
+    """``H3_TP2_FP8_CONSUMER_FUSE`` (h3_tp2/fp8_consumers.py:813): "1"/"all"/"on"/"true" = every site, a comma list of
+    qkv,out,fc2 selects sites, anything else or empty = none."""
+    v = (value or "").strip().lower()
+    if v in ("1", "all", "on", "true"):
+        return SITES
+    if v in ("", "0", "off", "false"):
+        return ()
+    chosen = {part.strip() for part in v.split(",")}
+    return tuple(site for site in SITES if site in chosen)

@@ -106,6 +106,38 @@ def probe_fused(device) -> bool:  # noqa: ANN001
     return bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
 
 
+def _rows(v: torch.Tensor) -> torch.Tensor:
+    return v.reshape(-1, 1).float()
+
+
+def _cols(v: torch.Tensor) -> torch.Tensor:
+    return v.reshape(1, -1).float()
+
+
+def epilogue_torch(acc: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None,
+                   out_dtype: torch.dtype) -> torch.Tensor:
+    """The kernel's epilogue in eager torch on an fp32 product (h3_tp2/fp8_gemm.py:174): the column scale first, then
+    the row scale, in fp32; with a bias, row scale x that product + bias as one fma, carried out in float64 (where the
+    fp32 product is exact) and rounded to fp32; then one rounding to ``out_dtype``.  A CPU function by design (the
+    reference's eager mirror), not a fallback of the GPU path."""
+    t = _cols(sb) * acc.float()
+    if bias is None:
+        y = _rows(sa) * t
+    else:
+        y = (_rows(sa).double() * t.double() + _cols(bias).double()).float()
+    return y.to(out_dtype)
+
+
+def scale_bias_cast_torch(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None,
+                          out_dtype: torch.dtype) -> torch.Tensor:
+    """The two-pass scale pass in eager torch (h3_tp2/fp8_gemm.py:120): column scale, row scale, then the bias as a
+    separate fp32 add (not an fma), one rounding to ``out_dtype``."""
+    y = (_cols(sb) * x32.float()) * _rows(sa)
+    if bias is not None:
+        y = y + _cols(bias)
+    return y.to(out_dtype)
+
+
 def epilogue_reference_order() -> str:
     return "t = scale_b * acc; y = scale_a * t (bias: fma(scale_a, t, bias)); one rounding"
 

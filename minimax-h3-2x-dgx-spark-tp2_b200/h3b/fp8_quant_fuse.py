@@ -45,3 +45,43 @@ def silu_mul_quant(x: torch.Tensor, stock=None, div_mode: int = ops.DIV_IEEE):  
     """h3_tp2/fp8_quant_fuse.py:392: silu_and_mul on bf16 [M, 2d] + per-token quant."""
     del stock
     return ops.silu_mul_quant(x, div_mode=div_mode)
+
+
+def quant_torch(h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token dynamic e4m3 quant in eager torch (vLLM ``QuantFP8.forward_native``, h3_tp2/fp8_quant_fuse.py:302):
+    scale = max(amax / 448, 1/229376) per row (NaN propagates), q = e4m3(clamp(h * (1 / scale), +-448)).  Returns
+    (q [M, K] e4m3, scale [M, 1] fp32).  A CPU function by design, not a fallback of ``quant``."""
+    amax = h.abs().amax(dim=-1, keepdim=True).float()
+    amax = torch.where(torch.isnan(h).any(dim=-1, keepdim=True), torch.full_like(amax, float("nan")), amax)
+    scale = torch.clamp(amax / FP8_MAX, min=MIN_SCALE)
+    q = torch.clamp(h.float() * torch.reciprocal(scale), -FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q, scale
+
+
+def unpack_stock(recv: torch.Tensor, heads: int) -> torch.Tensor:
+    """Stock's reverse unpack (h3_tp2/fp8_quant_fuse.py:371): receive [P, M, hl, d] -> [1, M, H, d] contiguous."""
+    p, m, hl, d = recv.shape
+    if p * hl != heads:
+        raise ValueError(f"unpack_stock: {p} x {hl} heads received, {heads} expected")
+    return recv.permute(1, 0, 2, 3).reshape(1, m, heads, d).contiguous()
+
+
+_ON = ("1", "all", "on", "true")
+_OFF = ("", "0", "off", "false")
+
+
+def parse_sites(value: str | None) -> tuple[str, ...]:
+    """``H3_TP2_FP8_QUANT_FUSE`` (h3_tp2/fp8_quant_fuse.py:836): "1"/"all"/"on"/"true" = every site, a comma list
+    selects sites (in SITES order), anything else or empty = none."""
+    v = (value or "").strip().lower()
+    if v in _ON:
+        return SITES
+    if v in _OFF:
+        return ()
+    chosen = {part.strip() for part in v.split(",")}
+    return tuple(site for site in SITES if site in chosen)
+
+
+def is_explicit(value: str | None) -> bool:
+    """True when the switch names its sites rather than turning all on or off (h3_tp2/fp8_quant_fuse.py:847)."""
+    return (value or "").strip().lower() not in _ON + _OFF

@@ -24,6 +24,18 @@ def quant_rows(base: torch.Tensor, m: int, p: int, seg: int, stride_p: int, stri
     return ops.quant_rows(base, m, p, seg, stride_p, stride_m, div_mode=div_mode)
 
 
+def quant_reference_eager(x: torch.Tensor, out=None):  # noqa: ANN001,ANN201
+    """Per-token dynamic e4m3 quant in eager torch (h3_tp2/ulysses_outq.py:126; ``fp8_quant_fuse.quant_torch``): (q,
+    scale [.., 1]), or copied into ``out = (q, scale)`` and returned.  A CPU function by design."""
+    from .fp8_quant_fuse import quant_torch  # noqa: PLC0415
+    q, scale = quant_torch(x)
+    if out is None:
+        return q, scale
+    out[0].copy_(q)
+    out[1].copy_(scale)
+    return out
+
+
 def quant_from_recv(recv: torch.Tensor, warps: int = 8, div_mode: int = ops.DIV_IEEE):
     """h3_tp2/ulysses_outq.py:138: recv [P, M, hl, d] -> the quant of stock's unpacked [M, P*hl*d] rows."""
     del warps

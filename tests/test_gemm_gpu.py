@@ -250,3 +250,29 @@ def test_wrappers_refuse_what_the_kernels_would_misread(dev):
     with pytest.raises(ValueError, match="unit column stride"):
         ops.fp8_gemm(a, w, sa, sb, None, out=torch.empty(32, 4, dtype=torch.bfloat16, device=dev).t())
     assert ops.device_status() == 0
+
+
+def test_gate_rms_consumer(dev):
+    """fp8_consumers.gate_rms_fused: (residual + gate[idx] * out-projection, its modulated RMSNorm) as bf16, the
+    residual written into the placeholder; within 1 bf16 ulp of the eager oracle (fma against separate roundings)."""
+    from oracle import rms as orms
+    M, N, K = 300, 512, 256
+    a, w, sa, sb = _serving_like(M, N, K, seed=11, dev=dev)
+    g = torch.Generator(device=dev).manual_seed(12)
+    residual = torch.randn(M, N, device=dev, generator=g).to(BF16)
+    gate = (0.1 * torch.randn(4, N, device=dev, generator=g)).to(BF16)
+    weight = (1.0 + 0.1 * torch.randn(N, device=dev, generator=g)).to(BF16)
+    shift = (0.1 * torch.randn(4, N, device=dev, generator=g)).to(BF16)
+    scale = (0.1 * torch.randn(4, N, device=dev, generator=g)).to(BF16)
+    idx = torch.randint(0, 4, (M,), device=dev, generator=g)
+    ph = torch.empty(M, N, device=dev, dtype=BF16)
+    st = fp8_consumers.Stash(a, w, sa, sb, None, ph)
+    r_out, mod = fp8_consumers.gate_rms_fused(st, residual, gate, weight, shift, scale, idx, 1e-6)
+    assert r_out.data_ptr() == ph.data_ptr() and mod.shape == (M, N) and mod.dtype == BF16
+    branch = ops.fp8_gemm(a, w, sa, sb).cpu()
+    ref_r, ref_m = orms.gate_rms_norm_scale_shift(residual.cpu(), gate.cpu(), branch, weight.cpu(), shift.cpu(),
+                                                  scale.cpu(), idx.cpu(), 1e-6)
+    for got, ref in ((r_out.cpu(), ref_r), (mod.cpu(), ref_m)):
+        ud = ulp_diff_bf16(got, ref)
+        assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.99
+    assert ops.device_status() == 0
