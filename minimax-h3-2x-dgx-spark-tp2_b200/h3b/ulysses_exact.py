@@ -18,9 +18,38 @@ from . import ops
 
 MODES = ("1", "2", "fwd", "verify")
 
+# call counters (h3_tp2/ulysses_exact.py:88 ``stats``) and the two producer hooks (:144, :151)
+_stats = {k: 0 for k in ("pack", "redirect", "fallback", "out_copy", "unpack_hook", "verify_equal", "verify_differs")}
+_hooks = {"key": None, "unpack": None}
+
+
+def stats() -> dict[str, int]:
+    return dict(_stats)
+
+
+def set_key_hook(fn) -> None:  # noqa: ANN001
+    """``fn(send_k)`` runs on this rank's packed keys [P, M, hl, d] right before their exchange; None: nothing runs
+    (h3_tp2/ulysses_exact.py:144)."""
+    _hooks["key"] = fn
+
+
+def set_unpack_hook(fn) -> None:  # noqa: ANN001
+    """``fn(recv [P, M, hl, d], heads)`` may replace the reverse unpack: it returns stock's [1, M, H, d] result, or None
+    for the ordinary unpack (h3_tp2/ulysses_exact.py:151)."""
+    _hooks["unpack"] = fn
+
 
 def _a2a(out: torch.Tensor, inp: torch.Tensor, group=None) -> None:  # noqa: ANN001
     dist.all_to_all_single(out, inp, group=group)
+
+
+def _stock_a2a_4d(x: torch.Tensor, scatter_idx: int, gather_idx: int, pg) -> torch.Tensor:  # noqa: ANN001
+    """vLLM-Omni's stock all-to-all (the comparison side of ``verify``); needs vLLM-Omni."""
+    try:
+        from vllm_omni.diffusion.distributed.comm import all_to_all_4D  # noqa: PLC0415
+    except ImportError as exc:  # pragma: no cover - vLLM-Omni is not part of this image
+        raise RuntimeError("the stock all-to-all needs vLLM-Omni (not installed): pass stock_fwd / stock_back") from exc
+    return all_to_all_4D(x, scatter_idx, gather_idx, group=pg)
 
 
 def send_shape(m: int, heads: int, d: int, ws: int) -> tuple[int, int, int, int]:
@@ -69,6 +98,7 @@ def exchange_back(o: torch.Tensor, heads: int, ws: int, a2a, pg=None, defer: boo
     ``Deferred`` (whose ``quantize()`` reads the receive buffer) is returned instead of the unpacked tensor."""
     o3 = o[0]
     if not o3.is_contiguous():
+        _stats["out_copy"] += 1
         o3 = o3.contiguous()
     s, hl, d = o3.shape
     m = s // ws
@@ -77,6 +107,12 @@ def exchange_back(o: torch.Tensor, heads: int, ws: int, a2a, pg=None, defer: boo
     if defer:
         from . import ulysses_outq
         return ulysses_outq.defer(recv, heads)
+    hook = _hooks["unpack"]
+    if hook is not None:
+        res = hook(recv, heads)
+        if res is not None:
+            _stats["unpack_hook"] += 1
+            return res
     res = (unpack_fn or unpack)(recv)
     return res.reshape(1, m, heads, d)
 
@@ -98,13 +134,17 @@ def exact_forward(query, key, value, run_attn, *, ws, pg=None, a2a=None, sends=N
         return buf
 
     if sends:
+        _stats["redirect"] += 1
         send_q, send_k = sends[0], sends[1]
         send_v = sends[2] if len(sends) > 2 else None
         sends.clear()
     else:
+        _stats["pack"] += 1
         send_q, send_k, send_v = do_pack(query[0]), do_pack(key[0]), None
     q = exchange_fwd(send_q, a2a, pg)
     del send_q
+    if _hooks["key"] is not None:
+        _hooks["key"](send_k)
     k = exchange_fwd(send_k, a2a, pg)
     del send_k
     if send_v is None:
@@ -118,6 +158,54 @@ def exact_forward(query, key, value, run_attn, *, ws, pg=None, a2a=None, sends=N
             raise ValueError("exact_forward: back='stock' needs stock_back")
         return stock_back(o)
     return exchange_back(o, heads, ws, a2a, pg, defer=back == "defer", unpack_fn=unpack_fn)
+
+
+def _same(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Bitwise equality (NaN payloads included) of same-shape, same-dtype tensors."""
+    if a.shape != b.shape or a.dtype != b.dtype:
+        return False
+    if a.element_size() == 2:
+        return torch.equal(a.contiguous().view(torch.int16), b.contiguous().view(torch.int16))
+    return torch.equal(a, b)
+
+
+def _same_layout(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Same shape and the same strides in every dimension longer than 1 (a stride of a size-1 dimension is
+    arbitrary)."""
+    return a.shape == b.shape and all(sa == sb for n, sa, sb in zip(a.shape, a.stride(), b.stride()) if n > 1)
+
+
+def verify_forward(query, key, value, run_attn, *, ws, pg=None, a2a=None, stock_fwd=None, stock_back=None,  # noqa: ANN001,ANN201
+                   pack=None, unpack_fn=None):
+    """Runs the stock exchange (``stock_fwd`` seq->head and ``stock_back`` head->seq, default vLLM-Omni's
+    ``all_to_all_4D``) and the exact one on the same q/k/v [1, M, H, d]; returns (stock result, {"q", "k", "v",
+    "attn", "result": bitwise equal}) (h3_tp2/ulysses_exact.py:232).  ``pack`` / ``unpack_fn`` as in
+    ``exact_forward``."""
+    a2a = a2a or _a2a
+    stock_fwd = stock_fwd or (lambda t: _stock_a2a_4d(t, 2, 1, pg))
+    stock_back = stock_back or (lambda t: _stock_a2a_4d(t, 1, 2, pg))
+    _, m, heads, d = value.shape
+    sq, sk, sv = stock_fwd(query), stock_fwd(key), stock_fwd(value)
+    so = run_attn(sq, sk, sv)
+    sres = stock_back(so)
+    eq = {}
+    received = []
+    for name, x, ref in (("q", query, sq), ("k", key, sk), ("v", value, sv)):
+        if pack is not None:
+            send = pack(x[0], ws)
+        else:
+            send = torch.empty(send_shape(m, heads, d, ws), dtype=x.dtype, device=x.device)
+            pack_into(send, x[0], ws)
+        r = exchange_fwd(send, a2a, pg)
+        eq[name] = _same_layout(r, ref) and _same(r, ref)
+        received.append(r)
+    del sq, sk, sv
+    o = run_attn(*received)
+    eq["attn"] = _same(o, so)
+    res = exchange_back(o, heads, ws, a2a, pg, unpack_fn=unpack_fn)
+    eq["result"] = res.is_contiguous() and _same(res, sres)
+    _stats["verify_equal" if all(eq.values()) else "verify_differs"] += 1
+    return sres, eq
 
 
 def eligible_shape(query, key, value, ws: int) -> bool:  # noqa: ANN001
@@ -146,11 +234,15 @@ def make_forward_impl(orig, mode: str, strategy_info, *, a2a=None):  # noqa: ANN
     def _forward_impl(self, query, key, value, attn_metadata=None):  # noqa: ANN001
         info = strategy_info(self, attn_metadata)
         if info is None or not eligible_shape(query, key, value, info[1]):
+            _stats["fallback"] += 1
             return orig(self, query, key, value, attn_metadata)
         pg, ws = info
+        attn = lambda q, k, v: local_attention(q, k, v, attn_metadata)  # noqa: E731
+        if mode == "verify":   # both exchanges on the same tensors; the stock result is returned
+            res, _ = verify_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a)
+            return res
         back = {"2": "defer", "fwd": "exact"}.get(mode, "exact")
-        res = exact_forward(query, key, value, lambda q, k, v: local_attention(q, k, v, attn_metadata), ws=ws, pg=pg,
-                            a2a=a2a, back=back)
+        res = exact_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a, back=back)
         if back == "defer":
             return res.materialize()
         return res

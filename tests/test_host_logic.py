@@ -180,3 +180,43 @@ def test_gemm_tile_raster_covers_every_tile_once(M, N):
     # within a group of 8 row blocks, consecutive tiles walk down the rows of one column block first
     if num_mb >= 2 and num_nb >= 2:
         assert seen[1] == (1, 0)
+
+
+def test_exact_forward_hooks_and_counters():
+    """set_key_hook sees each rank's packed keys before their exchange; set_unpack_hook replaces the reverse unpack;
+    stats() counts the packed forwards (h3_tp2/ulysses_exact.py:88,144,151)."""
+    ws, m, heads, d = 2, 4, 4, 8
+    qs, ks, vs = ([torch.randn(1, m, heads, d) for _ in range(ws)] for _ in range(3))
+    seen = []
+    ulysses_exact.set_key_hook(lambda send_k: seen.append(tuple(send_k.shape)))
+    ulysses_exact.set_unpack_hook(lambda recv, h: torch.full((1, recv.shape[1], h, recv.shape[3]), 7.0))
+    before = ulysses_exact.stats()
+    try:
+        res = ou.run_ranks(lambda r, a2a: ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws,
+                                                                      a2a=a2a, pack=ou.pack, unpack_fn=ou.unpack), ws)
+    finally:
+        ulysses_exact.set_key_hook(None)
+        ulysses_exact.set_unpack_hook(None)
+    after = ulysses_exact.stats()
+    assert seen == [(ws, m, heads // ws, d)] * ws
+    assert all(t.shape == (1, m, heads, d) and bool((t == 7.0).all()) for t in res)
+    assert after["pack"] - before["pack"] == ws and after["unpack_hook"] - before["unpack_hook"] == ws
+
+
+def test_verify_forward_compares_with_the_stock_exchange():
+    """verify_forward runs the stock all-to-alls and the exact exchange on the same tensors: all equal for a correct
+    layout, and a stock side that differs is reported (h3_tp2/ulysses_exact.py:232)."""
+    ws, m, heads, d = 2, 4, 4, 8
+    qs, ks, vs = ([torch.randn(1, m, heads, d) for _ in range(ws)] for _ in range(3))
+
+    def body(r, a2a, skew=0.0):
+        return ulysses_exact.verify_forward(
+            qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a, pack=ou.pack, unpack_fn=ou.unpack,
+            stock_fwd=lambda t: ou.stock_all_to_all_4d(t, 2, 1, ws, a2a),
+            stock_back=lambda t: ou.stock_all_to_all_4d(t, 1, 2, ws, a2a) + skew)
+
+    for res, eq in ou.run_ranks(body, ws):
+        assert eq == {"q": True, "k": True, "v": True, "attn": True, "result": True}
+        assert res.shape == (1, m, heads, d)
+    for _, eq in ou.run_ranks(lambda r, a2a: body(r, a2a, skew=1.0), ws):
+        assert eq["q"] and eq["attn"] and not eq["result"]
