@@ -94,8 +94,9 @@ def exchange_fwd(send: torch.Tensor, a2a, pg=None) -> torch.Tensor:  # noqa: ANN
 def exchange_back(o: torch.Tensor, heads: int, ws: int, a2a, pg=None, defer: bool = False,  # noqa: ANN001
                   unpack_fn=None):
     """Attention output [1, P*M, hl, d] -> [1, M, H, d]: one all-to-all of ``o`` itself, then the unpack
-    (h3_tp2/ulysses_exact.py:156).  With ``defer`` the receive buffer is handed to ``ulysses_outq.defer`` and its
-    ``Deferred`` (whose ``quantize()`` reads the receive buffer) is returned instead of the unpacked tensor."""
+    (h3_tp2/ulysses_exact.py:156).  With ``defer`` the receive buffer is offered to ``ulysses_outq.defer``: when this
+    forward was armed for it, its stride-0 placeholder is returned instead of the unpacked tensor (the out-projection
+    quant then reads the receive buffer); otherwise the unpack runs as without."""
     o3 = o[0]
     if not o3.is_contiguous():
         _stats["out_copy"] += 1
@@ -104,15 +105,18 @@ def exchange_back(o: torch.Tensor, heads: int, ws: int, a2a, pg=None, defer: boo
     m = s // ws
     recv = torch.empty((ws, m, hl, d), dtype=o3.dtype, device=o3.device)
     a2a(recv, o3, group=pg)
-    if defer:
+    if defer:  # the armed forward's out-projection quant reads the receive buffer (a placeholder stands for copy 5)
         from . import ulysses_outq
-        return ulysses_outq.defer(recv, heads)
-    hook = _hooks["unpack"]
-    if hook is not None:
-        res = hook(recv, heads)
-        if res is not None:
-            _stats["unpack_hook"] += 1
-            return res
+        ph = ulysses_outq.defer(recv, heads)
+        if ph is not None:
+            return ph
+    else:
+        hook = _hooks["unpack"]
+        if hook is not None:
+            res = hook(recv, heads)
+            if res is not None:
+                _stats["unpack_hook"] += 1
+                return res
     res = (unpack_fn or unpack)(recv)
     return res.reshape(1, m, heads, d)
 
@@ -242,10 +246,7 @@ def make_forward_impl(orig, mode: str, strategy_info, *, a2a=None):  # noqa: ANN
             res, _ = verify_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a)
             return res
         back = {"2": "defer", "fwd": "exact"}.get(mode, "exact")
-        res = exact_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a, back=back)
-        if back == "defer":
-            return res.materialize()
-        return res
+        return exact_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a, back=back)
 
     return _forward_impl
 

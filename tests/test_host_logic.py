@@ -5,6 +5,7 @@ import torch
 
 from _util import same_bits, t16
 from h3b import fp8_gemm, ops, plugin, ulysses_exact, ulysses_outq
+from oracle import quant as oq
 from oracle import ulysses as ou
 
 
@@ -27,26 +28,94 @@ def test_exact_forward_matches_reference_outputs(golden, ws):
         assert same_bits(res[r], t16(g[f"ws{ws}_out{r}"]))
 
 
-def test_exact_forward_with_presupplied_sends_and_defer():
+class _Quant:
+    """Stands in for vLLM's QuantFP8 (dynamic, per token): the oracle's quant."""
+    static = False
+    is_group_quant = False
+    use_per_token_if_dynamic = True
+    num_token_padding = None
+
+    def __init__(self):
+        self.calls = 0
+
+    def __call__(self, x, scale=None, scale_ub=None):
+        self.calls += 1
+        return oq.quant(x)
+
+
+def _owner(heads, d):
+    """An attention whose out-projection reaches ``quant_method.fp8_linear.quant_fp8`` (the prepared path)."""
+    from types import SimpleNamespace
+    kernel = SimpleNamespace(quant_fp8=_Quant())
+    layer = SimpleNamespace(tp_size=1, input_size_per_partition=heads * d, quant_method=SimpleNamespace(fp8_linear=kernel))
+    return SimpleNamespace(out_proj=layer, num_heads=heads, head_dim=d), kernel
+
+
+@pytest.fixture
+def outq_cpu(monkeypatch):
+    """The deferral's two kernels on the CPU (the oracle's), and a fresh self-check state."""
+    monkeypatch.setitem(ulysses_outq._kernels, "quant_from_recv", oq.quant_from_recv)
+    monkeypatch.setitem(ulysses_outq._kernels, "unpack_rows", lambda recv: ou.unpack(recv).reshape(recv.shape[1], -1))
+    monkeypatch.setitem(ulysses_outq._state, "checked", False)
+    monkeypatch.setitem(ulysses_outq._state, "disabled", None)
+
+
+def test_exact_forward_with_presupplied_sends_and_defer(outq_cpu):
+    """Mode 2: an armed forward's reverse exchange returns a stride-0 placeholder; the prepared out-projection quant
+    recognises it and quantises the receive buffer (after the first call's self-check), bit-equal to copy 5 + quant."""
     ws, m, heads, d = 2, 4, 4, 8
-    qs = [torch.randn(1, m, heads, d) for _ in range(ws)]
-    ks = [torch.randn(1, m, heads, d) for _ in range(ws)]
-    vs = [torch.randn(1, m, heads, d) for _ in range(ws)]
+    qs = [torch.randn(1, m, heads, d).to(torch.bfloat16) for _ in range(ws)]
+    ks = [torch.randn(1, m, heads, d).to(torch.bfloat16) for _ in range(ws)]
+    vs = [torch.randn(1, m, heads, d).to(torch.bfloat16) for _ in range(ws)]
 
     def body(r, a2a):
+        owner, kernel = _owner(heads, d)
+        prev = ulysses_outq.arm(owner, m)
         sends = [ou.pack(t[r][0], ws) for t in (qs, ks, vs)]
-        res = ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a, sends=sends,
-                                          back="defer")
+        ph = ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a, sends=sends,
+                                         back="defer", unpack_fn=ou.unpack)
         assert sends == []
-        return res
+        assert ulysses_outq.is_placeholder(ph) and ph.shape == (1, m, heads, d)
+        out = kernel.quant_fp8(ph.view(m, heads * d))
+        ulysses_outq.disarm(prev, check=True)
+        return out
 
-    res = ou.run_ranks(body, ws)
+    res = ou.run_ranks(lambda r, a2a: body(r, a2a), ws)
     ref = ou.run_ranks(lambda r, a2a: ulysses_exact.exact_forward(qs[r], ks[r], vs[r], _layout_attn, ws=ws, a2a=a2a,
                                                                   pack=ou.pack, unpack_fn=ou.unpack), ws)
     for r in range(ws):
-        assert isinstance(res[r], ulysses_outq.Deferred)
-        assert res[r].shape == (1, m, heads, d)
-        assert torch.equal(ou.unpack(res[r].recv).view(1, m, heads, d), ref[r])
+        rq, rs = oq.quant(ref[r].reshape(m, heads * d))
+        assert same_bits(res[r][0], rq) and torch.equal(res[r][1], rs)
+    assert ulysses_outq._state["checked"] and ulysses_outq._state["disabled"] is None
+
+
+def test_deferral_guards_and_self_check_failure(outq_cpu, monkeypatch):
+    m, heads, d, ws = 4, 4, 8, 2
+    recv = torch.randn(ws, m, heads // ws, d).to(torch.bfloat16)
+    # not armed: no placeholder (the caller unpacks)
+    assert ulysses_outq.defer(recv, heads) is None
+    owner, kernel = _owner(heads, d)
+    prev = ulysses_outq.arm(owner, m)
+    ph = ulysses_outq.defer(recv, heads)
+    # an armed forward that returns without consuming its deferral raises
+    with pytest.raises(RuntimeError, match="without its out-projection"):
+        ulysses_outq.disarm(prev, check=True)
+    # a placeholder reaching a quant with no pending deferral raises
+    with pytest.raises(RuntimeError, match="placeholder"):
+        kernel.quant_fp8(ph.view(m, heads * d))
+    # a receive-buffer quant that differs from copy 5 + quant disables the path for the process: stock result returned
+    monkeypatch.setitem(ulysses_outq._kernels, "quant_from_recv",
+                        lambda r: (oq.quant_from_recv(r)[0], oq.quant_from_recv(r)[1] * 2))
+    prev = ulysses_outq.arm(owner, m)
+    ph = ulysses_outq.defer(recv, heads)
+    q, s = kernel.quant_fp8(ph.view(m, heads * d))
+    ulysses_outq.disarm(prev, check=True)
+    rq, rs = oq.quant(ou.unpack(recv).reshape(m, -1))
+    assert same_bits(q, rq) and torch.equal(s, rs)
+    assert ulysses_outq._state["disabled"]
+    prev = ulysses_outq.arm(owner, m)
+    assert ulysses_outq.defer(recv, heads) is None
+    ulysses_outq.disarm(prev, check=True)
 
 
 def test_send_shape_and_by_dest_views():
