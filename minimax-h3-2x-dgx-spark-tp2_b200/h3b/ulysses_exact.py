@@ -11,6 +11,9 @@ NVLink (or any injected ``a2a(out, inp, group=)``).
 """
 from __future__ import annotations
 
+import threading
+from dataclasses import dataclass
+
 import torch
 import torch.distributed as dist
 
@@ -19,7 +22,8 @@ from . import ops
 MODES = ("1", "2", "fwd", "verify")
 
 # call counters (h3_tp2/ulysses_exact.py:88 ``stats``) and the two producer hooks (:144, :151)
-_stats = {k: 0 for k in ("pack", "redirect", "fallback", "out_copy", "unpack_hook", "verify_equal", "verify_differs")}
+_stats = {k: 0 for k in ("pack", "redirect", "materialize", "fallback", "out_copy", "unpack_hook", "verify_equal",
+                         "verify_differs")}
 _hooks = {"key": None, "unpack": None}
 
 
@@ -75,12 +79,18 @@ def unpack(send: torch.Tensor) -> torch.Tensor:
 
 def rope_into_send(send_q, send_k, q, k, q_weight, k_weight, rope_table, eps, launch=None) -> None:  # noqa: ANN001
     """The norm+RoPE producer writing straight into the send buffers (h3_tp2/ulysses_exact.py:264): q/k [M, H, d]
-    views of the qkv output -> send_q / send_k [P, M, H/P, d].  ``launch`` (the reference's per-destination launcher
-    argument) is accepted for signature compatibility; one CUDA kernel covers all destinations."""
-    del launch
-    ws = send_q.shape[0]
-    ops.norm_rope_send(q, q_weight, rope_table, eps, ws, out=send_q)
-    ops.norm_rope_send(k, k_weight, rope_table, eps, ws, out=send_k)
+    views of the qkv output -> send_q / send_k [P, M, H/P, d].  Without ``launch`` one CUDA kernel covers all
+    destinations; with it (the reference's launcher ``launch(x_block, weight, rope_table, eps, out)``) it is called
+    once per destination and tensor on that destination's heads."""
+    ws, _, hl, _ = send_q.shape
+    if launch is None:
+        ops.norm_rope_send(q, q_weight, rope_table, eps, ws, out=send_q)
+        ops.norm_rope_send(k, k_weight, rope_table, eps, ws, out=send_k)
+        return
+    for p in range(ws):
+        heads = slice(p * hl, (p + 1) * hl)
+        launch(q[:, heads], q_weight, rope_table, eps, send_q[p])
+        launch(k[:, heads], k_weight, rope_table, eps, send_k[p])
 
 
 def exchange_fwd(send: torch.Tensor, a2a, pg=None) -> torch.Tensor:  # noqa: ANN001
@@ -138,7 +148,6 @@ def exact_forward(query, key, value, run_attn, *, ws, pg=None, a2a=None, sends=N
         return buf
 
     if sends:
-        _stats["redirect"] += 1
         send_q, send_k = sends[0], sends[1]
         send_v = sends[2] if len(sends) > 2 else None
         sends.clear()
@@ -212,6 +221,173 @@ def verify_forward(query, key, value, run_attn, *, ws, pg=None, a2a=None, stock_
     return sres, eq
 
 
+# ---------------------------------------------------------------------------------------------------------------
+# producer redirection: placeholders, pending send buffers, the armed attention forward
+# ---------------------------------------------------------------------------------------------------------------
+
+_SELFCHECK_ROWS = 64   # producer calls of this many rows or fewer (a consumer's self-check) are never redirected
+_tls = threading.local()  # armed: (attention, rows) of the running forward; pending: Pending
+
+
+def _placeholder(like: torch.Tensor) -> torch.Tensor:
+    """A tensor of ``like``'s shape owning one element (every stride 0): nothing may read it."""
+    return like.new_empty(1).as_strided(tuple(like.shape), (0,) * like.ndim)
+
+
+def _is_placeholder(t: torch.Tensor) -> bool:
+    return t.numel() > 1 and all(st == 0 for st in t.stride())
+
+
+@dataclass
+class Pending:
+    """Send buffers a redirected producer filled for the attention that follows (h3_tp2/ulysses_exact.py:320): q and k
+    (and v) [P, M, hl, d] each, the placeholders the model holds for q and k, and the model's v view when the
+    producer wrote v into send_v instead."""
+    sends: list
+    q_ph: torch.Tensor
+    k_ph: torch.Tensor
+    ws: int
+    v_view: torch.Tensor | None = None
+    unpack_fn: object = None   # [P, M, hl, d] -> [M, H, d]; default: the unpack kernel
+
+    def matches(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> bool:
+        ok = (query.ndim == 4 and query.data_ptr() == self.q_ph.data_ptr() and key.data_ptr() == self.k_ph.data_ptr()
+              and tuple(query.shape[1:]) == tuple(self.q_ph.shape))
+        if ok and self.v_view is not None:
+            ok = (value.ndim == 4 and value.data_ptr() == self.v_view.data_ptr()
+                  and tuple(value.shape[1:]) == tuple(self.v_view.shape) and value[0].stride() == self.v_view.stride())
+        return ok
+
+    def materialize(self):  # noqa: ANN201
+        """The real q, k [1, M, H, d] (and v written into the model's view) for a stock fallback."""
+        _stats["materialize"] += 1
+        un = self.unpack_fn or unpack
+        q, k = un(self.sends[0]).unsqueeze(0), un(self.sends[1]).unsqueeze(0)
+        if self.v_view is not None:
+            self.v_view.copy_(un(self.sends[2]))
+        self.sends = []
+        return q, k
+
+
+def take_pending(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> Pending | None:
+    """This thread's pending send buffers if q/k are their placeholders (consumed), else None; placeholder q/k without
+    their buffers raise (h3_tp2/ulysses_exact.py:348)."""
+    pend = getattr(_tls, "pending", None)
+    if pend is not None and pend.matches(query, key, value):
+        _tls.pending = None
+        return pend
+    if _is_placeholder(query) or _is_placeholder(key):
+        raise RuntimeError("h3b ulysses exact: placeholder q/k reached attention without their send buffers")
+    return None
+
+
+def _take_arm(rows: int):  # noqa: ANN202
+    """The attention whose forward is running, once, if ``rows`` is its row count (not a self-check sub-call) and it
+    has no VSA gate (h3_tp2/ulysses_exact.py:358)."""
+    arm = getattr(_tls, "armed", None)
+    if arm is None or rows != arm[1] or rows <= _SELFCHECK_ROWS:
+        return None
+    _tls.armed = None
+    owner = arm[0]
+    return owner if getattr(owner, "to_gate_compress", None) is None else None
+
+
+def make_armed_forward(orig_fwd, outq: bool = False):  # noqa: ANN001,ANN201
+    """Wrap the model attention's ``forward(self, x, ...)`` so the producers know which attention their q/k feed and,
+    with ``outq``, so its reverse exchange may leave copy 5 to its out-projection quant (h3_tp2/ulysses_exact.py:376)."""
+
+    def forward(self, x, *a, **kw):  # noqa: ANN001,ANN202
+        prev = getattr(_tls, "armed", None)
+        rows = int(x.shape[0]) if hasattr(x, "shape") and x.ndim >= 1 else -1
+        _tls.armed = (self, rows)
+        if outq:
+            from . import ulysses_outq  # noqa: PLC0415
+            oprev = ulysses_outq.arm(self, rows)
+        done = False
+        try:
+            out = orig_fwd(self, x, *a, **kw)
+            done = True
+            return out
+        finally:
+            _tls.armed = prev
+            _tls.pending = None    # send buffers never outlive the forward that made them
+            if outq:
+                ulysses_outq.disarm(oprev, check=done)
+
+    forward._h3b_exact_armed = True
+    return forward
+
+
+def rope_supported(q: torch.Tensor, k: torch.Tensor, rope_table: torch.Tensor, interleaved: bool) -> bool:
+    """What the norm+RoPE send kernel takes: bf16 q/k [M, H, 128] with unit head-dim stride, half-split (not
+    interleaved) rotation over a width that is a multiple of 8 and at most 128, on the GPU."""
+    return (not interleaved and q.is_cuda and q.dtype == k.dtype == torch.bfloat16 and q.shape[-1] == 128
+            and q.stride(-1) == 1 and k.stride(-1) == 1 and rope_table.shape[-1] % 8 == 0
+            and rope_table.shape[-1] <= 128)
+
+
+def make_rope(orig, strategy_info, launch=None, supported=None, *, unpack_fn=None):  # noqa: ANN001,ANN201
+    """Wrap the transformer's ``fused_qk_norm_rope(q, k, q_weight, k_weight, rope_table, eps, *, head_dim,
+    rotary_dim, interleaved)`` (h3_tp2/ulysses_exact.py:403): inside an armed attention forward whose attention will run
+    strict Ulysses, q and k are normalised, rotated and written per destination into fresh send buffers and
+    placeholders are returned; any other call runs ``orig``.  ``launch`` / ``supported``: a per-destination launcher and
+    its guard (default: the send kernel and ``rope_supported``); ``unpack_fn`` for a fallback's materialisation."""
+    supported = supported or rope_supported
+
+    def fused_qk_norm_rope(q, k, q_weight, k_weight, rope_table, eps, *, head_dim=None, rotary_dim=None,  # noqa: ANN001,ANN202
+                           interleaved=False):
+        owner = _take_arm(int(q.shape[0])) if q.ndim == 3 else None
+        info = strategy_info(owner.attention, None) if owner is not None else None
+        if (info is None or q.shape != k.shape or head_dim not in (None, q.shape[-1])
+                or rotary_dim not in (None, rope_table.shape[-1])
+                or rope_table.shape != (q.shape[0], rope_table.shape[-1])
+                or not eligible_shape(q.unsqueeze(0), k.unsqueeze(0), k.unsqueeze(0), info[1])
+                or not supported(q, k, rope_table, interleaved)):
+            return orig(q, k, q_weight, k_weight, rope_table, eps, head_dim=head_dim, rotary_dim=rotary_dim,
+                        interleaved=interleaved)
+        ws = info[1]
+        m, heads, d = q.shape
+        sends = [torch.empty(send_shape(m, heads, d, ws), dtype=q.dtype, device=q.device) for _ in range(2)]
+        rope_into_send(sends[0], sends[1], q, k, q_weight.contiguous(), k_weight.contiguous(),
+                       rope_table.contiguous(), eps, launch)
+        _tls.pending = Pending(sends=sends, q_ph=_placeholder(q), k_ph=_placeholder(k), ws=ws, unpack_fn=unpack_fn)
+        _stats["redirect"] += 1
+        return _tls.pending.q_ph, _tls.pending.k_ph
+
+    fused_qk_norm_rope._h3b_exact = True
+    return fused_qk_norm_rope
+
+
+def make_fused_producer(orig, fc, strategy_info, *, unpack_fn=None):  # noqa: ANN001,ANN201
+    """Wrap ``fp8_consumers.qk_norm_rope_fused(st, num_heads, num_kv_heads, head_dim, q_weight, k_weight, rope_table,
+    eps)`` (h3_tp2/ulysses_exact.py:433): inside an armed forward the qkv GEMM with the norm + RoPE epilogue writes q, k
+    and v per destination (``fc.qkv_into_send``), placeholders stand for q and k and the model's v view of the stash's
+    placeholder is returned unwritten; any other call runs ``orig``."""
+
+    def qk_norm_rope_fused(st, num_heads, num_kv_heads, head_dim, q_weight, k_weight, rope_table, eps):  # noqa: ANN001,ANN202
+        t = int(st.a.shape[0])
+        owner = _take_arm(t)
+        info = strategy_info(owner.attention, None) if owner is not None else None
+        hd = num_heads * head_dim
+        if (info is None or num_kv_heads != num_heads or num_heads % info[1] != 0 or head_dim != 128
+                or st.bias is not None or st.ph is None or st.ph.dim() != 2 or st.ph.shape != (t, 3 * hd)
+                or not st.ph.is_contiguous()):
+            return orig(st, num_heads, num_kv_heads, head_dim, q_weight, k_weight, rope_table, eps)
+        ws = info[1]
+        sends = list(fc.qkv_into_send(st, num_heads, ws, q_weight.contiguous(), k_weight.contiguous(),
+                                      rope_table.contiguous(), eps))
+        like = st.ph[:, :hd].view(t, num_heads, head_dim)
+        v_view = st.ph[:, 2 * hd:].view(t, num_kv_heads, head_dim)   # the model's v view (left unwritten)
+        pend = Pending(sends=sends, q_ph=_placeholder(like), k_ph=_placeholder(like), ws=ws, v_view=v_view,
+                       unpack_fn=unpack_fn)
+        _tls.pending = pend
+        _stats["redirect"] += 1
+        return pend.q_ph, pend.k_ph, v_view
+
+    qk_norm_rope_fused._h3b_exact = True
+    return qk_norm_rope_fused
+
+
 def eligible_shape(query, key, value, ws: int) -> bool:  # noqa: ANN001
     """Strict Ulysses eligibility (h3_tp2/ulysses_exact.py:367-373)."""
     if query.ndim != 4 or key.shape != query.shape or value.shape != query.shape:
@@ -229,26 +405,66 @@ def local_attention(q, k, v, attn_metadata=None):  # noqa: ANN001,ANN201
     return ops.flash_attn(q, k, v, valid_kv=valid)
 
 
-def make_forward_impl(orig, mode: str, strategy_info, *, a2a=None):  # noqa: ANN001,ANN201
+def make_forward_impl(orig, mode: str, strategy_info, *, a2a=None, stock_fwd=None, stock_back=None, on_first=None,  # noqa: ANN001,ANN201
+                      attn=None, pack=None, unpack_fn=None):
     """Wrap ``Attention._forward_impl(self, query, key, value, attn_metadata=None)`` (h3_tp2/ulysses_exact.py:472):
-    eligible strict-Ulysses calls run ``exact_forward`` with the B200 attention; anything else runs ``orig``."""
+    eligible strict-Ulysses calls run ``exact_forward`` (on the send buffers a redirected producer filled, when q/k are
+    its placeholders) with the B200 attention; a placeholder call that is not eligible is materialised and, like
+    anything else, runs ``orig``.  ``on_first()`` runs once, on the first call (attaches the producer hooks).
+    ``attn(q, k, v, attn_metadata)`` (default ``local_attention``), ``pack`` / ``unpack_fn``: as in
+    ``exact_forward``."""
     if mode not in MODES:
         raise ValueError(f"H3_TP2_ULYSSES_EXACT must be one of {MODES}, got {mode!r}")
+    attn = attn or local_attention
+    hooked = {"done": False}
 
     def _forward_impl(self, query, key, value, attn_metadata=None):  # noqa: ANN001
+        if on_first is not None and not hooked["done"]:
+            hooked["done"] = True
+            on_first()
+        pend = take_pending(query, key, value)
         info = strategy_info(self, attn_metadata)
-        if info is None or not eligible_shape(query, key, value, info[1]):
+        ok = info is not None and eligible_shape(query, key, value, info[1])  # placeholders carry the real shape
+        if pend is not None and (not ok or pend.ws != info[1]):
+            query, key = pend.materialize()
+            pend = None
+        if not ok:
             _stats["fallback"] += 1
             return orig(self, query, key, value, attn_metadata)
         pg, ws = info
-        attn = lambda q, k, v: local_attention(q, k, v, attn_metadata)  # noqa: E731
+
+        def run(q, k, v):  # noqa: ANN001,ANN202
+            return attn(q, k, v, attn_metadata)
+
         if mode == "verify":   # both exchanges on the same tensors; the stock result is returned
-            res, _ = verify_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a)
+            res, _ = verify_forward(query, key, value, run, ws=ws, pg=pg, a2a=a2a, stock_fwd=stock_fwd,
+                                    stock_back=stock_back, pack=pack, unpack_fn=unpack_fn)
             return res
-        back = {"2": "defer", "fwd": "exact"}.get(mode, "exact")
-        return exact_forward(query, key, value, attn, ws=ws, pg=pg, a2a=a2a, back=back)
+        sends = None
+        if pend is not None:
+            sends, pend.sends = pend.sends, []
+        back = {"fwd": "stock", "2": "defer"}.get(mode, "exact")
+        sb = stock_back or (lambda t: _stock_a2a_4d(t, 1, 2, pg))
+        return exact_forward(query, key, value, run, ws=ws, pg=pg, a2a=a2a, sends=sends, back=back, stock_back=sb,
+                             pack=pack, unpack_fn=unpack_fn)
 
     return _forward_impl
+
+
+def _hook_producers(strategy_info, mode: str = "1") -> None:  # noqa: ANN001
+    """Attach the arming wrapper and the producer hook to vLLM-Omni's MiniMax H3 model (the first wrapped attention
+    call does this; h3_tp2/ulysses_exact.py:521)."""
+    from vllm_omni.diffusion.models.minimax_h3 import minimax_h3_transformer as tr  # noqa: PLC0415
+
+    att_cls = tr.MiniMaxH3Attention
+    if not getattr(att_cls.forward, "_h3b_exact_armed", False):
+        att_cls.forward = make_armed_forward(att_cls.forward, outq=mode == "2")
+    if getattr(tr.fused_qk_norm_rope, "_h3b_consumer_fuse", False):
+        from . import fp8_consumers as fc  # noqa: PLC0415
+        if not getattr(fc.qk_norm_rope_fused, "_h3b_exact", False):
+            fc.qk_norm_rope_fused = make_fused_producer(fc.qk_norm_rope_fused, fc, strategy_info)
+    elif not getattr(tr.fused_qk_norm_rope, "_h3b_exact", False):
+        tr.fused_qk_norm_rope = make_rope(tr.fused_qk_norm_rope, strategy_info)
 
 
 def install(mode: str = "1") -> None:
@@ -265,5 +481,6 @@ def install(mode: str = "1") -> None:
         if prev != mode:
             raise RuntimeError(f"h3b ulysses exact already installed with mode {prev}, cannot change to {mode}")
         return
-    cls._forward_impl = make_forward_impl(cls._forward_impl, mode, vllm_strategy_info)
+    hook = None if mode == "verify" else (lambda: _hook_producers(vllm_strategy_info, mode))  # verify: stock producers
+    cls._forward_impl = make_forward_impl(cls._forward_impl, mode, vllm_strategy_info, on_first=hook)
     cls._h3b_exact = mode
