@@ -36,7 +36,7 @@ def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
 def plan(env: dict | None = None) -> dict:
     """The patches ``_apply`` would install for an environment (pure; used by tests)."""
     env = os.environ if env is None else env
-    out = {"ulysses": None, "fp8_gemm": None, "quant_fuse": None, "overlap": None, "nocopy": None,
+    out = {"ulysses": None, "fp8_gemm": None, "swiglu": 0, "quant_fuse": None, "overlap": None, "nocopy": None,
            "a2a_timing": False}
     # the reference's precedence (h3_tp2/plugin.py:278-308): the combined exchange only when forced (it runs the
     # overlap's head groups itself), else the exact exchange (default "2"; replaces the overlap when both are set),
@@ -53,6 +53,10 @@ def plan(env: dict | None = None) -> dict:
     level = env.get("H3_TP2_FP8_GEMM", "cutlass").strip().lower()
     if level not in ("", "0", "off"):
         out["fp8_gemm"] = level
+        # the fused SwiGLU MLP rides on the FP8 GEMM dispatcher (h3_tp2/plugin.py:461-469): level 1 by default, 2 also
+        # quantises the SwiGLU output for fc2
+        sw = env.get("H3_TP2_FP8_FUSE_SWIGLU", "1").strip()
+        out["swiglu"] = int(sw) if sw in ("1", "2") else 0
     fuse = env.get("H3_TP2_FP8_QUANT_FUSE", "1").strip().lower()
     if fuse not in ("", "0", "off"):
         out["quant_fuse"] = fuse
@@ -78,6 +82,18 @@ def _apply(role: str) -> None:
     if p["fp8_gemm"]:
         from . import fp8_gemm  # noqa: PLC0415
         fp8_gemm.install(p["fp8_gemm"])
+        if p["swiglu"]:
+            from . import fp8_swiglu  # noqa: PLC0415
+            fp8_swiglu.install(level=p["swiglu"])
+    if p["quant_fuse"]:
+        from . import fp8_quant_fuse  # noqa: PLC0415
+        sites = fp8_quant_fuse.parse_sites(p["quant_fuse"])
+        try:
+            done = fp8_quant_fuse.install(sites, explicit=fp8_quant_fuse.is_explicit(p["quant_fuse"]))
+        except Exception:  # noqa: BLE001  (a failing optional fusion keeps the stock quant, as the reference does)
+            logger.warning("h3b plugin: FP8 quant fuse install failed; separate quant kernels", exc_info=True)
+            done = []
+        logger.warning("h3b plugin: FP8 quant fuse sites installed: %s", ", ".join(done) or "none")
 
 
 def register() -> None:

@@ -135,6 +135,10 @@ def test_eligibility():
 def test_plugin_plan_defaults_and_switches():
     p = plugin.plan({})
     assert p["ulysses"] == "2" and p["fp8_gemm"] == "cutlass" and p["overlap"] is None
+    assert p["swiglu"] == 1 and p["quant_fuse"] == "1"
+    assert plugin.plan({"H3_TP2_FP8_FUSE_SWIGLU": "2"})["swiglu"] == 2
+    assert plugin.plan({"H3_TP2_FP8_FUSE_SWIGLU": "0"})["swiglu"] == 0
+    assert plugin.plan({"H3_TP2_FP8_GEMM": "0"})["swiglu"] == 0      # the MLP fusion rides on the GEMM dispatcher
     p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_FP8_GEMM": "0", "H3_TP2_A2A_TIMING": "1"})
     assert p["ulysses"] == "2" and p["overlap"] is None and p["fp8_gemm"] is None and p["a2a_timing"]  # exact wins
     p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_ULYSSES_EXACT": "0"})
