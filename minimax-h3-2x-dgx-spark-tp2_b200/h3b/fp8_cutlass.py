@@ -8,6 +8,7 @@ that is not bf16).
 """
 from __future__ import annotations
 
+import functools
 import logging
 import threading
 
@@ -63,18 +64,48 @@ def route(a, b, scale_a, scale_b, out_dtype, bias):  # noqa: ANN001,ANN201
 
 
 def block_want(block, sites=SITES) -> dict:  # noqa: ANN001
-    """{(weight data_ptr, weight.t() shape): site} for the block's quantised linears (h3_tp2/fp8_cutlass.py:252);
-    ``block`` exposes ``to_qkv`` / ``to_out`` / ``fc1`` style linears with a ``weight`` of shape [N, K]."""
-    names = {"qkv": ("to_qkv", "qkv"), "out": ("to_out", "out_proj", "o_proj"), "fc1": ("fc1", "w13", "gate_up_proj")}
+    """{(weight data_ptr, weight shape): site} for the DiT block's FP8 qkv / out / fc1 weights (h3_tp2/fp8_cutlass.py:252):
+    ``block.attn.qkv_proj``, ``block.attn.out_proj``, ``block.mlp.fc1``, whose e4m3 weight is stored [K, N] (the
+    dispatcher's ``b``)."""
+    attn, mlp = getattr(block, "attn", None), getattr(block, "mlp", None)
+    layers = {"qkv": getattr(attn, "qkv_proj", None), "out": getattr(attn, "out_proj", None),
+              "fc1": getattr(mlp, "fc1", None)}
     want = {}
     for site in sites:
-        for n in names[site]:
-            lin = getattr(block, n, None)
-            w = getattr(lin, "weight", None)
-            if w is not None:
-                want[(w.data_ptr(), tuple(w.t().shape))] = site
-                break
+        w = getattr(layers.get(site), "weight", None)
+        if isinstance(w, torch.Tensor) and w.dtype == torch.float8_e4m3fn and w.dim() == 2:
+            want[(w.data_ptr(), tuple(w.shape))] = site
     return want
+
+
+def make_block_forward(orig_forward, sites=SITES):  # noqa: ANN001,ANN201
+    """The DiT block's forward with the router told the block's weights for its duration (h3_tp2/fp8_cutlass.py:266)."""
+    @functools.wraps(orig_forward)
+    def forward(self, *args, **kwargs):  # noqa: ANN001,ANN202
+        compiling = getattr(getattr(torch, "compiler", None), "is_compiling", None)
+        if compiling is not None and compiling():
+            return orig_forward(self, *args, **kwargs)
+        prev = getattr(_tls, "want", None)
+        _tls.want = block_want(self, sites)
+        try:
+            return orig_forward(self, *args, **kwargs)
+        finally:
+            _tls.want = prev
+
+    forward._h3b_cutlass = True
+    return forward
+
+
+def install_sites(tr=None, sites=SITES) -> bool:  # noqa: ANN001
+    """Wrap ``MiniMaxH3DiTBlock.forward`` of the transformer module ``tr`` (default: vLLM-Omni's MiniMax H3) and register
+    the router with the FP8 dispatcher (h3_tp2/fp8_cutlass.py:285)."""
+    if tr is None:
+        from vllm_omni.diffusion.models.minimax_h3 import minimax_h3_transformer as tr  # noqa: PLC0415
+    cls = tr.MiniMaxH3DiTBlock
+    if not getattr(cls.forward, "_h3b_cutlass", False):
+        cls.forward = make_block_forward(cls.forward, sites)
+    fp8_gemm.set_router(route)
+    return True
 
 
 def selfcheck(gemm: DslGemm | None = None, device="cuda") -> list[str]:  # noqa: ANN001

@@ -82,6 +82,13 @@ def _apply(role: str) -> None:
     if p["fp8_gemm"]:
         from . import fp8_gemm  # noqa: PLC0415
         fp8_gemm.install(p["fp8_gemm"])
+        if p["fp8_gemm"] == "cutlass":   # the block's qkv / out / fc1 GEMMs routed by weight (h3_tp2/plugin.py:446-456)
+            from . import fp8_cutlass  # noqa: PLC0415
+            try:
+                fp8_cutlass.install_sites()
+            except Exception:  # noqa: BLE001  (the dispatcher's own path stays)
+                logger.warning("h3b plugin: FP8 GEMM block wiring failed; the dispatcher's path", exc_info=True)
+                fp8_gemm._routers.clear()
         if p["swiglu"]:
             from . import fp8_swiglu  # noqa: PLC0415
             fp8_swiglu.install(level=p["swiglu"])

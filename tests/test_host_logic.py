@@ -293,3 +293,24 @@ def test_verify_forward_compares_with_the_stock_exchange():
         assert res.shape == (1, m, heads, d)
     for _, eq in ou.run_ranks(lambda r, a2a: body(r, a2a, skew=1.0), ws):
         assert eq["q"] and eq["attn"] and not eq["result"]
+
+
+def test_cutlass_block_wiring_registers_the_running_block_weights(monkeypatch):
+    """fp8_cutlass: inside a wrapped DiT block forward the router knows the block's qkv / out / fc1 weights by pointer
+    and shape ([K, N] as vLLM stores them); outside it nothing is routed (h3_tp2/fp8_cutlass.py:252-294)."""
+    from types import SimpleNamespace
+    from h3b import fp8_cutlass
+    lin = lambda k, n: SimpleNamespace(weight=torch.zeros(k, n, dtype=torch.float8_e4m3fn))  # noqa: E731
+    block = SimpleNamespace(attn=SimpleNamespace(qkv_proj=lin(32, 96), out_proj=lin(32, 32)),
+                            mlp=SimpleNamespace(fc1=lin(32, 128)))
+    want = fp8_cutlass.block_want(block)
+    assert sorted(want.values()) == ["fc1", "out", "qkv"]
+    assert want[(block.attn.qkv_proj.weight.data_ptr(), (32, 96))] == "qkv"
+    seen = []
+    fwd = fp8_cutlass.make_block_forward(lambda self, x: seen.append(dict(fp8_cutlass._tls.want)) or x)
+    assert fwd(block, 7) == 7 and seen == [want]
+    assert getattr(fp8_cutlass._tls, "want", None) is None
+    tr = SimpleNamespace(MiniMaxH3DiTBlock=type("Block", (), {"forward": lambda self, x: x}))
+    monkeypatch.setattr(fp8_gemm, "_routers", [])
+    assert fp8_cutlass.install_sites(tr) and tr.MiniMaxH3DiTBlock.forward._h3b_cutlass
+    assert fp8_gemm._routers == [fp8_cutlass.route]
