@@ -476,6 +476,8 @@ def install(mode: str = "1") -> None:
     from .plugin import vllm_strategy_info  # noqa: PLC0415
     mode = mode.strip().lower()
     cls = layer_mod.Attention
+    if getattr(cls, "_h3b_overlap", 0) or getattr(cls, "_h3b_nocopy", 0):
+        raise RuntimeError("h3b: a grouped Ulysses exchange (overlap or nocopy) is installed; exact replaces it")
     prev = getattr(cls, "_h3b_exact", None)
     if prev:
         if prev != mode:
