@@ -56,11 +56,88 @@ def _bias(bias: torch.Tensor | None, n: int, what: str) -> torch.Tensor | None:
     return bias.reshape(-1).contiguous()
 
 
+def _out(out: torch.Tensor | None, shape: tuple[int, ...], dtype: torch.dtype, like: torch.Tensor, what: str, *,
+         dense: bool = True) -> torch.Tensor:
+    """A fresh output, or the caller's checked against the shape, dtype and device the kernel writes (``dense``: also
+    contiguous; the kernels take a base pointer and write the whole extent)."""
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=like.device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or out.device != like.device or (
+            dense and not out.is_contiguous()):
+        raise ValueError(f"{what}: out must be {'contiguous ' if dense else ''}{tuple(shape)} {dtype} on "
+                         f"{like.device}, got {tuple(out.shape)} {out.dtype} on {out.device}")
+    return out
+
+
+def _norm_rope_args(weights, table: torch.Tensor, m: int, what: str):  # noqa: ANN001,ANN202
+    """Norm weights (128 bf16 values each) and the RoPE table [>= m, R] as fp32 with unit column stride: the kernels
+    read 128 weights and table rows 0 .. m-1."""
+    out = []
+    for wt in weights:
+        _need_cuda(wt)
+        _dt(wt, torch.bfloat16, what=f"{what} norm weight")
+        if wt.numel() != 128:
+            raise ValueError(f"{what}: norm weight has {wt.numel()} values, expected 128 (head_dim)")
+        out.append(wt.reshape(-1).contiguous())
+    _need_cuda(table)
+    if table.dim() != 2 or table.shape[0] < m or table.shape[1] > 128:
+        raise ValueError(f"{what}: rope table must be [>= {m}, R <= 128], got {tuple(table.shape)}")
+    table = table.float()
+    if table.stride(-1) != 1:
+        table = table.contiguous()
+    return out, table
+
+
+def _rows(t: torch.Tensor, rows: int, cols: int, what: str, dtype: torch.dtype = torch.bfloat16) -> None:
+    """A [rows, cols] input of ``dtype`` with unit column stride (the row kernels take a base pointer and a row
+    stride)."""
+    _dt(t, dtype, what=what)
+    if t.dim() != 2 or tuple(t.shape) != (rows, cols) or (t.numel() and t.stride(1) != 1):
+        raise ValueError(f"{what}: must be [{rows}, {cols}] with unit column stride, got {tuple(t.shape)}")
+
+
+def _weight(weight: torch.Tensor, n: int, what: str) -> torch.Tensor:
+    _dt(weight, torch.bfloat16, what=f"{what} weight")
+    if weight.numel() != n:
+        raise ValueError(f"{what}: weight has {weight.numel()} values, expected {n}")
+    return weight.reshape(-1).contiguous()
+
+
+def _modulation(shift, scale, indices, rows: int, hidden: int, what: str, gate=None):  # noqa: ANN001,ANN202
+    """AdaLN rows read as row ``indices[r]`` (row 0 without indices) of shift / scale (and gate): each [B, hidden] bf16
+    ([B, 1, hidden] is viewed as [B, hidden]) with unit column stride; index values are the caller's contract, as in
+    the reference's kernels.  Returns (shift, scale, gate, indices) as the kernels take them."""
+    if (shift is None) != (scale is None):
+        raise ValueError(f"{what}: shift and scale go together")
+    out = []
+    for name, t in (("shift", shift), ("scale", scale), ("gate", gate)):
+        if t is not None:
+            _dt(t, torch.bfloat16, what=f"{what} {name}")
+            if t.dim() == 3 and t.shape[1] == 1:
+                t = t[:, 0]
+            if t.dim() != 2 or t.shape[1] != hidden or t.shape[0] < 1 or t.stride(1) != 1:
+                raise ValueError(f"{what}: {name} must be [B >= 1, {hidden}] with unit column stride, got "
+                                 f"{tuple(t.shape)}")
+        out.append(t)
+    if indices is not None:
+        if indices.dtype.is_floating_point or indices.dtype == torch.bool or indices.numel() != rows:
+            raise ValueError(f"{what}: indices must be {rows} integers, got {indices.numel()} {indices.dtype}")
+        indices = indices.reshape(-1).to(torch.int64).contiguous()
+    return (*out, indices)
+
+
+def _span(t: torch.Tensor) -> int:
+    """Elements reachable from ``t``'s data pointer through its shape and (non-negative) strides."""
+    return 0 if t.numel() == 0 else 1 + sum((n - 1) * st for n, st in zip(t.shape, t.stride()))
+
+
 def vec_scales(scale_a: torch.Tensor, scale_b: torch.Tensor, M: int, N: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row / per-column fp32 scale vectors (a scalar scale is broadcast), as fp8_gemm._vec_scales
     (h3_tp2/fp8_gemm.py:228-236)."""
     sa = scale_a.reshape(-1).float()
     sb = scale_b.reshape(-1).float()
+    if sa.numel() not in (1, M) or sb.numel() not in (1, N):
+        raise ValueError(f"scales: {sa.numel()} row and {sb.numel()} column scales for [{M}, {N}] (1 or one each)")
     if sa.numel() == 1:
         sa = sa.expand(M)
     if sb.numel() == 1:
@@ -79,6 +156,11 @@ def quant_rows(base: torch.Tensor, m: int, p: int, seg: int, stride_p: int, stri
     (element offsets from ``base``'s data pointer).  Returns (q [m, p*seg] e4m3, scale [m, 1] fp32)."""
     _need_cuda(base)
     _dt(base, torch.bfloat16, what="quant_rows")
+    if m < 0 or p < 1 or seg < 0 or stride_p < 0 or stride_m < 0 or any(st < 0 for st in base.stride()):
+        raise ValueError(f"quant_rows: m {m} p {p} seg {seg} strides {stride_p}, {stride_m}")
+    if m and seg and (p - 1) * stride_p + (m - 1) * stride_m + seg > _span(base):
+        raise ValueError(f"quant_rows: rows reach element {(p - 1) * stride_p + (m - 1) * stride_m + seg} of a base "
+                         f"that spans {_span(base)}")
     q = torch.empty((m, p * seg), dtype=E4M3, device=base.device)
     s = torch.empty((m, 1), dtype=torch.float32, device=base.device)
     if m:
@@ -110,12 +192,17 @@ def rms_quant(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor | None 
               ph: torch.Tensor | None = None, *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
     """RMSNorm (+ AdaLN modulation) + per-token quant (``fp8_quant_fuse.rms_quant``, h3_tp2/fp8_quant_fuse.py:330)."""
     _need_cuda(x, weight, shift, scale, indices, ph)
+    if x.dim() != 2:
+        raise ValueError("rms_quant: x must be [rows, hidden]")
     rows, hidden = x.shape
+    _rows(x, rows, hidden, "rms_quant x")
+    weight = _weight(weight, hidden, "rms_quant")
+    shift, scale, _, indices = _modulation(shift, scale, indices, rows, hidden, "rms_quant")
+    if ph is not None:
+        _out(ph, (rows, hidden), torch.bfloat16, x, "rms_quant placeholder")
     q = torch.empty((rows, hidden), dtype=E4M3, device=x.device)
     s = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
-    if indices is not None:
-        indices = indices.to(torch.int64).contiguous()
-    _lib.call("h3b_rms_quant_e4m3", x.data_ptr(), rows, hidden, x.stride(0), weight.contiguous().data_ptr(),
+    _lib.call("h3b_rms_quant_e4m3", x.data_ptr(), rows, hidden, x.stride(0), weight.data_ptr(),
               _ptr(shift), shift.stride(0) if shift is not None else 0, _ptr(scale),
               scale.stride(0) if scale is not None else 0, _ptr(indices), float(eps), _ptr(ph), q.data_ptr(),
               s.data_ptr(), div_mode, _stream(x))
@@ -128,14 +215,20 @@ def gate_rms_quant(residual: torch.Tensor, gate: torch.Tensor, branch: torch.Ten
     """Gated residual + RMSNorm + modulation + quant (``fp8_quant_fuse.gate_rms_quant``,
     h3_tp2/fp8_quant_fuse.py:350).  Returns (residual_out bf16, q e4m3, scale [M, 1])."""
     _need_cuda(residual, gate, branch, weight, shift, scale, indices)
+    if residual.dim() != 2:
+        raise ValueError("gate_rms_quant: residual must be [rows, hidden]")
     rows, hidden = residual.shape
+    _rows(residual, rows, hidden, "gate_rms_quant residual")
+    _rows(branch, rows, hidden, "gate_rms_quant branch")
+    weight = _weight(weight, hidden, "gate_rms_quant")
+    if gate is None:
+        raise ValueError("gate_rms_quant: gate is required")
+    shift, scale, gate, indices = _modulation(shift, scale, indices, rows, hidden, "gate_rms_quant", gate=gate)
     res_out = torch.empty((rows, hidden), dtype=torch.bfloat16, device=residual.device)
     q = torch.empty((rows, hidden), dtype=E4M3, device=residual.device)
     s = torch.empty((rows, 1), dtype=torch.float32, device=residual.device)
-    if indices is not None:
-        indices = indices.to(torch.int64).contiguous()
     _lib.call("h3b_gate_rms_quant_e4m3", residual.data_ptr(), residual.stride(0), gate.data_ptr(), gate.stride(0),
-              branch.data_ptr(), branch.stride(0), weight.contiguous().data_ptr(), _ptr(shift),
+              branch.data_ptr(), branch.stride(0), weight.data_ptr(), _ptr(shift),
               shift.stride(0) if shift is not None else 0, _ptr(scale), scale.stride(0) if scale is not None else 0,
               _ptr(indices), rows, hidden, float(eps), res_out.data_ptr(), q.data_ptr(), s.data_ptr(), div_mode,
               _stream(residual))
@@ -145,7 +238,10 @@ def gate_rms_quant(residual: torch.Tensor, gate: torch.Tensor, branch: torch.Ten
 def silu_mul_quant(x: torch.Tensor, *, div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
     """silu_and_mul on bf16 [M, 2d] + per-token quant (``fp8_quant_fuse.silu_mul_quant``, :392)."""
     _need_cuda(x)
+    if x.dim() != 2 or x.shape[1] % 2:
+        raise ValueError(f"silu_mul_quant: x must be [rows, 2d], got {tuple(x.shape)}")
     rows, width = x.shape
+    _rows(x, rows, width, "silu_mul_quant x")
     d = width // 2
     q = torch.empty((rows, d), dtype=E4M3, device=x.device)
     s = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
@@ -158,6 +254,7 @@ def scale_bias_cast(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias:
                     out_dtype: torch.dtype) -> torch.Tensor:
     """The two-pass path's scale pass (``fp8_gemm._scale_bias_cast``, h3_tp2/fp8_gemm.py:38)."""
     _need_cuda(x32, sa, sb, bias)
+    _dt(x32, torch.float32, what="scale_bias_cast x32")
     M, N = x32.shape
     sa, sb = vec_scales(sa, sb, M, N)
     bias = _bias(bias, N, "scale_bias_cast")
@@ -172,6 +269,9 @@ def scale_bias_cast(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias:
 def scale_swiglu(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
     """``fp8_swiglu.scale_swiglu`` (h3_tp2/fp8_swiglu.py:180): fp32 fc1 product -> bf16 SwiGLU [M, half]."""
     _need_cuda(x32, sa, sb, bias)
+    _dt(x32, torch.float32, what="scale_swiglu x32")
+    if x32.dim() != 2 or x32.shape[1] % 2:
+        raise ValueError(f"scale_swiglu: x32 must be [M, 2 * half], got {tuple(x32.shape)}")
     M, width = x32.shape
     half = width // 2
     sa, sb = vec_scales(sa, sb, M, width)
@@ -186,6 +286,9 @@ def scale_swiglu_quant(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bi
                        div_mode: int = DIV_IEEE) -> tuple[torch.Tensor, torch.Tensor]:
     """``fp8_swiglu.scale_swiglu_quant`` (h3_tp2/fp8_swiglu.py:191): SwiGLU + per-token quant for fc2."""
     _need_cuda(x32, sa, sb, bias)
+    _dt(x32, torch.float32, what="scale_swiglu x32")
+    if x32.dim() != 2 or x32.shape[1] % 2:
+        raise ValueError(f"scale_swiglu: x32 must be [M, 2 * half], got {tuple(x32.shape)}")
     M, width = x32.shape
     half = width // 2
     sa, sb = vec_scales(sa, sb, M, width)
@@ -318,9 +421,7 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
     desc = _lib.QkvSend()
     if interleaved:
         ishape = (groups, ws, M, 3, heads // (ws * groups), 128)
-        buf = sends if sends is not None else torch.empty(ishape, dtype=torch.bfloat16, device=a.device)
-        if tuple(buf.shape) != ishape or not buf.is_contiguous():
-            raise ValueError(f"fp8_gemm_qkv_send: interleaved send buffer must be contiguous {ishape}")
+        buf = _out(sends, ishape, torch.bfloat16, a, "fp8_gemm_qkv_send interleaved send buffer")
         desc.send[0] = buf.data_ptr()
         desc.qkv_interleaved = 1
         result = buf
@@ -328,20 +429,20 @@ def fp8_gemm_qkv_send(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: to
         if sends is None:
             sends = [torch.empty(shape, dtype=torch.bfloat16, device=a.device) for _ in range(2)]
             sends.append(torch.empty(shape, dtype=torch.float16 if v_f16 else torch.bfloat16, device=a.device))
+        if len(sends) != 3:
+            raise ValueError("fp8_gemm_qkv_send: three send buffers (q, k, v)")
         for i in range(3):
-            if tuple(sends[i].shape) != shape or not sends[i].is_contiguous():
-                raise ValueError(f"fp8_gemm_qkv_send: send buffers must be contiguous {shape}")
+            dt = torch.float16 if (i == 2 and v_f16) else torch.bfloat16
+            _out(sends[i], shape, dt, a, f"fp8_gemm_qkv_send send buffer {'qkv'[i]}")
             desc.send[i] = sends[i].data_ptr()
         result = sends
     desc.heads, desc.head_dim, desc.ws, desc.v_f16 = heads, 128, ws, int(bool(v_f16))
     desc.groups = int(groups)
     if qk_norm is not None:
         qw, kw, table, eps = qk_norm
-        _need_cuda(qw, kw, table)
-        qw, kw = qw.contiguous(), kw.contiguous()
-        table = table.float()
-        if table.stride(-1) != 1:
-            table = table.contiguous()
+        if bias is not None:
+            raise ValueError("fp8_gemm_qkv_send: the norm + RoPE epilogue has no bias term (q and k would drop it)")
+        (qw, kw), table = _norm_rope_args((qw, kw), table, M, "fp8_gemm_qkv_send")
         desc.q_norm_weight, desc.k_norm_weight = qw.data_ptr(), kw.data_ptr()
         desc.rope_table, desc.rope_stride, desc.rot = table.data_ptr(), table.stride(0), table.shape[-1]
         desc.eps = float(eps)
@@ -369,6 +470,7 @@ def _as3(t: torch.Tensor) -> torch.Tensor:
 
 def bf16_to_f16(x: torch.Tensor, range_flag: torch.Tensor | None = None) -> torch.Tensor:
     _need_cuda(x)
+    _dt(x, torch.bfloat16, what="bf16_to_f16 x")
     y = torch.empty(x.shape, dtype=torch.float16, device=x.device)
     _lib.call("h3b_bf16_to_f16", x.contiguous().data_ptr(), y.data_ptr(), x.numel(), _ptr(range_flag), _stream(x))
     return y
@@ -386,13 +488,16 @@ def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: floa
     _dt(k3, torch.bfloat16, what="flash_attn k")
     s_q, heads, d = q3.shape
     s_kv = k3.shape[0]
+    if k3.shape != (s_kv, heads, d) or v3.shape != k3.shape:
+        raise ValueError(f"flash_attn: k and v must be [S_kv, {heads}, {d}] like q's heads, got {tuple(k3.shape)} "
+                         f"and {tuple(v3.shape)}")
+    _dt(v3, torch.bfloat16, torch.float16, what="flash_attn v")
+    o = _out(out, tuple(q.shape), torch.bfloat16, q, "flash_attn", dense=False)
+    o3 = _as3(o)
     if v3.dtype == torch.bfloat16 and pv_f16:
         if range_flag is None:
             range_flag = torch.zeros(1, dtype=torch.int32, device=q.device)
         v3 = bf16_to_f16(v3.contiguous(), range_flag)
-    _dt(v3, torch.bfloat16, torch.float16, what="flash_attn v")
-    o = out if out is not None else torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
-    o3 = _as3(o)
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(d)
     _lib.call("h3b_flash_attn_fwd", q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0),
               k3.stride(1), v3.data_ptr(), v3.stride(0), v3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1),
@@ -416,6 +521,12 @@ def flash_attn_p2p(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer_back,
     ws = len(peer_back)
     if ws < 1 or ws > _lib.MAX_RANKS or s_q % ws:
         raise ValueError(f"flash_attn_p2p: {ws} peers for {s_q} query rows")
+    if k3.shape[1:] != (heads, d) or v3.shape != k3.shape:
+        raise ValueError(f"flash_attn_p2p: k and v must be [S_kv, {heads}, {d}], got {tuple(k3.shape)} and "
+                         f"{tuple(v3.shape)}")
+    for b in peer_back:
+        if isinstance(b, torch.Tensor):
+            _out(b, (ws, s_q // ws, heads, d), torch.bfloat16, b, "flash_attn_p2p reverse receive buffer")
     ptrs = (ctypes.c_void_p * ws)(*[_addr(b) for b in peer_back])
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(d)
     f16 = v3.dtype == torch.float16
@@ -446,8 +557,13 @@ def pack_by_dest(x: torch.Tensor, ws: int, out: torch.Tensor | None = None, *, t
     m, h, d = x.shape
     if x.stride(2) != 1:
         raise ValueError("pack_by_dest: unit innermost stride needed")
+    _dt(x, torch.bfloat16, torch.float16, what="pack_by_dest x")
+    if to_f16 and x.dtype != torch.bfloat16:
+        raise TypeError("pack_by_dest: to_f16 converts bf16 input")
+    if ws <= 0 or h % ws:
+        raise ValueError(f"pack_by_dest: {h} heads over {ws} ranks")
     dt = torch.float16 if to_f16 else x.dtype
-    send = out if out is not None else torch.empty((ws, m, h // ws, d), dtype=dt, device=x.device)
+    send = _out(out, (ws, m, h // ws, d), dt, x, "pack_by_dest")
     _lib.call("h3b_pack_by_dest", x.data_ptr(), m, h, d, x.stride(0), x.stride(1), ws, send.data_ptr(),
               int(bool(to_f16)), _ptr(range_flag), _stream(x))
     return send
@@ -462,11 +578,12 @@ def norm_rope_send(x: torch.Tensor, weight: torch.Tensor, table: torch.Tensor, e
     m, h, d = x.shape
     if d != 128 or x.stride(2) != 1:
         raise ValueError("norm_rope_send: x must be [M, H, 128] with unit innermost stride")
-    table = table.float()
-    if table.stride(-1) != 1:
-        table = table.contiguous()
-    send = out if out is not None else torch.empty((ws, m, h // ws, d), dtype=torch.bfloat16, device=x.device)
-    _lib.call("h3b_norm_rope_send", x.data_ptr(), m, h, x.stride(0), x.stride(1), weight.contiguous().data_ptr(),
+    _dt(x, torch.bfloat16, what="norm_rope_send x")
+    if ws <= 0 or h % ws:
+        raise ValueError(f"norm_rope_send: {h} heads over {ws} ranks")
+    (weight,), table = _norm_rope_args((weight,), table, m, "norm_rope_send")
+    send = _out(out, (ws, m, h // ws, d), torch.bfloat16, x, "norm_rope_send")
+    _lib.call("h3b_norm_rope_send", x.data_ptr(), m, h, x.stride(0), x.stride(1), weight.data_ptr(),
               table.data_ptr(), table.stride(0), table.shape[-1], float(eps), ws, send.data_ptr(), _stream(x))
     return send
 
@@ -474,8 +591,9 @@ def norm_rope_send(x: torch.Tensor, weight: torch.Tensor, table: torch.Tensor, e
 def unpack_recv(recv: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """recv [P, M, hl, d] -> [M, P*hl, d] contiguous (copy 5 of the reverse exchange, :181-183)."""
     _need_cuda(recv)
+    _dt(recv, torch.bfloat16, torch.float16, what="unpack_recv recv")
     p, m, hl, d = recv.shape
-    o = out if out is not None else torch.empty((m, p * hl, d), dtype=recv.dtype, device=recv.device)
+    o = _out(out, (m, p * hl, d), recv.dtype, recv, "unpack_recv")
     _lib.call("h3b_unpack_recv", recv.contiguous().data_ptr(), p, m, hl, d, o.data_ptr(), _stream(recv))
     return o
 
