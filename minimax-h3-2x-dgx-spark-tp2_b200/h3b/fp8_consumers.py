@@ -53,11 +53,11 @@ def qk_norm_rope_fused(st: Stash, num_heads: int, num_kv_heads: int, head_dim: i
 
 
 def qkv_into_send(st: Stash, num_heads: int, ws: int, q_weight: torch.Tensor, k_weight: torch.Tensor,
-                  rope_table: torch.Tensor, eps: float):
+                  rope_table: torch.Tensor, eps: float, sends=None):  # noqa: ANN001
     """The qkv GEMM of ``st`` with the norm + RoPE epilogue writing per destination (the producer ``ulysses_exact``'s
     redirection uses; h3_tp2/ulysses_exact.py:278 ``fused_into_send``): (send_q, send_k, send_v) [P, M, H/P, 128] bf16,
-    q and k normalised and rotated, v the plain scale pass."""
-    return ops.fp8_gemm_qkv_send(st.a, st.w, st.sa, st.sb, num_heads, ws,
+    q and k normalised and rotated, v the plain scale pass; into ``sends`` when given."""
+    return ops.fp8_gemm_qkv_send(st.a, st.w, st.sa, st.sb, num_heads, ws, sends=sends,
                                  qk_norm=(q_weight, k_weight, rope_table.float(), eps))
 
 

@@ -93,6 +93,18 @@ def rope_into_send(send_q, send_k, q, k, q_weight, k_weight, rope_table, eps, la
         launch(k[:, heads], k_weight, rope_table, eps, send_k[p])
 
 
+def fused_into_send(fc, st, heads: int, head_dim: int, q_weight, k_weight, rope_table, eps, sends) -> None:  # noqa: ANN001
+    """Consumer-fused producer (:278): the qkv projection of stash ``st`` written per destination into send_q / send_k
+    / send_v [P, T, H/P, d], q and k normalised and rotated.  The reference runs three scale passes over the stashed
+    fp32 product; here the qkv GEMM's epilogue does all three (``fc.qkv_into_send``), so the stash holds the FP8
+    operands and the norm epilogue takes no bias."""
+    if head_dim != 128:
+        raise ValueError(f"fused_into_send: head_dim {head_dim} (the epilogue covers 128)")
+    if getattr(st, "bias", None) is not None:
+        raise ValueError("fused_into_send: the norm + RoPE epilogue takes no bias")
+    fc.qkv_into_send(st, heads, sends[0].shape[0], q_weight, k_weight, rope_table, eps, sends=sends)
+
+
 def exchange_fwd(send: torch.Tensor, a2a, pg=None) -> torch.Tensor:  # noqa: ANN001
     """One forward all-to-all; the receive buffer viewed [1, P*M, hl, d] (h3_tp2/ulysses_exact.py:130)."""
     recv = torch.empty_like(send)

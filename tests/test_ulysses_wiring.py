@@ -184,3 +184,32 @@ def test_placeholder_without_buffers_and_bad_mode_raise():
         ux.take_pending(ph, ph, ph)
     with pytest.raises(ValueError):
         ux.make_forward_impl(lambda *a: None, "3", INFO)
+
+
+def test_fused_into_send_fills_the_given_buffers():
+    """``fused_into_send`` (the reference's consumer-fused producer) writes the projection of the stash into the send
+    buffers it is given, q and k normalised and rotated; a bias or another head size is refused."""
+    t, heads = 24, 4
+    st = _stash(t, heads, 3)
+    _, _, _, wq, wk, table = _inputs(t, heads, 128, 32, 4)
+    seen = {}
+
+    def qkv_into_send(st_, num_heads, ws, qw, kw, tab, eps, sends=None):
+        packed = _fake_fc(heads).qkv_into_send(st_, num_heads, ws, qw, kw, tab, eps)
+        for dst, src in zip(sends, packed):
+            dst.copy_(src)
+        seen["ws"] = ws
+
+    fc = SimpleNamespace(qkv_into_send=qkv_into_send)
+    sends = [torch.empty(ux.send_shape(t, heads, 128, WS), dtype=torch.bfloat16) for _ in range(3)]
+    ux.fused_into_send(fc, st, heads, 128, wq, wk, table, 1e-6, sends)
+    q, k, v = _eager_qkv(st, heads)
+    assert seen["ws"] == WS
+    assert torch.equal(sends[0], ou.pack(ou.norm_rope(q, wq, table, 1e-6), WS))
+    assert torch.equal(sends[1], ou.pack(ou.norm_rope(k, wk, table, 1e-6), WS))
+    assert torch.equal(sends[2], ou.pack(v, WS))
+    with pytest.raises(ValueError, match="head_dim"):
+        ux.fused_into_send(fc, st, heads, 64, wq, wk, table, 1e-6, sends)
+    biased = fp8_consumers.Stash(st.a, st.w, st.sa, st.sb, torch.zeros(3 * heads * 128, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="bias"):
+        ux.fused_into_send(fc, biased, heads, 128, wq, wk, table, 1e-6, sends)
