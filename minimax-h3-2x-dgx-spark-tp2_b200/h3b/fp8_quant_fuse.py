@@ -17,6 +17,7 @@ site for the process).
 from __future__ import annotations
 
 import functools
+import logging
 import threading
 from typing import Any, Callable
 
@@ -24,6 +25,7 @@ import torch
 
 from . import ops
 
+logger = logging.getLogger("h3b.fp8_quant_fuse")
 SITES = ("qkv", "out", "fc1", "fc2")
 FP8_MAX = 448.0
 MIN_SCALE = 1.0 / (FP8_MAX * 512.0)
@@ -484,15 +486,25 @@ def _lora_types() -> tuple:
         return ()
 
 
-def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=None, lora_types=None,  # noqa: ANN001
-            ulysses_mode: str | None = None, explicit: bool = False) -> list[str]:
+def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=None, check_source: bool = True,  # noqa: ANN001
+            lora_types=None, ulysses_mode: str | None = None, explicit: bool = False, level: str | None = None,
+            env=None) -> list[str]:  # noqa: ANN001
     """Patch the transformer module ``tr`` (default: vLLM-Omni's MiniMax H3), ``QuantFP8.forward`` and
-    ``SiluAndMul.forward`` for the given sites (h3_tp2/fp8_quant_fuse.py:923); returns the installed sites.  The out site
-    needs the exact exchange in mode 1 (mode 2 leaves the unpack to ``ulysses_outq``).  The upstream code between each
-    producer and its quant is checked by structure at plan time (``block_plan``), not by source fingerprints."""
-    del explicit
+    ``SiluAndMul.forward`` for the given sites (h3_tp2/fp8_quant_fuse.py:923); returns the installed sites.  Skipped,
+    with a warning, as the reference skips them: everything under ``VLLM_BATCH_INVARIANT``; out unless the exact
+    exchange runs in mode 1 (mode 2 leaves the unpack to ``ulysses_outq``); fc1 when the consumer fuse owns
+    ``indexed_gate_rms_norm_scale_shift``; fc2 below the ``cutlass`` GEMM level (fc1's output reaches ``SiluAndMul``
+    only there); with ``check_source`` a site whose upstream code (``sources.QUANT_SITE_SOURCES``) is not the
+    reviewed source.  ``explicit``: the sites were named, which only changes the wording of the out site's mode-2
+    line.  ``level`` / ``env`` default to the installed GEMM level and the process environment."""
+    import os  # noqa: PLC0415
+    from . import fp8_consumers, fp8_gemm, sources  # noqa: PLC0415
+    env = os.environ if env is None else env
     sites = tuple(site for site in SITES if site in sites)
     if not sites:
+        return []
+    if env.get("VLLM_BATCH_INVARIANT", "0").strip() not in ("", "0"):
+        logger.warning("h3b fp8 quant fuse: VLLM_BATCH_INVARIANT changes the FP8 linear path; skipped")
         return []
     if tr is None:
         from vllm_omni.diffusion.models.minimax_h3 import minimax_h3_transformer as tr  # noqa: PLC0415
@@ -503,6 +515,7 @@ def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=
     block_cls = tr.MiniMaxH3DiTBlock
     if getattr(block_cls.forward, "_h3b_quant_fuse", False):
         return list(_state["sites"])
+    skip: dict[str, str] = {}
     if "out" in sites:
         mode = ulysses_mode
         if mode is None:
@@ -511,8 +524,31 @@ def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=
                 mode = getattr(layer_mod.Attention, "_h3b_exact", None)
             except ImportError:
                 mode = None
-        if mode != "1":
+        if mode == "2":
+            logger.warning("h3b fp8 quant fuse: site out %s: the exact exchange's mode 2 makes no reverse unpack copy "
+                           "to fuse into (the out-projection quant reads the receive buffer)",
+                           "requested but ignored" if explicit else "skipped automatically")
             sites = tuple(site for site in sites if site != "out")
+            if not sites:
+                return []
+        elif mode != "1":
+            skip["out"] = f"needs the exact exchange in mode 1 (installed: {mode})"
+    if "fc1" in sites and ("out" in fp8_consumers._state.get("sites", ()) or
+                           getattr(tr.indexed_gate_rms_norm_scale_shift, "_h3b_consumer_fuse", False)):
+        skip["fc1"] = "the consumer fuse's out site owns indexed_gate_rms_norm_scale_shift"
+    level = fp8_gemm._state.get("level") if level is None else level
+    if "fc2" in sites and level != "cutlass":
+        skip["fc2"] = "fc1's output reaches SiluAndMul only at the cutlass GEMM level"
+    if check_source:
+        fps = sources.quant_fingerprints(tr)
+        for site in sites:
+            bad = [f"{n} {fps.get(n)} (reviewed {sources.quant_expected(n)})" for n in sources.QUANT_SITE_SOURCES[site]
+                   if fps.get(n) != sources.quant_expected(n)]
+            if bad and site not in skip:
+                skip[site] = "upstream source changed: " + ", ".join(bad)
+    for site, why in skip.items():
+        logger.warning("h3b fp8 quant fuse: site %s skipped (%s)", site, why)
+    sites = tuple(site for site in sites if site not in skip)
     if not sites:
         return []
     _state["quant_cls"] = quant_cls
@@ -530,9 +566,8 @@ def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=
         from . import ulysses_exact  # noqa: PLC0415
         ulysses_exact.set_unpack_hook(unpack_hook)
     block_cls.forward = make_block_forward(block_cls.forward, sites, _lora_types() if lora_types is None else lora_types)
-    import os  # noqa: PLC0415
     _state["sites"] = sites
-    _state["verify"] = os.environ.get("H3_TP2_FP8_QUANT_FUSE_VERIFY", "0").strip() == "1"
-    mode = os.environ.get("H3_TP2_FP8_QUANT_FUSE_MODE", "auto").strip().lower()
+    _state["verify"] = env.get("H3_TP2_FP8_QUANT_FUSE_VERIFY", "0").strip() == "1"
+    mode = env.get("H3_TP2_FP8_QUANT_FUSE_MODE", "auto").strip().lower()
     _state["modes"] = {"0": (0,), "1": (1,)}.get(mode, (0, 1))
     return list(sites)

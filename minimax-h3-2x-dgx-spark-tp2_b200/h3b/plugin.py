@@ -36,8 +36,8 @@ def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
 def plan(env: dict | None = None) -> dict:
     """The patches ``_apply`` would install for an environment (pure; used by tests)."""
     env = os.environ if env is None else env
-    out = {"ulysses": None, "fp8_gemm": None, "swiglu": 0, "quant_fuse": None, "overlap": None, "nocopy": None,
-           "a2a_timing": False}
+    out = {"ulysses": None, "fp8_gemm": None, "swiglu": 0, "consumer_fuse": None, "quant_fuse": None, "overlap": None,
+           "nocopy": None, "a2a_timing": False}
     # the reference's precedence (h3_tp2/plugin.py:278-308): the combined exchange only when forced (it runs the
     # overlap's head groups itself), else the exact exchange (default "2"; replaces the overlap when both are set),
     # else the overlap
@@ -57,6 +57,10 @@ def plan(env: dict | None = None) -> dict:
         # quantises the SwiGLU output for fc2
         sw = env.get("H3_TP2_FP8_FUSE_SWIGLU", "1").strip()
         out["swiglu"] = int(sw) if sw in ("1", "2") else 0
+        # consumers fused with the qkv / out / fc2 GEMMs (h3_tp2/plugin.py:479-481): tensor32 and cutlass levels only
+        cf = env.get("H3_TP2_FP8_CONSUMER_FUSE", "1").strip().lower()
+        if level in ("tensor32", "cutlass") and cf not in ("", "0"):
+            out["consumer_fuse"] = cf
     fuse = env.get("H3_TP2_FP8_QUANT_FUSE", "1").strip().lower()
     if fuse not in ("", "0", "off"):
         out["quant_fuse"] = fuse
@@ -92,6 +96,14 @@ def _apply(role: str) -> None:
         if p["swiglu"]:
             from . import fp8_swiglu  # noqa: PLC0415
             fp8_swiglu.install(level=p["swiglu"])
+        if p["consumer_fuse"]:
+            from . import fp8_consumers  # noqa: PLC0415
+            try:
+                cdone = fp8_consumers.install(fp8_consumers.parse_sites(p["consumer_fuse"]))
+            except Exception:  # noqa: BLE001  (an optional fusion must not take the rank down: stock consumers)
+                logger.warning("h3b plugin: FP8 consumer fuse install failed; stock consumers", exc_info=True)
+                cdone = []
+            logger.warning("h3b plugin: FP8 consumer fuse sites installed: %s", ", ".join(cdone) or "none")
     if p["quant_fuse"]:
         from . import fp8_quant_fuse  # noqa: PLC0415
         sites = fp8_quant_fuse.parse_sites(p["quant_fuse"])

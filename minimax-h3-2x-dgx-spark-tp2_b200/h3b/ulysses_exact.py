@@ -11,6 +11,7 @@ NVLink (or any injected ``a2a(out, inp, group=)``).
 """
 from __future__ import annotations
 
+import logging
 import threading
 from dataclasses import dataclass
 
@@ -18,6 +19,8 @@ import torch
 import torch.distributed as dist
 
 from . import ops
+
+logger = logging.getLogger("h3b.ulysses_exact")
 
 MODES = ("1", "2", "fwd", "verify")
 
@@ -467,10 +470,22 @@ def _hook_producers(strategy_info, mode: str = "1") -> None:  # noqa: ANN001
     """Attach the arming wrapper and the producer hook to vLLM-Omni's MiniMax H3 model (the first wrapped attention
     call does this; h3_tp2/ulysses_exact.py:521)."""
     from vllm_omni.diffusion.models.minimax_h3 import minimax_h3_transformer as tr  # noqa: PLC0415
+    _hook_producers_on(tr, strategy_info, mode)
 
+
+def _hook_producers_on(tr, strategy_info, mode: str = "1") -> None:  # noqa: ANN001
+    """``_hook_producers`` on the transformer module ``tr``: in mode 2 the deferral's upstream path is checked first,
+    on the attention forward as upstream wrote it (a changed path keeps the reverse unpack, ``ulysses_outq.prepare``
+    refuses every attention)."""
     att_cls = tr.MiniMaxH3Attention
     if not getattr(att_cls.forward, "_h3b_exact_armed", False):
-        att_cls.forward = make_armed_forward(att_cls.forward, outq=mode == "2")
+        outq = mode == "2"
+        if outq:
+            from . import ulysses_outq  # noqa: PLC0415
+            reason = ulysses_outq.check_sources(att_cls.forward)
+            logger.warning("h3b ulysses exact: the reverse unpack %s", "left to the out-projection quant (self-check "
+                           "on the first call)" if reason is None else f"kept ({reason})")
+        att_cls.forward = make_armed_forward(att_cls.forward, outq=outq)
     if getattr(tr.fused_qk_norm_rope, "_h3b_consumer_fuse", False):
         from . import fp8_consumers as fc  # noqa: PLC0415
         if not getattr(fc.qk_norm_rope_fused, "_h3b_exact", False):

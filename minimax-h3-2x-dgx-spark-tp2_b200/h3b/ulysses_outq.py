@@ -60,7 +60,7 @@ def unpack_rows(recv: torch.Tensor) -> torch.Tensor:
 # ---------------------------------------------------------------------------------------------------------------
 
 _tls = threading.local()    # owner: (attention, rows) armed for one deferral; pending: Deferred
-_state: dict = {"disabled": None, "checked": False}
+_state: dict = {"disabled": None, "checked": False, "sources": None}   # sources: why the upstream path is not reviewed
 _stats = {k: 0 for k in ("deferred", "quant_recv", "selfcheck_pass", "selfcheck_fail", "not_prepared")}
 # the two kernels the deferral runs (module-level so host-logic tests can substitute CPU implementations)
 _kernels = {"quant_from_recv": lambda recv: quant_from_recv(recv), "unpack_rows": lambda recv: unpack_rows(recv)}
@@ -198,8 +198,8 @@ class OutQuant:
 
 def layer_mismatch(owner) -> str | None:  # noqa: ANN001
     """None when ``owner.out_proj`` reaches a dynamic per-token quant as ``quant_method.fp8_linear.quant_fp8`` on the
-    whole [M, H*d] input (a single-rank row-parallel linear), else the reason (h3_tp2/ulysses_outq.py:330; checked by
-    structure here, not by the upstream sources' fingerprints)."""
+    whole [M, H*d] input (a single-rank row-parallel linear), else the reason (h3_tp2/ulysses_outq.py:330; the upstream
+    sources on the path are checked once by ``check_sources``)."""
     layer = getattr(owner, "out_proj", None)
     if layer is None:
         return "no out_proj"
@@ -220,15 +220,31 @@ def layer_mismatch(owner) -> str | None:  # noqa: ANN001
     return None
 
 
+def source_fingerprints(attn_forward) -> dict[str, str | None]:  # noqa: ANN001
+    """The fingerprints of every upstream function between the attention output and the quant (:300);
+    ``attn_forward`` = the attention's forward as upstream wrote it, before wrapping."""
+    from . import sources  # noqa: PLC0415
+    return sources.outq_fingerprints(attn_forward)
+
+
+def check_sources(attn_forward) -> str | None:  # noqa: ANN001
+    """None when every function on the path has the reviewed source, else the reason, kept for ``prepare`` (:319)."""
+    from . import sources  # noqa: PLC0415
+    bad = sources.changed(sources.OUTQ_REVIEWED, source_fingerprints(attn_forward), sources.OUTQ_REVIEWED)
+    _state["sources"] = ("upstream source changed: " + ", ".join(bad)) if bad else None
+    return _state["sources"]
+
+
 def prepare(owner) -> bool:  # noqa: ANN001
     """Once per attention: True when its out-projection's quant can take a deferred receive buffer, and then that
-    layer's ``quant_fp8`` is wrapped in ``OutQuant`` (h3_tp2/ulysses_outq.py:370)."""
+    layer's ``quant_fp8`` is wrapped in ``OutQuant`` (h3_tp2/ulysses_outq.py:370); never while ``check_sources``
+    found the upstream path changed."""
     layer = getattr(owner, "out_proj", None)
     if layer is None:
         return False
     ok = getattr(layer, "_h3b_outq", None)
     if ok is None:
-        ok = layer_mismatch(owner) is None
+        ok = _state["sources"] is None and layer_mismatch(owner) is None
         if ok:
             kernel = layer.quant_method.fp8_linear
             if not isinstance(kernel.quant_fp8, OutQuant):

@@ -19,12 +19,15 @@ Reference functions exercised (paths inside the reference project):
   rope:     h3_tp2/ulysses_exact.py:264 rope_into_send with the eager norm+RoPE stand-in tests/test_ulysses_exact.py:107
   nocopy:   h3_tp2/ulysses_nocopy.py:74 send_shape, :84 pack_qkv, :105 qkv_views, :112 back_into, :124 nocopy_forward
             (one combined q/k/v exchange per head group) with FakeA2A, and the stock exchange for comparison
+  sources:  h3_tp2/step_cache.py:72 fingerprint_source on sample texts, and the reviewed-source tables
+            (h3_tp2/fp8_consumers.py:67-89, h3_tp2/fp8_quant_fuse.py:856-877, h3_tp2/ulysses_outq.py:59) -> sources.json
   gate:     h3_tp2/fp8_consumers.py:367 _gate_torch (the eager mirror of _scale_indexed_gate_kernel) on an exact
             integer fp32 product, gate rows as a row-strided chunk view (recipe of tests/test_fp8_consumer_fuse.py:118)
 """
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import sys
 from pathlib import Path
@@ -309,6 +312,24 @@ def gen_gate(fc) -> dict:
                 idx=idx.numpy().copy(), y=bits16(y), ybias=bits16(yb))
 
 
+SOURCE_SAMPLES = [
+    "",
+    "def f(x):\n    return x\n",
+    "@decorator\ndef f(x):  # trailing comment stays\n\n    # a comment line\n    y = x * 2\t \n    return y\n",
+    '    @functools.wraps(g)\n    def wrapper(*a, **kw):\n        """doc # not a comment"""\n        return g(*a, **kw)\n',
+    "x = 'été'\n   \n#\n@\nz = 1",
+]
+
+
+def gen_sources(step_cache, fc, fq, outq) -> dict:
+    """The upstream-source fingerprint (h3_tp2/step_cache.py:72 fingerprint_source) of a few source texts, and the
+    reviewed tables of h3_tp2/fp8_consumers.py:67-89, h3_tp2/fp8_quant_fuse.py:856-877, h3_tp2/ulysses_outq.py:59."""
+    return {"samples": SOURCE_SAMPLES, "fingerprints": [step_cache.fingerprint_source(t) for t in SOURCE_SAMPLES],
+            "consumer_expected": fc.EXPECTED, "consumer_sites": {k: list(v) for k, v in fc.SITE_SOURCES.items()},
+            "quant_expected_extra": fq.EXPECTED_EXTRA, "quant_sites": {k: list(v) for k, v in fq.SITE_SOURCES.items()},
+            "outq_expected": outq.EXPECTED}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("H3_TP2_REFERENCE"),
@@ -320,6 +341,7 @@ def main() -> None:
     sys.path.insert(0, str(ref))
     sys.path.insert(0, str(ref / "tests"))
     from h3_tp2 import fp8_consumers, fp8_gemm, fp8_quant_fuse, fp8_swiglu, ulysses_exact, ulysses_nocopy, ulysses_outq  # noqa: PLC0415,E501
+    from h3_tp2 import step_cache  # noqa: PLC0415
     import fake_h3_consumers  # noqa: PLC0415
     import test_ulysses_exact  # noqa: PLC0415
 
@@ -332,6 +354,8 @@ def main() -> None:
     np.savez_compressed(HERE / "rope.npz", **gen_rope(ulysses_exact, test_ulysses_exact))
     np.savez_compressed(HERE / "gate.npz", **gen_gate(fp8_consumers))
     np.savez_compressed(HERE / "nocopy.npz", **gen_nocopy(ulysses_nocopy, test_ulysses_exact))
+    (HERE / "sources.json").write_text(json.dumps(gen_sources(step_cache, fp8_consumers, fp8_quant_fuse, ulysses_outq),
+                                                  indent=1, sort_keys=True) + "\n")
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -58,6 +58,7 @@ def outq_cpu(monkeypatch):
     monkeypatch.setitem(ulysses_outq._kernels, "unpack_rows", lambda recv: ou.unpack(recv).reshape(recv.shape[1], -1))
     monkeypatch.setitem(ulysses_outq._state, "checked", False)
     monkeypatch.setitem(ulysses_outq._state, "disabled", None)
+    monkeypatch.setitem(ulysses_outq._state, "sources", None)
 
 
 def test_exact_forward_with_presupplied_sends_and_defer(outq_cpu):
@@ -87,6 +88,35 @@ def test_exact_forward_with_presupplied_sends_and_defer(outq_cpu):
         rq, rs = oq.quant(ref[r].reshape(m, heads * d))
         assert same_bits(res[r][0], rq) and torch.equal(res[r][1], rs)
     assert ulysses_outq._state["checked"] and ulysses_outq._state["disabled"] is None
+
+
+def test_deferral_needs_the_reviewed_upstream_path(outq_cpu, monkeypatch):
+    """Mode 2's producer hook checks the upstream sources on the attention forward as upstream wrote it: a changed
+    path keeps the reverse unpack (``prepare`` refuses every attention); the reviewed path lets it through."""
+    import sys
+    from types import SimpleNamespace
+
+    from h3b import sources
+    monkeypatch.setitem(sys.modules, "vllm", None)              # vLLM's linear path is not looked up (a slow import)
+
+    class MiniMaxH3Attention:
+        def forward(self, x):
+            return x
+
+    def rope(*a, **kw):
+        return a[:2]
+    upstream = MiniMaxH3Attention.forward
+    tr = SimpleNamespace(MiniMaxH3Attention=MiniMaxH3Attention, fused_qk_norm_rope=rope)
+    ulysses_exact._hook_producers_on(tr, lambda layer, md: None, "2")
+    assert MiniMaxH3Attention.forward._h3b_exact_armed and tr.fused_qk_norm_rope._h3b_exact
+    assert ulysses_outq._state["sources"].startswith("upstream source changed: attn_forward")
+    owner, kernel = _owner(4, 8)
+    assert not ulysses_outq.prepare(owner) and not isinstance(kernel.quant_fp8, ulysses_outq.OutQuant)
+    assert sources.outq_fingerprints(upstream) == {"attn_forward": sources.fingerprint(upstream)}
+    monkeypatch.setattr(sources, "outq_fingerprints", lambda fwd: dict(sources.OUTQ_REVIEWED))
+    assert ulysses_outq.check_sources(upstream) is None
+    owner, kernel = _owner(4, 8)
+    assert ulysses_outq.prepare(owner) and isinstance(kernel.quant_fp8, ulysses_outq.OutQuant)
 
 
 def test_deferral_guards_and_self_check_failure(outq_cpu, monkeypatch):
@@ -139,6 +169,10 @@ def test_plugin_plan_defaults_and_switches():
     assert plugin.plan({"H3_TP2_FP8_FUSE_SWIGLU": "2"})["swiglu"] == 2
     assert plugin.plan({"H3_TP2_FP8_FUSE_SWIGLU": "0"})["swiglu"] == 0
     assert plugin.plan({"H3_TP2_FP8_GEMM": "0"})["swiglu"] == 0      # the MLP fusion rides on the GEMM dispatcher
+    assert p["consumer_fuse"] == "1"
+    assert plugin.plan({"H3_TP2_FP8_GEMM": "tensor32", "H3_TP2_FP8_CONSUMER_FUSE": "fc2,out"})["consumer_fuse"] == "fc2,out"
+    assert plugin.plan({"H3_TP2_FP8_GEMM": "fused"})["consumer_fuse"] is None     # no stash at the fused level
+    assert plugin.plan({"H3_TP2_FP8_CONSUMER_FUSE": "0"})["consumer_fuse"] is None
     p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_FP8_GEMM": "0", "H3_TP2_A2A_TIMING": "1"})
     assert p["ulysses"] == "2" and p["overlap"] is None and p["fp8_gemm"] is None and p["a2a_timing"]  # exact wins
     p = plugin.plan({"H3_TP2_A2A_OVERLAP": "2", "H3_TP2_ULYSSES_EXACT": "0"})

@@ -100,6 +100,10 @@ def _eager_site_kernels(monkeypatch):
     monkeypatch.setattr(fq, "silu_mul_quant", lambda x, stock=None: oq.quant(og.silu_and_mul(x)))
 
 
+# the stand-in module is not the reviewed upstream source, fc1's output reaches the activation as at the cutlass level
+_AS_REVIEWED = {"check_source": False, "level": "cutlass", "env": {}}
+
+
 @pytest.fixture
 def fuse(monkeypatch):
     """Fresh module state, CPU tensors admitted, eager site kernels."""
@@ -126,7 +130,7 @@ def test_fused_block_equals_stock_bit_for_bit(fuse):
     blk = tr.MiniMaxH3DiTBlock()
     args = _inputs(100)
     ref = blk.forward(*args)                                    # the stock block
-    installed = fq.install(("qkv", "fc1", "fc2"), tr, quant_cls=Quant, act_cls=Act, lora_types=())
+    installed = fq.install(("qkv", "fc1", "fc2"), tr, quant_cls=Quant, act_cls=Act, lora_types=(), **_AS_REVIEWED)
     assert installed == ["qkv", "fc1", "fc2"]
     got = tr.MiniMaxH3DiTBlock.forward(blk, *args)
     for a, b in zip(got, ref):
@@ -141,7 +145,7 @@ def test_stash_met_by_another_quant_is_materialised(fuse):
     Quant, Act = _make_classes()
     tr = _tr(Quant, Act)
     blk = tr.MiniMaxH3DiTBlock()
-    fq.install(("qkv",), tr, quant_cls=Quant, act_cls=Act, lora_types=())
+    fq.install(("qkv",), tr, quant_cls=Quant, act_cls=Act, lora_types=(), **_AS_REVIEWED)
     x, shift, scale, gate, idx = _inputs(80, 1)
     ctx = fq._Ctx(blk, fq.block_plan(blk, ("qkv",))[0])
     fq._tls.ctx = ctx
@@ -162,7 +166,7 @@ def test_a_fused_producer_that_differs_disables_its_site(fuse, monkeypatch):
     blk = tr.MiniMaxH3DiTBlock()
     monkeypatch.setattr(fq, "silu_mul_quant", lambda x, stock=None: (oq.quant(og.silu_and_mul(x))[0],
                                                                     oq.quant(og.silu_and_mul(x))[1] * 2))
-    fq.install(("fc2",), tr, quant_cls=Quant, act_cls=Act, lora_types=())
+    fq.install(("fc2",), tr, quant_cls=Quant, act_cls=Act, lora_types=(), **_AS_REVIEWED)
     args = _inputs(70, 2)
     got = tr.MiniMaxH3DiTBlock.forward(blk, *args)
     assert "fc2" in fq._state["disabled"] and fq.stats()["fused_fc2"] == 0
@@ -185,3 +189,29 @@ def test_plan_refuses_blocks_it_cannot_fuse(fuse):
     blk.attn.qkv_proj.tp_size = 1
     blk.attn.qkv_proj.quant_method.fp8_linear.quant_fp8.static = True
     assert fq.block_plan(blk, ("qkv",))[0] is None
+
+
+def test_install_rules(fuse, monkeypatch):
+    """The reference's skip rules: the source check, fc2 below the cutlass level, fc1 beside the consumer fuse's out
+    site, the out site outside mode 1, everything under VLLM_BATCH_INVARIANT."""
+    import sys
+    from h3b import fp8_consumers
+    monkeypatch.setitem(sys.modules, "vllm", None)          # vLLM's linear path is not looked up (a slow import)
+    Quant, Act = _make_classes()
+    tr = _tr(Quant, Act)
+    tr.MiniMaxH3Attention = type("MiniMaxH3Attention", (), {"forward": lambda self, x: x})
+    tr.MiniMaxH3MLP = type("MiniMaxH3MLP", (), {"forward": lambda self, x: x})
+    kw = {"quant_cls": Quant, "act_cls": Act, "lora_types": ()}
+    assert fq.install(("qkv", "fc1", "fc2"), tr, level="cutlass", env={}, **kw) == []        # not reviewed source
+    assert fq.install(("qkv", "fc1", "fc2"), tr, env={"VLLM_BATCH_INVARIANT": "1"}, check_source=False, **kw) == []
+    assert fq.install(("out",), tr, ulysses_mode="2", **_AS_REVIEWED, **kw) == []
+    assert fq.install(("out",), tr, ulysses_mode=None, **_AS_REVIEWED, **kw) == []
+    owned = _tr(Quant, Act)
+
+    def consumer_fused(*a):
+        return orms.gate_rms_norm_scale_shift(*a)
+    consumer_fused._h3b_consumer_fuse = True
+    owned.indexed_gate_rms_norm_scale_shift = consumer_fused
+    assert fq.install(("fc1", "fc2"), owned, check_source=False, level="tensor32", env={}, **kw) == []
+    assert "out" not in fp8_consumers._state["sites"]
+    assert fq.install(("fc1", "fc2"), tr, check_source=False, level="tensor32", env={}, **kw) == ["fc1"]
