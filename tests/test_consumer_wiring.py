@@ -117,7 +117,8 @@ def _install(tr, sites=fc.SITES, **kw):
     kw.setdefault("level", "tensor32")
     kw.setdefault("nocopy", False)
     kw.setdefault("check_source", False)          # the stand-in module is not the reviewed upstream source
-    return fc.install(sites, tr, lora_types=(), **kw)
+    kw.setdefault("lora_types", ())
+    return fc.install(sites, tr, **kw)
 
 
 def test_installed_block_equals_stock():
@@ -232,3 +233,75 @@ def test_install_skips_sites_whose_upstream_source_is_not_the_reviewed_one():
     assert _install(tr, check_source=True) == []
     assert stock == (tr.fused_qk_norm_rope, tr.indexed_gate, tr.MiniMaxH3DiTBlock.forward)
     assert fp8_gemm._stash_hooks == []
+
+
+@pytest.mark.parametrize("sites", [("qkv",), ("out",), ("fc2",), ("out", "fc2")])
+def test_site_subsets(sites):
+    tr = _module()
+    block = tr.MiniMaxH3DiTBlock()
+    x, idx, table = _inputs(11)
+    ref = block.forward(x, idx, rope_table=table)
+    assert _install(tr, sites) == list(sites)
+    assert torch.equal(tr.MiniMaxH3DiTBlock.forward(block, x, idx, rope_table=table), ref)
+    st = fc.stats()
+    assert [st[f"fused_{s}"] for s in fc.SITES] == [int(s in sites) for s in fc.SITES] and st["materialize"] == 0
+
+
+def test_plan_rejections_and_lora():
+    tr = _module()
+    block = tr.MiniMaxH3DiTBlock()
+    table = torch.zeros(4, 96)
+    want, _ = fc.block_plan(block, table, fc.SITES)
+    assert sorted(want.values()) == sorted(fc.SITES)
+    assert fc.block_plan(block, None, fc.SITES)[0] is None                          # no rope table
+    assert fc.block_plan(block, table, fc.SITES, lora_types=(SimpleNamespace,))[0] is None
+    block.mlp.fc2.tp_size = 2
+    assert "tp_size" in fc.block_plan(block, table, fc.SITES)[1]                    # an all-reduce reads the output
+    block.mlp.fc2.tp_size = 1
+    block.attn.out_proj.output_size_per_partition += 16                             # a padded N is sliced and copied
+    assert fc.block_plan(block, table, fc.SITES)[0] is None
+    block.attn.out_proj.output_size_per_partition -= 16
+    fc._state["disabled"].add("qkv")
+    assert sorted(fc.block_plan(block, table, fc.SITES)[0].values()) == ["fc2", "out"]
+
+    x, idx, table = _inputs(12)
+    ref = block.forward(x, idx, rope_table=table)
+    _install(tr, lora_types=(SimpleNamespace,))                                     # every layer counts as wrapped
+    assert torch.equal(tr.MiniMaxH3DiTBlock.forward(block, x, idx, rope_table=table), ref)
+    assert fc.stats()["stash"] == 0
+
+
+def test_foreign_site_stash_and_calls_outside_a_block():
+    """A consumer that meets another site's stash makes it real first; with no block context nothing is stashed."""
+    t = 6
+    a8, sa = oq.quant(torch.randn(t, C).to(BF16))
+    w8, sb = og.quant_weight(torch.randn(C, C))
+    ph = torch.empty(t, C, dtype=BF16)
+    ctx = fc._Ctx({})
+    ctx.pending["out"] = fc.Stash(a8, w8, sa.reshape(-1), sb, None, ph)
+    fc._tls.ctx = ctx
+    x, gate = torch.randn(t, C).to(BF16), (0.1 * torch.randn(1, C)).to(BF16)
+    idx = torch.zeros(t, dtype=torch.int64)
+    out = fc.make_gate_wrapper(og.indexed_gate)(x, gate, ph, idx)                  # fc2's consumer, out's stash
+    branch = og.scaled_mm(a8, w8, sa.reshape(-1), sb)
+    assert torch.equal(out, og.indexed_gate(x, gate, branch, idx)) and torch.equal(ph, branch)
+    assert fc.stats()["materialize"] == 1 and not ctx.pending and fc.stats()["fused_fc2"] == 0
+    fc._tls.ctx = None
+    layer = _layer(C, C, 5)
+    _install(_module())
+    y = _linear(layer, x)                                                          # a GEMM outside any block
+    assert fc.stats()["stash"] == 0 and y.shape == (t, C)
+
+
+def test_stash_hook_takes_only_the_planned_weights_once():
+    mine, other = _layer(64, C, 6), _layer(64, C, 7)
+    a8, sa = oq.quant(torch.randn(4, C).to(BF16))
+    ctx = fc._Ctx({(mine.weight.data_ptr(), tuple(mine.weight.shape)): "fc2"})
+    fc._tls.ctx = ctx
+    assert fc.stash_hook(a8, other.weight, sa, other.weight_scale, BF16, None) is None
+    assert fc.stash_hook(a8, mine.weight, sa, mine.weight_scale, torch.float16, None) is None   # bf16 outputs only
+    ph = fc.stash_hook(a8, mine.weight, sa, mine.weight_scale, BF16, None)
+    assert ph.shape == (4, 64) and ph.dtype == BF16 and set(ctx.pending) == {"fc2"}
+    st = ctx.pending["fc2"]
+    assert st.a is a8 and st.w.shape == (64, C) and st.w.data_ptr() == mine.weight.data_ptr() and st.sa.shape == (4,)
+    assert fc.stash_hook(a8, mine.weight, sa, mine.weight_scale, BF16, None) is None             # once per block
