@@ -215,3 +215,113 @@ def test_install_rules(fuse, monkeypatch):
     assert fq.install(("fc1", "fc2"), owned, check_source=False, level="tensor32", env={}, **kw) == []
     assert "out" not in fp8_consumers._state["sites"]
     assert fq.install(("fc1", "fc2"), tr, check_source=False, level="tensor32", env={}, **kw) == ["fc1"]
+
+
+def _installed(sites=("qkv", "fc1", "fc2")):
+    Quant, Act = _make_classes()
+    tr = _tr(Quant, Act)
+    blk = tr.MiniMaxH3DiTBlock()
+    ref_tr = _tr(*_make_classes())
+    ref_blk = ref_tr.MiniMaxH3DiTBlock.__new__(ref_tr.MiniMaxH3DiTBlock)
+    ref_blk.__dict__.update(blk.__dict__)
+    assert fq.install(sites, tr, quant_cls=Quant, act_cls=Act, lora_types=(), **_AS_REVIEWED) == list(sites)
+    return tr, blk, ref_tr, ref_blk, Quant
+
+
+def _equal(got, ref):
+    return all(torch.equal(a.view(torch.int16), b.view(torch.int16)) for a, b in zip(got, ref))
+
+
+def test_mode_with_the_stored_row_when_registers_differ(fuse, monkeypatch):
+    """A producer whose register-only mode (no bf16 row stored) differs from stock falls back to the mode that stores
+    the row (the reference's reload mode); the site stays on."""
+    tr, blk, ref_tr, ref_blk, _ = _installed(("qkv",))
+    real = fq.rms_quant
+
+    def regs_differ(x, weight, shift, scale, indices, eps, stock=None, ph=None):
+        q, s = real(x, weight, shift, scale, indices, eps, stock, ph)
+        return (q, s * 2) if ph is None else (q, s)
+
+    monkeypatch.setattr(fq, "rms_quant", regs_differ)
+    args = _inputs(90, 4)
+    ref = ref_tr.MiniMaxH3DiTBlock.forward(ref_blk, *args)
+    assert _equal(tr.MiniMaxH3DiTBlock.forward(blk, *args), ref)
+    st = fq.stats()
+    assert st["selfcheck_fail"] == 1 and st["selfcheck_pass"] == 1 and st["fused_qkv"] == 1
+    assert "qkv" not in fq._state["disabled"] and fq._state["checked"][("qkv", C, BF16, BF16, 1)]
+
+
+def test_layer_that_never_quantises_is_rerun(fuse):
+    """A planned layer that returns without its quant consuming the stash ran on the placeholder: it is materialised
+    and the layer run again."""
+    tr, blk, ref_tr, ref_blk, _ = _installed(("qkv",))
+
+    def unquantised(x, _w=blk.attn.qkv_proj.weight):
+        return (x.float() @ _w).to(BF16), None
+
+    blk.attn.qkv_proj.forward = unquantised
+    args = _inputs(90, 5)
+    ref = ref_tr.MiniMaxH3DiTBlock.forward(ref_blk, *args)
+    assert _equal(tr.MiniMaxH3DiTBlock.forward(blk, *args), ref)
+    assert fq.stats()["rerun"] == 1 and fq.stats()["materialize"] == 1 and fq.stats()["consumed"] == 0
+
+
+@pytest.mark.parametrize("how", ["static_scale", "other_shape"])
+def test_quant_calls_that_do_not_match_the_stash_get_real_rows(fuse, how):
+    """A quant with a static scale, or on another shape than the placeholder's, is not the planned call: the stash is
+    materialised first, so the layer's own quant sees the stock rows."""
+    tr, blk, _, _, _ = _installed(("qkv",))
+    lin = blk.attn.qkv_proj
+    quant = lin.quant_method.fp8_linear.quant_fp8
+
+    def forward(x, _lin=lin):
+        k = _lin.weight.shape[0]
+        if how == "static_scale":
+            q, s = quant(x.reshape(-1, k), torch.ones(1))
+        else:
+            q, s = quant(x.reshape(-1, k)[:-1])
+            q, s = torch.cat((q, q[-1:])), torch.cat((s, s[-1:]))
+        return (q.float() * s @ _lin.weight).to(BF16), None
+
+    lin.forward = forward
+    args = _inputs(70, 6)
+    got = tr.MiniMaxH3DiTBlock.forward(blk, *args)
+    h = orms.rms_norm_scale_shift(args[0], blk.norm1.weight, args[1], args[2], args[4], 1e-6)
+    q_ref, _ = forward(h)
+    assert torch.equal(got[0], orms.gate_rms_norm_scale_shift(args[0], args[3], q_ref[:, :C], blk.norm2.weight,
+                                                              args[1], args[2], args[4], 1e-6)[0])
+    assert fq.stats()["materialize"] == 1 and fq.stats()["consumed"] == 0
+
+
+def test_plan_exclusions(fuse):
+    Quant, Act = _make_classes()
+    tr = _tr(Quant, Act)
+    fq._state["quant_cls"] = Quant
+    blk = tr.MiniMaxH3DiTBlock()
+    blk.attn.to_gate_compress = object()                       # a VSA gate reads the qkv input a second time
+    assert sorted(fq.block_plan(blk, ("qkv", "fc1"))[0]) == ["fc1"]
+    blk.attn.to_gate_compress = None
+    assert fq.block_plan(blk, ("qkv",), lora_types=(Linear,)) == (None, "qkv: missing or LoRA-wrapped layer")
+    for attr, val in (("static", True), ("is_group_quant", True), ("use_per_token_if_dynamic", False),
+                      ("num_token_padding", 16)):
+        q = blk.attn.qkv_proj.quant_method.fp8_linear.quant_fp8
+        old = getattr(q, attr)
+        setattr(q, attr, val)
+        assert fq.block_plan(blk, ("qkv",))[0] is None, attr
+        setattr(q, attr, old)
+    blk.attn.qkv_proj.input_scale = torch.ones(1)              # a static input scale
+    assert fq.block_plan(blk, ("qkv",))[0] is None
+    del blk.attn.qkv_proj.input_scale
+    assert fq.block_plan(blk, ("qkv",))[0] is not None
+
+
+def test_producers_outside_a_block_and_verify_mode(fuse):
+    tr, blk, ref_tr, ref_blk, _ = _installed()
+    x, shift, scale, gate, idx = _inputs(40, 7)
+    h = tr.rms_norm_indexed_scale_shift(x, blk.norm1.weight, shift, scale, idx, 1e-6)   # no block context: stock
+    assert torch.equal(h, orms.rms_norm_scale_shift(x, blk.norm1.weight, shift, scale, idx, 1e-6))
+    assert fq.stats()["fused_qkv"] == 0
+    fq._state["verify"] = True
+    args = _inputs(80, 8)
+    assert _equal(tr.MiniMaxH3DiTBlock.forward(blk, *args), ref_tr.MiniMaxH3DiTBlock.forward(ref_blk, *args))
+    assert fq.stats()["verify_calls"] == 3 and fq.stats()["verify_mismatch"] == 0
