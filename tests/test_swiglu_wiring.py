@@ -85,3 +85,39 @@ def test_fc2_direct_refuses_layers_it_cannot_run():
     assert fp8_swiglu._fc2_direct(layer, q, s, (4,)) is None
     layer.bias, layer.tp_size = None, 2
     assert fp8_swiglu._fc2_direct(layer, q, s, (4,)) is None
+
+
+def test_stash_hook_takes_fc1_only_when_asked(eager):
+    """The hook stashes only while an MLP forward asks for it, only bf16 outputs of the expected even width, once."""
+    lin = _Linear(64, 192, 6)
+    a, s = oq.quant(torch.randn(8, 64).to(BF16))
+    hook = fp8_swiglu._stash_hook
+    assert hook(a, lin.weight, s, lin.weight_scale, BF16, None) is None             # not asked
+    fp8_swiglu._tls.stash_next, fp8_swiglu._tls.expect_n = True, 192
+    try:
+        assert hook(a, lin.weight, s, lin.weight_scale, torch.float16, None) is None
+        ph = hook(a, lin.weight, s, lin.weight_scale, BF16, None)
+        assert ph.shape == (8, 192) and ph.dtype == BF16 and not fp8_swiglu._tls.stash_next
+        ops_, sa, sb, bias = fp8_swiglu._tls.stash
+        assert ops_.a is a and ops_.b is lin.weight and ops_.shape == (8, 192) and sa.shape == (8,) and bias is None
+        assert hook(a, lin.weight, s, lin.weight_scale, BF16, None) is None         # once
+        fp8_swiglu._tls.stash_next, fp8_swiglu._tls.expect_n = True, 100             # a padded fc1
+        assert hook(a, lin.weight, s, lin.weight_scale, BF16, None) is None and not fp8_swiglu._tls.stash_next
+    finally:
+        fp8_swiglu._tls.stash_next, fp8_swiglu._tls.stash, fp8_swiglu._tls.expect_n = False, None, 0
+
+
+def test_mlp_forward_clears_state_on_exception_and_keeps_lora_stock(eager):
+    x = torch.randn(10, 64).to(BF16)
+
+    def failing(_x):
+        raise RuntimeError("fc1 failed")
+    fwd = fp8_swiglu.make_mlp_forward(lambda self, x: (_ for _ in ()).throw(AssertionError()), level=1)
+    mlp_fail = SimpleNamespace(fc1=failing, fc2=None, act_fn=None)
+    with pytest.raises(RuntimeError, match="fc1 failed"):
+        fwd(mlp_fail, x)
+    assert not fp8_swiglu._tls.stash_next and fp8_swiglu._tls.stash is None and fp8_swiglu._tls.expect_n == 0
+    lora = _mlp()
+    stock = []
+    fwd = fp8_swiglu.make_mlp_forward(lambda self, x: stock.append(1) or "stock", level=2, lora_layer_type=(_Linear,))
+    assert fwd(lora, x) == "stock" and stock == [1]
