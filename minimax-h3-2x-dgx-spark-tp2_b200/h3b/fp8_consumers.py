@@ -483,6 +483,10 @@ def install(sites: tuple[str, ...] = SITES, tr=None, *, check_source: bool = Tru
     if not sites:
         return []
     level = fp8_gemm._state.get("level") if level is None else level
+    if level not in ("tensor32", "cutlass"):
+        logger.warning("h3b fp8 consumer fuse: needs the FP8 GEMM dispatcher at the tensor32 or cutlass level "
+                       "(running: %s); skipped", level)
+        return []
     if level == "cutlass":
         from .fp8_cutlass import SITES as routed  # noqa: PLC0415
         dropped = [s for s in sites if s in routed]

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import functools
 import logging
+import os
 import threading
 
 import torch
@@ -20,8 +21,9 @@ logger = logging.getLogger("h3b.fp8_cutlass")
 
 SITES = ("qkv", "out", "fc1")
 _tls = threading.local()
-_state = {"ok": True}
-_stats = {"taken": 0, "fallthrough": 0}
+_state = {"ok": True, "verify": os.environ.get("H3_TP2_FP8_CUTLASS_VERIFY", "0").strip() == "1"}
+_stats = {"dsl": 0, "fallthrough": 0}
+_warned: set = set()
 
 
 class DslGemm:
@@ -49,18 +51,60 @@ def scaled_mm(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: 
 
 
 def route(a, b, scale_a, scale_b, out_dtype, bias):  # noqa: ANN001,ANN201
-    """fp8_gemm router: the kernel for the running block's registered sites (``block_want``), else None."""
+    """fp8_gemm router (h3_tp2/fp8_cutlass.py:134; runs before the stash hooks): the kernel for the running block's
+    registered sites (``block_want``), else None.  A launch that raises turns the router off for the process."""
     want = getattr(_tls, "want", None)
-    if not want or want.get((b.data_ptr(), tuple(b.shape))) is None:
+    if not want:
+        return None
+    site = want.get((b.data_ptr(), tuple(b.shape)))
+    if site is None:
         return None
     try:
         y = scaled_mm(a, b, scale_a, scale_b, out_dtype, bias)
     except Exception as exc:  # noqa: BLE001  (never take the rank down: later calls fall through)
-        logger.warning("h3b fp8 cutlass: launch failed (%s); falling through for the rest of this process", exc)
+        logger.warning("h3b fp8 cutlass: launch failed (%s: %s); falling through for the rest of this process",
+                       type(exc).__name__, exc)
         _state["ok"] = False
         y = None
-    _stats["taken" if y is not None else "fallthrough"] += 1
+    if y is None:
+        _stats["fallthrough"] += 1
+        if "ft-" + site not in _warned:
+            _warned.add("ft-" + site)
+            logger.warning("h3b fp8 cutlass: %s GEMM M=%d N=%d not taken (guards); the dispatcher's path", site,
+                           a.shape[0], b.shape[1])
+        return None
+    _stats["dsl"] += 1
+    if _state["verify"]:
+        _verify(site, a, b, scale_a, scale_b, out_dtype, bias, y)
     return y
+
+
+def _two_pass(a, b, scale_a, scale_b, out_dtype, bias):  # noqa: ANN001,ANN202
+    """The reference's two-pass arithmetic: the fp32 product (cuBLASLt on the GPU, a matmul on the CPU), then the
+    scale pass."""
+    M, N = a.shape[0], b.shape[1]
+    sa, sb = ops.vec_scales(scale_a, scale_b, M, N)
+    if a.is_cuda:
+        one = fp8_gemm.unit_scale(a.device)
+        x32 = torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.float32)
+        return ops.scale_bias_cast(x32, sa, sb, bias, out_dtype)
+    return fp8_gemm.epilogue_torch(a.float() @ b.float(), sa, sb, bias, out_dtype)
+
+
+def _verify(site, a, b, scale_a, scale_b, out_dtype, bias, y) -> None:  # noqa: ANN001
+    """``H3_TP2_FP8_CUTLASS_VERIFY=1`` (diagnosis only, slow): each routed output against the two-pass arithmetic on the
+    same operands; mismatches are counted and logged (the routed output is still returned) (h3_tp2/fp8_cutlass.py:166)."""
+    ref = _two_pass(a, b, scale_a, scale_b, out_dtype, bias)
+    diff = y.view(torch.int16) != ref.view(torch.int16)
+    nd = int(diff.sum())
+    _stats["verify_calls"] = _stats.get("verify_calls", 0) + 1
+    if nd:
+        _stats["verify_mismatch"] = _stats.get("verify_mismatch", 0) + 1
+        if _stats["verify_mismatch"] <= 20:
+            rows = diff.any(1).nonzero().flatten()
+            logger.warning("h3b fp8 cutlass VERIFY: %s M=%d N=%d K=%d call %d: %d elements differ from two-pass "
+                           "(rows %d..%d)", site, a.shape[0], b.shape[1], a.shape[1], _stats["dsl"], nd,
+                           int(rows.min()), int(rows.max()))
 
 
 def block_want(block, sites=SITES) -> dict:  # noqa: ANN001

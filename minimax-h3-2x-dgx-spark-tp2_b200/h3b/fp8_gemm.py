@@ -165,23 +165,51 @@ def route(a, b, scale_a, scale_b, out_dtype, bias=None, two_pass=None):  # noqa:
     return (two_pass or scaled_mm)(a, b, scale_a, scale_b, out_dtype, bias)
 
 
-def install(level: str = "tensor32") -> None:
-    """Replace vLLM's ``_custom_ops.cutlass_scaled_mm`` for eligible calls (h3_tp2/fp8_gemm.py:344).  ``level`` is
-    accepted for compatibility ("tensor32", "fused", "cutlass"): all run the same fused tcgen05 kernel here."""
+def _install_into(vops, level: str, probe=None, cutlass_probe=None) -> None:  # noqa: ANN001
+    """``install`` on the module ``vops`` that holds ``cutlass_scaled_mm``; ``probe(device)`` / ``cutlass_probe(device)``
+    default to ``probe_fused`` and ``fp8_cutlass.probe``."""
     if level not in ("tensor32", "fused", "cutlass"):
         raise ValueError(f"unknown FP8 GEMM level {level!r}")
-    from vllm import _custom_ops as vops  # noqa: PLC0415
-
     orig = vops.cutlass_scaled_mm
     if getattr(orig, "_h3b", False):
         return
+    probe = probe or probe_fused
+    if not probe("cuda"):
+        _state.update(level="stock", installed=False)
+        logger.warning("h3b: the tcgen05 FP8 GEMM does not serve on this device (needs sm_100 and the library's "
+                       "self-check); vLLM's stock kernel stays")
+        return
+    stats = {"two_pass": 0, "stock": 0}   # the reference's names: calls this dispatch took / left to the stock kernel
 
     def _mm(a, b, scale_a, scale_b, out_dtype, bias=None):  # noqa: ANN001
         if not (a.is_cuda and eligible(a, b, scale_a, scale_b, out_dtype, bias)):
+            stats["stock"] += 1
             return orig(a, b, scale_a, scale_b, out_dtype, bias)
+        stats["two_pass"] += 1
         return route(a, b, scale_a, scale_b, out_dtype, bias)
 
     _mm._h3b = True
+    _mm.stats = stats
     vops.cutlass_scaled_mm = _mm
     _state.update(level=level, installed=True)
-    logger.info("h3b: FP8 GEMM (tcgen05, fused scaled epilogue) installed for level %s", level)
+    if level == "cutlass":
+        if cutlass_probe is None:
+            from . import fp8_cutlass  # noqa: PLC0415
+            cutlass_probe = fp8_cutlass.probe
+        if cutlass_probe("cuda"):
+            from . import fp8_cutlass  # noqa: PLC0415
+            set_router(fp8_cutlass.route)
+        else:
+            _state["level"] = "tensor32"
+            logger.warning("h3b: FP8 GEMM cutlass level unavailable (block routing failed its self-check); tensor32")
+    logger.info("h3b: FP8 GEMM (tcgen05, fused scaled epilogue) installed for level %s", _state["level"])
+
+
+def install(level: str = "tensor32") -> None:
+    """Replace vLLM's ``_custom_ops.cutlass_scaled_mm`` for eligible calls (h3_tp2/fp8_gemm.py:344).  ``level`` is
+    accepted for compatibility ("tensor32", "fused", "cutlass"): all run the same fused tcgen05 kernel; "cutlass" also
+    routes the running DiT block's qkv / out / fc1 weights (``fp8_cutlass``), falling back to "tensor32" when that
+    check fails.  When the kernel does not serve on the device the stock kernel stays (``_state["level"]`` "stock");
+    ``_state["level"]`` is the level actually running."""
+    from vllm import _custom_ops as vops  # noqa: PLC0415
+    _install_into(vops, level)

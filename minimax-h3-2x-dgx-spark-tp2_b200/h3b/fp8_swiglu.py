@@ -7,11 +7,14 @@ silu(g) = g / (1 + exp(-g)) in fp32 (CUDA's ``expf``, IEEE division) rounded to 
 """
 from __future__ import annotations
 
+import logging
 import threading
 
 import torch
 
 from . import fp8_gemm, ops
+
+logger = logging.getLogger("h3b.fp8_swiglu")
 
 
 def scale_swiglu(x32: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
@@ -188,6 +191,12 @@ def install(level: int = 1) -> None:
         from vllm_omni.diffusion.models.minimax_h3 import minimax_h3_transformer as tr  # noqa: PLC0415
     except ImportError as exc:  # pragma: no cover - vLLM-Omni is not part of this image
         raise RuntimeError("h3b.fp8_swiglu.install needs vLLM-Omni (not installed)") from exc
+    if not fp8_gemm._state.get("installed"):
+        logger.warning("h3b: fused FP8 SwiGLU needs the FP8 GEMM dispatcher installed; skipped")
+        return
+    if torch.cuda.is_available() and not probe_gemm_swiglu("cuda"):
+        logger.warning("h3b: the fc1 + SwiGLU kernel does not serve on this device; fused FP8 SwiGLU skipped")
+        return
     try:
         from vllm.lora.layers import BaseLayerWithLoRA  # noqa: PLC0415
         lora = (BaseLayerWithLoRA,)

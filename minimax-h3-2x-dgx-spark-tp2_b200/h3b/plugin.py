@@ -86,17 +86,18 @@ def _apply(role: str) -> None:
     if p["fp8_gemm"]:
         from . import fp8_gemm  # noqa: PLC0415
         fp8_gemm.install(p["fp8_gemm"])
-        if p["fp8_gemm"] == "cutlass":   # the block's qkv / out / fc1 GEMMs routed by weight (h3_tp2/plugin.py:446-456)
+        level = fp8_gemm._state["level"]          # the level actually running ("stock": the kernel did not serve)
+        if level == "cutlass":   # the block's qkv / out / fc1 GEMMs routed by weight (h3_tp2/plugin.py:446-456)
             from . import fp8_cutlass  # noqa: PLC0415
             try:
                 fp8_cutlass.install_sites()
             except Exception:  # noqa: BLE001  (the dispatcher's own path stays)
                 logger.warning("h3b plugin: FP8 GEMM block wiring failed; the dispatcher's path", exc_info=True)
                 fp8_gemm._routers.clear()
-        if p["swiglu"]:
+        if p["swiglu"] and level != "stock":
             from . import fp8_swiglu  # noqa: PLC0415
             fp8_swiglu.install(level=p["swiglu"])
-        if p["consumer_fuse"]:
+        if p["consumer_fuse"] and level in ("tensor32", "cutlass"):
             from . import fp8_consumers  # noqa: PLC0415
             try:
                 cdone = fp8_consumers.install(fp8_consumers.parse_sites(p["consumer_fuse"]))

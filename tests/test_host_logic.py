@@ -348,3 +348,63 @@ def test_cutlass_block_wiring_registers_the_running_block_weights(monkeypatch):
     monkeypatch.setattr(fp8_gemm, "_routers", [])
     assert fp8_cutlass.install_sites(tr) and tr.MiniMaxH3DiTBlock.forward._h3b_cutlass
     assert fp8_gemm._routers == [fp8_cutlass.route]
+
+
+def test_dispatcher_install_levels(monkeypatch):
+    """``fp8_gemm.install``: the kernel's probe decides whether the dispatcher goes in at all (stock stays otherwise);
+    the cutlass level registers the block router after its own check, else runs as tensor32 (h3_tp2/fp8_gemm.py:344)."""
+    from types import SimpleNamespace
+    from h3b import fp8_cutlass
+    monkeypatch.setattr(fp8_gemm, "_routers", [])
+    monkeypatch.setattr(fp8_gemm, "_state", {"level": "tcgen05", "installed": False})
+
+    def stock(a, b, scale_a, scale_b, out_dtype, bias=None):
+        return "stock"
+    vops = SimpleNamespace(cutlass_scaled_mm=stock)
+    fp8_gemm._install_into(vops, "cutlass", probe=lambda dev: False)
+    assert vops.cutlass_scaled_mm is stock and fp8_gemm._state == {"level": "stock", "installed": False}
+    fp8_gemm._install_into(vops, "cutlass", probe=lambda dev: True, cutlass_probe=lambda dev: False)
+    assert fp8_gemm._state["level"] == "tensor32" and fp8_gemm._routers == []
+    mm = vops.cutlass_scaled_mm
+    a = torch.zeros(4, 32, dtype=torch.float8_e4m3fn)
+    assert mm(a, a.t(), torch.ones(4, 1), torch.ones(4), torch.bfloat16) == "stock"     # CPU tensors: stock
+    assert mm.stats == {"two_pass": 0, "stock": 1}
+    fp8_gemm._install_into(vops, "cutlass", probe=lambda dev: True, cutlass_probe=lambda dev: True)
+    assert vops.cutlass_scaled_mm is mm                                                  # installed once
+    vops2 = SimpleNamespace(cutlass_scaled_mm=stock)
+    fp8_gemm._install_into(vops2, "cutlass", probe=lambda dev: True, cutlass_probe=lambda dev: True)
+    assert fp8_gemm._state["level"] == "cutlass" and fp8_gemm._routers == [fp8_cutlass.route]
+    with pytest.raises(ValueError, match="unknown"):
+        fp8_gemm._install_into(SimpleNamespace(cutlass_scaled_mm=stock), "int8")
+
+
+def test_cutlass_router_order_failure_and_verify(monkeypatch):
+    """The block router runs before the stash hooks and only for the running block's weights; a launch that raises
+    turns it off for the process; verify mode compares each routed output with the two-pass arithmetic."""
+    from h3b import fp8_cutlass
+    a = torch.randint(-3, 4, (6, 32)).to(torch.float8_e4m3fn)
+    w = torch.randint(-3, 4, (48, 32)).to(torch.float8_e4m3fn)
+    b, other = w.t(), torch.zeros(48, 32, dtype=torch.float8_e4m3fn).t()
+    sa, sb = torch.full((6, 1), 0.5), torch.full((48,), 0.25)
+    monkeypatch.setattr(fp8_cutlass, "_state", {"ok": True, "verify": True})
+    monkeypatch.setattr(fp8_cutlass, "_stats", {"dsl": 0, "fallthrough": 0})
+    monkeypatch.setattr(fp8_gemm, "_routers", [fp8_cutlass.route])
+    monkeypatch.setattr(fp8_gemm, "_stash_hooks", [lambda *args: "stashed"])
+    mm = lambda a_, b_, sa_, sb_, dt, bias: fp8_cutlass._two_pass(a_, b_, sa_, sb_, dt, bias)  # noqa: E731
+    monkeypatch.setattr(fp8_cutlass, "scaled_mm", mm)
+    fp8_cutlass._tls.want = {(b.data_ptr(), tuple(b.shape)): "qkv"}
+    try:
+        y = fp8_gemm.route(a, b, sa, sb, torch.bfloat16)
+        assert isinstance(y, torch.Tensor) and fp8_cutlass.stats()["dsl"] == 1
+        assert fp8_cutlass.stats()["verify_calls"] == 1 and "verify_mismatch" not in fp8_cutlass.stats()
+        assert fp8_gemm.route(a, other, sa, sb, torch.bfloat16) == "stashed"             # not the block's weight
+        monkeypatch.setattr(fp8_cutlass, "scaled_mm", lambda *args: (_ for _ in ()).throw(RuntimeError("launch")))
+        assert fp8_gemm.route(a, b, sa, sb, torch.bfloat16) == "stashed" and not fp8_cutlass._state["ok"]
+        assert fp8_cutlass.stats()["fallthrough"] == 1
+        off_by_one = lambda *args: mm(*args).view(torch.int16).add(1).view(torch.bfloat16)  # noqa: E731
+        monkeypatch.setattr(fp8_cutlass, "scaled_mm", off_by_one)
+        fp8_cutlass._state["ok"] = True
+        fp8_gemm.route(a, b, sa, sb, torch.bfloat16)
+        assert fp8_cutlass.stats()["verify_mismatch"] == 1
+    finally:
+        fp8_cutlass._tls.want = None
