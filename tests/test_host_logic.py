@@ -408,3 +408,46 @@ def test_cutlass_router_order_failure_and_verify(monkeypatch):
         assert fp8_cutlass.stats()["verify_mismatch"] == 1
     finally:
         fp8_cutlass._tls.want = None
+
+
+def test_deferral_refusals_once_only_views_and_passthrough(outq_cpu):
+    """``defer`` refuses an unarmed forward, other rows, non-bf16 receive buffers, another head count and an
+    out-projection ``prepare`` refused; one deferral per armed forward; the model's views of the placeholder still
+    match; other inputs pass to the wrapped quant (attributes too); a placeholder in another shape raises
+    (h3_tp2/ulysses_outq.py:191-421)."""
+    m, heads, d, ws = 16, 4, 8, 2
+    k = heads * d
+    recv = torch.randn(ws, m, heads // ws, d).to(torch.bfloat16)
+    assert ulysses_outq.defer(recv, heads) is None                               # not armed
+    owner, kernel = _owner(heads, d)
+    for rows, buf, h in ((m + 1, recv, heads), (m, recv.float(), heads), (m, recv, heads + 2)):
+        prev = ulysses_outq.arm(owner, rows)
+        assert ulysses_outq.defer(buf, h) is None
+        ulysses_outq.disarm(prev, check=True)
+    refused, _ = _owner(heads, d)
+    refused.out_proj._h3b_outq = False                                            # prepare() said no
+    prev = ulysses_outq.arm(refused, m)
+    assert ulysses_outq.defer(recv, heads) is None
+    ulysses_outq.disarm(prev, check=True)
+
+    prev = ulysses_outq.arm(owner, m)
+    ph = ulysses_outq.defer(recv, heads)
+    assert ph.shape == (1, m, heads, d) and ulysses_outq.defer(recv, heads) is None      # once per armed forward
+    x = ph.squeeze(0).reshape(m, k).view(-1, k)                                   # the model's views
+    assert x.data_ptr() == ph.data_ptr() and x.stride() == (0, 0) and ulysses_outq._tls.pending.matches(x)
+    with pytest.raises(RuntimeError, match="another shape"):
+        kernel.quant_fp8(ph.reshape(m * k)[None].expand(1, m * k))
+    q, s = kernel.quant_fp8(x)
+    rq, rs = oq.quant(ou.unpack(recv).reshape(m, k))
+    assert same_bits(q, rq) and torch.equal(s, rs)
+    ulysses_outq.disarm(prev, check=True)
+
+    y = torch.randn(8, k).to(torch.bfloat16)
+    calls = kernel.quant_fp8._orig.calls
+    q, s = kernel.quant_fp8(y)                                                    # an ordinary input: the layer's quant
+    assert kernel.quant_fp8._orig.calls == calls + 1 and same_bits(q, oq.quant(y)[0])
+    assert kernel.quant_fp8.use_per_token_if_dynamic and not kernel.quant_fp8.static   # attributes reach the quant
+    prev = ulysses_outq.arm(owner, m)
+    ulysses_outq.defer(recv, heads)
+    ulysses_outq.disarm(prev, check=False)                                        # an exception is propagating
+    assert getattr(ulysses_outq._tls, "pending", None) is None
