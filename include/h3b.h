@@ -77,7 +77,8 @@ typedef struct h3b_qkv_send {
   int32_t groups;      /* head groups G (0 or 1: none); H % (G * P) == 0 */
   /* optional qk RMSNorm + partial RoPE on q and k before the store (the upstream norm+RoPE producer fused, see
    * h3b_norm_rope_send): per (token, head) n = bf16(y * rsqrt(mean(y^2) + eps) * w) of the bf16 GEMM output y, then
-   * the first `rot` dims rotate with rope_table[m] = cos | sin.  NULL weights: no norm (v is never normed). */
+   * the first `rot` dims rotate with rope_table[m] = cos | sin.  NULL weights: no norm (v is never normed).  The norm
+   * epilogue has no bias term: a bias with norm weights returns H3B_EUNSUPPORTED. */
   const void* q_norm_weight; /* bf16 [128] */
   const void* k_norm_weight; /* bf16 [128] */
   const float* rope_table;   /* [M, rot] f32, row stride rope_stride */

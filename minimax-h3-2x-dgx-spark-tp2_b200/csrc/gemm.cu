@@ -659,6 +659,7 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
     if ((send->q_norm_weight == nullptr) != (send->k_norm_weight == nullptr))
       return fail(H3B_EINVAL, "fp8_gemm qkv_send: q and k norm weights go together");
     if (send->q_norm_weight != nullptr) {
+      if (bias != nullptr) return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: the norm + RoPE epilogue has no bias term");
       if (send->rot < 0 || send->rot > 128 || send->rot % 32)
         return fail(H3B_EUNSUPPORTED, "fp8_gemm qkv_send: rot %d (0, 32, 64, 96 or 128)", send->rot);
       if (send->rot > 0 && send->rope_table == nullptr) return fail(H3B_EINVAL, "fp8_gemm qkv_send: rope table");

@@ -56,6 +56,16 @@ def _qkv_p2p(rank=0, groups=1, null_peer=False):
     return d
 
 
+def _qkv_norm():
+    d = _lib.QkvSend()
+    d.heads, d.head_dim, d.ws, d.groups = 2, 128, 2, 1
+    for i in range(3):
+        d.send[i] = 4096 * (1 + i)
+    d.q_norm_weight, d.k_norm_weight, d.rope_table = 8192, 8448, 8704
+    d.rope_stride, d.rot, d.eps = 64, 64, 1e-6
+    return d
+
+
 @pytest.mark.parametrize("call,status", [
     (lambda L: L.h3b_quant_rows_e4m3(None, -1, 1, 8, 0, 8, None, None, 0, None), _lib.H3B_EINVAL),
     (lambda L: L.h3b_quant_rows_e4m3(None, 4, 1, 8, 0, 8, None, None, 7, None), _lib.H3B_EINVAL),
@@ -98,6 +108,9 @@ def _qkv_p2p(rank=0, groups=1, null_peer=False):
                               ctypes.byref(_qkv_p2p(groups=2)), None), _lib.H3B_EUNSUPPORTED),
     (lambda L: L.h3b_fp8_gemm(16, 16, 16, 16, 16, 16, None, None, 0, 4, 3 * 2 * 128, 16, 0, 1,
                               ctypes.byref(_qkv_p2p(null_peer=True)), None), _lib.H3B_EALIGN),
+    # the norm + RoPE epilogue has no bias term: a bias with norm weights is refused, not dropped
+    (lambda L: L.h3b_fp8_gemm(16, 16, 16, 16, 16, 16, 16, None, 0, 4, 3 * 2 * 128, 16, 0, 1,
+                              ctypes.byref(_qkv_norm()), None), _lib.H3B_EUNSUPPORTED),
 ])
 def test_host_side_argument_errors(call, status):
     lib = _lib.load()
