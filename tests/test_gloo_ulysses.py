@@ -1,6 +1,7 @@
 """BASELINE config 0 on two CPU processes over gloo (world size 2): the Ulysses block with a real collective equals
 the single-process block, through both the oracle and the h3b orchestration (``ulysses_exact.exact_forward`` with
-``torch.distributed.all_to_all_single``).  A rank that dies before the exchange makes the survivor's collective fail
+``torch.distributed.all_to_all_single``), and the combined q/k/v exchange (``ulysses_nocopy.nocopy_forward``, one and two
+head groups; its layout runs in torch in these CPU processes).  A rank that dies before the exchange makes the survivor's collective fail
 within the process-group timeout (failure detection on the host, no GPU involved)."""
 import datetime
 import os
@@ -61,6 +62,27 @@ def _worker(rank, ws, port, mode, out_dir):
         def a2a(out, inp, group=None):
             dist.all_to_all_single(out, inp, group=group)
 
+        if mode == "nocopy":      # the combined q/k/v exchange, one and two head groups, over the real collective
+            from h3b import ops, ulysses_nocopy
+
+            ops._need_cuda = lambda *ts: None                   # this CPU process runs the layout in torch
+
+            def unpack_recv(recv, out=None):
+                p_, m_, hl, d = recv.shape
+                o_ = out if out is not None else torch.empty((m_, p_ * hl, d), dtype=recv.dtype)
+                o_.view(m_, p_, hl, d).copy_(recv.permute(1, 0, 2, 3))
+                return o_
+            ops.unpack_recv = unpack_recv
+            qkv = xl @ wqkv.t()
+            q, k, v = (t.reshape(1, m, 8, 128) for t in qkv.split(1024, dim=1))
+            res = {}
+            for groups in (1, 2):
+                o = ulysses_nocopy.nocopy_forward(q, k, v, lambda a, b, c: oa.sdpa(a[0], b[0], c[0]).unsqueeze(0),
+                                                  ws=ws, groups=groups, a2a=a2a)
+                res[f"g{groups}"] = o.reshape(m, 1024) @ wo.t()
+            torch.save(res, Path(out_dir) / f"r{rank}.pt")
+            return
+
         y_oracle = ob.fp32_block(xl, wqkv, wo, 8, ws, a2a)
         qkv = xl @ wqkv.t()
         q, k, v = (t.reshape(1, m, 8, 128) for t in qkv.split(1024, dim=1))
@@ -100,6 +122,25 @@ def test_config0_two_ranks_equal_single_process(tmp_path):
         got = torch.load(tmp_path / f"r{r}.pt")
         rows = ref[r * 2048:(r + 1) * 2048]
         for key in ("oracle", "h3b"):
+            err = float((got[key] - rows).norm() / rows.norm())
+            assert err < 1e-5, (key, r, err)
+
+
+def test_config0_combined_exchange_two_ranks(tmp_path):
+    """The combined q/k/v exchange (one all-to-all per head group, attention on strided views of the receive buffer)
+    over gloo equals the single-process block for one and two head groups."""
+    from oracle import attention as oa
+
+    procs = _spawn("nocopy", tmp_path)
+    assert all(p.exitcode == 0 for p in procs)
+    x, wqkv, wo = _cfg0()
+    qkv = x @ wqkv.t()
+    q, k, v = (t.reshape(4096, 8, 128) for t in qkv.split(1024, dim=1))
+    ref = oa.sdpa(q, k, v).reshape(4096, 1024) @ wo.t()
+    for r in range(2):
+        got = torch.load(tmp_path / f"r{r}.pt")
+        rows = ref[r * 2048:(r + 1) * 2048]
+        for key in ("g1", "g2"):
             err = float((got[key] - rows).norm() / rows.norm())
             assert err < 1e-5, (key, r, err)
 
