@@ -21,6 +21,8 @@ Reference functions exercised (paths inside the reference project):
             (one combined q/k/v exchange per head group) with FakeA2A, and the stock exchange for comparison
   sources:  h3_tp2/step_cache.py:72 fingerprint_source on sample texts, and the reviewed-source tables
             (h3_tp2/fp8_consumers.py:67-89, h3_tp2/fp8_quant_fuse.py:856-877, h3_tp2/ulysses_outq.py:59) -> sources.json
+  consumers: h3_tp2/fp8_consumers.py:316 _qk_rope_torch (q and k blocks, rope table fp32 and bf16) and :354
+            _gate_rms_torch on exact integer fp32 products
   gate:     h3_tp2/fp8_consumers.py:367 _gate_torch (the eager mirror of _scale_indexed_gate_kernel) on an exact
             integer fp32 product, gate rows as a row-strided chunk view (recipe of tests/test_fp8_consumer_fuse.py:118)
 """
@@ -312,6 +314,46 @@ def gen_gate(fc) -> dict:
                 idx=idx.numpy().copy(), y=bits16(y), ybias=bits16(yb))
 
 
+def gen_consumers(fc) -> dict:
+    """The consumer-fused qkv norm + RoPE and out-projection gated RMS of h3_tp2/fp8_consumers.py:316 _qk_rope_torch
+    and :354 _gate_rms_torch (the eager mirrors of its Triton consumer kernels) on exact integer fp32 products, the
+    rope table fp32 and bf16 (recipe of tests/test_fp8_consumer_fuse.py:78-116: rotary 96, head_dim 128)."""
+    g = torch.Generator().manual_seed(8)
+    T, H, D, K = 160, 2, 128, 256
+    N = 3 * H * D
+    a = torch.randint(-4, 5, (T, K), generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), generator=g).to(E4M3)
+    sa = torch.exp(torch.empty(T).uniform_(-6.0, -3.0, generator=g))
+    sb = torch.exp(torch.empty(N).uniform_(-6.5, -4.5, generator=g))
+    x32 = a.float() @ w.float().t()                 # exact (integer products, |sum| < 2^24)
+    qw, kw = ((1 + 0.1 * torch.randn(D, generator=g)).to(BF16) for _ in range(2))
+    pos = torch.arange(T, dtype=torch.float32)[:, None] * torch.exp(-torch.arange(48, dtype=torch.float32) / 8.0)
+    table = torch.cat((torch.cos(pos), torch.sin(pos)), dim=-1)
+    out = dict(qk_a=bits8(a), qk_w=bits8(w), qk_sa=f32(sa), qk_sb=f32(sb), qk_qw=bits16(qw), qk_kw=bits16(kw),
+               qk_table=f32(table), qk_shape=np.array([T, H, D]))
+    for tag, tab in (("f32", table), ("bf16", table.to(BF16))):
+        for name, col0, wt in (("q", 0, qw), ("k", H * D, kw)):
+            y = torch.empty(T, H, D, dtype=BF16)
+            fc._qk_rope_torch(x32, col0, sa, sb, None, wt, tab, 1e-6, H, D, (x32.stride(0), D, 1), y)
+            out[f"qk_{name}_{tag}"] = bits16(y)
+    Tg, C, Kg = 96, 512, 256
+    a = torch.randint(-4, 5, (Tg, Kg), generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (C, Kg), generator=g).to(E4M3)
+    sa = torch.exp(torch.empty(Tg).uniform_(-6.0, -3.0, generator=g))
+    sb = torch.exp(torch.empty(C).uniform_(-6.5, -4.5, generator=g))
+    x32 = a.float() @ w.float().t()
+    res = torch.randn(Tg, C, generator=g).to(BF16)
+    gate, shift, scale = ((0.2 * torch.randn(4, C, generator=g)).to(BF16) for _ in range(3))
+    nw = (1 + 0.1 * torch.randn(C, generator=g)).to(BF16)
+    idx = torch.randint(0, 4, (Tg,), generator=g)
+    r_out, m_out = torch.empty(Tg, C, dtype=BF16), torch.empty(Tg, C, dtype=BF16)
+    fc._gate_rms_torch(res, gate, x32, sa, sb, None, nw, shift, scale, idx, 1e-6, r_out, m_out)
+    out.update(gr_a=bits8(a), gr_w=bits8(w), gr_sa=f32(sa), gr_sb=f32(sb), gr_res=bits16(res), gr_gate=bits16(gate),
+               gr_shift=bits16(shift), gr_scale=bits16(scale), gr_nw=bits16(nw), gr_idx=idx.numpy().copy(),
+               gr_res_out=bits16(r_out), gr_mod_out=bits16(m_out))
+    return out
+
+
 SOURCE_SAMPLES = [
     "",
     "def f(x):\n    return x\n",
@@ -353,6 +395,7 @@ def main() -> None:
     np.savez_compressed(HERE / "ulysses.npz", **gen_ulysses(ulysses_exact, test_ulysses_exact))
     np.savez_compressed(HERE / "rope.npz", **gen_rope(ulysses_exact, test_ulysses_exact))
     np.savez_compressed(HERE / "gate.npz", **gen_gate(fp8_consumers))
+    np.savez_compressed(HERE / "consumers.npz", **gen_consumers(fp8_consumers))
     np.savez_compressed(HERE / "nocopy.npz", **gen_nocopy(ulysses_nocopy, test_ulysses_exact))
     (HERE / "sources.json").write_text(json.dumps(gen_sources(step_cache, fp8_consumers, fp8_quant_fuse, ulysses_outq),
                                                   indent=1, sort_keys=True) + "\n")

@@ -276,3 +276,31 @@ def test_gate_rms_consumer(dev):
         ud = ulp_diff_bf16(got, ref)
         assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.99
     assert ops.device_status() == 0
+
+
+def test_consumers_against_the_reference_mirrors(dev, golden):
+    """The qkv GEMM with the norm + RoPE epilogue and the out-projection gated-RMS consumer against the reference's
+    eager mirrors of its consumer kernels (h3_tp2/fp8_consumers.py:316, :354; tests/golden/consumers.npz) on exact
+    integer products: the GEMM output is the mirror's bf16 epilogue exactly, the norm differs by rsqrt and summation
+    order (the bounds of the oracle comparisons above)."""
+    g = golden("consumers")
+    T, H, D = (int(v) for v in g["qk_shape"])
+    st = fp8_consumers.Stash(t8(g["qk_a"]).to(dev), t8(g["qk_w"]).to(dev), tf(g["qk_sa"]).to(dev),
+                             tf(g["qk_sb"]).to(dev), None)
+    qw, kw = t16(g["qk_qw"]).to(dev), t16(g["qk_kw"]).to(dev)
+    table = tf(g["qk_table"])
+    for tag, tab in (("f32", table), ("bf16", table.to(BF16))):
+        q, k, _ = fp8_consumers.qk_norm_rope_fused(st, H, H, D, qw, kw, tab.to(dev), 1e-6)
+        for name, got in (("q", q), ("k", k)):
+            ref = t16(g[f"qk_{name}_{tag}"])
+            ud = ulp_diff_bf16(got.cpu(), ref)
+            assert (ud == 0).float().mean().item() > 0.98 and int(ud.max()) <= 8, (name, tag)
+            assert rel_l2(got.float().cpu(), ref.float()) <= 2e-3
+    st = fp8_consumers.Stash(t8(g["gr_a"]).to(dev), t8(g["gr_w"]).to(dev), tf(g["gr_sa"]).to(dev),
+                             tf(g["gr_sb"]).to(dev), None)
+    args = [t16(g[k]).to(dev) for k in ("gr_res", "gr_gate", "gr_nw", "gr_shift", "gr_scale")]
+    r_out, mod = fp8_consumers.gate_rms_fused(st, *args, torch.from_numpy(g["gr_idx"]).to(dev), 1e-6)
+    for got, key, bound in ((r_out, "gr_res_out", 1), (mod, "gr_mod_out", 2)):
+        ud = ulp_diff_bf16(got.cpu(), t16(g[key]))
+        assert int(ud.max()) <= bound and (ud == 0).float().mean().item() > 0.99, key
+    assert ops.device_status() == 0

@@ -173,3 +173,22 @@ def test_nocopy_combined_exchange(golden):
                                                               a2a=a2a), ws)
         for r in range(ws):
             assert same_bits(outs[r], t16(g[f"{key}_out{r}"])), (key, r)
+
+
+def test_consumer_mirrors(golden):
+    """The oracle's norm + RoPE and gated RMS on the bf16 GEMM output equal the reference's eager mirrors of its
+    consumer kernels (h3_tp2/fp8_consumers.py:316 _qk_rope_torch, :354 _gate_rms_torch) bit for bit, on exact integer
+    products, with the rope table in fp32 and in bf16."""
+    g = golden("consumers")
+    T, H, D = (int(v) for v in g["qk_shape"])
+    y = og.scaled_mm(t8(g["qk_a"]), t8(g["qk_w"]), tf(g["qk_sa"]), tf(g["qk_sb"]))
+    q, k = y[:, :H * D].reshape(T, H, D), y[:, H * D:2 * H * D].reshape(T, H, D)
+    table = tf(g["qk_table"])
+    for tag, tab in (("f32", table), ("bf16", table.to(BF16))):
+        for name, x, wt in (("q", q, t16(g["qk_qw"])), ("k", k, t16(g["qk_kw"]))):
+            assert same_bits(ou.norm_rope(x, wt, tab, 1e-6), t16(g[f"qk_{name}_{tag}"])), (name, tag)
+    branch = og.scaled_mm(t8(g["gr_a"]), t8(g["gr_w"]), tf(g["gr_sa"]), tf(g["gr_sb"]))
+    r_out, m_out = orms.gate_rms_norm_scale_shift(t16(g["gr_res"]), t16(g["gr_gate"]), branch, t16(g["gr_nw"]),
+                                                  t16(g["gr_shift"]), t16(g["gr_scale"]),
+                                                  torch.from_numpy(g["gr_idx"]), 1e-6)
+    assert same_bits(r_out, t16(g["gr_res_out"])) and same_bits(m_out, t16(g["gr_mod_out"]))
