@@ -8,8 +8,27 @@ from __future__ import annotations
 
 import logging
 import os
+import sys
+from types import ModuleType
 
 logger = logging.getLogger("h3b.plugin")
+
+_H3_MODULE = "vllm_omni.diffusion.models.minimax_h3.minimax_h3_transformer"
+
+
+def fused_swiglu_marker() -> str:
+    """The fused-SwiGLU class marker of the MiniMax H3 MLP as a startup diagnostic (h3_tp2/plugin.py:34): "present"
+    (this plugin patched it), "absent" (not patched) or "unknown" (the module or class is not loaded, or the marker has
+    an unexpected value).  Reads only an already-imported module's own dictionary: never imports the model and never
+    triggers a lazy module attribute lookup."""
+    module = sys.modules.get(_H3_MODULE)
+    cls = vars(module).get("MiniMaxH3MLP") if isinstance(module, ModuleType) else None
+    if not isinstance(cls, type):
+        return "unknown"
+    marker = cls.__dict__.get("_h3b_fused_swiglu")
+    if marker is True:
+        return "present"
+    return "absent" if marker in (None, False) else "unknown"
 
 
 def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
@@ -125,3 +144,5 @@ def register() -> None:
     except Exception:  # noqa: BLE001
         logger.exception("h3b plugin: a required patch failed; exiting (70)")
         os._exit(70)
+    logger.warning("h3b plugin (%s): fused SwiGLU marker %s (H3_TP2_FP8_GEMM=%s)", role, fused_swiglu_marker(),
+                   os.environ.get("H3_TP2_FP8_GEMM", "<default>"))

@@ -451,3 +451,32 @@ def test_deferral_refusals_once_only_views_and_passthrough(outq_cpu):
     ulysses_outq.defer(recv, heads)
     ulysses_outq.disarm(prev, check=False)                                        # an exception is propagating
     assert getattr(ulysses_outq._tls, "pending", None) is None
+
+
+def test_fused_swiglu_marker_never_imports_the_model(monkeypatch):
+    """The startup diagnostic reads the MLP class marker of an already-loaded module only (h3_tp2/plugin.py:34)."""
+    import sys
+    from types import ModuleType
+    name = "vllm_omni.diffusion.models.minimax_h3.minimax_h3_transformer"
+    monkeypatch.setitem(sys.modules, name, None)
+    assert plugin.fused_swiglu_marker() == "unknown"
+    monkeypatch.setitem(sys.modules, name, object())
+    assert plugin.fused_swiglu_marker() == "unknown"
+    lazy = ModuleType(name)
+
+    def fail_if_queried(_name):
+        raise AssertionError("the diagnostic looked an attribute up lazily")
+    lazy.__getattr__ = fail_if_queried
+    monkeypatch.setitem(sys.modules, name, lazy)
+    assert plugin.fused_swiglu_marker() == "unknown"
+    module = ModuleType(name)
+
+    class MiniMaxH3MLP:
+        pass
+    module.MiniMaxH3MLP = MiniMaxH3MLP
+    monkeypatch.setitem(sys.modules, name, module)
+    assert plugin.fused_swiglu_marker() == "absent"
+    MiniMaxH3MLP._h3b_fused_swiglu = True
+    assert plugin.fused_swiglu_marker() == "present"
+    MiniMaxH3MLP._h3b_fused_swiglu = "unexpected"
+    assert plugin.fused_swiglu_marker() == "unknown"
