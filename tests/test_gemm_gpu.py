@@ -309,7 +309,11 @@ def test_consumers_against_the_reference_mirrors(dev, golden):
         for name, got in (("q", q), ("k", k)):
             ref = t16(g[f"qk_{name}_{tag}"])
             ud = ulp_diff_bf16(got.cpu(), ref)
-            assert (ud == 0).float().mean().item() > 0.98 and int(ud.max()) <= 8, (name, tag)
+            # a normalised value one bf16 ulp off (rsqrt, summation order) is many ulps of a rotated output where
+            # a cos and b sin cancel: bounded against the head's largest value there
+            assert (ud == 0).float().mean().item() > 0.98 and (ud <= 8).float().mean().item() > 0.999, (name, tag)
+            err = (got.cpu().float() - ref.float()).abs()
+            assert bool((err <= ref.float().abs().amax(dim=-1, keepdim=True) * 2.0 ** -7).all()), (name, tag)
             assert rel_l2(got.float().cpu(), ref.float()) <= 2e-3
     st = fp8_consumers.Stash(t8(g["gr_a"]).to(dev), t8(g["gr_w"]).to(dev), tf(g["gr_sa"]).to(dev),
                              tf(g["gr_sb"]).to(dev), None)
