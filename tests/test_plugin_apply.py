@@ -1,0 +1,146 @@
+"""The plugin's ``_apply`` against stand-in vLLM / vLLM-Omni modules on the CPU: the switches install the modules in the
+reference's order, the FP8 dispatcher resolves its level, and the interplay rules hold (the cutlass level routes qkv /
+out ahead of the consumer fuse, the combined exchange owns the rope producer, the consumer fuse's out site owns the
+gated RMS, the quant fuse's out site needs the exact exchange in mode 1, its fc2 site the cutlass level).  Kernel
+probes and the upstream source fingerprints are stubbed as passing (the stand-ins are not vLLM-Omni's code)."""
+import sys
+from types import ModuleType
+
+import pytest
+
+from h3b import (fp8_consumers, fp8_cutlass, fp8_gemm, fp8_quant_fuse, fp8_swiglu, plugin, sources, ulysses_exact,
+                 ulysses_nocopy)
+
+
+def _stock(*a, **kw):  # noqa: ARG001
+    return "stock"
+
+
+def _modules():
+    """Fresh stand-ins for the modules the plugin patches (package modules with the classes and functions it reads)."""
+    mods = {}
+
+    def mod(name, **attrs):
+        m = ModuleType(name)
+        m.__dict__.update(attrs)
+        mods[name] = m
+        return m
+
+    class QuantFP8:
+        def forward(self, x, scale=None, scale_ub=None):  # noqa: ARG002
+            return "stock quant"
+
+    class SiluAndMul:
+        def forward(self, x):
+            return x
+
+    class Attention:
+        def _forward_impl(self, q, k, v, md=None):  # noqa: ARG002
+            return "stock attention"
+
+    class MiniMaxH3DiTBlock:
+        def forward(self, x):
+            return x
+
+    class MiniMaxH3Attention:
+        def forward(self, x):
+            return x
+
+    class MiniMaxH3MLP:
+        def forward(self, x):
+            return x
+
+    mod("vllm")
+    mod("vllm._custom_ops", cutlass_scaled_mm=_stock)
+    mod("vllm.model_executor")
+    mod("vllm.model_executor.layers")
+    mod("vllm.model_executor.layers.quantization")
+    mod("vllm.model_executor.layers.quantization.input_quant_fp8", QuantFP8=QuantFP8)
+    for name in ("vllm_omni", "vllm_omni.diffusion", "vllm_omni.diffusion.attention", "vllm_omni.diffusion.models",
+                 "vllm_omni.diffusion.models.minimax_h3", "vllm_omni.diffusion.layers"):
+        mod(name)
+    mod("vllm_omni.diffusion.attention.layer", Attention=Attention)
+    mod("vllm_omni.diffusion.layers.activation", SiluAndMul=SiluAndMul)
+    mod("vllm_omni.diffusion.models.minimax_h3.minimax_h3_transformer", MiniMaxH3DiTBlock=MiniMaxH3DiTBlock,
+        MiniMaxH3Attention=MiniMaxH3Attention, MiniMaxH3MLP=MiniMaxH3MLP, fused_qk_norm_rope=_stock,
+        indexed_gate=_stock, indexed_gate_rms_norm_scale_shift=_stock, rms_norm_indexed_scale_shift=_stock)
+    return mods
+
+
+@pytest.fixture
+def stack(monkeypatch):
+    mods = _modules()
+    for name, m in mods.items():
+        monkeypatch.setitem(sys.modules, name, m)
+    for name in ("vllm_omni.diffusion.layers.fused_qk_norm_rope", "vllm_omni.diffusion.layers.indexed_modulation",
+                 "vllm.lora", "vllm.lora.layers"):
+        monkeypatch.setitem(sys.modules, name, None)       # absent: imports of them fail at once
+    monkeypatch.setattr(fp8_gemm, "_state", {"level": "tcgen05", "installed": False})
+    monkeypatch.setattr(fp8_gemm, "_routers", [])
+    monkeypatch.setattr(fp8_gemm, "_stash_hooks", [])
+    monkeypatch.setattr(fp8_gemm, "probe_fused", lambda device: True)
+    monkeypatch.setattr(fp8_cutlass, "probe", lambda device="cuda": True)
+    monkeypatch.setattr(fp8_consumers, "_state", {"sites": (), "checked": {}, "disabled": set(),
+                                                  "device_types": ("cuda",)})
+    for key, val in (("sites", ()), ("checked", {}), ("disabled", set()), ("orig_quant", None), ("quant_cls", None),
+                     ("act_cls", None)):
+        monkeypatch.setitem(fp8_quant_fuse._state, key, val)
+    reviewed = dict(sources.REVIEWED, **sources.REVIEWED_EXTRA)
+    monkeypatch.setattr(sources, "consumer_fingerprints", lambda tr: dict(reviewed))
+    monkeypatch.setattr(sources, "quant_fingerprints", lambda tr: dict(reviewed))
+    for key in [k for k in __import__("os").environ if k.startswith("H3_TP2_") or k == "VLLM_BATCH_INVARIANT"]:
+        monkeypatch.delenv(key)
+    return mods
+
+
+def _tr(mods):
+    return mods["vllm_omni.diffusion.models.minimax_h3.minimax_h3_transformer"]
+
+
+def test_defaults(stack):
+    """Defaults: exact exchange mode 2, FP8 GEMM at the cutlass level with the block router, fused SwiGLU level 1,
+    the consumer fuse on fc2 only (the router takes qkv / out), the quant fuse on qkv / fc1 / fc2 (out: mode 2)."""
+    plugin._apply("dit")
+    tr, attn = _tr(stack), stack["vllm_omni.diffusion.attention.layer"].Attention
+    assert attn._h3b_exact == "2" and not getattr(attn, "_h3b_nocopy", 0)
+    assert stack["vllm._custom_ops"].cutlass_scaled_mm._h3b and fp8_gemm._state == {"level": "cutlass",
+                                                                                    "installed": True}
+    assert fp8_gemm._routers == [fp8_cutlass.route]
+    assert tr.MiniMaxH3MLP._h3b_fused_swiglu and plugin.fused_swiglu_marker() == "present"
+    assert fp8_consumers._state["sites"] == ("fc2",) and tr.indexed_gate._h3b_consumer_fuse
+    assert not getattr(tr.indexed_gate_rms_norm_scale_shift, "_h3b_consumer_fuse", False)
+    assert fp8_quant_fuse._state["sites"] == ("qkv", "fc1", "fc2")
+    assert fp8_gemm._stash_hooks == [fp8_swiglu._stash_hook, fp8_consumers.stash_hook]
+    block_fwd = tr.MiniMaxH3DiTBlock.forward
+    assert block_fwd._h3b_quant_fuse and block_fwd.__wrapped__._h3b_consumer_fuse
+    assert block_fwd.__wrapped__.__wrapped__._h3b_cutlass
+
+
+def test_nocopy_at_tensor32(stack, monkeypatch):
+    """The combined exchange owns the rope producer (no consumer qkv site); the consumer fuse's out site owns the gated
+    RMS (no quant-fuse fc1); without the exact exchange the quant fuse has no out site; fc2 needs the cutlass level."""
+    monkeypatch.setenv("H3_TP2_ULYSSES_NOCOPY", "force")
+    monkeypatch.setenv("H3_TP2_A2A_OVERLAP", "2")
+    monkeypatch.setenv("H3_TP2_FP8_GEMM", "tensor32")
+    plugin._apply("dit")
+    tr, attn = _tr(stack), stack["vllm_omni.diffusion.attention.layer"].Attention
+    assert attn._h3b_nocopy == 2 and not getattr(attn, "_h3b_exact", None)
+    assert tr.fused_qk_norm_rope._h3b_nocopy and tr.MiniMaxH3Attention.forward._h3b_nocopy_armed
+    assert fp8_gemm._state["level"] == "tensor32" and fp8_gemm._routers == []
+    assert fp8_consumers._state["sites"] == ("out", "fc2")
+    assert fp8_quant_fuse._state["sites"] == ("qkv",)
+    with pytest.raises(RuntimeError, match="exact replaces it"):
+        ulysses_exact.install("2")
+    with pytest.raises(RuntimeError, match="groups=2"):
+        ulysses_nocopy.install(4)
+
+
+def test_kernel_that_does_not_serve_keeps_stock(stack, monkeypatch):
+    """When the GEMM kernel's probe fails the stock dispatch stays and nothing rides on it."""
+    monkeypatch.setattr(fp8_gemm, "probe_fused", lambda device: False)
+    monkeypatch.setenv("H3_TP2_FP8_QUANT_FUSE", "0")
+    plugin._apply("dit")
+    tr = _tr(stack)
+    assert stack["vllm._custom_ops"].cutlass_scaled_mm is _stock and fp8_gemm._state["level"] == "stock"
+    assert fp8_gemm._routers == [] and fp8_gemm._stash_hooks == []
+    assert not getattr(tr.MiniMaxH3MLP, "_h3b_fused_swiglu", False) and fp8_consumers._state["sites"] == ()
