@@ -144,3 +144,22 @@ def test_kernel_that_does_not_serve_keeps_stock(stack, monkeypatch):
     assert stack["vllm._custom_ops"].cutlass_scaled_mm is _stock and fp8_gemm._state["level"] == "stock"
     assert fp8_gemm._routers == [] and fp8_gemm._stash_hooks == []
     assert not getattr(tr.MiniMaxH3MLP, "_h3b_fused_swiglu", False) and fp8_consumers._state["sites"] == ()
+
+
+def test_first_attention_call_hooks_the_producer(stack, monkeypatch):
+    """The exact exchange hooks its producer on the first attention call: at tensor32 the consumer-fused qkv (which the
+    consumer fuse installed) becomes the per-destination producer; in mode 2 the deferral's upstream path is checked
+    first (the stand-in attention forward is not the reviewed one, so the reverse unpack stays)."""
+    from h3b import ulysses_outq
+    monkeypatch.setattr(fp8_consumers, "qk_norm_rope_fused", fp8_consumers.qk_norm_rope_fused)   # restored after
+    monkeypatch.setitem(ulysses_outq._state, "sources", None)
+    monkeypatch.setenv("H3_TP2_FP8_GEMM", "tensor32")
+    plugin._apply("dit")
+    monkeypatch.setitem(sys.modules, "vllm", None)           # the source check finds no vLLM linear path to look up
+    tr = _tr(stack)
+    assert fp8_consumers._state["sites"] == ("qkv", "out", "fc2") and tr.fused_qk_norm_rope._h3b_consumer_fuse
+    ulysses_exact._hook_producers_on(tr, lambda layer, md: None, "2")
+    assert fp8_consumers.qk_norm_rope_fused._h3b_exact                 # the consumer-fused producer, redirected
+    assert not getattr(tr.fused_qk_norm_rope, "_h3b_exact", False)     # the wrapper itself stays the consumer's
+    assert tr.MiniMaxH3Attention.forward._h3b_exact_armed
+    assert ulysses_outq._state["sources"].startswith("upstream source changed")
