@@ -480,3 +480,51 @@ def test_fused_swiglu_marker_never_imports_the_model(monkeypatch):
     assert plugin.fused_swiglu_marker() == "present"
     MiniMaxH3MLP._h3b_fused_swiglu = "unexpected"
     assert plugin.fused_swiglu_marker() == "unknown"
+
+
+def test_a2a_timing_wraps_the_collective_the_4d_exchange_and_reports_per_diffuse(monkeypatch):
+    """``a2a_timing`` (h3_tp2/a2a_timing.py): the collective and ``comm.all_to_all_4D`` are timed with events, the totals
+    are reported (and cleared) at the end of each ``diffuse``, and uninstall restores everything."""
+    from types import SimpleNamespace
+    import torch.distributed as dist
+    from h3b import a2a_timing
+
+    class Event:
+        def record(self):
+            pass
+
+        def elapsed_time(self, end):  # noqa: ARG002
+            return 2.0                                              # ms
+
+    monkeypatch.setattr(a2a_timing, "_event", Event)
+    monkeypatch.setattr(a2a_timing, "_sync", lambda: None)
+    calls = []
+    monkeypatch.setattr(dist, "all_to_all_single", lambda out, inp, group=None: calls.append("a2a") or out.copy_(inp))
+    comm_dist = SimpleNamespace(all_to_all_single=dist.all_to_all_single)
+
+    def all_to_all_4d(x, *a, **kw):  # noqa: ARG001  (stock: permute copies around the collective comm looks up)
+        out = torch.empty_like(x)
+        comm_dist.all_to_all_single(out, x)
+        return out
+    comm = SimpleNamespace(dist=comm_dist, all_to_all_4D=all_to_all_4d)
+    reports = []
+
+    class Pipeline:
+        def diffuse(self, x):
+            comm.all_to_all_4D(x)
+            dist.all_to_all_single(torch.empty_like(x), x)
+            return "latents"
+
+    orig_diffuse = Pipeline.diffuse
+    a2a_timing.install(comm=comm, pipeline_cls=Pipeline)
+    real_report = a2a_timing.report
+    monkeypatch.setattr(a2a_timing, "report", lambda phase="diffuse": reports.append(real_report(phase)))
+    try:
+        assert Pipeline().diffuse(torch.zeros(4, 8)) == "latents"
+        assert calls == ["a2a", "a2a"]
+        assert reports == [{"outer": {"calls": 1, "s": 0.002, "bytes": 128},
+                            "inner": {"calls": 2, "s": 0.004, "bytes": 256}}]
+        assert real_report() is None                                  # cleared by the diffuse report
+    finally:
+        a2a_timing.uninstall()
+    assert Pipeline.diffuse is orig_diffuse and not getattr(dist.all_to_all_single, "_h3b_a2a_timing", False)
