@@ -32,8 +32,10 @@ def fused_swiglu_marker() -> str:
 
 
 def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
-    """(pg, ws) when vLLM-Omni would run strict Ulysses for ``layer`` with nothing this path does not handle
-    (no ring, no joint tensors, no masks), else None (h3_tp2/ulysses_nocopy.py:336-362)."""
+    """(pg, ws) when vLLM-Omni would run strict Ulysses for ``layer`` with nothing this path does not handle, else None
+    (h3_tp2/ulysses_nocopy.py:336-362): the active strategy is plain Ulysses (no ring, no synchronous or permuting
+    all-to-all, no ring group), strict mode with scatter 2 / gather 1, no paged KV and no custom attention on the
+    layer, no mask, joint tensors or VSA gate in the metadata, and more than one rank."""
     from vllm_omni.diffusion.attention.parallel.ulysses import UlyssesParallelAttention  # noqa: PLC0415
     from vllm_omni.diffusion.forward_context import get_ulysses_mode  # noqa: PLC0415
     import torch.distributed as dist  # noqa: PLC0415
@@ -41,15 +43,22 @@ def vllm_strategy_info(layer, attn_metadata):  # noqa: ANN001,ANN201
     strategy = layer._get_active_parallel_strategy()
     if not isinstance(strategy, UlyssesParallelAttention) or getattr(layer, "use_ring", False):
         return None
-    if get_ulysses_mode(default="strict") != "strict":
+    if get_ulysses_mode(default="strict") != "strict" or (strategy._scatter_idx, strategy._gather_idx) != (2, 1):
         return None
-    if attn_metadata is not None and any(getattr(attn_metadata, n, None) is not None for n in
-                                         ("attn_mask", "joint_query", "joint_key", "joint_value", "joint_attn_mask")):
+    if strategy._use_sync or getattr(strategy, "_ulysses_a2a_permute", False) or strategy._sp_group.ring_world_size > 1:
         return None
-    if (strategy._scatter_idx, strategy._gather_idx) != (2, 1):
+    if getattr(layer, "_scheduler_paged_kv", False) or getattr(layer, "_has_custom_attention", False):
+        return None
+    if layer._active_paged_kv_adapter() is not None:
+        return None
+    if attn_metadata is not None and (
+            any(getattr(attn_metadata, n, None) is not None for n in
+                ("attn_mask", "joint_query", "joint_key", "joint_value", "joint_attn_mask"))
+            or "gate_compress" in (getattr(attn_metadata, "extra", None) or {})):
         return None
     pg = strategy._ulysses_pg
-    return pg, dist.get_world_size(pg)
+    ws = dist.get_world_size(pg)
+    return (pg, ws) if ws > 1 else None
 
 
 def plan(env: dict | None = None) -> dict:

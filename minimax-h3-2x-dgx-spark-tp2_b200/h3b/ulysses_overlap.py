@@ -147,8 +147,8 @@ def install(groups: int) -> None:
 
     def _forward_impl(self, query, key, value, attn_metadata=None):  # noqa: ANN001
         info = vllm_strategy_info(self, attn_metadata)
-        if (info is None or query.ndim != 4 or query.shape[0] != 1 or not query.is_cuda
-                or query.shape[2] % (groups * info[1])):
+        if (info is None or query.ndim != 4 or query.shape[0] != 1 or not (query.is_cuda and key.is_cuda and value.is_cuda)
+                or key.shape != query.shape or value.shape != query.shape or query.shape[2] % (groups * info[1])):
             return orig(self, query, key, value, attn_metadata)
         pg, ws = info
         return grouped_forward(query, key, value, lambda q, k, v: local_attention(q, k, v, attn_metadata), ws=ws,

@@ -163,3 +163,55 @@ def test_first_attention_call_hooks_the_producer(stack, monkeypatch):
     assert not getattr(tr.fused_qk_norm_rope, "_h3b_exact", False)     # the wrapper itself stays the consumer's
     assert tr.MiniMaxH3Attention.forward._h3b_exact_armed
     assert ulysses_outq._state["sources"].startswith("upstream source changed")
+
+
+def test_strategy_info_takes_only_plain_strict_ulysses(monkeypatch):
+    """``vllm_strategy_info``: (pg, ws) for plain strict Ulysses over more than one rank, None for everything the stock
+    path must keep (h3_tp2/ulysses_nocopy.py:336-362)."""
+    from types import SimpleNamespace
+    import torch.distributed as dist
+
+    class UlyssesParallelAttention:
+        def __init__(self, **kw):
+            self.__dict__.update(dict(_scatter_idx=2, _gather_idx=1, _use_sync=False, _ulysses_pg="pg",
+                                      _sp_group=SimpleNamespace(ring_world_size=1)), **kw)
+
+    mode = {"m": "strict"}
+    for name, attrs in (("vllm_omni", {}), ("vllm_omni.diffusion", {}), ("vllm_omni.diffusion.attention", {}),
+                        ("vllm_omni.diffusion.attention.parallel", {}),
+                        ("vllm_omni.diffusion.attention.parallel.ulysses",
+                         {"UlyssesParallelAttention": UlyssesParallelAttention}),
+                        ("vllm_omni.diffusion.forward_context", {"get_ulysses_mode": lambda default: mode["m"]})):
+        m = ModuleType(name)
+        m.__dict__.update(attrs)
+        monkeypatch.setitem(sys.modules, name, m)
+    ws = {"n": 2}
+    monkeypatch.setattr(dist, "get_world_size", lambda pg: ws["n"])
+
+    def layer(strategy=None, **kw):
+        s = strategy or UlyssesParallelAttention()
+        ns = SimpleNamespace(_get_active_parallel_strategy=lambda: s, _active_paged_kv_adapter=lambda: None)
+        ns.__dict__.update(kw)
+        return ns
+
+    md = SimpleNamespace(attn_mask=None, joint_query=None, joint_key=None, joint_value=None, joint_attn_mask=None,
+                         extra={})
+    info = plugin.vllm_strategy_info
+    assert info(layer(), md) == ("pg", 2) and info(layer(), None) == ("pg", 2)
+    assert info(layer(strategy=object()), md) is None                              # not Ulysses
+    assert info(layer(use_ring=True), md) is None
+    for kw in ({"_use_sync": True}, {"_ulysses_a2a_permute": True}, {"_scatter_idx": 1},
+               {"_sp_group": SimpleNamespace(ring_world_size=2)}):
+        assert info(layer(strategy=UlyssesParallelAttention(**kw)), md) is None, kw
+    assert info(layer(_scheduler_paged_kv=True), md) is None
+    assert info(layer(_has_custom_attention=True), md) is None
+    paged = layer()
+    paged._active_paged_kv_adapter = lambda: object()
+    assert info(paged, md) is None
+    for field in ("attn_mask", "joint_query", "joint_attn_mask"):
+        assert info(layer(), SimpleNamespace(**dict(vars(md), **{field: object()}))) is None, field
+    assert info(layer(), SimpleNamespace(**dict(vars(md), extra={"gate_compress": 1}))) is None
+    mode["m"] = "relaxed"
+    assert info(layer(), md) is None
+    mode["m"], ws["n"] = "strict", 1
+    assert info(layer(), md) is None                                               # one rank: nothing to exchange
