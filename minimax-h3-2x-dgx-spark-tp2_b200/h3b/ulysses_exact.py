@@ -452,8 +452,13 @@ def make_forward_impl(orig, mode: str, strategy_info, *, a2a=None, stock_fwd=Non
             return attn(q, k, v, attn_metadata)
 
         if mode == "verify":   # both exchanges on the same tensors; the stock result is returned
-            res, _ = verify_forward(query, key, value, run, ws=ws, pg=pg, a2a=a2a, stock_fwd=stock_fwd,
-                                    stock_back=stock_back, pack=pack, unpack_fn=unpack_fn)
+            res, eq = verify_forward(query, key, value, run, ws=ws, pg=pg, a2a=a2a, stock_fwd=stock_fwd,
+                                     stock_back=stock_back, pack=pack, unpack_fn=unpack_fn)
+            differs = not all(eq.values())
+            if differs or _stats["verify_equal"] % 500 == 0:
+                logger.warning("h3b ulysses exact verify: %s (%d equal, %d differ so far)",
+                               " ".join(f"{n}={'eq' if e else 'DIFF'}" for n, e in eq.items()),
+                               _stats["verify_equal"], _stats["verify_differs"])
             return res
         sends = None
         if pend is not None:
