@@ -12,11 +12,21 @@ quant).  A placeholder that reaches anything else, or a deferral the forward nev
 """
 from __future__ import annotations
 
+import logging
 import threading
 
 import torch
 
 from . import ops
+
+logger = logging.getLogger("h3b.ulysses_outq")
+_warned: set = set()
+
+
+def _warn_once(key: str, msg: str, *args) -> None:  # noqa: ANN002
+    if key not in _warned:
+        _warned.add(key)
+        logger.warning("h3b ulysses_outq: " + msg, *args)
 
 FP8_MAX = 448.0
 FP8_MIN = -448.0
@@ -157,6 +167,7 @@ def _selfcheck(pend: Deferred, orig):  # noqa: ANN001,ANN202
     else:
         _stats["selfcheck_fail"] += 1
         _state["disabled"] = "self-check: " + why
+        logger.warning("h3b ulysses_outq: %s; the reverse unpack stays for this process", _state["disabled"])
     return stock
 
 
@@ -232,6 +243,8 @@ def check_sources(attn_forward) -> str | None:  # noqa: ANN001
     from . import sources  # noqa: PLC0415
     bad = sources.changed(sources.OUTQ_REVIEWED, source_fingerprints(attn_forward), sources.OUTQ_REVIEWED)
     _state["sources"] = ("upstream source changed: " + ", ".join(bad)) if bad else None
+    if bad:
+        _warn_once("sources", "%s; the reverse unpack stays", _state["sources"])
     return _state["sources"]
 
 
@@ -244,11 +257,14 @@ def prepare(owner) -> bool:  # noqa: ANN001
         return False
     ok = getattr(layer, "_h3b_outq", None)
     if ok is None:
-        ok = _state["sources"] is None and layer_mismatch(owner) is None
+        reason = _state["sources"] or layer_mismatch(owner)
+        ok = reason is None
         if ok:
             kernel = layer.quant_method.fp8_linear
             if not isinstance(kernel.quant_fp8, OutQuant):
                 kernel.quant_fp8 = OutQuant(kernel.quant_fp8)
+        else:
+            _warn_once("layer-" + reason, "out-projection not eligible (%s); the reverse unpack stays there", reason)
         layer._h3b_outq = ok
     return bool(ok)
 
