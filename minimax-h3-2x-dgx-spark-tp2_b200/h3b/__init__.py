@@ -5,8 +5,8 @@ Modules mirror the reference plugin's hot-path modules (knapcio/MiniMax-H3-2x-DG
 ``ulysses_exact``, ``ulysses_outq``, ``ulysses_overlap``, ``ulysses_nocopy``, ``fp8_gemm``, ``fp8_cutlass``,
 ``fp8_quant_fuse``, ``fp8_swiglu``, ``fp8_consumers``, ``a2a_timing`` and ``plugin``, with ``sources`` the
 reviewed-upstream-source gate of their model wiring; ``ops`` holds the tensor-level kernel entry points and ``block``
-the DiT attention block built from them.  All compute runs in the CUDA library ``libh3b.so`` (C ABI ``include/h3b.h``); nothing falls
-back to the CPU.
+the DiT attention block built from them.  All compute runs in the CUDA library ``libh3b.so`` (C ABI
+``include/h3b.h``); nothing falls back to the CPU.
 """
 from . import _lib, ops  # noqa: F401
 
