@@ -94,7 +94,7 @@ def probe_fused(device) -> bool:  # noqa: ANN001
     """True when the tcgen05 kernel can serve on ``device``: an sm_100 GPU and the library loads; a small GEMM
     against integer inputs (exact in any summation order) confirms it (h3_tp2/fp8_gemm.py:251)."""
     dev = torch.device(device)
-    if dev.type != "cuda" or torch.cuda.get_device_capability(dev) != (10, 0):
+    if dev.type != "cuda" or not torch.cuda.is_available() or torch.cuda.get_device_capability(dev) != (10, 0):
         return False
     g = torch.Generator(device=dev).manual_seed(0)
     a = torch.randint(-3, 4, (130, 64), device=dev, generator=g).to(torch.float8_e4m3fn)

@@ -66,7 +66,7 @@ def probe_gemm_swiglu(device) -> bool:  # noqa: ANN001
     (exact accumulators in any summation order) within 1 bf16 ulp (torch's exp against CUDA's expf)
     (h3_tp2/fp8_swiglu.py:258)."""
     dev = torch.device(device)
-    if dev.type != "cuda" or torch.cuda.get_device_capability(dev) != (10, 0):
+    if dev.type != "cuda" or not torch.cuda.is_available() or torch.cuda.get_device_capability(dev) != (10, 0):
         return False
     g = torch.Generator(device=dev).manual_seed(0)
     a = torch.randint(-3, 4, (130, 64), device=dev, generator=g).to(torch.float8_e4m3fn)

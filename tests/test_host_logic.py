@@ -528,3 +528,10 @@ def test_a2a_timing_wraps_the_collective_the_4d_exchange_and_reports_per_diffuse
     finally:
         a2a_timing.uninstall()
     assert Pipeline.diffuse is orig_diffuse and not getattr(dist.all_to_all_single, "_h3b_a2a_timing", False)
+
+
+def test_probes_answer_false_without_a_gpu():
+    """The install probes never raise on a host without a GPU: the dispatcher then leaves the stock kernel in place."""
+    from h3b import fp8_swiglu
+    assert fp8_gemm.probe_fused("cuda") is False and fp8_gemm.probe_fused("cpu") is False
+    assert fp8_swiglu.probe_gemm_swiglu("cuda") is False
