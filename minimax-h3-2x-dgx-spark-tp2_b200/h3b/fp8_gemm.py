@@ -165,6 +165,15 @@ def route(a, b, scale_a, scale_b, out_dtype, bias=None, two_pass=None):  # noqa:
     return (two_pass or scaled_mm)(a, b, scale_a, scale_b, out_dtype, bias)
 
 
+def _route_summary() -> str:
+    """At the cutlass level, how many of the taken calls the block router served (h3_tp2/fp8_gemm.py:304)."""
+    if _state["level"] != "cutlass":
+        return ""
+    from . import fp8_cutlass  # noqa: PLC0415
+    st = fp8_cutlass.stats()
+    return f" (block router: taken {st['dsl']}, fell through {st['fallthrough']})"
+
+
 def _install_into(vops, level: str, probe=None, cutlass_probe=None) -> None:  # noqa: ANN001
     """``install`` on the module ``vops`` that holds ``cutlass_scaled_mm``; ``probe(device)`` / ``cutlass_probe(device)``
     default to ``probe_fused`` and ``fp8_cutlass.probe``."""
@@ -180,12 +189,21 @@ def _install_into(vops, level: str, probe=None, cutlass_probe=None) -> None:  # 
                        "self-check); vLLM's stock kernel stays")
         return
     stats = {"two_pass": 0, "stock": 0}   # the reference's names: calls this dispatch took / left to the stock kernel
+    seen: set = set()
 
     def _mm(a, b, scale_a, scale_b, out_dtype, bias=None):  # noqa: ANN001
         if not (a.is_cuda and eligible(a, b, scale_a, scale_b, out_dtype, bias)):
             stats["stock"] += 1
             return orig(a, b, scale_a, scale_b, out_dtype, bias)
         stats["two_pass"] += 1
+        shape = (a.shape[0], b.shape[1], a.shape[1])
+        if len(seen) < 64 and shape not in seen:          # each distinct shape once (h3_tp2/fp8_gemm.py:375-381)
+            seen.add(shape)
+            logger.info("h3b: FP8 GEMM shape M=%d N=%d K=%d", *shape)
+        n = stats["two_pass"] + stats["stock"]
+        if n == 2000 or n % 20000 == 0:
+            logger.info("h3b: FP8 GEMM dispatch so far: taken %d, stock %d%s", stats["two_pass"], stats["stock"],
+                        _route_summary())
         return route(a, b, scale_a, scale_b, out_dtype, bias)
 
     _mm._h3b = True
