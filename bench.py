@@ -4,14 +4,20 @@
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL over NVLink)
 
 Workload: 124,992 tokens (31 x 48 x 84), hidden 5120, 40 heads x 128, B = 1, bf16 activations
-x ~ N(0,1) (seed 0 + rank), weights N(0, 0.02) quantised per output channel to e4m3 (seed 1), dynamic per-token e4m3
+x ~ N(0,1) (seed = rank), weights N(0, 0.02) quantised per output channel to e4m3 (seed 1), dynamic per-token e4m3
 activation quant; Ulysses degree P = number of ranks (each rank holds 124,992 / P rows).  One step = one block
 forward on every rank.  Inputs are larger than L2 (x is 1.28 GB / P, the attention streams 2.6 GB of K/V per head
 group), so no explicit flush is needed.  Rank 0 prints one JSON line.
 
+After the timed regions every rank checks its part of one more forward against the CPU oracle on 64 sampled rows
+(``parity`` in the JSON line, the worst over ranks): the qkv projection rows it received from every rank, the
+attention of its heads for those rows against the device's K/V, the reverse exchange, and the whole block's output
+rows through the oracle's attention, quant and out projection.
+
 ``--impl reference`` times the reference's CPU path for the same workload on the host cores (the oracle port of
-h3_tp2's eager arithmetic: per-token quant, FP8 GEMM epilogue, fp32 SDPA) on a bounded per-head sample scaled to the
-whole block, as the driver's reference arm.
+h3_tp2's eager arithmetic: per-token quant, FP8 GEMM epilogue, fp32 SDPA) on a bounded per-head sample, as the
+driver's reference arm; its ``ms_per_step`` is the measured sample time and ``block_ms_extrapolated`` the whole
+block scaled from it.
 """
 from __future__ import annotations
 
@@ -145,7 +151,8 @@ class ClockSampler:
 
 def cpu_sample(tokens: int, q_rows: int = 1024, threads: int | None = None) -> dict:
     """Time one head's attention for ``q_rows`` queries against all ``tokens`` keys (fp32 SDPA) plus that slice's
-    share of the FP8 projections (per-token quant + the eager GEMM epilogue), then scale to 40 heads x all rows."""
+    share of the FP8 projections (per-token quant + the eager GEMM epilogue); the block figure scales it to 40 heads x
+    all rows."""
     from oracle import attention as oa  # noqa: PLC0415
     from oracle import gemm as og  # noqa: PLC0415
     from oracle import quant as oq  # noqa: PLC0415
@@ -160,8 +167,8 @@ def cpu_sample(tokens: int, q_rows: int = 1024, threads: int | None = None) -> d
     k = torch.randn(tokens, 1, d, generator=g).to(torch.bfloat16)
     v = torch.randn(tokens, 1, d, generator=g).to(torch.bfloat16)
     t0 = time.perf_counter()
-    q8, sx = oq.quant(x)                                  # the whole row's quant (shared by all heads; counted once
-    qkv = og.scaled_mm(q8, wq[0], sx, wq[1])              # per head below as 1/40 of it is an underestimate: keep)
+    q8, sx = oq.quant(x)                                  # the whole rows' quant, counted once per head (an
+    qkv = og.scaled_mm(q8, wq[0], sx, wq[1])              # overestimate of this head's share of it)
     q = qkv[:, :d].reshape(q_rows, 1, d)
     t1 = time.perf_counter()
     o = oa.sdpa(q, k, v, chunk=256).to(torch.bfloat16)
@@ -169,15 +176,101 @@ def cpu_sample(tokens: int, q_rows: int = 1024, threads: int | None = None) -> d
     o8, so = oq.quant(o.reshape(q_rows, d))
     og.scaled_mm(o8, wo[0], so, wo[1])
     t3 = time.perf_counter()
-    scale_rows = tokens / q_rows
-    proj_s = ((t1 - t0) + (t3 - t2)) * scale_rows * HEADS
-    attn_s = (t2 - t1) * scale_rows * HEADS
-    total_s = proj_s + attn_s
-    fl = sum(block_flops(tokens).values())
-    return {"seconds_per_block": total_s, "tflops": fl / total_s / 1e12, "sample_seconds": t3 - t0,
-            "threads": torch.get_num_threads(),
+    sample_s = t3 - t0
+    scale = tokens / q_rows * HEADS
+    # the sample's own work: one head of attention for q_rows rows + its projection share
+    sample_fl = 4.0 * q_rows * tokens * d + 2.0 * q_rows * HIDDEN * 3 * d + 2.0 * q_rows * d * HIDDEN
+    return {"seconds": sample_s, "block_seconds": sample_s * scale, "tflops": sample_fl / sample_s / 1e12,
+            "attn_seconds": t2 - t1, "threads": torch.get_num_threads(),
             "sample": f"1 of {HEADS} heads, {q_rows} of {tokens} query rows vs all {tokens} keys (fp32 SDPA) + that "
-                      f"slice's FP8 projection share; scaled x{scale_rows * HEADS:.0f}"}
+                      f"slice's FP8 projection share; the block time scales it x{scale:.0f}"}
+
+
+def _cfg0_worker(rank: int, ws: int, port: int, threads: int, reps: int, out: str) -> None:
+    """One rank of BASELINE configs[0] (fp32, gloo): the reference's exact_forward data flow with fp32 projections
+    (the oracle port, oracle.block.fp32_block), timed reps times after one warm-up."""
+    import datetime  # noqa: PLC0415
+    for pth in (str(PKG), str(ROOT)):
+        if pth not in sys.path:
+            sys.path.insert(0, pth)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.set_num_threads(threads)
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=120))
+    try:
+        from oracle import block as ob  # noqa: PLC0415
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(4096, 1024, generator=g)
+        wqkv = torch.randn(3 * 1024, 1024, generator=g) * 0.02
+        wo = torch.randn(1024, 1024, generator=g) * 0.02
+        m = x.shape[0] // ws
+        xl = x[rank * m:(rank + 1) * m].contiguous()
+
+        def a2a(o, i):
+            dist.all_to_all_single(o, i)
+
+        times = []
+        for it in range(reps + 1):
+            dist.barrier()
+            t0 = time.perf_counter()
+            ob.fp32_block(xl, wqkv, wo, 8, ws, a2a)
+            dist.barrier()
+            if it:
+                times.append(time.perf_counter() - t0)
+        if rank == 0:
+            Path(out).write_text(json.dumps(times))
+    finally:
+        dist.destroy_process_group()
+
+
+def cpu_cfg0(cores: int, reps: int = 5) -> dict:
+    """BASELINE configs[0] whole: 2 gloo processes x cores/2 threads, median of ``reps`` after one warm-up."""
+    import socket  # noqa: PLC0415
+    import tempfile  # noqa: PLC0415
+
+    import torch.multiprocessing as mp  # noqa: PLC0415
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    per = max(1, cores // 2)
+    with tempfile.TemporaryDirectory() as tmp:
+        out = str(Path(tmp) / "t.json")
+        mp.start_processes(_cfg0_worker, args=(2, port, per, reps, out), nprocs=2, start_method="spawn")
+        times = json.loads(Path(out).read_text())
+    return {"ms": statistics.median(times) * 1e3, "cores": 2 * per, "processes": 2, "reps": reps}
+
+
+def cpu_cfg1_slice(cores: int) -> dict:
+    """BASELINE configs[1] (66,960 tokens), one head: the whole head's fp32 SDPA (all queries, all keys) plus its share
+    of the FP8 projections (quant of all rows, 3 x 128 qkv columns, 128 rows of the out projection), timed once; the
+    block figure scales it x40 (all heads)."""
+    from oracle import attention as oa  # noqa: PLC0415
+    from oracle import gemm as og  # noqa: PLC0415
+    from oracle import quant as oq  # noqa: PLC0415
+    torch.set_num_threads(cores)
+    n, d = 66_960, HEAD_DIM
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(n, HIDDEN, generator=g).to(torch.bfloat16)
+    wq = og.quant_weight(torch.randn(3 * d, HIDDEN, generator=g) * 0.02)
+    wo = og.quant_weight(torch.randn(HIDDEN, d, generator=g) * 0.02)
+    t0 = time.perf_counter()
+    q8, sx = oq.quant(x)
+    qkv = og.scaled_mm(q8, wq[0], sx, wq[1]).reshape(n, 3, 1, d)
+    o = oa.sdpa(qkv[:, 0], qkv[:, 1], qkv[:, 2], chunk=1024).to(torch.bfloat16)
+    o8, so = oq.quant(o.reshape(n, d))
+    og.scaled_mm(o8, wo[0], so, wo[1])
+    sec = time.perf_counter() - t0
+    return {"ms": sec * 1e3, "ms_scaled": sec * 1e3 * HEADS, "cores": cores,
+            "sample": f"configs[1] one head of {HEADS}: all {n} queries x {n} keys fp32 SDPA + its projection share, "
+                      f"scaled x{HEADS}"}
+
+
+def config_dict(tokens: int, world: int) -> dict:
+    """The workload both arms print (identical dicts: the reference arm runs the same configuration)."""
+    return {"workload": f"cfg2 DiT attention block: {tokens} tokens (31x48x84), hidden {HIDDEN}, {HEADS} heads x "
+                        f"{HEAD_DIM}, Ulysses SP={world}", "tokens": tokens, "rows_per_rank": tokens // world,
+            "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM, "sp": world,
+            "l2": "inputs larger than L2 (no flush)"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
@@ -187,16 +280,17 @@ def run_reference(args, rank: int, world: int) -> None:
     torch.set_num_threads(threads)
     tokens = args.tokens or TOKENS
     for _ in range(args.warmup):
-        cpu_sample(tokens, q_rows=256, threads=threads)
+        cpu_sample(tokens, q_rows=args.ref_rows, threads=threads)
     samples = [cpu_sample(tokens, q_rows=args.ref_rows, threads=threads) for _ in range(args.steps)]
-    sec = statistics.median(s["seconds_per_block"] for s in samples)
-    fl = sum(block_flops(tokens).values())
-    value = fl / sec / 1e12
+    value = statistics.median(s["tflops"] for s in samples)
+    step_ms = statistics.median(s["seconds"] for s in samples) * 1e3
+    block_ms = statistics.median(s["block_seconds"] for s in samples) * 1e3
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (CPU eager path)", "data": "synthetic",
-            "config": {"workload": f"cfg2 DiT attention block, {tokens} tokens, hidden {HIDDEN}, {HEADS}x{HEAD_DIM}",
-                       "tokens": tokens, "sp": world},
+            "config": config_dict(tokens, world),
+            "step": "one bounded sample of the block (the cpu_baseline sample), timed on the host cores",
+            "block_ms_extrapolated": block_ms,
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": samples[0]["threads"], "kind": "port",
                              "sample": samples[0]["sample"]},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -204,12 +298,85 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # ---------------------------------------------------------------------------------------------------------------
-# GPU arm
+# parity at the benchmark's shape: sampled rows of one more forward against the CPU oracle, on every rank
 # ---------------------------------------------------------------------------------------------------------------
 
 
-# DRAM bytes (read + write) of one attention launch at cfg2 SP=1, from the ncu launch list of this bench
-ATTN_TRAFFIC_BYTES = 33.82e9
+def make_x(rank: int, m: int, dev) -> torch.Tensor:
+    """Rank ``rank``'s input rows (any rank can regenerate any other's from its seed)."""
+    g = torch.Generator(device=dev).manual_seed(rank)
+    return torch.randn(m, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
+
+
+def block_parity(blk, keep: dict, rank: int, world: int, m: int, dev, pg, rows: int = 64) -> dict:
+    """This rank's share of the block at ``rows`` sampled local rows (the same rows on every rank), against the CPU
+    oracle (oracle.quant / oracle.gemm / oracle.attention):
+      qkv       the q/k/v rows this rank received from every rank (its head group's columns) against the oracle's
+                quant + FP8 projection of those ranks' inputs (regenerated from their seeds);
+      attention every rank's oracle attention for its head group at those query rows (the oracle's q against the
+                device's K/V of all tokens), exchanged back, against this rank's reverse receive buffer;
+      out       the device's y rows against the oracle's quant + out projection of the device's reverse buffer rows;
+      block     the device's y rows against the oracle's quant + out projection of the oracle's attention rows.
+    Thresholds: GEMM-based stages rel-L2 <= 1e-2 (the FP8 GEMM contract); attention rel-L2 <= 2e-3 and max-abs <=
+    2e-2 (the attention contract); block rel-L2 <= 1e-2."""
+    from oracle import attention as oa  # noqa: PLC0415
+    from oracle import gemm as og  # noqa: PLC0415
+    from oracle import quant as oq  # noqa: PLC0415
+
+    def rel(a, b):
+        a, b = a.double(), b.double()
+        return float((a - b).norm() / b.norm().clamp_min(1e-300))
+
+    H, d = HEADS, HEAD_DIM
+    hl = H // world
+    idx = torch.linspace(0, m - 1, rows).round().long()
+    idx_d = idx.to(dev)
+    xs = torch.stack([make_x(p, m, dev)[idx_d].cpu() for p in range(world)])            # [P, R, C]
+    cols = torch.cat([torch.arange(w * H * d + rank * hl * d, w * H * d + (rank + 1) * hl * d) for w in range(3)])
+    wq8, sq = blk.wqkv8[cols.to(dev)].cpu(), blk.sqkv[cols.to(dev)].cpu()
+    q8, sx = oq.quant(xs.reshape(world * rows, HIDDEN))
+    qkv = og.scaled_mm(q8, wq8, sx, sq).reshape(world * rows, 3, hl, d)                 # bf16
+    tok = (torch.arange(world)[:, None] * m + idx[None, :]).reshape(-1).to(dev)         # [P*R] gathered rows
+    got = torch.stack([keep[n][tok].float().cpu() for n in ("q", "k", "v")], dim=1)
+    r_qkv = rel(got, qkv.float())
+    # oracle attention of this rank's heads for all P*R sampled tokens, against the device's K/V (one head at a time)
+    o_or = torch.empty(world * rows, hl, d)
+    for h in range(hl):
+        kh = keep["k"][:, h:h + 1].contiguous().cpu()
+        vh = keep["v"][:, h:h + 1].contiguous().cpu()
+        o_or[:, h:h + 1] = oa.sdpa(qkv[:, 0, h:h + 1], kh, vh, chunk=world * rows)
+    o_or = o_or.reshape(world, rows, hl, d)                                              # [dest rank, R, hl, d]
+    if world > 1:
+        recv = torch.empty_like(o_or, device=dev)
+        dist.all_to_all_single(recv, o_or.to(dev).contiguous(), group=pg)
+        attn_or = recv.cpu()                                                             # [head group, R, hl, d]
+    else:
+        attn_or = o_or
+    back = keep["back"][:, idx_d].float().cpu()                                          # [head group, R, hl, d]
+    r_attn = rel(back, attn_or)
+    a_attn = float((back - attn_or).abs().max())
+    wo8, so_w = blk.wo8.cpu(), blk.so.cpu()
+    y = keep["y"][idx_d].float().cpu()
+    ob8, obs = oq.quant(back.permute(1, 0, 2, 3).reshape(rows, H * d).to(torch.bfloat16))
+    r_out = rel(y, og.scaled_mm(ob8, wo8, obs, so_w).float())
+    oa8, oas = oq.quant(attn_or.permute(1, 0, 2, 3).reshape(rows, H * d).to(torch.bfloat16))
+    r_block = rel(y, og.scaled_mm(oa8, wo8, oas, so_w).float())
+    vals = [r_qkv, r_attn, a_attn, r_out, r_block]
+    if world > 1:
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+        vals = t.tolist()
+    r_qkv, r_attn, a_attn, r_out, r_block = vals
+    ok = r_qkv <= 1e-2 and r_attn <= 2e-3 and a_attn <= 2e-2 and r_out <= 1e-2 and r_block <= 1e-2
+    return {"rows": rows, "tokens_checked": rows * world, "rel_l2": {"qkv": r_qkv, "attention": r_attn,
+            "out": r_out, "block": r_block}, "max_abs": {"attention": a_attn},
+            "tolerance": {"qkv": 1e-2, "attention": [2e-3, 2e-2], "out": 1e-2, "block": 1e-2},
+            "oracle": "oracle.quant + oracle.gemm + oracle.attention (fp32 SDPA) on the CPU", "ok": bool(ok)}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------------------------
 
 
 def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
@@ -243,8 +410,7 @@ def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
 def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
     from h3b import ops  # noqa: PLC0415
 
-    g = torch.Generator(device=dev).manual_seed(rank)
-    x = torch.randn(m, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
+    x = make_x(rank, m, dev)
 
     def barrier():
         if world > 1:
@@ -334,35 +500,56 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
     attn_fl_per_launch = fl["attention"] / world
     achieved = attn_fl_per_launch / (attn_ms * 1e-3) / 1e12
     peak = peaks["bf16_sustained"]
+    # ---- parity: one more forward, its sampled rows against the CPU oracle on every rank (outside the timings) ----
+    keep = {}
+    blk.forward(x, keep=keep)
+    torch.cuda.synchronize(dev)
+    status = ops.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} in the parity forward")
+    if world > 1:
+        torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
+    parity = block_parity(blk, keep, rank, world, m, dev, pg)
+    del keep
+
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "e4m3 projections (f32 acc), bf16 attention (f16 P.V, f32 softmax)",
-        "data": "synthetic",
-        "config": {"workload": f"cfg2 DiT attention block: {tokens} tokens (31x48x84), hidden {HIDDEN}, "
-                               f"{HEADS} heads x {HEAD_DIM}, Ulysses SP={world}", "tokens": tokens,
-                   "rows_per_rank": m, "hidden": HIDDEN, "heads": HEADS, "head_dim": HEAD_DIM, "sp": world,
-                   "head_groups": blk.groups, "l2": "inputs larger than L2 (no flush)",
-                   "exchange": {"p2p": "peer memory (epilogue stores over NVLink + epoch barriers)",
-                                "nccl": "NCCL all_to_all_single (q, k, v, out)",
-                                "nocopy": "NCCL all_to_all_single (combined q/k/v per head group, out)"}[args.exchange]
-                               if world > 1 else "none (SP=1)"},
+        "data": "synthetic", "config": config_dict(tokens, world),
+        "exchange": {"p2p": "peer memory (epilogue stores over NVLink + epoch barriers)",
+                     "nccl": "NCCL all_to_all_single (q, k, v, out)",
+                     "nocopy": "NCCL all_to_all_single (combined q/k/v per head group, out)"}[args.exchange]
+                    if world > 1 else "none (SP=1)",
+        "head_groups": blk.groups,
         "ms_per_stage": stage_ms,
         "roofline": {"bound": "tensor", "kernel": "flash_attn", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": f"{peaks['source']} bf16 dense, sustained (kernel timed inside a long step)",
-                     "traffic": ATTN_TRAFFIC_BYTES if (world == 1 and tokens == TOKENS) else None,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one attention launch "
-                                       "in the launch-list capture of this bench at cfg2 SP=1"},
+                     "traffic": None,
+                     "traffic_source": "not measured by this run (DRAM bytes need an ncu capture; the committed "
+                                       "profiles hold them)"},
         "e2e": {"value": total_fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": m * HIDDEN * 2, "d2h_bytes_per_step": m * HIDDEN * 2},
         "gpu_launches": (blk.KERNELS_PER_FORWARD + (blk.P2P_BARRIERS if p2p else 0)) * args.steps,
         "clocks": clocks.summary(),
+        "parity": parity,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_sample(tokens, q_rows=args.ref_rows, threads=os.cpu_count())
-        line["cpu_baseline"] = {"value": cb["tflops"], "unit": "TFLOP/s", "cores": cb["threads"], "kind": "port",
-                                "sample": cb["sample"], "ms_per_block": cb["seconds_per_block"] * 1e3}
+        cores = os.cpu_count() or 1
+        cpu_sample(tokens, q_rows=256, threads=cores)            # warm-up (thread pool, page faults)
+        cbs = [cpu_sample(tokens, q_rows=args.ref_rows, threads=cores) for _ in range(3)]
+        c0 = cpu_cfg0(cores)
+        c1 = cpu_cfg1_slice(cores)
+        line["cpu_baseline"] = {
+            "value": statistics.median(c["tflops"] for c in cbs), "unit": "TFLOP/s", "cores": cbs[0]["threads"],
+            "kind": "port", "sample": cbs[0]["sample"] + " (median of 3 after a warm-up)",
+            "ms_per_block": statistics.median(c["block_seconds"] for c in cbs) * 1e3,
+            "cfg0_ms": c0["ms"], "cfg0_cores": c0["cores"],
+            "cfg0": f"configs[0] whole: 4096 tokens, hidden 1024, 8 x 128, fp32, 2 gloo processes x "
+                    f"{c0['cores'] // 2} threads, median of {c0['reps']} after 1 warm-up",
+            "cfg1_slice_ms": c1["ms"], "cfg1_slice_ms_scaled": c1["ms_scaled"], "cfg1_cores": c1["cores"],
+            "cfg1": c1["sample"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
 

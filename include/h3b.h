@@ -101,7 +101,7 @@ typedef struct h3b_qkv_send {
 /* ---------------------------------------------------------------------------------------------------------------
  * library information
  * ------------------------------------------------------------------------------------------------------------- */
-H3B_API int h3b_abi_version(void); /* 3: h3b_qkv_send gained the peer-memory fields (2) and qkv_interleaved (3) */
+H3B_API int h3b_abi_version(void); /* 3: h3b_qkv_send gained the peer-memory fields (2) and qkv_interleaved (3); 4: the *_bf16v attention entry points and h3b_noalloc_status */
 H3B_API const char* h3b_status_string(int status);
 H3B_API const char* h3b_last_error(void);
 /* Reads and clears the sticky device status word of the current device (0 or a negative h3b_status). Synchronises
@@ -207,29 +207,55 @@ H3B_API int h3b_fp8_gemm_gate(const void* a, int64_t lda, const void* w, int64_t
  * With v_f16 the P.V product runs in f16 (P in [0, 256] after the online max, V exactly representable when |v| lies
  * in f16's normal range); with bf16 V it runs in bf16.  range_flag (device int or NULL) is the flag that the f16
  * conversion of v raised; when it holds 1 the kernel writes nothing and records H3B_ERANGE in the device status word
- * (the caller then reruns with bf16 v). */
+ * (the caller then reruns with bf16 v).  h3b_flash_attn_fwd_bf16v makes that choice on the device instead. */
 H3B_API int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok, int64_t k_head,
                        const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok, int64_t o_head,
                        int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
                        int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream);
 
+/* The drop-in local attention for a bf16 v of any range, as the reference's cuDNN SDPA takes it
+ * (h3_tp2/ulysses_exact.py:495-496): same arguments and result as h3b_flash_attn_fwd with a bf16 v, plus two
+ * caller-allocated scratch buffers, both 16-byte aligned: v16 [valid_kv, heads, 128] f16 (contiguous) and ctl of
+ * H3B_ATTN_CTL_BYTES(heads) bytes (int32 range flag at byte 0, bytes 4-15 left alone, per (head, column) maxima from
+ * byte 16).  Enqueued on `stream`: the flag and maxima are cleared; v16 = f16(v[:valid_kv]), the flag set to 1 if a
+ * finite value overflows f16; the f16 P.V kernel computes o unless the flag is set; only if it is set, v16 is
+ * rewritten as f16(v * 2^-e) with e >= 0 the smallest exponent that brings each (head, column) of v into f16's range,
+ * and the f16 P.V kernel computes o with each output column multiplied back by 2^e (exact power-of-two scaling).  The
+ * choice is made on the device (no host read), so o is always written; the flag afterwards says which pass ran.
+ * Rows of v and k at or beyond valid_kv are never read. */
+#define H3B_ATTN_CTL_BYTES(heads) (16ll + 512ll * (long long)(heads))
+H3B_API int h3b_flash_attn_fwd_bf16v(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                     int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o,
+                                     int64_t o_tok, int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv,
+                                     int32_t heads, int32_t head_dim, float scale, void* v16, void* ctl,
+                                     h3b_stream_t stream);
+
 /* No counterpart in the reference: an attention entry point for callers that cannot allocate device memory (plugins
  * whose host framework owns all device memory and exposes no allocator to them; processes that must not allocate
- * after start-up, such as real-time services with a fixed memory plan).  Same arguments and result as h3b_flash_attn_fwd with
- * a bf16 v (v_f16 = 0 there means bf16 P.V; here v is bf16 and the P.V product runs in f16 whenever v fits, bf16
- * otherwise), but it allocates nothing: the f16 copy of v and its control words live in a fixed file-scope device
- * array of H3B_NOALLOC_SCRATCH_BYTES (32 MiB + 256 B) that every GPU loading the library holds until exit.
- * Limit: s_kv * heads * 128 <= H3B_NOALLOC_MAX_V_ELEMS (s_kv * heads <= 131072), else H3B_EUNSUPPORTED.
+ * after start-up, such as real-time services with a fixed memory plan).  Same arguments and result as
+ * h3b_flash_attn_fwd_bf16v (a bf16 v of any range), but it allocates nothing: the f16 copy of v, the control words
+ * and a status word live in a fixed file-scope device array of H3B_NOALLOC_SCRATCH_BYTES (32 MiB + 128.25 KiB)
+ * that every GPU loading the library holds until exit.
+ * Limits: valid_kv * heads * 128 <= H3B_NOALLOC_MAX_V_ELEMS (valid_kv * heads <= 131072) and heads <=
+ * H3B_NOALLOC_MAX_HEADS, else H3B_EUNSUPPORTED.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and sets the kernels'
  * shared-memory limit; make that first call before any stream capture.  All calls share the array: calls that
- * overlap on the GPU (other streams, other threads) race and must be serialised by the caller.  Device-side wait
- * failures are recorded in the array's own status word, not in h3b_device_status(). */
+ * overlap on the GPU (other streams, other threads) race and must be serialised by the caller.  A device-side wait
+ * that gives up is recorded in the array's own status word (not in h3b_device_status()); it stays set, and later
+ * calls on that device skip their work, until h3b_noalloc_status() reads and clears it. */
 #define H3B_NOALLOC_MAX_V_ELEMS (16ll << 20)
-#define H3B_NOALLOC_SCRATCH_BYTES (256ll + 2ll * H3B_NOALLOC_MAX_V_ELEMS)
+#define H3B_NOALLOC_MAX_HEADS 256
+#define H3B_NOALLOC_CTL_BYTES (256ll * ((H3B_ATTN_CTL_BYTES(H3B_NOALLOC_MAX_HEADS) + 255ll) / 256ll))
+#define H3B_NOALLOC_SCRATCH_BYTES (H3B_NOALLOC_CTL_BYTES + 2ll * H3B_NOALLOC_MAX_V_ELEMS)
 H3B_API int h3b_flash_attn_fwd_noalloc(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
                                        int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o,
                                        int64_t o_tok, int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv,
                                        int32_t heads, int32_t head_dim, float scale, h3b_stream_t stream);
+
+/* No counterpart in the reference: the status word of h3b_flash_attn_fwd_noalloc on the current device.  Waits for
+ * the device (cudaDeviceSynchronize), returns 0 or the h3b_status a call recorded since the last read, and clears
+ * it.  Allocates nothing. */
+H3B_API int h3b_noalloc_status(void);
 
 /* Peer-memory variant of h3b_flash_attn_fwd for the Ulysses reverse exchange (no reference counterpart: it replaces
  * the head->seq dist.all_to_all_single of h3_tp2/ulysses_exact.py:94): instead of o, each output row t of this
@@ -241,6 +267,14 @@ H3B_API int h3b_flash_attn_fwd_p2p(const void* q, int64_t q_tok, int64_t q_head,
                                    void* const* peer_back, int32_t ws, int32_t rank, int64_t m_rows, int64_t s_q,
                                    int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
                                    int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream);
+
+/* Peer-memory variant of h3b_flash_attn_fwd_bf16v (bf16 v of any range, chosen on the device; v16 and ctl as there),
+ * with the output rows stored as h3b_flash_attn_fwd_p2p stores them. */
+H3B_API int h3b_flash_attn_fwd_p2p_bf16v(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                         int64_t k_head, const void* v, int64_t v_tok, int64_t v_head,
+                                         void* const* peer_back, int32_t ws, int32_t rank, int64_t m_rows,
+                                         int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim,
+                                         float scale, void* v16, void* ctl, h3b_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * peer memory (CUDA IPC over NVLink; no multicast) for the Ulysses P2P exchange.  No reference counterpart: the

@@ -101,7 +101,7 @@ int num_sms() {
 
 extern "C" {
 
-int h3b_abi_version(void) { return 3; }
+int h3b_abi_version(void) { return 4; }
 
 const char* h3b_status_string(int status) {
   switch (status) {

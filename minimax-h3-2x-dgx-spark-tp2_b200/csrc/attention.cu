@@ -17,6 +17,8 @@
 // below bf16's, which keeps the output within rel-L2 2e-3 of fp32 SDPA.  Every wait is bounded; no multicast.
 #include <stdlib.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace h3b {
@@ -40,12 +42,23 @@ struct Params {
   int nkv;
   const int32_t* range_flag;
   int range_mode;  // 0: flag set -> record H3B_ERANGE, skip; 1: flag set -> skip; 2: run only when the flag is set
+  // the scaled fallback for a v beyond f16's range: per (head, column) the bits of max |v| (finite values); the f16 v
+  // given holds v * 2^-e and the output column is multiplied by 2^e, e = colscale_exp(colmax[head * 128 + c])
+  const uint32_t* colmax;
   // m_rows > 0: output row t goes to rank t / m_rows, row (rank * m_rows + t % m_rows) of peer_o[t / m_rows]
   int64_t m_rows;
   int rank;
   uint16_t* peer_o[H3B_MAX_RANKS];
   WaitCtl wc;
 };
+
+// Exponent e >= 0 of the power of two that brings a column of bf16 values whose largest magnitude has the bits
+// `amax_bits` into f16's range: amax * 2^-e <= 65504.  A bf16 magnitude m * 2^E has m <= 1.9921875 < 65504 / 2^15,
+// so e = max(0, E - 15) suffices (and is the smallest such e).
+__host__ __device__ __forceinline__ int colscale_exp(uint32_t amax_bits) {
+  const int e = static_cast<int>((amax_bits >> 23) & 0xFFu) - 127 - 15;
+  return e > 0 ? e : 0;
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -143,16 +156,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * BQ;
-  bool aborted_at_entry = status_bad(p.wc);
+  // The range flag was written by an earlier launch on this stream, so every thread reads the same value and the
+  // whole CTA leaves together, before it touches barriers or TMEM: a launch that is skipped costs almost nothing.
   if (p.range_flag != nullptr) {
     const bool raised = *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0;
     if (p.range_mode == 0 && raised) {
       if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
-      aborted_at_entry = true;
-    } else if ((p.range_mode == 1 && raised) || (p.range_mode == 2 && !raised)) {
-      aborted_at_entry = true;
+      return;
     }
+    if ((p.range_mode == 1 && raised) || (p.range_mode == 2 && !raised)) return;
   }
+  const bool aborted_at_entry = status_bad(p.wc);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -389,14 +403,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(o_tmem + cc, o);
           tmem_ld_wait();
           reg_fence(o);
+          // per-column factor: 1 / l, times 2^e on the scaled fallback (a power of two: the product is exact)
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = inv_l;
+          if (p.colmax != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              f[i] = inv_l * __int_as_float((127 + colscale_exp(__ldg(p.colmax + head * D + cc + i))) << 23);
+          }
           if (p.m_rows > 0) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               uint32_t w[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv_l,
-                                                         __uint_as_float(o[8 * v + 2 * e + 1]) * inv_l);
+                const int i = 8 * v + 2 * e;
+                __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(o[i]) * f[i], __uint_as_float(o[i + 1]) * f[i + 1]);
                 w[e] = *reinterpret_cast<uint32_t*>(&b);
               }
               srow[((cc >> 3) + v) ^ (lane & 15)] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -407,8 +430,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               uint32_t w[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv_l,
-                                                         __uint_as_float(o[8 * v + 2 * e + 1]) * inv_l);
+                const int i = 8 * v + 2 * e;
+                __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(o[i]) * f[i], __uint_as_float(o[i + 1]) * f[i + 1]);
                 w[e] = *reinterpret_cast<uint32_t*>(&b);
               }
               *reinterpret_cast<uint4*>(orow + cc + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -473,14 +496,17 @@ static cudaError_t set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-// once per device: the shared-memory opt-in of every kernel variant
+// once per device: the shared-memory opt-in of every kernel variant (first calls from several threads serialise
+// on the mutex; a device is marked done only after every attribute was set)
 static int attn_attrs() {
   using namespace h3b::attn;
   static bool done[64] = {false};
+  static std::mutex mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "flash_attn: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(H3B_EUNSUPPORTED, "flash_attn: device index %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
   if (done[dev]) return H3B_OK;
   e = set_smem(flash_attn_kernel<true, 0>, SMEM_BYTES);
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<true, 2>, SMEM_BYTES);
@@ -500,9 +526,11 @@ static int launch_attention(const void* q, int64_t q_tok, int64_t q_head, const 
   int rc = attn_attrs();
   if (rc) return rc;
   CUtensorMap tq, tk, tv;
+  // K and V maps end at valid_kv: the last key tile's rows beyond it come from the TMA's zero fill, never from
+  // memory (padding rows may hold anything, even values whose product with a zero P would not be zero)
   rc = make_qkv_map(&tq, q, p.s_q, p.heads, q_tok, q_head, BQ);
-  if (!rc) rc = make_qkv_map(&tk, k, p.s_kv, p.heads, k_tok, k_head, BKV);
-  if (!rc) rc = make_qkv_map(&tv, v, p.s_kv, p.heads, v_tok, v_head, BKV);
+  if (!rc) rc = make_qkv_map(&tk, k, p.valid_kv, p.heads, k_tok, k_head, BKV);
+  if (!rc) rc = make_qkv_map(&tv, v, p.valid_kv, p.heads, v_tok, v_head, BKV);
   if (rc) return rc;
   p.nkv = static_cast<int>((p.valid_kv + BKV - 1) / BKV);
   dim3 grid(static_cast<unsigned>((p.s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(p.heads));
@@ -521,43 +549,268 @@ static int launch_attention(const void* q, int64_t q_tok, int64_t q_head, const 
   return H3B_OK;
 }
 
-#ifndef H3B_ATTENTION_KERNEL_ONLY
+namespace h3b {
+namespace attn {
+
+// v [rows, heads, 128] bf16 (token stride v_tok, head stride v_head) -> out [rows, heads, 128] f16 contiguous;
+// *flag = 1 when a finite value overflows f16.  Only the rows the attention reads are converted (rows = valid_kv),
+// so padding rows beyond them can hold anything.
+__global__ void v_to_f16_kernel(const uint16_t* __restrict__ v, int64_t rows, int heads, int64_t v_tok,
+                                int64_t v_head, uint16_t* __restrict__ out, int32_t* flag) {
+  const int64_t total = rows * heads * 16;  // 16-byte granules of 8 elements
+  bool bad = false;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = t & 15, th = t >> 4;
+    const int64_t h = th % heads, tok = th / heads;
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(v + tok * v_tok + h * v_head) + c);
+    uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = __uint_as_float(w[i] << 16), b = __uint_as_float(w[i] & 0xFFFF0000u);
+      bad |= (fabsf(a) > 65504.0f && isfinite(a)) || (fabsf(b) > 65504.0f && isfinite(b));
+      __half2 hv = __floats2half2_rn(a, b);
+      w[i] = *reinterpret_cast<uint32_t*>(&hv);
+    }
+    reinterpret_cast<uint4*>(out)[t] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicExch(flag, 1);
+}
+
+// Only when *flag is set (a v beyond f16's range): colmax[h * 128 + c] = bits of max |v[t, h, c]| over the finite
+// values of rows t < rows (non-negative floats order as their bits).  Grid (x, heads), 256 threads: thread i keeps
+// the maxima of the 8 columns of granule i % 16 over its tokens, the CTA merges them in shared memory and adds them
+// to the global maxima with one atomic per column.
+__global__ void v_colmax_kernel(const uint16_t* __restrict__ v, int64_t rows, int64_t v_tok, int64_t v_head,
+                                const int32_t* flag, uint32_t* colmax) {
+  if (*reinterpret_cast<const volatile int32_t*>(flag) == 0) return;
+  __shared__ uint32_t cm[D];
+  if (threadIdx.x < D) cm[threadIdx.x] = 0;
+  __syncthreads();
+  const int h = blockIdx.y, c = threadIdx.x & 15;
+  uint32_t m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int64_t tok = blockIdx.x * static_cast<int64_t>(blockDim.x / 16) + (threadIdx.x >> 4); tok < rows;
+       tok += static_cast<int64_t>(gridDim.x) * (blockDim.x / 16)) {
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(v + tok * v_tok + h * v_head) + c);
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t a = (w[i] << 16) & 0x7FFFFFFFu, b = w[i] & 0x7FFF0000u;
+      if (a < 0x7F800000u) m[2 * i] = max(m[2 * i], a);  // finite magnitudes only
+      if (b < 0x7F800000u) m[2 * i + 1] = max(m[2 * i + 1], b);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) atomicMax(&cm[c * 8 + i], m[i]);
+  __syncthreads();
+  if (threadIdx.x < D) atomicMax(colmax + h * D + threadIdx.x, cm[threadIdx.x]);
+}
+
+// Only when *flag is set: out[t, h, c] = f16(v[t, h, c] * 2^-e), e = colscale_exp(colmax[h * 128 + c]); every
+// finite value then fits f16, and the power-of-two scale is exact (the attention multiplies the output column back).
+__global__ void v_to_f16_scaled_kernel(const uint16_t* __restrict__ v, int64_t rows, int heads, int64_t v_tok,
+                                       int64_t v_head, uint16_t* __restrict__ out, const int32_t* flag,
+                                       const uint32_t* __restrict__ colmax) {
+  if (*reinterpret_cast<const volatile int32_t*>(flag) == 0) return;
+  const int64_t total = rows * heads * 16;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = t & 15, th = t >> 4;
+    const int64_t h = th % heads, tok = th / heads;
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(v + tok * v_tok + h * v_head) + c);
+    uint32_t w[4] = {x.x, x.y, x.z, x.w};
+    const uint32_t* cmx = colmax + h * D + c * 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float sa = __int_as_float((127 - colscale_exp(__ldg(cmx + 2 * i))) << 23);
+      const float sb = __int_as_float((127 - colscale_exp(__ldg(cmx + 2 * i + 1))) << 23);
+      __half2 hv = __floats2half2_rn(__uint_as_float(w[i] << 16) * sa, __uint_as_float(w[i] & 0xFFFF0000u) * sb);
+      w[i] = *reinterpret_cast<uint32_t*>(&hv);
+    }
+    reinterpret_cast<uint4*>(out)[t] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+}  // namespace attn
+}  // namespace h3b
+
+// The attention of a bf16 v of any range, decided on the device (no host read).  ctl (H3B_ATTN_CTL_BYTES(heads),
+// 16-byte aligned): int32 range flag at byte 0, bytes 4-15 untouched, colmax [heads * 128] uint32 from byte 16.
+//   1. clear the flag and colmax; convert the valid rows of v to f16 into v16 (flag = 1 on a finite overflow)
+//   2. the f16 P.V kernel, unless the flag is set                                   (the path of every v that fits)
+//   3. only if the flag is set: colmax, then v16 = f16(v * 2^-e) per (head, column)
+//   4. only if the flag is set: the f16 P.V kernel on that v16, the output columns multiplied by 2^e
+// Launches whose condition does not hold leave at once.  p carries everything but the range fields and nkv; p.wc says
+// where a wait failure is recorded.
+static int attention_bf16v(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok, int64_t k_head,
+                           const void* v, int64_t v_tok, int64_t v_head, void* v16, void* ctl, h3b::attn::Params p,
+                           cudaStream_t st) {
+  using namespace h3b::attn;
+  int32_t* flag = static_cast<int32_t*>(ctl);
+  uint32_t* colmax = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(ctl) + 16);
+  cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int32_t), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(colmax, 0, static_cast<size_t>(p.heads) * D * sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "flash_attn: clearing the range flag");
+  const int64_t granules = p.valid_kv * p.heads * 16;
+  int64_t blocks = (granules + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  const uint16_t* v_in = static_cast<const uint16_t*>(v);
+  uint16_t* v_out = static_cast<uint16_t*>(v16);
+  v_to_f16_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(v_in, p.valid_kv, p.heads, v_tok, v_head, v_out, flag);
+  H3B_CHECK_LAUNCH("flash_attn: v conversion launch");
+  p.range_flag = flag;
+  p.range_mode = 1;  // f16 P.V unless v overflowed f16
+  int rc = launch_attention(q, q_tok, q_head, k, k_tok, k_head, v16, static_cast<int64_t>(p.heads) * 128, 128, true,
+                            p, st);
+  if (rc) return rc;
+  // the scaled fallback: every launch below reads the flag first and leaves when v fitted
+  int64_t gx = (static_cast<int64_t>(num_sms()) * 4 + p.heads - 1) / p.heads;
+  const int64_t gx_max = (p.valid_kv + 15) / 16;
+  if (gx > gx_max) gx = gx_max;
+  if (gx > 65535) gx = 65535;
+  v_colmax_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(p.heads)), 256, 0, st>>>(
+      v_in, p.valid_kv, v_tok, v_head, flag, colmax);
+  H3B_CHECK_LAUNCH("flash_attn: v column maxima launch");
+  v_to_f16_scaled_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(v_in, p.valid_kv, p.heads, v_tok, v_head, v_out,
+                                                                     flag, colmax);
+  H3B_CHECK_LAUNCH("flash_attn: scaled v conversion launch");
+  p.range_mode = 2;  // only if v overflowed: f16 P.V on the scaled copy
+  p.colmax = colmax;
+  return launch_attention(q, q_tok, q_head, k, k_tok, k_head, v16, static_cast<int64_t>(p.heads) * 128, 128, true, p,
+                          st);
+}
+
+// Argument checks shared by the local entry points (ABI names in messages); on success *p holds everything but the
+// range fields, nkv and the wait control.
+static int local_params(const char* who, const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                        int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok,
+                        int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim,
+                        float scale, h3b::attn::Params* p) {
+  if (s_q < 0 || s_kv <= 0 || heads <= 0)
+    return fail(H3B_EINVAL, "%s: s_q %lld s_kv %lld heads %d", who, (long long)s_q, (long long)s_kv, heads);
+  if (head_dim != 128) return fail(H3B_EUNSUPPORTED, "%s: head_dim %d (only 128)", who, head_dim);
+  if (heads > 65535 || s_q > (1ll << 31) - 1 || s_kv > (1ll << 31) - 1)
+    return fail(H3B_EUNSUPPORTED, "%s: size limits (heads <= 65535, s_q and s_kv < 2^31)", who);
+  if (valid_kv < 0) valid_kv = s_kv;
+  if (valid_kv == 0 || valid_kv > s_kv)
+    return fail(H3B_EINVAL, "%s: valid_kv %lld of %lld", who, (long long)valid_kv, (long long)s_kv);
+  *p = h3b::attn::Params{};
+  p->s_q = s_q;
+  p->valid_kv = valid_kv;
+  if (s_q == 0) return H3B_OK;  // nothing to compute: the callers return before any launch
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return fail(H3B_EINVAL, "%s: null pointer", who);
+  const int64_t strides[8] = {q_tok, q_head, k_tok, k_head, v_tok, v_head, o_tok, o_head};
+  for (int64_t st : strides)
+    if (st <= 0 || st % 8) return fail(H3B_EALIGN, "%s: token/head strides must be positive multiples of 8", who);
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(o)) & 15u)
+    return fail(H3B_EALIGN, "%s: q, k, v, o must be 16-byte aligned", who);
+  p->s_kv = s_kv;
+  p->heads = heads;
+  p->scale_log2 = scale * 1.4426950408889634f;
+  p->o = static_cast<uint16_t*>(o);
+  p->o_tok = o_tok;
+  p->o_head = o_head;
+  return H3B_OK;
+}
+
+// the same for the peer-memory entry points: output row t of this rank's heads goes to rank t / m_rows
+static int p2p_params(const char* who, const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                      int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* const* peer_back,
+                      int32_t ws, int32_t rank, int64_t m_rows, int64_t s_q, int64_t s_kv, int64_t valid_kv,
+                      int32_t heads, int32_t head_dim, float scale, h3b::attn::Params* p) {
+  if (peer_back == nullptr || ws < 1 || ws > H3B_MAX_RANKS || rank < 0 || rank >= ws)
+    return fail(H3B_EINVAL, "%s: ws %d rank %d", who, ws, rank);
+  if (m_rows <= 0 || s_q != m_rows * ws)
+    return fail(H3B_EINVAL, "%s: s_q %lld must be ws * m_rows (%d * %lld)", who, (long long)s_q, ws, (long long)m_rows);
+  for (int r = 0; r < ws; ++r)
+    if (peer_back[r] == nullptr || (reinterpret_cast<uintptr_t>(peer_back[r]) & 15u))
+      return fail(H3B_EALIGN, "%s: peer buffer %d null or not 16-byte aligned", who, r);
+  // receive buffers [P, m_rows, heads, 128]: the own buffer stands in for o in the checks
+  const int64_t o_tok = static_cast<int64_t>(heads) * 128;
+  int rc = local_params(who, q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, peer_back[rank], o_tok, 128, s_q,
+                        s_kv, valid_kv, heads, head_dim, scale, p);
+  if (rc) return rc;
+  for (int r = 0; r < ws; ++r) p->peer_o[r] = static_cast<uint16_t*>(peer_back[r]);
+  p->m_rows = m_rows;
+  p->rank = rank;
+  return H3B_OK;
+}
+
+static int library_wait(const char* who, h3b::attn::Params* p) {
+  p->wc.status = device_status_word();
+  p->wc.timeout = wait_timeout_ns();
+  if (p->wc.status == nullptr) return fail(H3B_ECUDA, "%s: device status word", who);
+  return H3B_OK;
+}
+
+namespace h3b {
+namespace attn {
+
+// The bf16-v attention for a caller that brings its own scratch (the allocation-free entry point): the checks of
+// h3b_flash_attn_fwd_bf16v, a limit on the f16 copy of v (valid_kv * heads * 128 <= max_v16 elements) and on heads
+// (the control words: H3B_NOALLOC_MAX_HEADS), then, unless there is nothing to compute, `scratch` supplies the f16
+// buffer, the control words (as attention_bf16v lays them out) and the status word for the waits.
+int bf16v_with_scratch(const char* who, const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                       int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok,
+                       int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim,
+                       float scale, int64_t max_v16, int (*scratch)(void** v16, void** ctl, int** status),
+                       cudaStream_t st) {
+  Params p;
+  // heads <= 65535 and s_kv < 2^31 are checked first, so valid_kv * heads * 128 below cannot wrap
+  int rc = local_params(who, q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, o, o_tok, o_head, s_q, s_kv,
+                        valid_kv, heads, head_dim, scale, &p);
+  if (rc) return rc;
+  if (heads > H3B_NOALLOC_MAX_HEADS)
+    return fail(H3B_EUNSUPPORTED, "%s: %d heads (at most %d with the fixed scratch); use h3b_flash_attn_fwd_bf16v",
+                who, heads, H3B_NOALLOC_MAX_HEADS);
+  if (p.valid_kv > max_v16 / (static_cast<int64_t>(heads) * 128))
+    return fail(H3B_EUNSUPPORTED,
+                "%s: valid_kv * heads * 128 = %lld exceeds the fixed scratch of %lld f16 elements (valid_kv * heads "
+                "<= %lld); use h3b_flash_attn_fwd_bf16v",
+                who, (long long)(p.valid_kv * heads * 128), (long long)max_v16, (long long)(max_v16 / 128));
+  if (s_q == 0) return H3B_OK;
+  void* v16 = nullptr;
+  void* ctl = nullptr;
+  rc = scratch(&v16, &ctl, &p.wc.status);
+  if (rc) return rc;
+  p.wc.timeout = wait_timeout_ns();
+  return attention_bf16v(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v16, ctl, p, st);
+}
+
+}  // namespace attn
+}  // namespace h3b
 
 extern "C" int h3b_flash_attn_fwd(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
                                   int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o, int64_t o_tok,
                                   int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv, int32_t heads,
                                   int32_t head_dim, float scale, int32_t v_f16, const int32_t* range_flag,
                                   h3b_stream_t stream) {
-  using namespace h3b::attn;
-  if (s_q < 0 || s_kv <= 0 || heads <= 0) return fail(H3B_EINVAL, "flash_attn: s_q %lld s_kv %lld heads %d", (long long)s_q, (long long)s_kv, heads);
-  if (head_dim != 128) return fail(H3B_EUNSUPPORTED, "flash_attn: head_dim %d (only 128)", head_dim);
-  if (valid_kv < 0) valid_kv = s_kv;
-  if (valid_kv == 0 || valid_kv > s_kv) return fail(H3B_EINVAL, "flash_attn: valid_kv %lld of %lld", (long long)valid_kv, (long long)s_kv);
-  if (s_q == 0) return H3B_OK;
-  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return fail(H3B_EINVAL, "flash_attn: null pointer");
-  if (heads > 65535 || s_q > (1ll << 31) - 1 || s_kv > (1ll << 31) - 1) return fail(H3B_EUNSUPPORTED, "flash_attn: size limits");
-  const int64_t strides[8] = {q_tok, q_head, k_tok, k_head, v_tok, v_head, o_tok, o_head};
-  for (int64_t s : strides)
-    if (s <= 0 || s % 8) return fail(H3B_EALIGN, "flash_attn: token/head strides must be positive multiples of 8");
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
-       reinterpret_cast<uintptr_t>(o)) & 15u)
-    return fail(H3B_EALIGN, "flash_attn: q, k, v, o must be 16-byte aligned");
-
-  Params p{};
-  p.s_q = s_q;
-  p.s_kv = s_kv;
-  p.valid_kv = valid_kv;
-  p.heads = heads;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  p.o = static_cast<uint16_t*>(o);
-  p.o_tok = o_tok;
-  p.o_head = o_head;
+  h3b::attn::Params p;
+  int rc = local_params("flash_attn", q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, o, o_tok, o_head, s_q,
+                        s_kv, valid_kv, heads, head_dim, scale, &p);
+  if (!rc) rc = library_wait("flash_attn", &p);
+  if (rc || s_q == 0) return rc;
   p.range_flag = v_f16 ? range_flag : nullptr;
-  p.wc.status = device_status_word();
-  p.wc.timeout = wait_timeout_ns();
-  if (p.wc.status == nullptr) return fail(H3B_ECUDA, "flash_attn: device status word");
   return launch_attention(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v_f16 != 0, p,
                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_flash_attn_fwd_bf16v(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
+                                        int64_t k_head, const void* v, int64_t v_tok, int64_t v_head, void* o,
+                                        int64_t o_tok, int64_t o_head, int64_t s_q, int64_t s_kv, int64_t valid_kv,
+                                        int32_t heads, int32_t head_dim, float scale, void* v16, void* ctl,
+                                        h3b_stream_t stream) {
+  h3b::attn::Params p;
+  int rc = local_params("flash_attn_bf16v", q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, o, o_tok, o_head,
+                        s_q, s_kv, valid_kv, heads, head_dim, scale, &p);
+  if (!rc) rc = library_wait("flash_attn_bf16v", &p);
+  if (rc || s_q == 0) return rc;
+  if (v16 == nullptr || ctl == nullptr || ((reinterpret_cast<uintptr_t>(v16) | reinterpret_cast<uintptr_t>(ctl)) & 15u))
+    return fail(H3B_EINVAL, "flash_attn_bf16v: v16 and ctl are required, 16-byte aligned");
+  return attention_bf16v(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v16, ctl, p,
+                         reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int h3b_flash_attn_fwd_p2p(const void* q, int64_t q_tok, int64_t q_head, const void* k, int64_t k_tok,
@@ -565,45 +818,30 @@ extern "C" int h3b_flash_attn_fwd_p2p(const void* q, int64_t q_tok, int64_t q_he
                                       void* const* peer_back, int32_t ws, int32_t rank, int64_t m_rows, int64_t s_q,
                                       int64_t s_kv, int64_t valid_kv, int32_t heads, int32_t head_dim, float scale,
                                       int32_t v_f16, const int32_t* range_flag, h3b_stream_t stream) {
-  using namespace h3b::attn;
-  if (peer_back == nullptr || ws < 1 || ws > H3B_MAX_RANKS || rank < 0 || rank >= ws)
-    return fail(H3B_EINVAL, "flash_attn_p2p: ws %d rank %d", ws, rank);
-  if (s_q < 0 || s_kv <= 0 || heads <= 0) return fail(H3B_EINVAL, "flash_attn_p2p: s_q %lld s_kv %lld heads %d", (long long)s_q, (long long)s_kv, heads);
-  if (m_rows <= 0 || s_q != m_rows * ws)
-    return fail(H3B_EINVAL, "flash_attn_p2p: s_q %lld must be ws * m_rows (%d * %lld)", (long long)s_q, ws, (long long)m_rows);
-  if (head_dim != 128) return fail(H3B_EUNSUPPORTED, "flash_attn_p2p: head_dim %d (only 128)", head_dim);
-  if (valid_kv < 0) valid_kv = s_kv;
-  if (valid_kv == 0 || valid_kv > s_kv) return fail(H3B_EINVAL, "flash_attn_p2p: valid_kv %lld of %lld", (long long)valid_kv, (long long)s_kv);
-  if (q == nullptr || k == nullptr || v == nullptr) return fail(H3B_EINVAL, "flash_attn_p2p: null pointer");
-  if (heads > 65535 || s_q > (1ll << 31) - 1 || s_kv > (1ll << 31) - 1) return fail(H3B_EUNSUPPORTED, "flash_attn_p2p: size limits");
-  const int64_t strides[6] = {q_tok, q_head, k_tok, k_head, v_tok, v_head};
-  for (int64_t s : strides)
-    if (s <= 0 || s % 8) return fail(H3B_EALIGN, "flash_attn_p2p: token/head strides must be positive multiples of 8");
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)
-    return fail(H3B_EALIGN, "flash_attn_p2p: q, k, v must be 16-byte aligned");
-
-  Params p{};
-  for (int r = 0; r < ws; ++r) {
-    if (peer_back[r] == nullptr || (reinterpret_cast<uintptr_t>(peer_back[r]) & 15u))
-      return fail(H3B_EALIGN, "flash_attn_p2p: peer buffer %d null or not 16-byte aligned", r);
-    p.peer_o[r] = static_cast<uint16_t*>(peer_back[r]);
-  }
-  p.s_q = s_q;
-  p.s_kv = s_kv;
-  p.valid_kv = valid_kv;
-  p.heads = heads;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  p.o = p.peer_o[rank];
-  p.o_tok = static_cast<int64_t>(heads) * 128;  // receive buffers [P, m_rows, heads, 128]
-  p.o_head = 128;
-  p.m_rows = m_rows;
-  p.rank = rank;
+  h3b::attn::Params p;
+  int rc = p2p_params("flash_attn_p2p", q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, peer_back, ws, rank,
+                      m_rows, s_q, s_kv, valid_kv, heads, head_dim, scale, &p);
+  if (!rc) rc = library_wait("flash_attn_p2p", &p);
+  if (rc) return rc;
   p.range_flag = v_f16 ? range_flag : nullptr;
-  p.wc.status = device_status_word();
-  p.wc.timeout = wait_timeout_ns();
-  if (p.wc.status == nullptr) return fail(H3B_ECUDA, "flash_attn_p2p: device status word");
   return launch_attention(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v_f16 != 0, p,
                           reinterpret_cast<cudaStream_t>(stream));
 }
 
-#endif  // H3B_ATTENTION_KERNEL_ONLY
+extern "C" int h3b_flash_attn_fwd_p2p_bf16v(const void* q, int64_t q_tok, int64_t q_head, const void* k,
+                                            int64_t k_tok, int64_t k_head, const void* v, int64_t v_tok,
+                                            int64_t v_head, void* const* peer_back, int32_t ws, int32_t rank,
+                                            int64_t m_rows, int64_t s_q, int64_t s_kv, int64_t valid_kv,
+                                            int32_t heads, int32_t head_dim, float scale, void* v16, void* ctl,
+                                            h3b_stream_t stream) {
+  h3b::attn::Params p;
+  int rc = p2p_params("flash_attn_p2p_bf16v", q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, peer_back, ws,
+                      rank, m_rows, s_q, s_kv, valid_kv, heads, head_dim, scale, &p);
+  if (!rc) rc = library_wait("flash_attn_p2p_bf16v", &p);
+  if (rc) return rc;
+  if (v16 == nullptr || ctl == nullptr || ((reinterpret_cast<uintptr_t>(v16) | reinterpret_cast<uintptr_t>(ctl)) & 15u))
+    return fail(H3B_EINVAL, "flash_attn_p2p_bf16v: v16 and ctl are required, 16-byte aligned");
+  return attention_bf16v(q, q_tok, q_head, k, k_tok, k_head, v, v_tok, v_head, v16, ctl, p,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+

@@ -18,7 +18,7 @@ EPI_PLAIN, EPI_QKV_SEND, EPI_SWIGLU = 0, 1, 2
 
 _p, _i32, _i64, _f32, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64
 MAX_RANKS = 8   # H3B_MAX_RANKS
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class QkvSend(ctypes.Structure):
@@ -53,8 +53,11 @@ SIGNATURES = {
                                     ctypes.POINTER(QkvSend), _p]),
     "h3b_flash_attn_fwd": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
                                           _i64, _i32, _i32, _f32, _i32, _p, _p]),
+    "h3b_flash_attn_fwd_bf16v": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64,
+                                                _i64, _i64, _i32, _i32, _f32, _p, _p, _p]),
     "h3b_flash_attn_fwd_noalloc": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64,
                                                   _i64, _i64, _i64, _i32, _i32, _f32, _p]),
+    "h3b_noalloc_status": (ctypes.c_int, []),
     "h3b_pack_by_dest": (ctypes.c_int, [_p, _i64, _i32, _i32, _i64, _i64, _i32, _p, _i32, _p, _p]),
     "h3b_unpack_recv": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _p]),
     "h3b_norm_rope_send": (ctypes.c_int, [_p, _i64, _i32, _i64, _i64, _p, _p, _i64, _i32, _f32, _i32, _p, _p]),
@@ -63,6 +66,8 @@ SIGNATURES = {
                                          _i64, _i64, _p]),
     "h3b_flash_attn_fwd_p2p": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i32, _i32, _i64,
                                               _i64, _i64, _i64, _i32, _i32, _f32, _i32, _p, _p]),
+    "h3b_flash_attn_fwd_p2p_bf16v": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i32, _i32,
+                                                    _i64, _i64, _i64, _i64, _i32, _i32, _f32, _p, _p, _p]),
     "h3b_p2p_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_p), ctypes.POINTER(IpcHandle)]),
     "h3b_p2p_open": (ctypes.c_int, [ctypes.POINTER(IpcHandle), ctypes.POINTER(_p)]),
     "h3b_p2p_close": (ctypes.c_int, [_p]),

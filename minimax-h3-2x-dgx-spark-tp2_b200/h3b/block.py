@@ -2,10 +2,10 @@
 
     x [M, C] bf16 (this rank's sequence rows)
       -> per-token e4m3 quant                                  (ops.quant; fp8_quant_fuse qkv site)
-      -> qkv FP8 GEMM, epilogue writes q, k, v straight into the send buffers [P, M, H/P, d]
-         (v as f16, exactly converted from its bf16 value, for the f16 P.V product)
+      -> qkv FP8 GEMM, epilogue writes q, k, v straight into the send buffers [P, M, H/P, d] (bf16)
       -> seq->head all-to-all x3 (NCCL over NVLink; skipped at P = 1)
-      -> flash attention over all P*M tokens for H/P heads     (tcgen05, non-causal, d = 128)
+      -> flash attention over all P*M tokens for H/P heads     (tcgen05, non-causal, d = 128; f16 P.V when v
+                                                                fits f16, bf16 P.V otherwise, chosen on the device)
       -> head->seq all-to-all of the output as is (skipped at P = 1)
       -> per-token quant straight from the receive buffer      (ulysses_outq: no unpack copy)
       -> out FP8 GEMM -> y [M, C] bf16
@@ -43,7 +43,7 @@ def block_flops(tokens: int, hidden: int, heads: int, head_dim: int = 128) -> di
 class AttentionBlock:
     def __init__(self, hidden: int, heads: int, *, device, head_dim: int = 128, seed: int = 1, ws: int = 1, pg=None,
                  weights: tuple | None = None, init_device=None, a2a=None, groups: int | None = None,
-                 exchange: str = "nccl", rank: int | None = None, range_check: bool = False):
+                 exchange: str = "nccl", rank: int | None = None):
         if head_dim != 128:
             raise ValueError("head_dim 128 only")
         if heads % ws:
@@ -57,7 +57,13 @@ class AttentionBlock:
             wo = torch.randn(hidden, heads * head_dim, generator=g, device=gdev) * 0.02
             weights = (*quant_weight(wqkv), *quant_weight(wo))
         self.wqkv8, self.sqkv, self.wo8, self.so = (t.to(self.device) for t in weights)
-        self.range_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # v crosses the exchange in bf16, the value the reference computes; each attention converts the v it received
+        # to f16 and runs the f16 P.V product on it, or (decided on the device when some value does not fit f16) on a
+        # copy scaled by a power of two per (head, column) (ops.flash_attn), so any bf16 v is served without a host
+        # read.  The attention's control words: range_flag (word 0) holds 1 after a forward whose (last) attention
+        # took the scaled pass.
+        self._ctl = ops.attn_ctl(heads, self.device)
+        self.range_flag = self._ctl[:1]
         self.a2a = a2a   # injected collective a2a(out, inp, group=None); default: NCCL all_to_all_single
         from .ulysses_overlap import default_groups
         self.groups = default_groups(heads, ws) if groups is None else int(groups)
@@ -73,32 +79,22 @@ class AttentionBlock:
         self.exchange_kind = exchange
         self.rank = rank if rank is not None else (dist.get_rank(pg) if exchange == "p2p" and ws > 1 else 0)
         self._peers = None
-        # v travels as f16 for the f16 P.V product.  With ``range_check`` a v outside f16's range (|v| > 65504) is
-        # caught after the qkv projection (one host read of the group-wide flag per forward), and the block then
-        # switches to bf16 v and bf16 P.V for good and recomputes the projection.  The read waits for the copy
-        # engine, so a large device-to-host copy in flight on another stream delays the rest of the forward (11 ms
-        # per block measured with the bench's overlapped output copies): it is off by default, and without it the
-        # attention refuses f16 P.V on such a v (H3B_ERANGE in the device status word, output unwritten).
-        self.range_check = range_check
-        self.v_f16 = True
+        self._v16 = None
 
     def _peer_exchange(self, m: int):
         from .ulysses_p2p import PeerExchange
-        if self._peers is None or self._peers.m != m or self._peers.v_f16 != self.v_f16:
+        if self._peers is None or self._peers.m != m:
             if self._peers is not None:
                 self.close()
-            self._peers = PeerExchange(m, self.heads, self.ws, self.rank, self.device, pg=self.pg,
-                                       v_f16=self.v_f16)
+            self._peers = PeerExchange(m, self.heads, self.ws, self.rank, self.device, pg=self.pg)
         return self._peers
 
-    def _v_overflowed(self, flag: torch.Tensor) -> bool:
-        """True when the qkv projection just written left f16's range in some v (``flag``: the group-wide flag).  The
-        block then switches to bf16 v for good; the caller recomputes the projection."""
-        if not (self.v_f16 and self.range_check) or not bool(flag.item()):
-            return False
-        self.v_f16 = False
-        flag.zero_()
-        return True
+    def _v16_for(self, rows: int, heads: int) -> torch.Tensor:
+        """The f16 copy of v the attention writes (kept across forwards of the same size)."""
+        n = rows * heads * 128
+        if self._v16 is None or self._v16.numel() < n:
+            self._v16 = torch.empty(n, dtype=torch.float16, device=self.device)
+        return self._v16[:n]
 
     def close(self) -> None:
         """Releases the peer buffers of the p2p exchange (collective over the group)."""
@@ -106,14 +102,6 @@ class AttentionBlock:
             pg = self.pg
             self._peers.close(host_barrier=lambda: dist.barrier(group=pg))
             self._peers = None
-
-    def share_range_flag(self) -> None:
-        """Max of the v-overflow flags of all ranks (a rank's flag covers only the v slabs it sent, while its attention
-        reads the slabs every rank sent), through the same all-to-all the exchange uses."""
-        if self.ws == 1:
-            return
-        recv = self.exchange(self.range_flag.repeat(self.ws))
-        torch.amax(recv, dim=0, keepdim=True, out=self.range_flag)
 
     def exchange(self, send: torch.Tensor) -> torch.Tensor:
         if self.ws == 1:
@@ -130,9 +118,13 @@ class AttentionBlock:
 
     STAGES = ("quant_x", "qkv_gemm", "a2a_fwd", "attention", "a2a_back", "quant_out", "out_gemm")
 
-    def forward(self, x: torch.Tensor, marks: list | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, marks: list | None = None, keep: dict | None = None) -> torch.Tensor:
         """x [M, C] bf16 -> y [M, C] bf16.  ``marks``: if a list, a CUDA event is recorded on the current stream
-        after each stage (``STAGES``), preceded by one at the start, for per-stage device timing."""
+        after each stage (``STAGES``), preceded by one at the start, for per-stage device timing.  ``keep``: if a dict
+        (exchanges without head groups), it receives the attention's inputs q/k/v [P*M, H/P, d] as this rank received
+        them, the reverse receive buffer back [P, M, H/P, d] and y, for a parity check of every stage."""
+        if keep is not None and self.ws > 1 and (self.exchange_kind == "nocopy" or self.groups > 1):
+            raise ValueError("forward(keep=...): exchanges without head groups only")
         def mark():
             if marks is not None:
                 ev = torch.cuda.Event(enable_timing=True)
@@ -144,39 +136,36 @@ class AttentionBlock:
         mark()
         q8, sx = ops.quant(x)
         mark()
+        scale = 1.0 / math.sqrt(d)
         if self.ws > 1 and self.exchange_kind == "p2p":
             px = self._peer_exchange(m)
             px.forward_qkv(q8, self.wqkv8, sx, self.sqkv)
             mark()
             px.barrier()
-            if self._v_overflowed(px.range_flag):  # every rank saw the same flag (raised on all ranks)
-                px = self._peer_exchange(m)         # rebuilt with bf16 v (collective)
-                px.forward_qkv(q8, self.wqkv8, sx, self.sqkv)
-                px.barrier()
             mark()
-            px.attention(1.0 / math.sqrt(d))
+            px.attention(scale, ctl=self._ctl)
             mark()
             px.barrier()
             mark()
+            if keep is not None:
+                n = self.ws * m
+                keep.update(q=px.q.view(n, hl, d), k=px.k.view(n, hl, d), v=px.v.view(n, hl, d), back=px.back)
             o8, so = ops.quant_from_recv(px.back)
         elif self.ws > 1 and self.exchange_kind == "nocopy":
             from .ulysses_nocopy import qkv_views
             from .ulysses_overlap import quant_grouped_back
             G = self.groups
-            send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=self.v_f16,
-                                         range_flag=self.range_flag, groups=G, interleaved=True)
-            self.share_range_flag()
-            if self._v_overflowed(self.range_flag):
-                send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=False,
-                                             groups=G, interleaved=True)
+            send = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, groups=G,
+                                         interleaved=True)
             mark()
             recv = torch.empty_like(send)
             for g in range(G):
                 self.exchange_into(recv[g], send[g])
             mark()
             hgl = self.heads // (G * self.ws)
-            outs = [ops.flash_attn(*qkv_views(recv[g], v_f16=self.v_f16), scale=1.0 / math.sqrt(d),
-                                   range_flag=self.range_flag, pv_f16=self.v_f16) for g in range(G)]
+            v16 = self._v16_for(self.ws * m, hgl)
+            outs = [ops.flash_attn(*qkv_views(recv[g]), scale=scale, ctl=self._ctl, v16=v16)
+                    for g in range(G)]
             mark()
             back = torch.empty((G, self.ws, m, hgl, d), dtype=torch.bfloat16, device=self.device)
             for g in range(G):
@@ -185,42 +174,40 @@ class AttentionBlock:
             o8, so = ops.quant_from_recv(back[0]) if G == 1 else quant_grouped_back(back)
         elif self.ws > 1 and self.groups > 1:
             from .ulysses_overlap import grouped_attention, quant_grouped_back
-            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=self.v_f16,
-                                          range_flag=self.range_flag, groups=self.groups)
-            self.share_range_flag()
-            if self._v_overflowed(self.range_flag):
-                sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=False,
-                                              groups=self.groups)
+            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, groups=self.groups)
             mark()
             mark()      # with head groups the exchanges overlap the attention: the attention stage holds all three
-            pv_f16 = self.v_f16
+            # one f16 scratch per group: the groups' attentions may overlap the next group's exchange on other
+            # streams, but they run one after another on the compute stream
+            v16 = self._v16_for(self.ws * m, self.heads // (self.groups * self.ws))
             back = grouped_attention(sends, self.ws, self.groups,
-                                     lambda q, k, v: ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d),
-                                                                    range_flag=self.range_flag, pv_f16=pv_f16),
+                                     lambda q, k, v: ops.flash_attn(q, k, v, scale=scale, ctl=self._ctl, v16=v16),
                                      pg=self.pg, a2a=self.a2a)
             mark()
             mark()
             o8, so = quant_grouped_back(back)
         else:
-            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=self.v_f16,
-                                          range_flag=self.range_flag)
-            self.share_range_flag()
-            if self._v_overflowed(self.range_flag):
-                sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, v_f16=False)
+            sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws)
             mark()
             q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
             mark()
-            o = ops.flash_attn(q, k, v, scale=1.0 / math.sqrt(d), range_flag=self.range_flag, pv_f16=self.v_f16)
+            o = ops.flash_attn(q, k, v, scale=scale, ctl=self._ctl, v16=self._v16_for(self.ws * m, hl))
             mark()
             back = self.exchange(o.view(self.ws, m, hl, d))
             mark()
+            if keep is not None:
+                keep.update(q=q, k=k, v=v, back=back)
             o8, so = ops.quant_from_recv(back)
         mark()
         y = ops.fp8_gemm(o8, self.wo8, so, self.so)
         mark()
+        if keep is not None:
+            keep["y"] = y
         return y
 
-    KERNELS_PER_FORWARD = 5   # h3b launches per forward: quant, qkv GEMM, attention, quant, out GEMM
+    # h3b launches per forward: quant, qkv GEMM, the attention's six (v conversion, attention; then the scaled pass's
+    # column maxima, conversion and attention, which leave at once when v fits f16), quant, out GEMM
+    KERNELS_PER_FORWARD = 10
     P2P_BARRIERS = 2          # extra h3b launches per forward with exchange "p2p" (the two epoch barriers)
 
     __call__ = forward

@@ -476,12 +476,51 @@ def bf16_to_f16(x: torch.Tensor, range_flag: torch.Tensor | None = None) -> torc
     return y
 
 
+def _v16_scratch(v16: torch.Tensor | None, rows: int, heads: int, ref: torch.Tensor) -> torch.Tensor:
+    """The f16 copy of v that the bf16-v attention writes: [rows, heads, 128] f16, contiguous (given or allocated)."""
+    if v16 is None:
+        return torch.empty((rows, heads, 128), dtype=torch.float16, device=ref.device)
+    _need_cuda(v16)
+    _dt(v16, torch.float16, what="flash_attn v16 scratch")
+    if v16.numel() < rows * heads * 128 or not v16.is_contiguous() or v16.device != ref.device:
+        raise ValueError(f"flash_attn: v16 scratch needs {rows * heads * 128} contiguous f16 values on {ref.device}")
+    return v16
+
+
+def attn_ctl_words(heads: int) -> int:
+    """int32 words of the control buffer of the bf16-v attention (H3B_ATTN_CTL_BYTES(heads) bytes): the range flag in
+    word 0 (1 after a call whose v did not fit f16), the per (head, column) maxima of the scaled pass from word 4."""
+    return 4 + 128 * heads
+
+
+def attn_ctl(heads: int, device) -> torch.Tensor:
+    return torch.zeros(attn_ctl_words(heads), dtype=torch.int32, device=device)
+
+
+def _ctl(ctl: torch.Tensor | None, heads: int, ref: torch.Tensor) -> torch.Tensor:
+    if ctl is None:
+        return attn_ctl(heads, ref.device)
+    _need_cuda(ctl)
+    _dt(ctl, torch.int32, what="flash_attn ctl")
+    if ctl.numel() < attn_ctl_words(heads) or not ctl.is_contiguous() or ctl.device != ref.device:
+        raise ValueError(f"flash_attn: ctl needs {attn_ctl_words(heads)} contiguous int32 words on {ref.device}")
+    return ctl
+
+
 def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float | None = None,
                valid_kv: int | None = None, out: torch.Tensor | None = None, pv_f16: bool = True,
-               range_flag: torch.Tensor | None = None) -> torch.Tensor:
+               range_flag: torch.Tensor | None = None, v16: torch.Tensor | None = None,
+               ctl: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(q k^T * scale) v, non-causal, head_dim 128, batch 1: q/k/v [S, H, d] or [1, S, H, d] (any token/head
-    strides that are multiples of 8).  bf16 v is converted exactly to f16 for the f16 P.V product unless
-    ``pv_f16=False``; an f16 v is used as is.  Returns o with q's shape (bf16, contiguous)."""
+    strides that are multiples of 8).  Returns o with q's shape (bf16, contiguous).
+
+    A bf16 v is taken in its whole range, as the reference's cuDNN SDPA takes it (h3_tp2/ulysses_exact.py:495-496):
+    its valid rows are converted to f16 (into ``v16``, allocated if not given) and the device runs the f16 P.V
+    product on that copy when every value fits f16, else on a copy scaled by a power of two per (head, column) whose
+    output columns are scaled back (``h3b_flash_attn_fwd_bf16v``).  ``ctl`` (``attn_ctl(heads)``, allocated if not
+    given) then holds 1 in word 0 when the scaled pass ran.  ``pv_f16=False`` runs bf16 P.V directly.  An f16 v (a
+    producer's exact f16 copy) is used as is; a ``range_flag`` holding 1 then makes the kernel write nothing and
+    record H3B_ERANGE in the device status word."""
     _need_cuda(q, k, v)
     q3, k3, v3 = _as3(q), _as3(k), _as3(v)
     _dt(q3, torch.bfloat16, what="flash_attn q")
@@ -494,24 +533,29 @@ def flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: floa
     _dt(v3, torch.bfloat16, torch.float16, what="flash_attn v")
     o = _out(out, tuple(q.shape), torch.bfloat16, q, "flash_attn", dense=False)
     o3 = _as3(o)
-    if v3.dtype == torch.bfloat16 and pv_f16:
-        if range_flag is None:
-            range_flag = torch.zeros(1, dtype=torch.int32, device=q.device)
-        v3 = bf16_to_f16(v3.contiguous(), range_flag)
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(d)
-    _lib.call("h3b_flash_attn_fwd", q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0),
-              k3.stride(1), v3.data_ptr(), v3.stride(0), v3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1),
-              s_q, s_kv, -1 if valid_kv is None else int(valid_kv), heads, d, sc, int(v3.dtype == torch.float16),
-              _ptr(range_flag) if v3.dtype == torch.float16 else None, _stream(q))
+    vk = -1 if valid_kv is None else int(valid_kv)
+    common = (q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0), k3.stride(1), v3.data_ptr(),
+              v3.stride(0), v3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1), s_q, s_kv, vk, heads, d, sc)
+    if v3.dtype == torch.bfloat16 and pv_f16:
+        rows = s_kv if valid_kv is None else max(0, min(int(valid_kv), s_kv))
+        scratch = _v16_scratch(v16, rows, heads, q)
+        c = _ctl(ctl, heads, q)
+        _lib.call("h3b_flash_attn_fwd_bf16v", *common, scratch.data_ptr(), c.data_ptr(), _stream(q))
+        return o
+    f16 = v3.dtype == torch.float16
+    _lib.call("h3b_flash_attn_fwd", *common, int(f16), _ptr(range_flag) if f16 else None, _stream(q))
     return o
 
 
 def flash_attn_p2p(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer_back, rank: int, *,
                    scale: float | None = None, valid_kv: int | None = None,
-                   range_flag: torch.Tensor | None = None) -> None:
-    """Attention of this rank's heads over the gathered sequence (q/k/v [P*M, H/P, d], v f16 or bf16) whose output
-    row t is stored into rank t // M's reverse receive buffer ``peer_back[t // M]`` ([P, M, H/P, d] bf16, slot
-    ``rank``; tensors or device addresses): the head->seq all-to-all folded into the epilogue."""
+                   range_flag: torch.Tensor | None = None, v16: torch.Tensor | None = None,
+                   ctl: torch.Tensor | None = None) -> None:
+    """Attention of this rank's heads over the gathered sequence (q/k/v [P*M, H/P, d]) whose output row t is stored
+    into rank t // M's reverse receive buffer ``peer_back[t // M]`` ([P, M, H/P, d] bf16, slot ``rank``; tensors or
+    device addresses): the head->seq all-to-all folded into the epilogue.  A bf16 v is taken in its whole range as in
+    ``flash_attn`` (``v16`` / ``ctl`` as there); an f16 v is used as is (a set ``range_flag`` refuses it)."""
     _need_cuda(q, k, v)
     q3, k3, v3 = _as3(q), _as3(k), _as3(v)
     _dt(q3, torch.bfloat16, what="flash_attn_p2p q")
@@ -529,11 +573,17 @@ def flash_attn_p2p(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer_back,
             _out(b, (ws, s_q // ws, heads, d), torch.bfloat16, b, "flash_attn_p2p reverse receive buffer")
     ptrs = (ctypes.c_void_p * ws)(*[_addr(b) for b in peer_back])
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(d)
-    f16 = v3.dtype == torch.float16
-    _lib.call("h3b_flash_attn_fwd_p2p", q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0),
-              k3.stride(1), v3.data_ptr(), v3.stride(0), v3.stride(1), ptrs, ws, int(rank), s_q // ws, s_q,
-              k3.shape[0], -1 if valid_kv is None else int(valid_kv), heads, d, sc, int(f16),
-              _ptr(range_flag) if f16 else None, _stream(q))
+    s_kv = k3.shape[0]
+    vk = -1 if valid_kv is None else int(valid_kv)
+    common = (q3.data_ptr(), q3.stride(0), q3.stride(1), k3.data_ptr(), k3.stride(0), k3.stride(1), v3.data_ptr(),
+              v3.stride(0), v3.stride(1), ptrs, ws, int(rank), s_q // ws, s_q, s_kv, vk, heads, d, sc)
+    if v3.dtype == torch.bfloat16:
+        rows = s_kv if valid_kv is None else max(0, min(int(valid_kv), s_kv))
+        scratch = _v16_scratch(v16, rows, heads, q)
+        c = _ctl(ctl, heads, q)
+        _lib.call("h3b_flash_attn_fwd_p2p_bf16v", *common, scratch.data_ptr(), c.data_ptr(), _stream(q))
+        return
+    _lib.call("h3b_flash_attn_fwd_p2p", *common, 1, _ptr(range_flag), _stream(q))
 
 
 def p2p_signal_wait(peer_flags, my_flags, rank: int, epoch: int, stream: int) -> None:

@@ -97,7 +97,7 @@ class PeerExchange:
     process group's ``all_gather_object``)."""
 
     def __init__(self, m: int, heads: int, ws: int, rank: int, device, *, pg=None, allgather=None,
-                 v_f16: bool = True):
+                 v_f16: bool = False):
         if ws < 1 or ws > _lib.MAX_RANKS or heads % ws or not 0 <= rank < ws:
             raise ValueError(f"PeerExchange: ws {ws} (1..{_lib.MAX_RANKS}), heads {heads}, rank {rank}")
         self.m, self.heads, self.ws, self.rank = m, heads, ws, rank
@@ -105,6 +105,7 @@ class PeerExchange:
         self.hl = heads // ws
         self.v_f16 = v_f16
         self.epoch = 0
+        self._v16 = None   # f16 copy of the received v (bf16 v only), allocated by the first attention
         shape = (ws, m, self.hl, 128)
         slab = _round(ws * m * self.hl * 128 * 2)
         self._off = {"q": _FLAGS_BYTES, "k": _FLAGS_BYTES + slab, "v": _FLAGS_BYTES + 2 * slab,
@@ -166,12 +167,22 @@ class PeerExchange:
         ops.fp8_gemm_qkv_send(q8, wqkv8, sx, sqkv, self.heads, self.ws, bias=bias, v_f16=self.v_f16,
                               p2p=self.qkv_targets())
 
-    def attention(self, scale: float) -> None:
-        """This rank's heads over the whole sequence, each output row stored into its owner's back buffer."""
+    def attention(self, scale: float, ctl: torch.Tensor | None = None) -> None:
+        """This rank's heads over the whole sequence, each output row stored into its owner's back buffer.  With bf16
+        v (the default) the received v is converted to f16 here and the device runs the f16 P.V product on it, or on
+        a copy scaled per (head, column) when some value does not fit f16 (``ctl``: ``ops.attn_ctl`` control words,
+        word 0 then says which pass ran); an f16 v buffer (``v_f16=True``: the peers' epilogues converted it and
+        raised the buffer's range flag on an overflow) is used as is and refused on an overflow."""
         n = self.ws * self.m
-        ops.flash_attn_p2p(self.q.view(n, self.hl, 128), self.k.view(n, self.hl, 128),
-                           self.v.view(n, self.hl, 128), self.back_targets(), self.rank, scale=scale,
-                           range_flag=self.range_flag)
+        if self.v_f16:
+            ops.flash_attn_p2p(self.q.view(n, self.hl, 128), self.k.view(n, self.hl, 128),
+                               self.v.view(n, self.hl, 128), self.back_targets(), self.rank, scale=scale,
+                               range_flag=self.range_flag)
+            return
+        if self._v16 is None:
+            self._v16 = torch.empty((n, self.hl, 128), dtype=torch.float16, device=self.device)
+        ops.flash_attn_p2p(self.q.view(n, self.hl, 128), self.k.view(n, self.hl, 128), self.v.view(n, self.hl, 128),
+                           self.back_targets(), self.rank, scale=scale, v16=self._v16, ctl=ctl)
 
     # ---- teardown (collective; the q/k/v/back/range_flag views dangle afterwards) ----
     def close(self, host_barrier=None) -> None:

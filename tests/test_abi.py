@@ -38,7 +38,7 @@ def test_binding_signatures_cover_the_header():
 
 def test_status_strings_and_version():
     lib = _lib.load()
-    assert lib.h3b_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.h3b_abi_version() == _lib.ABI_VERSION == 4
     assert lib.h3b_status_string(0) == b"ok"
     assert lib.h3b_status_string(_lib.H3B_ETIMEOUT) == b"device wait timed out"
 

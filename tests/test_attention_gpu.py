@@ -2,7 +2,7 @@
 import pytest
 import torch
 
-from _util import BF16, rel_l2
+from _util import BF16, F16, rel_l2
 from h3b import ops
 from oracle import attention as oa
 
@@ -72,14 +72,57 @@ def test_ulysses_receive_views_and_head_independence(dev):
     assert torch.equal(o_str.view(torch.int16), o_all[0, :, 1:3].contiguous().view(torch.int16))
 
 
-def test_f16_range_flag_refuses(dev):
+def test_f16_v_with_raised_flag_refuses(dev):
+    """An f16 v comes from a producer that converted it; with that producer's range flag raised the kernel writes
+    nothing and records H3B_ERANGE (the caller asked for f16 P.V on an f16 copy that is not v)."""
     q, k, v = _qkv(128, 128, 1, seed=2)
-    v[5, 0, 3] = 80000.0
-    flag = torch.zeros(1, dtype=torch.int32, device=dev)
-    ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), range_flag=flag)
+    flag = torch.ones(1, dtype=torch.int32, device=dev)
+    o = torch.full((128, 1, 128), 7.0, dtype=BF16, device=dev)
+    ops.flash_attn(q.to(dev), k.to(dev), v.to(F16).to(dev), range_flag=flag, out=o)
     assert ops.device_status() == ops._lib.H3B_ERANGE
+    assert (o.float() == 7.0).all()
+
+
+@pytest.mark.parametrize("big", [80000.0, -3.0e9, 1.0e30])
+def test_bf16_v_outside_f16_is_served(dev, big):
+    """A bf16 v with values beyond f16's range takes the scaled pass (decided on the device): the output is written
+    and stays within the f16 path's tolerance of fp32 SDPA.  Max-abs is measured relative to the output's scale."""
+    q, k, v = _qkv(300, 777, 3, seed=4)
+    v[5, 0, 3] = big            # one huge value in one column
+    v[100:110, 2, :] = big / 2  # whole rows of another head
+    ctl = ops.attn_ctl(3, dev)
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), ctl=ctl)
+    assert int(ctl[0].item()) == 1 and ops.device_status() == 0
+    ref = oa.sdpa(q, k, v)
+    o = o.float().cpu()
+    assert rel_l2(o, ref) <= 2e-3, rel_l2(o, ref)
+    # per (head, column): error against that column's scale (the scale is exact: ordinary columns keep f16 accuracy)
+    colscale = ref.abs().amax(dim=0, keepdim=True).clamp_min(1.0)
+    assert ((o - ref).abs() / colscale).max().item() <= 2e-2
+    # ordinary heads and columns equal the plain f16 pass bit for bit (their scale is 2^0)
+    o_plain = ops.flash_attn(q[:, 1:2].to(dev), k[:, 1:2].to(dev), v[:, 1:2].to(dev)).cpu()
+    assert torch.equal(o[:, 1:2].to(BF16).view(torch.int16), o_plain.view(torch.int16))
+
+
+def test_bf16_v_padding_rows_are_never_read(dev):
+    """Rows of v (and k) beyond valid_kv may hold anything (here inf, nan and values beyond f16): the attention
+    neither reads them nor takes the scaled pass because of them."""
+    q, k, v = _qkv(256, 700, 2, seed=6)
+    valid = 517
+    v[valid:] = float("nan")
+    v[valid + 3] = 1e30
+    k[valid:] = float("inf")
+    ctl = ops.attn_ctl(2, dev)
+    o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), valid_kv=valid, ctl=ctl)
+    assert int(ctl[0].item()) == 0
+    _check(o, oa.sdpa(q[:, :], k[:valid], v[:valid]))
+    assert ops.device_status() == 0
+
+
+def test_bf16_pv_variant_direct(dev):
+    q, k, v = _qkv(512, 512, 2, seed=8)
     o = ops.flash_attn(q.to(dev), k.to(dev), v.to(dev), pv_f16=False)
-    assert torch.isfinite(o.float()).all()
+    _check(o, oa.sdpa(q, k, v), tol_rel=4e-3)
 
 
 @pytest.mark.parametrize("poly", ["0", "2", "3", "4"])

@@ -530,8 +530,11 @@ def test_a2a_timing_wraps_the_collective_the_4d_exchange_and_reports_per_diffuse
     assert Pipeline.diffuse is orig_diffuse and not getattr(dist.all_to_all_single, "_h3b_a2a_timing", False)
 
 
-def test_probes_answer_false_without_a_gpu():
-    """The install probes never raise on a host without a GPU: the dispatcher then leaves the stock kernel in place."""
+def test_probes_answer_false_without_a_gpu(monkeypatch):
+    """The install probes never raise on a host without a GPU: the dispatcher then leaves the stock kernel in place.
+    The host is made GPU-less here, so the test means the same on a GPU box."""
+    import torch
     from h3b import fp8_swiglu
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
     assert fp8_gemm.probe_fused("cuda") is False and fp8_gemm.probe_fused("cpu") is False
     assert fp8_swiglu.probe_gemm_swiglu("cuda") is False

@@ -1,7 +1,7 @@
 """The peer-memory Ulysses exchange on one GPU: the kernels' peer-store epilogues (ranks emulated one after another,
 every "peer" buffer a local tensor, so nothing waits on anything) give exactly the bytes the all-to-all would deliver;
 a one-rank PeerExchange runs the whole block; the epoch barrier gives up with H3B_ETIMEOUT when a flag never
-arrives; and a v overflow on one rank reaches every rank's flag."""
+arrives; a v overflow on one rank reaches every rank's flag; and the peer attention serves a v beyond f16."""
 import math
 
 import pytest
@@ -130,25 +130,19 @@ def test_barrier_gives_up_on_a_missing_peer(dev):
     assert ops.device_status() == 0
 
 
-def test_range_flag_shared_across_ranks(dev):
-    """Only rank 1's rows overflow f16 in v, yet rank 0 attends over v slabs rank 1 sent: the flag exchange after the
-    qkv GEMM sets both ranks' flags (so the f16 attention of either rank reports H3B_ERANGE)."""
-    ws, n, hidden, heads = 2, 512, 256, 4
-    weights = ob.make_weights(hidden, heads, seed=6)
-    x = torch.randn(n, hidden, generator=torch.Generator().manual_seed(8)).to(BF16)
-    x[n // 2:] *= 1e7
-    x = x.to(dev)
-    m = n // ws
-
-    def body(r, a2a):
-        blk = AttentionBlock(hidden, heads, device=dev, weights=weights, ws=ws, a2a=a2a)
-        q8, sx = ops.quant(x[r * m:(r + 1) * m].contiguous())
-        ops.fp8_gemm_qkv_send(q8, blk.wqkv8, sx, blk.sqkv, heads, ws, v_f16=True, range_flag=blk.range_flag)
-        torch.cuda.synchronize()
-        own = int(blk.range_flag.item())
-        blk.share_range_flag()
-        torch.cuda.synchronize()
-        return own, int(blk.range_flag.item())
-
-    assert ou.run_ranks(body, ws) == [(0, 1), (1, 1)]
+def test_peer_attention_serves_v_outside_f16(dev):
+    """The peer-memory attention with a bf16 v beyond f16's range (the scaled pass, chosen on the device) stores into
+    every owner's reverse buffer exactly the rows the local attention computes."""
+    ws, m, hl = 2, 192, 2
+    g = torch.Generator().manual_seed(21)
+    q, k, v = (torch.randn(ws * m, hl, 128, generator=g).to(BF16).to(dev) for _ in range(3))
+    v[40, 1, 7] = 2.0e6
+    back = [torch.full((ws, m, hl, 128), -1, dtype=BF16, device=dev) for _ in range(ws)]
+    ctl = ops.attn_ctl(hl, dev)
+    ops.flash_attn_p2p(q, k, v, back, 1, ctl=ctl)
+    o = ops.flash_attn(q, k, v)
+    torch.cuda.synchronize()
+    assert int(ctl[0].item()) == 1
+    for t in range(ws):
+        assert same_bits(back[t][1], o[t * m:(t + 1) * m]), t
     assert ops.device_status() == 0

@@ -104,11 +104,19 @@ def test_flash_attn(calls):
     _refused(calls, ValueError, lambda: ops.flash_attn(q, q, q, out=torch.empty(s - 8, h, 128, dtype=BF16)), "out must")
     _refused(calls, ValueError, lambda: ops.flash_attn(q, q, q, out=torch.empty(s, h, 128, dtype=F16)), "out must")
     _refused(calls, TypeError, lambda: ops.bf16_to_f16(q.float()))
+    # the bf16-v pass's scratch: an f16 copy of the valid rows of v and the control words, each checked for size
+    _refused(calls, ValueError, lambda: ops.flash_attn(q, q, q, v16=torch.empty(s - 1, h, 128, dtype=F16)), "v16")
+    _refused(calls, TypeError, lambda: ops.flash_attn(q, q, q, v16=torch.empty(s, h, 128, dtype=BF16)))
+    _refused(calls, ValueError, lambda: ops.flash_attn(q, q, q, ctl=torch.empty(ops.attn_ctl_words(h) - 1,
+                                                                                 dtype=torch.int32)), "ctl")
+    ops.flash_attn(q, q, q, valid_kv=20, v16=torch.empty(20, h, 128, dtype=F16))   # v16 holds the valid rows only
     kv = torch.zeros(2 * s, h, 128, dtype=BF16)
     ops.flash_attn(q, kv, kv.to(F16))                              # more keys than queries, f16 v as is
     wide = torch.empty(s, h + 1, 128, dtype=BF16)
-    ops.flash_attn(q.unsqueeze(0), q, q, out=wide[:, :h].unsqueeze(0))  # a strided output view
-    assert calls == ["h3b_flash_attn_fwd", "h3b_bf16_to_f16", "h3b_flash_attn_fwd"]
+    ops.flash_attn(q.unsqueeze(0), q, q, out=wide[:, :h].unsqueeze(0))  # a strided output view, bf16 v
+    ops.flash_attn(q, q, q, pv_f16=False)                          # bf16 P.V asked for
+    assert calls == ["h3b_flash_attn_fwd_bf16v", "h3b_flash_attn_fwd", "h3b_flash_attn_fwd_bf16v",
+                     "h3b_flash_attn_fwd"]
 
 
 def test_flash_attn_p2p(calls):
@@ -120,8 +128,9 @@ def test_flash_attn_p2p(calls):
     _refused(calls, ValueError, lambda: ops.flash_attn_p2p(q, q, q[:-8], good, 0), "k and v")
     _refused(calls, ValueError, lambda: ops.flash_attn_p2p(q[:-1], q, q, good, 0), "peers")
     ops.flash_attn_p2p(q, q, q.to(F16), good, 1)
-    ops.flash_attn_p2p(q, q, q, [4096, 8192], 0)                   # device addresses are the caller's to size
-    assert calls == ["h3b_flash_attn_fwd_p2p"] * 2
+    ops.flash_attn_p2p(q, q, q.to(F16), [4096, 8192], 0)           # device addresses are the caller's to size
+    ops.flash_attn_p2p(q, q, q, good, 0)                           # bf16 v: the pass that takes any range
+    assert calls == ["h3b_flash_attn_fwd_p2p"] * 2 + ["h3b_flash_attn_fwd_p2p_bf16v"]
 
 
 def test_quant_rows_span(calls):
