@@ -134,7 +134,7 @@ class AttentionBlock:
         m = x.shape[0]
         hl, d = self.heads // self.ws, self.head_dim
         mark()
-        q8, sx = ops.quant(x)
+        q8, sx = torch.ops.h3b.quant(x)
         mark()
         scale = 1.0 / math.sqrt(d)
         if self.ws > 1 and self.exchange_kind == "p2p":
@@ -150,7 +150,7 @@ class AttentionBlock:
             if keep is not None:
                 n = self.ws * m
                 keep.update(q=px.q.view(n, hl, d), k=px.k.view(n, hl, d), v=px.v.view(n, hl, d), back=px.back)
-            o8, so = ops.quant_from_recv(px.back)
+            o8, so = torch.ops.h3b.quant_from_recv(px.back)
         elif self.ws > 1 and self.exchange_kind == "nocopy":
             from .ulysses_nocopy import qkv_views
             from .ulysses_overlap import quant_grouped_back
@@ -164,14 +164,14 @@ class AttentionBlock:
             mark()
             hgl = self.heads // (G * self.ws)
             v16 = self._v16_for(self.ws * m, hgl)
-            outs = [ops.flash_attn(*qkv_views(recv[g]), scale=scale, ctl=self._ctl, v16=v16)
+            outs = [torch.ops.h3b.flash_attn_scratch(*qkv_views(recv[g]), scale, None, v16, self._ctl)
                     for g in range(G)]
             mark()
             back = torch.empty((G, self.ws, m, hgl, d), dtype=torch.bfloat16, device=self.device)
             for g in range(G):
                 self.exchange_into(back[g], outs[g].view(self.ws, m, hgl, d))
             mark()
-            o8, so = ops.quant_from_recv(back[0]) if G == 1 else quant_grouped_back(back)
+            o8, so = torch.ops.h3b.quant_from_recv(back[0]) if G == 1 else quant_grouped_back(back)
         elif self.ws > 1 and self.groups > 1:
             from .ulysses_overlap import grouped_attention, quant_grouped_back
             sends = ops.fp8_gemm_qkv_send(q8, self.wqkv8, sx, self.sqkv, self.heads, self.ws, groups=self.groups)
@@ -181,7 +181,7 @@ class AttentionBlock:
             # streams, but they run one after another on the compute stream
             v16 = self._v16_for(self.ws * m, self.heads // (self.groups * self.ws))
             back = grouped_attention(sends, self.ws, self.groups,
-                                     lambda q, k, v: ops.flash_attn(q, k, v, scale=scale, ctl=self._ctl, v16=v16),
+                                     lambda q, k, v: torch.ops.h3b.flash_attn_scratch(q, k, v, scale, None, v16, self._ctl),
                                      pg=self.pg, a2a=self.a2a)
             mark()
             mark()
@@ -191,15 +191,15 @@ class AttentionBlock:
             mark()
             q, k, v = (self.exchange(s).view(self.ws * m, hl, d) for s in sends)
             mark()
-            o = ops.flash_attn(q, k, v, scale=scale, ctl=self._ctl, v16=self._v16_for(self.ws * m, hl))
+            o = torch.ops.h3b.flash_attn_scratch(q, k, v, scale, None, self._v16_for(self.ws * m, hl), self._ctl)
             mark()
             back = self.exchange(o.view(self.ws, m, hl, d))
             mark()
             if keep is not None:
                 keep.update(q=q, k=k, v=v, back=back)
-            o8, so = ops.quant_from_recv(back)
+            o8, so = torch.ops.h3b.quant_from_recv(back)
         mark()
-        y = ops.fp8_gemm(o8, self.wo8, so, self.so)
+        y = torch.ops.h3b.fp8_gemm(o8, self.wo8, so, self.so, None, torch.bfloat16)
         mark()
         if keep is not None:
             keep["y"] = y

@@ -47,7 +47,10 @@ class Stash:
 
     def materialize(self) -> torch.Tensor:
         """The ordinary bf16 output (into the placeholder when one was given)."""
-        return ops.fp8_gemm(self.a, self.w, self.sa, self.sb, self.bias, out=self.ph)
+        if self.ph is None:
+            return torch.ops.h3b.fp8_gemm(self.a, self.w, self.sa, self.sb, self.bias, torch.bfloat16)
+        torch.ops.h3b.fp8_gemm_out(self.a, self.w, self.sa, self.sb, self.bias, self.ph)
+        return self.ph
 
     def rows(self, r: int) -> "Stash":
         return Stash(self.a[:r], self.w, self.sa[:r], self.sb, self.bias, None)
@@ -83,7 +86,10 @@ def gate_fused(st: Stash, x: torch.Tensor, gate: torch.Tensor, indices: torch.Te
     out = st.ph if (reuse_placeholder and st.ph is not None and x.is_contiguous()) else None
     if x.shape[0] == 0:
         return out if out is not None else torch.empty_like(x)
-    return ops.fp8_gemm_gate(st.a, st.w, st.sa, st.sb, x, gate, indices, st.bias, out=out)
+    if out is None:
+        return torch.ops.h3b.fp8_gemm_gate(st.a, st.w, st.sa, st.sb, x, gate, indices, st.bias)
+    torch.ops.h3b.fp8_gemm_gate_out(st.a, st.w, st.sa, st.sb, x, gate, indices, st.bias, out)
+    return out
 
 
 def gate_rms_fused(st: Stash, residual: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor,
@@ -97,9 +103,9 @@ def gate_rms_fused(st: Stash, residual: torch.Tensor, gate: torch.Tensor, weight
     modulated_out = torch.empty_like(residual)
     if rows == 0:
         return residual_out, modulated_out
-    branch = ops.fp8_gemm(st.a, st.w, st.sa, st.sb, st.bias)
-    r_out, _, _ = ops.gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, eps)
-    ops.rms_quant(r_out, weight, shift, scale, indices, eps, modulated_out)
+    branch = torch.ops.h3b.fp8_gemm(st.a, st.w, st.sa, st.sb, st.bias, torch.bfloat16)
+    r_out, _, _ = torch.ops.h3b.gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, float(eps))
+    torch.ops.h3b.rms_quant(r_out, weight, shift, scale, indices, float(eps), modulated_out)
     if residual_out is not r_out:
         residual_out.copy_(r_out)
     return residual_out, modulated_out

@@ -40,7 +40,7 @@ def scaled_mm(a: torch.Tensor, b: torch.Tensor, scale_a: torch.Tensor, scale_b: 
               bias: torch.Tensor | None = None) -> torch.Tensor:
     """One tcgen05 FP8 GEMM with the scaled epilogue (the reference's ``scaled_mm_tensor32`` / ``scaled_mm_fused`` /
     ``fp8_cutlass.scaled_mm`` arithmetic)."""
-    return ops.fp8_gemm(a, b.t(), scale_a, scale_b, bias, out_dtype)
+    return torch.ops.h3b.fp8_gemm(a, b.t(), scale_a, scale_b, bias, out_dtype)
 
 
 scaled_mm_tensor32 = scaled_mm     # h3_tp2/fp8_gemm.py:149
@@ -57,7 +57,8 @@ def launch_fused(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.T
     if y.dtype == torch.float32:
         raise NotImplementedError("launch_fused: fp32 y (the raw accumulator) is not provided by the fused tcgen05 "
                                   "kernel; it writes the scaled bf16 / f16 output")
-    return ops.fp8_gemm(a, b.t(), sa, sb, bias, y.dtype, out=y)
+    torch.ops.h3b.fp8_gemm_out(a, b.t(), sa, sb, bias, y)
+    return y
 
 
 def fused_config() -> tuple[int, int, int, int, int]:
@@ -101,7 +102,7 @@ def probe_fused(device) -> bool:  # noqa: ANN001
     w = torch.randint(-3, 4, (272, 64), device=dev, generator=g).to(torch.float8_e4m3fn)
     sa = torch.full((130,), 0.5, device=dev)
     sb = torch.full((272,), 0.25, device=dev)
-    y = ops.fp8_gemm(a, w, sa, sb)
+    y = torch.ops.h3b.fp8_gemm(a, w, sa, sb, None, torch.bfloat16)
     ref = ((a.float() @ w.float().t()) * 0.25 * 0.5).to(torch.bfloat16)
     return bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
 

@@ -33,13 +33,13 @@ MIN_SCALE = 1.0 / (FP8_MAX * 512.0)
 
 def quant(h: torch.Tensor, div_mode: int = ops.DIV_IEEE):
     """h3_tp2/fp8_quant_fuse.py:318."""
-    return ops.quant(h, div_mode=div_mode)
+    return torch.ops.h3b.quant(h, div_mode)
 
 
 def rms_quant(x, weight, shift, scale, indices, eps, stock=None, ph=None, div_mode: int = ops.DIV_IEEE):  # noqa: ANN001,ANN201
     """h3_tp2/fp8_quant_fuse.py:330: (fp8 [M, H], scale [M, 1]); ``ph`` also receives the bf16 row."""
     del stock
-    return ops.rms_quant(x, weight, shift, scale, indices, eps, ph, div_mode=div_mode)
+    return torch.ops.h3b.rms_quant(x, weight, shift, scale, indices, float(eps), ph, div_mode)
 
 
 def gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, eps, stock=None, ph=None,  # noqa: ANN001,ANN201
@@ -48,18 +48,18 @@ def gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, eps, s
     del stock
     if ph is not None:
         raise NotImplementedError("gate_rms_quant: the bf16 copy (ph) is not produced on this path")
-    return ops.gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, eps, div_mode=div_mode)
+    return torch.ops.h3b.gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, float(eps), div_mode)
 
 
 def unpack_quant(recv: torch.Tensor, div_mode: int = ops.DIV_IEEE):
     """h3_tp2/fp8_quant_fuse.py:379: the reverse unpack + per-token quant of [M, P*hl*d]."""
-    return ops.quant_from_recv(recv.contiguous(), div_mode=div_mode)
+    return torch.ops.h3b.quant_from_recv(recv.contiguous(), div_mode)
 
 
 def silu_mul_quant(x: torch.Tensor, stock=None, div_mode: int = ops.DIV_IEEE):  # noqa: ANN001
     """h3_tp2/fp8_quant_fuse.py:392: silu_and_mul on bf16 [M, 2d] + per-token quant."""
     del stock
-    return ops.silu_mul_quant(x, div_mode=div_mode)
+    return torch.ops.h3b.silu_mul_quant(x, div_mode)
 
 
 def quant_torch(h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -31,17 +31,17 @@ def gemm_swiglu(a: torch.Tensor, b: torch.Tensor, sa: torch.Tensor, sb: torch.Te
                 cfg=None) -> torch.Tensor:  # noqa: ANN001
     """h3_tp2/fp8_swiglu.py:230: fc1 + epilogue + SwiGLU in one kernel; b [K, 2F] with b.t() contiguous."""
     del cfg
-    return ops.fp8_gemm_swiglu(a, b.t(), sa, sb, bias)
+    return torch.ops.h3b.fp8_gemm_swiglu(a, b.t(), sa, sb, bias)
 
 
 def ffn(x: torch.Tensor, norm_weight: torch.Tensor, w1: torch.Tensor, s1: torch.Tensor, w2: torch.Tensor,
         s2: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """BASELINE config 4's FFN: RMSNorm + per-token quant -> fc1 (gate/up, SwiGLU epilogue) -> per-token quant ->
     fc2.  x [M, C] bf16, w1 [2F, C] e4m3 with per-channel s1, w2 [C, F] e4m3 with s2 -> [M, C] bf16."""
-    q, sq = ops.rms_quant(x, norm_weight, eps=eps)
-    h = ops.fp8_gemm_swiglu(q, w1, sq, s1)
-    hq, sh = ops.quant(h)
-    return ops.fp8_gemm(hq, w2, sh, s2)
+    q, sq = torch.ops.h3b.rms_quant(x, norm_weight, None, None, None, float(eps), None)
+    h = torch.ops.h3b.fp8_gemm_swiglu(q, w1, sq, s1, None)
+    hq, sh = torch.ops.h3b.quant(h)
+    return torch.ops.h3b.fp8_gemm(hq, w2, sh, s2, None, torch.bfloat16)
 
 
 def swiglu_epilogue_torch(acc: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
@@ -73,7 +73,7 @@ def probe_gemm_swiglu(device) -> bool:  # noqa: ANN001
     w = torch.randint(-3, 4, (512, 64), device=dev, generator=g).to(torch.float8_e4m3fn)
     sa = torch.full((130,), 0.5, device=dev)
     sb = torch.full((512,), 0.03125, device=dev)
-    y = ops.fp8_gemm_swiglu(a, w, sa, sb)
+    y = torch.ops.h3b.fp8_gemm_swiglu(a, w, sa, sb, None)
     ref = swiglu_epilogue_torch(a.float().cpu() @ w.float().cpu().t(), sa.cpu(), sb.cpu(), None)
     diff = (y.cpu().view(torch.int16).int() - ref.view(torch.int16).int()).abs()
     return bool(diff.max().item() <= 1)
@@ -120,11 +120,11 @@ def _stash_hook(a, b, scale_a, scale_b, out_dtype, bias):  # noqa: ANN001,ANN202
 
 
 def _quant(h: torch.Tensor):  # noqa: ANN202
-    return ops.quant(h)
+    return torch.ops.h3b.quant(h)
 
 
 def _gemm(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor) -> torch.Tensor:
-    return ops.fp8_gemm(a, w, sa, sb)
+    return torch.ops.h3b.fp8_gemm(a, w, sa, sb, None, torch.bfloat16)
 
 
 def _fc2_direct(fc2, q: torch.Tensor, scale: torch.Tensor, lead) -> torch.Tensor | None:  # noqa: ANN001

@@ -662,47 +662,100 @@ def set_wait_timeout_ns(ns: int) -> None:
 
 
 # ---------------------------------------------------------------------------------------------------------------
-# torch.ops.h3b registrations (the op signatures the drop-in shims call)
+# torch.ops.h3b: the op surface the drop-in shims call (registered once, when this module is imported)
 # ---------------------------------------------------------------------------------------------------------------
+# The reference reaches its GEMM through vLLM's custom op (``ops.cutlass_scaled_mm``, h3_tp2/fp8_gemm.py:386) and its
+# quant through ``QuantFP8``; the shims here call these ops, whose CUDA kernels are the functions above.  Only the
+# CUDA dispatch key has a kernel: a CPU tensor raises (no CPU fallback).  Each op also has a fake (meta) kernel that
+# gives its output shapes, so the ops trace.  Ops that write into a caller's tensor say so in their schema (``a!``).
 
-_REGISTERED = False
+SCHEMAS = {
+    "quant": "quant(Tensor h, int div_mode=0) -> (Tensor, Tensor)",
+    "quant_rows": "quant_rows(Tensor base, int m, int p, int seg, int stride_p, int stride_m, int div_mode=0) "
+                  "-> (Tensor, Tensor)",
+    "quant_from_recv": "quant_from_recv(Tensor recv, int div_mode=0) -> (Tensor, Tensor)",
+    "rms_quant": "rms_quant(Tensor x, Tensor weight, Tensor? shift, Tensor? scale, Tensor? indices, float eps, "
+                 "Tensor(a!)? ph, int div_mode=0) -> (Tensor, Tensor)",
+    "gate_rms_quant": "gate_rms_quant(Tensor residual, Tensor gate, Tensor branch, Tensor weight, Tensor? shift, "
+                      "Tensor? scale, Tensor? indices, float eps, int div_mode=0) -> (Tensor, Tensor, Tensor)",
+    "silu_mul_quant": "silu_mul_quant(Tensor x, int div_mode=0) -> (Tensor, Tensor)",
+    "fp8_gemm": "fp8_gemm(Tensor a, Tensor w, Tensor sa, Tensor sb, Tensor? bias, ScalarType out_dtype) -> Tensor",
+    "fp8_gemm_out": "fp8_gemm_out(Tensor a, Tensor w, Tensor sa, Tensor sb, Tensor? bias, Tensor(a!) out) -> ()",
+    "fp8_gemm_swiglu": "fp8_gemm_swiglu(Tensor a, Tensor w, Tensor sa, Tensor sb, Tensor? bias) -> Tensor",
+    "fp8_gemm_gate": "fp8_gemm_gate(Tensor a, Tensor w, Tensor sa, Tensor sb, Tensor x, Tensor gate, Tensor indices, "
+                     "Tensor? bias) -> Tensor",
+    "fp8_gemm_gate_out": "fp8_gemm_gate_out(Tensor a, Tensor w, Tensor sa, Tensor sb, Tensor x, Tensor gate, "
+                         "Tensor indices, Tensor? bias, Tensor(a!) out) -> ()",
+    "flash_attn": "flash_attn(Tensor q, Tensor k, Tensor v, float? scale=None, int? valid_kv=None) -> Tensor",
+    "flash_attn_scratch": "flash_attn_scratch(Tensor q, Tensor k, Tensor v, float? scale, int? valid_kv, "
+                          "Tensor(a!) v16, Tensor(b!) ctl) -> Tensor",
+}
 
 
-def register_torch_ops() -> None:
-    global _REGISTERED
-    if _REGISTERED:
-        return
-    from torch.library import custom_op
+def _kernels() -> dict:
+    return {
+        "quant": lambda h, div_mode=DIV_IEEE: quant(h, div_mode=div_mode),
+        "quant_rows": lambda base, m, p, seg, sp, sm, div_mode=DIV_IEEE: quant_rows(base, m, p, seg, sp, sm,
+                                                                                     div_mode=div_mode),
+        "quant_from_recv": lambda recv, div_mode=DIV_IEEE: quant_from_recv(recv, div_mode=div_mode),
+        "rms_quant": lambda x, w, sh, sc, idx, eps, ph, div_mode=DIV_IEEE: rms_quant(x, w, sh, sc, idx, eps, ph,
+                                                                                   div_mode=div_mode),
+        "gate_rms_quant": lambda r, g, b, w, sh, sc, idx, eps, div_mode=DIV_IEEE: gate_rms_quant(
+            r, g, b, w, sh, sc, idx, eps, div_mode=div_mode),
+        "silu_mul_quant": lambda x, div_mode=DIV_IEEE: silu_mul_quant(x, div_mode=div_mode),
+        "fp8_gemm": lambda a, w, sa, sb, bias, dt: fp8_gemm(a, w, sa, sb, bias, dt),
+        "fp8_gemm_out": lambda a, w, sa, sb, bias, out: (fp8_gemm(a, w, sa, sb, bias, out=out), None)[1],
+        "fp8_gemm_swiglu": lambda a, w, sa, sb, bias: fp8_gemm_swiglu(a, w, sa, sb, bias),
+        "fp8_gemm_gate": lambda a, w, sa, sb, x, g, idx, bias: fp8_gemm_gate(a, w, sa, sb, x, g, idx, bias),
+        "fp8_gemm_gate_out": lambda a, w, sa, sb, x, g, idx, bias, out: (
+            fp8_gemm_gate(a, w, sa, sb, x, g, idx, bias, out=out), None)[1],
+        "flash_attn": lambda q, k, v, scale=None, valid_kv=None: flash_attn(q, k, v, scale=scale, valid_kv=valid_kv),
+        "flash_attn_scratch": lambda q, k, v, scale, valid_kv, v16, ctl: flash_attn(q, k, v, scale=scale,
+                                                                                    valid_kv=valid_kv, v16=v16,
+                                                                                    ctl=ctl),
+    }
 
-    @custom_op("h3b::quant_rows", mutates_args=())
-    def _quant_rows(base: torch.Tensor, m: int, p: int, seg: int, stride_p: int, stride_m: int,
-                    div_mode: int) -> tuple[torch.Tensor, torch.Tensor]:
-        return quant_rows(base, m, p, seg, stride_p, stride_m, div_mode=div_mode)
 
-    @custom_op("h3b::fp8_gemm", mutates_args=())
-    def _fp8_gemm(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor,
-                  bias: torch.Tensor | None, out_f16: bool) -> torch.Tensor:
-        return fp8_gemm(a, w, sa, sb, bias, torch.float16 if out_f16 else torch.bfloat16)
+def _fakes() -> dict:
+    f32 = torch.float32
 
-    @custom_op("h3b::fp8_gemm_swiglu", mutates_args=())
-    def _fp8_gemm_swiglu(a: torch.Tensor, w: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor,
-                         bias: torch.Tensor | None) -> torch.Tensor:
-        return fp8_gemm_swiglu(a, w, sa, sb, bias)
+    def q_and_s(rows, cols, like):
+        return like.new_empty((rows, cols), dtype=E4M3), like.new_empty((rows, 1), dtype=f32)
 
-    @custom_op("h3b::flash_attn", mutates_args=())
-    def _flash_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, valid_kv: int) -> torch.Tensor:
-        return flash_attn(q, k, v, scale=scale, valid_kv=None if valid_kv < 0 else valid_kv)
+    def attn_out(q):
+        return q.new_empty(q.shape, dtype=torch.bfloat16)
 
-    @custom_op("h3b::rms_quant", mutates_args=())
-    def _rms_quant(x: torch.Tensor, weight: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
-        return rms_quant(x, weight, eps=eps)
+    return {
+        "quant": lambda h, div_mode=0: q_and_s(h.shape[0], h.shape[1], h),
+        "quant_rows": lambda base, m, p, seg, sp, sm, div_mode=0: q_and_s(m, p * seg, base),
+        "quant_from_recv": lambda recv, div_mode=0: q_and_s(recv.shape[1], recv.shape[0] * recv.shape[2] *
+                                                            recv.shape[3], recv),
+        "rms_quant": lambda x, w, sh, sc, idx, eps, ph, div_mode=0: q_and_s(x.shape[0], x.shape[1], x),
+        "gate_rms_quant": lambda r, g, b, w, sh, sc, idx, eps, div_mode=0: (
+            r.new_empty(r.shape, dtype=torch.bfloat16), *q_and_s(r.shape[0], r.shape[1], r)),
+        "silu_mul_quant": lambda x, div_mode=0: q_and_s(x.shape[0], x.shape[1] // 2, x),
+        "fp8_gemm": lambda a, w, sa, sb, bias, dt: a.new_empty((a.shape[0], w.shape[0]), dtype=dt),
+        "fp8_gemm_out": lambda a, w, sa, sb, bias, out: None,
+        "fp8_gemm_swiglu": lambda a, w, sa, sb, bias: a.new_empty((a.shape[0], w.shape[0] // 2),
+                                                                  dtype=torch.bfloat16),
+        "fp8_gemm_gate": lambda a, w, sa, sb, x, g, idx, bias: x.new_empty((a.shape[0], w.shape[0]),
+                                                                           dtype=torch.bfloat16),
+        "fp8_gemm_gate_out": lambda a, w, sa, sb, x, g, idx, bias, out: None,
+        "flash_attn": lambda q, k, v, scale=None, valid_kv=None: attn_out(q),
+        "flash_attn_scratch": lambda q, k, v, scale, valid_kv, v16, ctl: attn_out(q),
+    }
 
-    @custom_op("h3b::silu_mul_quant", mutates_args=())
-    def _silu_mul_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        return silu_mul_quant(x)
 
-    @custom_op("h3b::pack_by_dest", mutates_args=())
-    def _pack_by_dest(x: torch.Tensor, ws: int) -> torch.Tensor:
-        return pack_by_dest(x, ws)
+def _register() -> None:
+    if hasattr(torch.ops, "h3b") and hasattr(torch.ops.h3b, "flash_attn"):
+        return   # a second import of this module in the same process (the ops are process-wide)
+    lib = torch.library.Library("h3b", "DEF")
+    kernels, fakes = _kernels(), _fakes()
+    for name, schema in SCHEMAS.items():
+        lib.define(schema)
+        lib.impl(name, kernels[name], "CUDA")
+        torch.library.register_fake(f"h3b::{name}", fakes[name], lib=lib)
+    globals()["_LIBRARY"] = lib   # the registrations live as long as the library object
 
-    _REGISTERED = True
+
+_register()

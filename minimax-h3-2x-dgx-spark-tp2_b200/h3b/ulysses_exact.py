@@ -417,7 +417,7 @@ def local_attention(q, k, v, attn_metadata=None):  # noqa: ANN001,ANN201
     valid = None
     if attn_metadata is not None:
         valid = getattr(attn_metadata, "valid_kv_length", None)
-    return ops.flash_attn(q, k, v, valid_kv=valid)
+    return torch.ops.h3b.flash_attn(q, k, v, None, valid)
 
 
 def make_forward_impl(orig, mode: str, strategy_info, *, a2a=None, stock_fwd=None, stock_back=None, on_first=None,  # noqa: ANN001,ANN201

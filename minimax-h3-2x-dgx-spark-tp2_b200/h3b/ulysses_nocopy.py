@@ -95,7 +95,7 @@ def local_attention(q, k, v, attn_metadata=None):  # noqa: ANN001,ANN201
     valid = None
     if attn_metadata is not None:
         valid = getattr(attn_metadata, "valid_kv_length", None)
-    return ops.flash_attn(q, k, v, valid_kv=valid)
+    return torch.ops.h3b.flash_attn(q, k, v, None, valid)
 
 
 def nocopy_forward(query, key, value, run_attn, *, ws, groups, pg=None, a2a=None, send_box=None, comm=None,  # noqa: ANN001,ANN201

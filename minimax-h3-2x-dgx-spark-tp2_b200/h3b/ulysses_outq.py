@@ -38,7 +38,7 @@ def quant_rows(base: torch.Tensor, m: int, p: int, seg: int, stride_p: int, stri
     """h3_tp2/ulysses_outq.py:109 (``warps`` is accepted for signature compatibility; the CUDA kernel picks its own
     launch shape).  Returns (q [M, P*seg] e4m3, scale [M, 1] fp32)."""
     del warps
-    return ops.quant_rows(base, m, p, seg, stride_p, stride_m, div_mode=div_mode)
+    return torch.ops.h3b.quant_rows(base, m, p, seg, stride_p, stride_m, div_mode)
 
 
 def quant_reference_eager(x: torch.Tensor, out=None):  # noqa: ANN001,ANN201
@@ -56,7 +56,7 @@ def quant_reference_eager(x: torch.Tensor, out=None):  # noqa: ANN001,ANN201
 def quant_from_recv(recv: torch.Tensor, warps: int = 8, div_mode: int = ops.DIV_IEEE):
     """h3_tp2/ulysses_outq.py:138: recv [P, M, hl, d] -> the quant of stock's unpacked [M, P*hl*d] rows."""
     del warps
-    return ops.quant_from_recv(recv, div_mode=div_mode)
+    return torch.ops.h3b.quant_from_recv(recv, div_mode)
 
 
 def unpack_rows(recv: torch.Tensor) -> torch.Tensor:

@@ -91,7 +91,7 @@ def quant_grouped_back(back: torch.Tensor, div_mode: int = ops.DIV_IEEE):
     """The out-projection quant straight from the grouped reverse receive buffer [G, P, M, hgl, d]."""
     G, P, M, hgl, d = back.shape
     seg = hgl * d
-    return ops.quant_rows(back, M, G * P, seg, M * seg, seg, div_mode=div_mode)
+    return torch.ops.h3b.quant_rows(back, M, G * P, seg, M * seg, seg, div_mode)
 
 
 def _a2a_seq_to_heads(x: torch.Tensor, ws: int, pg, recv: torch.Tensor, a2a=None) -> torch.Tensor:  # noqa: ANN001

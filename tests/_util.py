@@ -60,3 +60,24 @@ def ulp_diff_bf16(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 def rel_l2(x: torch.Tensor, ref: torch.Tensor) -> float:
     x, ref = x.detach().double().cpu(), ref.detach().double().cpu()
     return float((x - ref).norm() / ref.norm().clamp_min(1e-300))
+
+
+class CpuKernels:
+    """Registers eager stand-ins as the CPU kernels of ``torch.ops.h3b`` ops for the duration of a test (the product
+    registers CUDA kernels only, so a CPU tensor reaching an op otherwise raises).  Used by the host-wiring tests,
+    which exercise the call protocol on the CPU, not the kernels."""
+
+    def __init__(self, **impls):
+        self.impls = impls
+        self.lib = None
+
+    def __enter__(self):
+        import h3b.ops  # noqa: F401  (the op definitions)
+        self.lib = torch.library.Library("h3b", "IMPL")
+        for name, fn in self.impls.items():
+            self.lib.impl(name, fn, "CPU")
+        return self
+
+    def __exit__(self, *exc):
+        self.lib._destroy()
+        self.lib = None

@@ -7,6 +7,8 @@ from pathlib import Path
 
 import torch
 
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
 ROOT = Path(__file__).resolve().parents[1]
 KEYS = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
         "vs_baseline", "dtype", "data", "config"}
@@ -39,3 +41,60 @@ def test_gpu_arm_fails_loudly_without_a_gpu():
     res = _run("--tokens", "4096", "--steps", "1", "--warmup", "1", "--no-cpu-baseline")
     assert res.returncode != 0
     assert not [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_reference_arm_times_the_sample_it_ran():
+    """ms_per_step is the measured sample time (it must fit in the run), the whole-block figure is a separate,
+    labelled extrapolation, and the config dict is the GPU arm's (same workload)."""
+    import bench
+    res = _run("--impl", "reference", "--tokens", "4096", "--steps", "3", "--warmup", "1", "--ref-rows", "64")
+    d = json.loads([ln for ln in res.stdout.splitlines() if ln.startswith("{")][0])
+    assert d["ms_per_step"] * d["steps"] < 60_000
+    assert d["block_ms_extrapolated"] > d["ms_per_step"]
+    assert d["config"] == bench.config_dict(4096, 1)
+
+
+def _fake_block_run(m, world_rows=None, plant=None):
+    """The GPU arm's parity inputs built on the CPU from the oracle (rank 0 of 1): weights, x from bench.make_x, and
+    the forward's kept tensors as the oracle computes them; ``plant`` corrupts one of them."""
+    import bench
+    from oracle import attention as oa
+    from oracle import block as ob
+    from oracle import gemm as og
+    from oracle import quant as oq
+    H, d, C = bench.HEADS, bench.HEAD_DIM, bench.HIDDEN
+    wqkv8, sqkv, wo8, so = ob.make_weights(C, H, seed=1)
+    blk = type("Blk", (), {"wqkv8": wqkv8, "sqkv": sqkv, "wo8": wo8, "so": so})()
+    x = bench.make_x(0, m, torch.device("cpu"))
+    q8, sx = oq.quant(x)
+    qkv = og.scaled_mm(q8, wqkv8, sx, sqkv)
+    q, k, v = (t.reshape(m, H, d) for t in qkv.split(H * d, dim=1))
+    o = oa.sdpa(q, k, v).to(torch.bfloat16)
+    o8, so_ = oq.quant(o.reshape(m, H * d))
+    y = og.scaled_mm(o8, wo8, so_, so)
+    keep = {"q": q, "k": k, "v": v, "back": o.reshape(1, m, H, d), "y": y}
+    if plant is not None:
+        plant(keep)
+    return blk, keep
+
+
+def test_block_parity_passes_on_oracle_data_and_catches_a_planted_error():
+    import bench
+    m = 192
+    blk, keep = _fake_block_run(m)
+    par = bench.block_parity(blk, keep, 0, 1, m, torch.device("cpu"), None, rows=16)
+    assert par["ok"], par
+    # the kept attention rows are bf16 (the oracle's fp32 rows rounded): that rounding is all that differs
+    assert par["rel_l2"]["attention"] < 2e-3 and par["rel_l2"]["block"] < 1e-6 and par["rel_l2"]["qkv"] == 0
+
+    def plant(keep):   # one value of the kept K: every sampled query row's attention moves
+        keep["k"][5, 3] += 40.0
+    blk, keep = _fake_block_run(m, plant=plant)
+    par = bench.block_parity(blk, keep, 0, 1, m, torch.device("cpu"), None, rows=16)
+    assert not par["ok"]
+
+    def plant_y(keep):  # one output row of the block
+        keep["y"][0] *= 1.5
+    blk, keep = _fake_block_run(m, plant=plant_y)
+    par = bench.block_parity(blk, keep, 0, 1, m, torch.device("cpu"), None, rows=16)
+    assert not par["ok"] and par["rel_l2"]["out"] > 1e-2

@@ -11,6 +11,7 @@ import pytest
 import torch
 
 from h3b import fp8_consumers as fc
+from _util import CpuKernels
 from h3b import fp8_gemm, ops
 from oracle import gemm as og
 from oracle import quant as oq
@@ -51,6 +52,9 @@ def _fused_gate(st, x, gate, indices, reuse_placeholder=True):  # noqa: ARG001
 
 @pytest.fixture(autouse=True)
 def _eager(monkeypatch):
+    kernels = CpuKernels(fp8_gemm=lambda a, w, sa, sb, bias, dt: _gemm(a, w, sa, sb, bias, dt),
+                         fp8_gemm_out=lambda a, w, sa, sb, bias, out: (_gemm(a, w, sa, sb, bias, out=out), None)[1])
+    kernels.__enter__()
     monkeypatch.setattr(ops, "fp8_gemm", _gemm)
     monkeypatch.setattr(fc, "qk_norm_rope_fused", _fused_qk)
     monkeypatch.setattr(fc, "gate_rms_fused", _fused_gate_rms)
@@ -61,6 +65,7 @@ def _eager(monkeypatch):
     monkeypatch.setattr(fp8_gemm, "_routers", [])
     yield
     fc._tls.ctx = None
+    kernels.__exit__()
 
 
 def _layer(n, k, seed):
