@@ -23,13 +23,12 @@ the stock consumer; a mismatch disables the site for the process.
 """
 from __future__ import annotations
 
-import functools
 import logging
-import threading
 from typing import Any
 
 import torch
 
+from . import _fusewire as _fw
 from . import ops
 
 logger = logging.getLogger("h3b.fp8_consumers")
@@ -140,12 +139,10 @@ def parse_sites(value: str | None) -> tuple[str, ...]:
 
 
 # --------------------------------------------------------------------------------------------------------------------
-# the wiring: stash hook, block plan, consumer wrappers (h3_tp2/fp8_consumers.py:498-919)
+# the wiring (the reference's protocol, h3_tp2/fp8_consumers.py:498-919, on the shared machinery of h3b._fusewire)
 # --------------------------------------------------------------------------------------------------------------------
 
-_SELFCHECK_ROWS = 64
 _ROTARY_DIMS = (32, 64, 96, 128)      # what the norm + RoPE epilogue rotates (the reference's Triton copy: 96 only)
-_tls = threading.local()              # ctx: the _Ctx of the DiT block whose forward is running in this thread
 _state: dict[str, Any] = {"sites": (), "checked": {}, "disabled": set(), "device_types": ("cuda",)}
 _stats: dict[str, int] = {k: 0 for k in ("stash", "materialize", "fused_qkv", "fused_out", "fused_fc2",
                                          "selfcheck_pass", "selfcheck_fail")}
@@ -156,18 +153,21 @@ def stats() -> dict[str, int]:
     return dict(_stats)
 
 
-def _warn_once(key: str, msg: str, *args) -> None:  # noqa: ANN002
-    if key not in _warned:
-        _warned.add(key)
-        logger.warning("h3b fp8 consumer fuse: " + msg, *args)
+def _note_realized(site: str, why: str) -> None:
+    _stats["materialize"] += 1
+    if why not in _warned:
+        _warned.add(why)
+        logger.warning("h3b fp8 consumer fuse: %s: stash of %s materialised, stock consumer", why, site)
 
 
-class _Ctx:
-    __slots__ = ("want", "pending")
+_scopes = _fw.ScopeRegistry(lambda st: st.materialize(), _note_realized)
+_tls = _scopes.local       # ``_tls.ctx``: the running block's scope (plan: (weight pointer, weight shape) -> site)
+_verdicts = _fw.Verdicts(lambda: _state, lambda: _stats, logger, "fp8 consumer fuse")
 
-    def __init__(self, want: dict):
-        self.want = want                            # (weight data_ptr, weight shape) -> site
-        self.pending: dict[str, Stash] = {}
+
+def scope(block, want: dict) -> _fw.BlockScope:  # noqa: ANN001
+    """The context in which a planned block's forward runs; ``want`` maps the planned GEMMs' weights to their sites."""
+    return _fw.BlockScope(_scopes, block, want)
 
 
 def _vec(scale: torch.Tensor, n: int) -> torch.Tensor:
@@ -176,61 +176,26 @@ def _vec(scale: torch.Tensor, n: int) -> torch.Tensor:
 
 
 def stash_hook(a, b, scale_a, scale_b, out_dtype, bias):  # noqa: ANN001,ANN201
-    """FP8 GEMM dispatcher hook (:531): when ``b`` ([K, N], the layer's stored weight) is the qkv / out / fc2 weight of
-    the running DiT block, keep the GEMM's operands and return an uninitialised bf16 placeholder for the consumer."""
-    ctx = getattr(_tls, "ctx", None)
-    if ctx is None or out_dtype is not torch.bfloat16:
+    """FP8 GEMM dispatcher hook (h3_tp2/fp8_consumers.py:531).  A bf16 GEMM whose weight ``b`` ([K, N], as the layer
+    stores it) is one of the running block's planned qkv / out / fc2 weights is not run: its operands are kept (each
+    planned weight once per block) and the model gets an uninitialised bf16 placeholder for the consumer."""
+    sc = _scopes.current()
+    if sc is None or out_dtype is not torch.bfloat16:
         return None
-    site = ctx.want.pop((b.data_ptr(), tuple(b.shape)), None)
+    site = sc.plan.pop((b.data_ptr(), tuple(b.shape)), None)
     if site is None:
         return None
-    if ctx.pending:                       # a stash that was never consumed: make it real before the next one
-        _materialize_all(ctx, f"unconsumed stash before {site}")
-    M, N = a.shape[0], b.shape[1]
-    ph = torch.empty((M, N), device=a.device, dtype=out_dtype)
-    ctx.pending[site] = Stash(a, b.t(), _vec(scale_a, M), _vec(scale_b, N), bias, ph)
+    if sc.handoffs:
+        _scopes.realize_all(sc, f"unconsumed stash before {site}")
+    rows, cols = a.shape[0], b.shape[1]
+    ph = torch.empty((rows, cols), device=a.device, dtype=out_dtype)
+    sc.handoffs[site] = Stash(a, b.t(), _vec(scale_a, rows), _vec(scale_b, cols), bias, ph)
     _stats["stash"] += 1
     return ph
 
 
-def _materialize_all(ctx: _Ctx, reason: str) -> None:
-    for site, st in list(ctx.pending.items()):
-        st.materialize()
-        _stats["materialize"] += 1
-        _warn_once("mat-" + reason, "%s: stash of %s materialised, stock consumer", reason, site)
-    ctx.pending.clear()
-
-
-def _bits(t: torch.Tensor) -> torch.Tensor:
-    t = t.contiguous()
-    return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
-
-
-def _selfcheck(key, fused_fn, stock_fn) -> bool:  # noqa: ANN001
-    """Once per (site, shape): fused against the plain GEMM + stock consumer on the first rows, bit for bit; a mismatch
-    (or a raising fused kernel) disables the site for the process (:561)."""
-    ok = _state["checked"].get(key)
-    if ok is not None:
-        return ok
-    try:
-        fused, stock = fused_fn(), stock_fn()
-        ok = len(fused) == len(stock) and all(f.shape == t.shape and f.dtype == t.dtype
-                                              and torch.equal(_bits(f), _bits(t)) for f, t in zip(fused, stock))
-    except Exception as exc:  # noqa: BLE001
-        logger.warning("h3b fp8 consumer fuse: self-check %s raised %s", key, exc)
-        ok = False
-    _state["checked"][key] = ok
-    _stats["selfcheck_pass" if ok else "selfcheck_fail"] += 1
-    if not ok:
-        _state["disabled"].add(key[0])
-        logger.warning("h3b fp8 consumer fuse: self-check %s not bit-identical to the GEMM + stock consumer; site %s "
-                       "disabled for this process", key, key[0])
-    return ok
-
-
 def _device_ok(*ts: torch.Tensor) -> bool:
-    dev = ts[0].device
-    return all(t.device == dev for t in ts) and dev.type in _state["device_types"]
+    return _fw.same_device(_state["device_types"], *ts)
 
 
 def _stash_ok(st: Stash) -> bool:
@@ -239,241 +204,305 @@ def _stash_ok(st: Stash) -> bool:
             and st.a.shape[0] == ph.shape[0] and st.w.shape[0] == ph.shape[1])
 
 
+def _qkv_split(ph: torch.Tensor, T: int, H: int, Hk: int, D: int) -> tuple:
+    """Upstream's split of the qkv output into q, k, v views [T, heads, D]."""
+    return (ph[:, :H * D].view(T, H, D), ph[:, H * D:(H + Hk) * D].view(T, Hk, D), ph[:, (H + Hk) * D:].view(T, Hk, D))
+
+
 def qk_mismatch(st: Stash, q, k, q_weight, k_weight, rope_table, head_dim, rotary_dim, interleaved) -> str | None:  # noqa: ANN001
     """None when (q, k) are exactly the q/k views of the stash's placeholder and the norm + RoPE epilogue covers the
-    call (:591), else the reason."""
+    call (h3_tp2/fp8_consumers.py:591), else the first reason it does not (checked in this order: layout of the call,
+    the placeholder, the views, the head and rotary sizes, the weights, bias, devices)."""
     ph = st.ph
-    if interleaved:
-        return "interleaved"
-    if q.dim() != 3 or k.dim() != 3 or q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
-        return "q/k rank or dtype"
-    T, H, D = q.shape
-    Hk = k.shape[1]
-    if ph is None or T == 0 or ph.dim() != 2 or ph.shape[0] != T or k.shape != (T, Hk, D) \
-            or ph.shape[1] != (H + 2 * Hk) * D:
-        return "shapes"
-    if Hk != H:
-        return "grouped kv heads"
-    if not _stash_ok(st):
-        return "placeholder/operand layout"
-    eq, ek = ph[:, :H * D].view(T, H, D), ph[:, H * D:(H + Hk) * D].view(T, Hk, D)   # upstream's split + view
-    if q.data_ptr() != eq.data_ptr() or k.data_ptr() != ek.data_ptr() or q.stride() != eq.stride() \
-            or k.stride() != ek.stride():
-        return "q/k are not the split views of the qkv placeholder"
-    if D != 128 or head_dim not in (None, D):
-        return "head_dim"
-    rot = rope_table.shape[-1] if rope_table.dim() == 2 else -1
-    if rot not in _ROTARY_DIMS or rotary_dim not in (None, rot) or rope_table.shape != (T, rot):
-        return "rotary"
-    if rope_table.dtype not in (torch.bfloat16, torch.float32) or q_weight.shape != (D,) or k_weight.shape != (D,) \
-            or q_weight.dtype != torch.bfloat16 or k_weight.dtype != torch.bfloat16:
-        return "rope table or norm weight dtype/shape"
-    if st.bias is not None:
-        return "bias (the norm epilogue has none)"
-    if not _device_ok(q, k, q_weight, k_weight, rope_table, st.a):
-        return "device"
+    checks = (
+        (lambda: not interleaved, "interleaved"),
+        (lambda: q.dim() == 3 and k.dim() == 3 and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16,
+         "q/k rank or dtype"),
+        (lambda: (ph is not None and q.shape[0] > 0 and ph.dim() == 2 and ph.shape[0] == q.shape[0]
+                  and k.shape == (q.shape[0], k.shape[1], q.shape[2])
+                  and ph.shape[1] == (q.shape[1] + 2 * k.shape[1]) * q.shape[2]), "shapes"),
+        (lambda: k.shape[1] == q.shape[1], "grouped kv heads"),
+        (lambda: _stash_ok(st), "placeholder/operand layout"),
+        (lambda: _views_are_placeholder(ph, q, k), "q/k are not the split views of the qkv placeholder"),
+        (lambda: q.shape[2] == 128 and head_dim in (None, 128), "head_dim"),
+        (lambda: _rotary_ok(rope_table, rotary_dim, q.shape[0]), "rotary"),
+        (lambda: (rope_table.dtype in (torch.bfloat16, torch.float32) and q_weight.shape == (128,)
+                  and k_weight.shape == (128,) and q_weight.dtype == torch.bfloat16
+                  and k_weight.dtype == torch.bfloat16), "rope table or norm weight dtype/shape"),
+        (lambda: st.bias is None, "bias (the norm epilogue has none)"),
+        (lambda: _device_ok(q, k, q_weight, k_weight, rope_table, st.a), "device"),
+    )
+    for holds, reason in checks:
+        if not holds():
+            return reason
     return None
+
+
+def _views_are_placeholder(ph: torch.Tensor, q: torch.Tensor, k: torch.Tensor) -> bool:
+    eq, ek, _ = _qkv_split(ph, q.shape[0], q.shape[1], k.shape[1], q.shape[2])
+    return (q.data_ptr(), q.stride(), k.data_ptr(), k.stride()) == (eq.data_ptr(), eq.stride(), ek.data_ptr(),
+                                                                    ek.stride())
+
+
+def _rotary_ok(rope_table: torch.Tensor, rotary_dim, T: int) -> bool:  # noqa: ANN001
+    rot = rope_table.shape[-1] if rope_table.dim() == 2 else -1
+    return rot in _ROTARY_DIMS and rotary_dim in (None, rot) and tuple(rope_table.shape) == (T, rot)
 
 
 def rows_mismatch(st: Stash, x: torch.Tensor, branch: torch.Tensor, *others: torch.Tensor) -> str | None:
-    """None when ``branch`` is exactly the stash's placeholder and ``x`` (the residual) a contiguous bf16 tensor of the
-    same shape on the same device as the other operands (gate / shift / scale, then the indices last) (:622)."""
+    """None when ``branch`` is exactly the stash's placeholder and ``x`` (the residual) a contiguous bf16 tensor of its
+    shape on the operands' device, with gate / shift / scale row-major bf16 of its width and the indices (last of
+    ``others``) one per row (h3_tp2/fp8_consumers.py:622); else the reason."""
     ph = st.ph
-    if ph is None or branch.data_ptr() != ph.data_ptr() or branch.shape != ph.shape or branch.stride() != ph.stride():
+    if ph is None or (branch.data_ptr(), branch.shape, branch.stride()) != (ph.data_ptr(), ph.shape, ph.stride()):
         return "branch is not the placeholder"
-    if x.dim() != 2 or x.shape != ph.shape or x.dtype != torch.bfloat16 or not x.is_contiguous() \
-            or not _stash_ok(st):
+    if not (x.dim() == 2 and x.shape == ph.shape and x.dtype == torch.bfloat16 and x.is_contiguous()
+            and _stash_ok(st)):
         return "residual shape/dtype/layout"
     if x.shape[0] == 0:
         return "no rows"
-    if any(o.dim() != 2 or o.stride(1) != 1 or o.dtype != torch.bfloat16 or o.shape[1] != x.shape[1]
-           for o in others[:-1]):
+    *rowwise, indices = others
+    if not all(o.dim() == 2 and o.stride(1) == 1 and o.dtype == torch.bfloat16 and o.shape[1] == x.shape[1]
+               for o in rowwise):
         return "gate/shift/scale layout"
-    if others[-1].dim() != 1 or others[-1].shape[0] != x.shape[0]:
+    if indices.dim() != 1 or indices.shape[0] != x.shape[0]:
         return "indices"
-    if not _device_ok(x, st.a, *others):
-        return "device"
-    return None
+    return None if _device_ok(x, st.a, *others) else "device"
 
 
-def _take(site: str):  # noqa: ANN202
-    ctx = getattr(_tls, "ctx", None)
-    if ctx is None or not ctx.pending:
-        return ctx, None
-    st = ctx.pending.get(site)
+_STOCK = object()   # "not taken": the wrapper runs the stock consumer
+
+
+class _Consumer:
+    """One consumer site: ``call`` is the wrapped function's argument tuple and ``st`` the site's stash."""
+    name = ""
+
+    def __init__(self, orig):  # noqa: ANN001
+        self.orig = orig
+
+    def mismatch(self, st: Stash, call: tuple) -> str | None:
+        raise NotImplementedError
+
+    def key(self, st: Stash, call: tuple) -> tuple:
+        raise NotImplementedError
+
+    def fused(self, st: Stash, call: tuple, r: int) -> tuple:
+        raise NotImplementedError
+
+    def stock(self, st: Stash, call: tuple, r: int) -> tuple:
+        raise NotImplementedError
+
+    def run(self, st: Stash, call: tuple):  # noqa: ANN201
+        raise NotImplementedError
+
+
+def _consume(site: _Consumer, call: tuple):  # noqa: ANN202
+    """The fused consumer's result when the running block holds this site's stash and the call is exactly its
+    consumer (the first such call per key also matching the GEMM + stock consumer bit for bit); else ``_STOCK``, after
+    making every stash real (another site's stash, an ineligible call, a failed comparison)."""
+    sc = _scopes.current()
+    if sc is None or not sc.handoffs:
+        return _STOCK
+    st = sc.handoffs.get(site.name)
     if st is None:
-        _materialize_all(ctx, f"{site} consumer saw another site's stash")
-    return ctx, st
+        _scopes.realize_all(sc, f"{site.name} consumer saw another site's stash")
+        return _STOCK
+    reason = f"{site.name} disabled by self-check" if _verdicts.off(site.name) else site.mismatch(st, call)
+    if reason is None:
+        r = min(_fw.CHECK_ROWS, st.a.shape[0])
+        if not _verdicts.judge(site.key(st, call), lambda: site.fused(st.rows(r), call, r),
+                               lambda: site.stock(st.rows(r), call, r)):
+            reason = f"{site.name} disabled by self-check"
+    if reason is not None:
+        _scopes.realize_all(sc, f"{site.name}: {reason}")
+        return _STOCK
+    del sc.handoffs[site.name]
+    out = site.run(st, call)
+    _stats["fused_" + site.name] += 1
+    return out
+
+
+class _QkNormRope(_Consumer):
+    """``fused_qk_norm_rope(q, k, q_weight, k_weight, rope_table, eps, head_dim, rotary_dim, interleaved)`` on the qkv
+    placeholder's q/k views: the qkv GEMM with the norm + RoPE epilogue (``qk_norm_rope_fused``, looked up at call
+    time so the Ulysses producer can replace it); v is written into the placeholder's v view, which the model reads."""
+    name = "qkv"
+
+    def mismatch(self, st, call):  # noqa: ANN001,ANN201
+        q, k, qw, kw, table, _, head_dim, rotary_dim, interleaved = call
+        return qk_mismatch(st, q, k, qw, kw, table, head_dim, rotary_dim, interleaved)
+
+    def key(self, st, call):  # noqa: ANN001,ANN201
+        return ("qkv", tuple(st.ph.shape[1:]), call[4].dtype)
+
+    def _shape(self, call):  # noqa: ANN001,ANN202
+        q, k = call[0], call[1]
+        return q.shape[1], k.shape[1], q.shape[-1]
+
+    def fused(self, st, call, r):  # noqa: ANN001,ANN201
+        H, Hk, D = self._shape(call)
+        _, _, qw, kw, table, eps, _, _, _ = call
+        return qk_norm_rope_fused(st, H, Hk, D, qw, kw, table[:r], eps)
+
+    def stock(self, st, call, r):  # noqa: ANN001,ANN201
+        H, Hk, D = self._shape(call)
+        _, _, qw, kw, table, eps, head_dim, rotary_dim, interleaved = call
+        qs, ks, vs = _qkv_split(st.materialize(), r, H, Hk, D)
+        oq, ok_ = self.orig(qs, ks, qw, kw, table[:r], eps, head_dim=head_dim, rotary_dim=rotary_dim,
+                            interleaved=interleaved)
+        return oq, ok_, vs
+
+    def run(self, st, call):  # noqa: ANN001,ANN201
+        H, Hk, D = self._shape(call)
+        q, _, qw, kw, table, eps, _, _, _ = call
+        out_q, out_k, v = qk_norm_rope_fused(st, H, Hk, D, qw, kw, table, eps)
+        v_view = _qkv_split(st.ph, q.shape[0], H, Hk, D)[2]
+        if v.data_ptr() != v_view.data_ptr():
+            v_view.copy_(v)
+        return out_q, out_k
+
+
+class _GateRmsNorm(_Consumer):
+    """``indexed_gate_rms_norm_scale_shift(residual, gate, branch, weight, shift, scale, indices, eps)`` on the out
+    placeholder (branch): ``gate_rms_fused``."""
+    name = "out"
+
+    def mismatch(self, st, call):  # noqa: ANN001,ANN201
+        residual, gate, branch, weight, shift, scale, indices, _ = call
+        reason = rows_mismatch(st, residual, branch, gate, shift, scale, indices)
+        if reason is None and (weight.shape != (residual.shape[1],) or weight.device != residual.device
+                               or weight.dtype != torch.bfloat16):
+            reason = "norm weight shape/device/dtype"
+        return reason
+
+    def key(self, st, call):  # noqa: ANN001,ANN201
+        return ("out", tuple(call[0].shape[1:]), call[1].dtype, call[3].dtype)
+
+    def fused(self, st, call, r):  # noqa: ANN001,ANN201
+        residual, gate, _, weight, shift, scale, indices, eps = call
+        return gate_rms_fused(st, residual[:r], gate, weight, shift, scale, indices[:r], eps)
+
+    def stock(self, st, call, r):  # noqa: ANN001,ANN201
+        residual, gate, _, weight, shift, scale, indices, eps = call
+        return self.orig(residual[:r], gate, st.materialize(), weight, shift, scale, indices[:r], eps)
+
+    def run(self, st, call):  # noqa: ANN001,ANN201
+        residual, gate, _, weight, shift, scale, indices, eps = call
+        return gate_rms_fused(st, residual, gate, weight, shift, scale, indices, eps)
+
+
+class _IndexedGate(_Consumer):
+    """``indexed_gate(x, gate, other, indices)`` on the fc2 placeholder (other): the fc2 GEMM with the indexed-gate
+    epilogue."""
+    name = "fc2"
+
+    def mismatch(self, st, call):  # noqa: ANN001,ANN201
+        x, gate, other, indices = call
+        return rows_mismatch(st, x, other, gate, indices)
+
+    def key(self, st, call):  # noqa: ANN001,ANN201
+        return ("fc2", tuple(call[0].shape[1:]), call[1].dtype)
+
+    def fused(self, st, call, r):  # noqa: ANN001,ANN201
+        x, gate, _, indices = call
+        return (gate_fused(st, x[:r].contiguous(), gate, indices[:r], reuse_placeholder=False),)
+
+    def stock(self, st, call, r):  # noqa: ANN001,ANN201
+        x, gate, _, indices = call
+        return (self.orig(x[:r].contiguous(), gate, st.materialize(), indices[:r]),)
+
+    def run(self, st, call):  # noqa: ANN001,ANN201
+        x, gate, _, indices = call
+        return gate_fused(st, x, gate, indices)
 
 
 def make_qk_wrapper(orig):  # noqa: ANN001,ANN201
-    """Wrap the transformer's ``fused_qk_norm_rope`` (:652): on the qkv stash's q/k views, the qkv GEMM with the norm +
-    RoPE epilogue (``qk_norm_rope_fused``, looked up at call time so the Ulysses producer can replace it)."""
+    """``fused_qk_norm_rope`` with the qkv consumer (h3_tp2/fp8_consumers.py:652)."""
+    site = _QkNormRope(orig)
+
     def fused_qk_norm_rope(q, k, q_weight, k_weight, rope_table, eps, *, head_dim=None, rotary_dim=None,  # noqa: ANN001,ANN202
                            interleaved=False):
-        ctx, st = _take("qkv")
-        if st is not None:
-            reason = "qkv disabled by self-check" if "qkv" in _state["disabled"] else \
-                qk_mismatch(st, q, k, q_weight, k_weight, rope_table, head_dim, rotary_dim, interleaved)
-            if reason is None:
-                H, Hk, D = q.shape[1], k.shape[1], q.shape[-1]
-                r = min(_SELFCHECK_ROWS, q.shape[0])
-
-                def _fused_sub():  # noqa: ANN202
-                    return qk_norm_rope_fused(st.rows(r), H, Hk, D, q_weight, k_weight, rope_table[:r], eps)
-
-                def _stock_sub():  # noqa: ANN202
-                    p = st.rows(r).materialize()
-                    qs, ks = p[:, :H * D].view(r, H, D), p[:, H * D:(H + Hk) * D].view(r, Hk, D)
-                    oq, ok_ = orig(qs, ks, q_weight, k_weight, rope_table[:r], eps, head_dim=head_dim,
-                                   rotary_dim=rotary_dim, interleaved=interleaved)
-                    return oq, ok_, p[:, (H + Hk) * D:].view(r, Hk, D)
-
-                if not _selfcheck(("qkv", tuple(st.ph.shape[1:]), rope_table.dtype), _fused_sub, _stock_sub):
-                    reason = "qkv disabled by self-check"
-            if reason is None:
-                del ctx.pending["qkv"]
-                out_q, out_k, v = qk_norm_rope_fused(st, H, Hk, D, q_weight, k_weight, rope_table, eps)
-                v_view = st.ph[:, (H + Hk) * D:].view(q.shape[0], Hk, D)
-                if v.data_ptr() != v_view.data_ptr():
-                    v_view.copy_(v)       # the model reads v from its own view of the placeholder
-                _stats["fused_qkv"] += 1
-                return out_q, out_k
-            _materialize_all(ctx, "qkv: " + reason)
-        return orig(q, k, q_weight, k_weight, rope_table, eps, head_dim=head_dim, rotary_dim=rotary_dim,
-                    interleaved=interleaved)
+        out = _consume(site, (q, k, q_weight, k_weight, rope_table, eps, head_dim, rotary_dim, interleaved))
+        if out is _STOCK:
+            return orig(q, k, q_weight, k_weight, rope_table, eps, head_dim=head_dim, rotary_dim=rotary_dim,
+                        interleaved=interleaved)
+        return out
 
     fused_qk_norm_rope._h3b_consumer_fuse = True
     return fused_qk_norm_rope
 
 
 def make_gate_rms_wrapper(orig):  # noqa: ANN001,ANN201
-    """Wrap ``indexed_gate_rms_norm_scale_shift`` (:688): on the out stash's placeholder, ``gate_rms_fused``."""
+    """``indexed_gate_rms_norm_scale_shift`` with the out consumer (h3_tp2/fp8_consumers.py:688)."""
+    site = _GateRmsNorm(orig)
+
     def indexed_gate_rms_norm_scale_shift(residual, gate, branch, weight, shift, scale, indices, eps):  # noqa: ANN001,ANN202
-        ctx, st = _take("out")
-        if st is not None:
-            reason = "out disabled by self-check" if "out" in _state["disabled"] else \
-                rows_mismatch(st, residual, branch, gate, shift, scale, indices)
-            if reason is None and (weight.shape != (residual.shape[1],) or weight.device != residual.device
-                                   or weight.dtype != torch.bfloat16):
-                reason = "norm weight shape/device/dtype"
-            if reason is None:
-                r = min(_SELFCHECK_ROWS, residual.shape[0])
-
-                def _fused_sub():  # noqa: ANN202
-                    return gate_rms_fused(st.rows(r), residual[:r], gate, weight, shift, scale, indices[:r], eps)
-
-                def _stock_sub():  # noqa: ANN202
-                    p = st.rows(r).materialize()
-                    return orig(residual[:r], gate, p, weight, shift, scale, indices[:r], eps)
-
-                if not _selfcheck(("out", tuple(residual.shape[1:]), gate.dtype, weight.dtype), _fused_sub,
-                                  _stock_sub):
-                    reason = "out disabled by self-check"
-            if reason is None:
-                del ctx.pending["out"]
-                res = gate_rms_fused(st, residual, gate, weight, shift, scale, indices, eps)
-                _stats["fused_out"] += 1
-                return res
-            _materialize_all(ctx, "out: " + reason)
-        return orig(residual, gate, branch, weight, shift, scale, indices, eps)
+        call = (residual, gate, branch, weight, shift, scale, indices, eps)
+        out = _consume(site, call)
+        return orig(*call) if out is _STOCK else out
 
     indexed_gate_rms_norm_scale_shift._h3b_consumer_fuse = True
     return indexed_gate_rms_norm_scale_shift
 
 
 def make_gate_wrapper(orig):  # noqa: ANN001,ANN201
-    """Wrap ``indexed_gate`` (:720): on the fc2 stash's placeholder, the fc2 GEMM with the indexed-gate epilogue."""
+    """``indexed_gate`` with the fc2 consumer (h3_tp2/fp8_consumers.py:720)."""
+    site = _IndexedGate(orig)
+
     def indexed_gate(x, gate, other, indices):  # noqa: ANN001,ANN202
-        ctx, st = _take("fc2")
-        if st is not None:
-            reason = "fc2 disabled by self-check" if "fc2" in _state["disabled"] else \
-                rows_mismatch(st, x, other, gate, indices)
-            if reason is None:
-                r = min(_SELFCHECK_ROWS, x.shape[0])
-
-                def _fused_sub():  # noqa: ANN202
-                    return (gate_fused(st.rows(r), x[:r].contiguous(), gate, indices[:r], reuse_placeholder=False),)
-
-                def _stock_sub():  # noqa: ANN202
-                    p = st.rows(r).materialize()
-                    return (orig(x[:r].contiguous(), gate, p, indices[:r]),)
-
-                if not _selfcheck(("fc2", tuple(x.shape[1:]), gate.dtype), _fused_sub, _stock_sub):
-                    reason = "fc2 disabled by self-check"
-            if reason is None:
-                del ctx.pending["fc2"]
-                out = gate_fused(st, x, gate, indices)
-                _stats["fused_fc2"] += 1
-                return out
-            _materialize_all(ctx, "fc2: " + reason)
-        return orig(x, gate, other, indices)
+        out = _consume(site, (x, gate, other, indices))
+        return orig(x, gate, other, indices) if out is _STOCK else out
 
     indexed_gate._h3b_consumer_fuse = True
     return indexed_gate
 
 
-def _lora_types():  # noqa: ANN202
-    try:
-        from vllm.lora.layers import BaseLayerWithLoRA  # noqa: PLC0415
-        return (BaseLayerWithLoRA,)
-    except ImportError:
-        return ()
+_lora_types = _fw.lora_types
+_SITE_LAYER = {"qkv": ("attn", "qkv_proj"), "out": ("attn", "out_proj"), "fc2": ("mlp", "fc2")}
+
+
+def _weight_key(site: str, layer, lora) -> tuple[tuple | None, str | None]:  # noqa: ANN001
+    """((weight pointer, weight shape), None) for a layer whose GEMM the stash hook can take, else (None, reason)."""
+    if layer is None or (lora and isinstance(layer, lora)):
+        return None, f"{site}: missing or LoRA-wrapped layer"
+    if getattr(layer, "tp_size", 1) != 1:
+        return None, f"{site}: tp_size != 1 (an all-reduce would read the placeholder)"
+    w = getattr(layer, "weight", None)
+    n = int(getattr(layer, "output_size_per_partition", 0) or 0)
+    if not (isinstance(w, torch.Tensor) and w.dtype == torch.float8_e4m3fn and w.dim() == 2 and w.shape[1] == n):
+        return None, f"{site}: weight is not an unpadded FP8 [K, N] tensor"
+    return (w.data_ptr(), tuple(w.shape)), None
 
 
 def block_plan(block, rope_table, sites, lora_types=()) -> tuple[dict | None, str]:  # noqa: ANN001
-    """{(weight data_ptr, weight shape): site} for this block's eligible GEMMs, or (None, reason) (:758)."""
+    """{(weight data_ptr, weight shape): site} for this block's eligible GEMMs, or (None, reason)
+    (h3_tp2/fp8_consumers.py:758)."""
     if rope_table is None:
         return None, "no rope table (q/k norm without fused rope)"
-    compiling = getattr(getattr(torch, "compiler", None), "is_compiling", None)
-    if compiling is not None and compiling():
+    if _fw.compiling():
         return None, "torch.compile tracing"
-    attn, mlp = getattr(block, "attn", None), getattr(block, "mlp", None)
-    layers = {"qkv": getattr(attn, "qkv_proj", None), "out": getattr(attn, "out_proj", None),
-              "fc2": getattr(mlp, "fc2", None)}
     want: dict = {}
-    for site in sites:
-        if site in _state["disabled"]:
-            continue
-        layer = layers[site]
-        if layer is None or (lora_types and isinstance(layer, lora_types)):
-            return None, f"{site}: missing or LoRA-wrapped layer"
-        if getattr(layer, "tp_size", 1) != 1:
-            return None, f"{site}: tp_size != 1 (an all-reduce would read the placeholder)"
-        w = getattr(layer, "weight", None)
-        n = int(getattr(layer, "output_size_per_partition", 0) or 0)
-        if not isinstance(w, torch.Tensor) or w.dtype != torch.float8_e4m3fn or w.dim() != 2 or w.shape[1] != n:
-            return None, f"{site}: weight is not an unpadded FP8 [K, N] tensor"
-        want[(w.data_ptr(), tuple(w.shape))] = site
+    for site in (s for s in sites if s not in _state["disabled"]):
+        owner, attr = _SITE_LAYER[site]
+        key, why = _weight_key(site, getattr(getattr(block, owner, None), attr, None), lora_types)
+        if key is None:
+            return None, why
+        want[key] = site
     return (want or None), "no site left"
 
 
-def make_block_forward(orig_forward, sites, lora_types=()):  # noqa: ANN001,ANN201
-    """Wrap the DiT block's forward (:787): plan the sites, run the block with the context set, materialise a stash
-    left at its end."""
-    @functools.wraps(orig_forward)
-    def forward(self, *args, **kwargs):  # noqa: ANN001,ANN202
-        want, reason = block_plan(self, kwargs.get("rope_table"), sites, lora_types)
-        if want is None:
-            _warn_once("plan-" + reason, "block not fused (%s); stock path", reason)
-            return orig_forward(self, *args, **kwargs)
-        prev = getattr(_tls, "ctx", None)
-        ctx = _Ctx(want)
-        _tls.ctx = ctx
-        ok = False
-        try:
-            out = orig_forward(self, *args, **kwargs)
-            ok = True
-            return out
-        finally:
-            _tls.ctx = prev
-            if ctx.pending:
-                if ok:   # make the placeholder real for whoever holds it
-                    _materialize_all(ctx, "stash left at the end of the block")
-                ctx.pending.clear()
+def _unplanned(reason: str) -> None:
+    key = "plan-" + reason
+    if key not in _warned:
+        _warned.add(key)
+        logger.warning("h3b fp8 consumer fuse: block not fused (%s); stock path", reason)
 
-    forward._h3b_consumer_fuse = True
-    return forward
+
+def make_block_forward(orig_forward, sites, lora_types=()):  # noqa: ANN001,ANN201
+    """The DiT block's forward, run in a scope with this block's planned weights (h3_tp2/fp8_consumers.py:787)."""
+    return _fw.wrap_block_forward(
+        orig_forward, _scopes, lambda blk, *a, **kw: block_plan(blk, kw.get("rope_table"), sites, lora_types),
+        _unplanned, "_h3b_consumer_fuse")
 
 
 def install(sites: tuple[str, ...] = SITES, tr=None, *, check_source: bool = True, lora_types=None,  # noqa: ANN001
@@ -529,12 +558,12 @@ def install(sites: tuple[str, ...] = SITES, tr=None, *, check_source: bool = Tru
         sites = tuple(keep)
     if not sites:
         return []
-    if "qkv" in sites:
-        tr.fused_qk_norm_rope = make_qk_wrapper(tr.fused_qk_norm_rope)
-    if "out" in sites:
-        tr.indexed_gate_rms_norm_scale_shift = make_gate_rms_wrapper(tr.indexed_gate_rms_norm_scale_shift)
-    if "fc2" in sites:
-        tr.indexed_gate = make_gate_wrapper(tr.indexed_gate)
+    # each site's consumer in the transformer module
+    for site, name, wrap in (("qkv", "fused_qk_norm_rope", make_qk_wrapper),
+                             ("out", "indexed_gate_rms_norm_scale_shift", make_gate_rms_wrapper),
+                             ("fc2", "indexed_gate", make_gate_wrapper)):
+        if site in sites:
+            setattr(tr, name, wrap(getattr(tr, name)))
     block_cls.forward = make_block_forward(block_cls.forward, sites, _lora_types() if lora_types is None else lora_types)
     fp8_gemm.set_stash_hook(stash_hook)
     _state["sites"] = sites

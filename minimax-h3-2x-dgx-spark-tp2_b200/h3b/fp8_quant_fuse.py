@@ -16,13 +16,12 @@ site for the process).
 """
 from __future__ import annotations
 
-import functools
 import logging
-import threading
 from typing import Any, Callable
 
 import torch
 
+from . import _fusewire as _fw
 from . import ops
 
 logger = logging.getLogger("h3b.fp8_quant_fuse")
@@ -104,11 +103,9 @@ def is_explicit(value: str | None) -> bool:
 
 
 # --------------------------------------------------------------------------------------------------------------------
-# the stash, the block context, the quant hook (h3_tp2/fp8_quant_fuse.py:404-860)
+# the wiring (the reference's protocol, h3_tp2/fp8_quant_fuse.py:404-921, on the shared machinery of h3b._fusewire)
 # --------------------------------------------------------------------------------------------------------------------
 
-_SELFCHECK_ROWS = 64
-_tls = threading.local()   # ctx: the _Ctx of the DiT block whose forward is running in this thread
 _state: dict[str, Any] = {"sites": (), "checked": {}, "disabled": set(), "orig_quant": None, "quant_cls": None,
                           "act_cls": None, "verify": False, "modes": (0, 1), "device_types": ("cuda",)}
 _stats: dict[str, int] = {k: 0 for k in ("fused_qkv", "fused_out", "fused_fc1", "fused_fc2", "consumed", "materialize",
@@ -120,74 +117,53 @@ def stats() -> dict[str, int]:
 
 
 class Pending:
-    """A producer's (fp8, scale) waiting for the quant of ``layer`` (h3_tp2/fp8_quant_fuse.py:432): ``ph`` is the bf16
-    placeholder the model holds, ``k`` the GEMM input width (the quant sees ``ph`` as a contiguous [numel / k, k]
-    view), ``fill(ph)`` runs the stock producer into the placeholder."""
+    """A producer's quantised output (fp8 ``q``, ``scale``) handed to the quant call of ``layer``.  The model holds
+    ``ph``, an uninitialised bf16 placeholder of the stock producer's output; the linear layer reshapes it to
+    [numel / k, k] (k: the GEMM input width) before its quant, so the claim compares that exact view, made once here.
+    ``fill(ph)`` writes the stock producer's output into the placeholder when the handoff has to become real."""
 
-    __slots__ = ("site", "ph", "k", "q", "scale", "quant", "layer", "fill")
+    __slots__ = ("site", "ph", "k", "q", "scale", "quant", "layer", "fill", "_view")
 
     def __init__(self, site: str, ph: torch.Tensor, k: int, q: torch.Tensor, scale: torch.Tensor, quant, layer,  # noqa: ANN001
                  fill: Callable[[torch.Tensor], None]):
         self.site, self.ph, self.k, self.q, self.scale = site, ph, k, q, scale
         self.quant, self.layer, self.fill = quant, layer, fill
+        # the quant input that is this placeholder: (data pointer, shape, strides, dtype, device), or None when the
+        # placeholder is not dense (then nothing can claim it)
+        self._view = (ph.data_ptr(), (ph.numel() // k, k), (k, 1), ph.dtype, ph.device) if ph.is_contiguous() else None
 
     def matches(self, quant_obj, x: torch.Tensor) -> bool:  # noqa: ANN001
-        ph, k = self.ph, self.k
-        return (quant_obj is self.quant and x.dim() == 2 and x.dtype == ph.dtype and x.device == ph.device
-                and x.data_ptr() == ph.data_ptr() and tuple(x.shape) == (ph.numel() // k, k)
-                and x.stride() == (k, 1) and ph.is_contiguous())
+        """True when ``quant_obj(x)`` is the planned quant of this placeholder."""
+        return (self._view is not None and quant_obj is self.quant and x.dim() == 2
+                and (x.data_ptr(), tuple(x.shape), x.stride(), x.dtype, x.device) == self._view)
 
     def materialize(self) -> torch.Tensor:
         self.fill(self.ph)
         return self.ph
 
 
-class _Ctx:
-    __slots__ = ("block", "plan", "pending")
-
-    def __init__(self, block, plan: dict):  # noqa: ANN001
-        self.block, self.plan, self.pending = block, plan, None   # plan: site -> (layer, its quant instance)
+def _realized(handoff: Pending) -> None:
+    handoff.materialize()
+    _stats["materialize"] += 1
 
 
-def _materialize(ctx: _Ctx) -> None:
-    p, ctx.pending = ctx.pending, None
-    if p is not None:
-        p.materialize()
-        _stats["materialize"] += 1
+_scopes = _fw.ScopeRegistry(_realized, lambda site, why: None)
+_tls = _scopes.local      # ``_tls.ctx``: the running block's scope (plan: site -> (layer, its quant instance))
+_verdicts = _fw.Verdicts(lambda: _state, lambda: _stats, logger, "fp8 quant fuse")
 
 
-def _bits(t: torch.Tensor) -> torch.Tensor:
-    t = t.contiguous()
-    return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
+def scope(block, plan: dict) -> _fw.BlockScope:  # noqa: ANN001
+    """The context in which a planned block's forward runs (``with scope(block, plan): ...``)."""
+    return _fw.BlockScope(_scopes, block, plan)
 
 
-def _selfcheck(key, fused_fn, stock_fn, *, last: bool = True) -> bool:  # noqa: ANN001
-    """Once per key: the fused outputs against the stock ones on the first rows, bit for bit; a failure of the ``last``
-    candidate disables the site (key[0]) for the process."""
-    ok = _state["checked"].get(key)
-    if ok is not None:
-        return ok
-    try:
-        fused, stock = fused_fn(), stock_fn()
-        ok = len(fused) == len(stock) and all(f.shape == t.shape and f.dtype == t.dtype and torch.equal(_bits(f), _bits(t))
-                                              for f, t in zip(fused, stock))
-    except Exception:  # noqa: BLE001  (a failing fused kernel counts as a mismatch)
-        ok = False
-    _state["checked"][key] = ok
-    _stats["selfcheck_pass" if ok else "selfcheck_fail"] += 1
-    if not ok and last:
-        _state["disabled"].add(key[0])
-    return ok
+def _outstanding(sc: _fw.BlockScope | None) -> Pending | None:
+    return None if sc is None or not sc.handoffs else next(iter(sc.handoffs.values()))
 
 
-def _pick_mode(key, fused_for, stock_fn):  # noqa: ANN001,ANN202
-    """The RMS sites: mode 0 (the bf16 row only in registers) if it passes, else mode 1 (the bf16 row stored too);
-    None when neither is bit-identical.  ``stock_fn()`` returns the stock outputs with the bf16 row last."""
-    modes = _state["modes"]
-    for m in modes:
-        if _selfcheck(key + (m,), lambda: fused_for(m), lambda: stock_fn()[:None if m else -1], last=m == modes[-1]):
-            return m
-    return None
+def _realize_outstanding(sc: _fw.BlockScope) -> None:
+    if sc.handoffs:
+        _scopes.realize_all(sc, "")
 
 
 def _stock_quant(quant_obj, h: torch.Tensor):  # noqa: ANN001,ANN202
@@ -196,42 +172,43 @@ def _stock_quant(quant_obj, h: torch.Tensor):  # noqa: ANN001,ANN202
 
 
 def _verify(p: Pending) -> None:
-    """``H3_TP2_FP8_QUANT_FUSE_VERIFY=1``: the stock pair on the whole tensor against the stash (counted)."""
-    h = p.materialize()
-    q_ref, s_ref = _stock_quant(p.quant, h.view(-1, p.k))
+    """``H3_TP2_FP8_QUANT_FUSE_VERIFY=1``: every handoff is also made real and quantised by the stock quant; the two
+    (fp8, scale) pairs must agree bit for bit (mismatches are counted)."""
+    q_ref, s_ref = _stock_quant(p.quant, p.materialize().view(-1, p.k))
     _stats["verify_calls"] += 1
-    if not (torch.equal(_bits(p.q), _bits(q_ref)) and torch.equal(_bits(p.scale), _bits(s_ref))):
+    if not _fw.same_bits((p.q, p.scale), (q_ref, s_ref)):
         _stats["verify_mismatch"] += 1
 
 
 def pending_placeholder(x: torch.Tensor) -> bool:
-    """True when ``x`` is this thread's pending stash placeholder (h3_tp2/fp8_quant_fuse.py:545)."""
-    ctx = getattr(_tls, "ctx", None)
-    p = ctx.pending if ctx is not None else None
+    """True when ``x`` is the placeholder of this thread's outstanding handoff (h3_tp2/fp8_quant_fuse.py:545)."""
+    p = _outstanding(_scopes.current())
     return p is not None and x.data_ptr() == p.ph.data_ptr()
 
 
 def make_quant_forward(orig):  # noqa: ANN001,ANN201
-    """Wrap ``QuantFP8.forward`` (h3_tp2/fp8_quant_fuse.py:553): the pending stash's (fp8, scale) for exactly its planned
-    instance and placeholder; every other call goes to ``orig`` untouched (after materialising a pending stash)."""
+    """``QuantFP8.forward`` (h3_tp2/fp8_quant_fuse.py:553).  A dynamic call (no static scale, no upper bound) on exactly
+    the outstanding handoff's placeholder, by exactly its planned quant instance, returns the handoff's (fp8, scale).
+    Any other call first makes an outstanding handoff real, then runs the stock quant with its arguments untouched.
+    A deferred-unpack placeholder of ``ulysses_outq`` must never get here (it holds no data): that raises."""
     def forward(self, x, *args, **kwargs):  # noqa: ANN001,ANN202
-        if isinstance(x, torch.Tensor):
+        is_tensor = isinstance(x, torch.Tensor)
+        if is_tensor:
             from . import ulysses_outq  # noqa: PLC0415
             if ulysses_outq.is_placeholder(x):
                 raise RuntimeError("h3b fp8 quant fuse: a deferred-unpack placeholder reached a quant outside the "
                                    "out-projection's")
-        ctx = getattr(_tls, "ctx", None)
-        p = ctx.pending if ctx is not None else None
+        sc = _scopes.current()
+        p = _outstanding(sc)
         if p is not None:
-            scale = args[0] if args else kwargs.get("scale")
-            scale_ub = args[1] if len(args) > 1 else kwargs.get("scale_ub")
-            if scale is None and scale_ub is None and isinstance(x, torch.Tensor) and p.matches(self, x):
-                ctx.pending = None
+            static = (args[0] if args else kwargs.get("scale"), args[1] if len(args) > 1 else kwargs.get("scale_ub"))
+            if static == (None, None) and is_tensor and p.matches(self, x):
+                sc.handoffs.pop(p.site)
                 if _state["verify"]:
                     _verify(p)
                 _stats["consumed"] += 1
                 return p.q, p.scale
-            _materialize(ctx)
+            _realize_outstanding(sc)
         return orig(self, x, *args, **kwargs)
 
     forward._h3b_quant_fuse = True
@@ -240,57 +217,69 @@ def make_quant_forward(orig):  # noqa: ANN001,ANN201
 
 
 def _layer_post_hook(module, args, output):  # noqa: ANN001,ANN202
-    """A planned layer that returned without its quant consuming the stash ran on the placeholder: materialise it and
-    run the layer again (h3_tp2/fp8_quant_fuse.py:575)."""
-    ctx = getattr(_tls, "ctx", None)
-    p = ctx.pending if ctx is not None else None
+    """After a planned layer's forward: if its handoff is still outstanding the layer ran on the uninitialised
+    placeholder, so the placeholder is made real and the layer runs again (h3_tp2/fp8_quant_fuse.py:575)."""
+    sc = _scopes.current()
+    p = _outstanding(sc)
     if p is None or p.layer is not module:
         return None
-    _materialize(ctx)
+    _realize_outstanding(sc)
     _stats["rerun"] += 1
     return module.forward(*args)
 
 
+# where each site's linear layer sits in a DiT block
+_SITE_LAYER = {"qkv": ("attn", "qkv_proj"), "out": ("attn", "out_proj"), "fc1": ("mlp", "fc1"), "fc2": ("mlp", "fc2")}
+
+
 def _quant_of(layer):  # noqa: ANN001,ANN202
-    """The layer's dynamic per-token quant instance (``quant_method.fp8_linear.quant_fp8``), or None."""
-    q = getattr(getattr(getattr(layer, "quant_method", None), "fp8_linear", None), "quant_fp8", None)
+    """The layer's quant instance if it is a dynamic per-token FP8 quant without static or group scales (what the fused
+    kernels compute), else None."""
+    qobj = getattr(getattr(getattr(layer, "quant_method", None), "fp8_linear", None), "quant_fp8", None)
     cls = _state["quant_cls"]
-    if cls is None or not isinstance(q, cls):
+    if cls is None or not isinstance(qobj, cls):
         return None
-    if getattr(q, "static", True) or not getattr(q, "use_per_token_if_dynamic", False) \
-            or getattr(q, "is_group_quant", True) or getattr(q, "num_token_padding", 0) is not None:
-        return None
-    if getattr(layer, "input_scale", None) is not None or getattr(layer, "input_scale_ub", None) is not None:
-        return None
-    return q
+    dynamic_per_token = (not getattr(qobj, "static", True) and getattr(qobj, "use_per_token_if_dynamic", False)
+                         and not getattr(qobj, "is_group_quant", True)
+                         and getattr(qobj, "num_token_padding", 0) is None)
+    scaled_input = getattr(layer, "input_scale", None) is not None or getattr(layer, "input_scale_ub", None) is not None
+    return qobj if dynamic_per_token and not scaled_input else None
+
+
+def _blocker(site: str, layer, lora) -> str | None:  # noqa: ANN001
+    """Why ``layer`` stops the whole block from being fused at ``site`` (None: it does not)."""
+    if layer is None or (lora and isinstance(layer, lora)):
+        return f"{site}: missing or LoRA-wrapped layer"
+    if getattr(layer, "tp_size", 1) != 1:
+        return f"{site}: tp_size != 1"
+    if _quant_of(layer) is None:
+        return f"{site}: not a dynamic per-token FP8 linear"
+    return None
+
+
+def _passed_over(site: str, block) -> bool:  # noqa: ANN001
+    """Sites left to the stock path in a block that is otherwise fused: qkv when a VSA gate reads the qkv input a
+    second time, fc2 when the MLP's activation is not the SiLU-and-mul this wiring wraps."""
+    if site == "qkv":
+        return getattr(getattr(block, "attn", None), "to_gate_compress", None) is not None
+    if site == "fc2":
+        act = _state["act_cls"]
+        return act is not None and not isinstance(getattr(getattr(block, "mlp", None), "act_fn", None), act)
+    return False
 
 
 def block_plan(block, sites, lora_types=()) -> tuple[dict | None, str]:  # noqa: ANN001
     """{site: (layer, quant instance)} for this block, or (None, reason) (h3_tp2/fp8_quant_fuse.py:614)."""
-    compiling = getattr(getattr(torch, "compiler", None), "is_compiling", None)
-    if compiling is not None and compiling():
+    if _fw.compiling():
         return None, "torch.compile tracing"
-    attn, mlp = getattr(block, "attn", None), getattr(block, "mlp", None)
-    layers = {"qkv": getattr(attn, "qkv_proj", None), "out": getattr(attn, "out_proj", None),
-              "fc1": getattr(mlp, "fc1", None), "fc2": getattr(mlp, "fc2", None)}
-    plan: dict = {}
-    for site in sites:
-        if site in _state["disabled"]:
-            continue
-        layer = layers[site]
-        if layer is None or (lora_types and isinstance(layer, lora_types)):
-            return None, f"{site}: missing or LoRA-wrapped layer"
-        if getattr(layer, "tp_size", 1) != 1:
-            return None, f"{site}: tp_size != 1"
-        q = _quant_of(layer)
-        if q is None:
-            return None, f"{site}: not a dynamic per-token FP8 linear"
-        if site == "qkv" and getattr(attn, "to_gate_compress", None) is not None:
-            continue                      # a VSA gate reads the qkv input a second time
-        if site == "fc2" and _state["act_cls"] is not None and not isinstance(getattr(mlp, "act_fn", None),
-                                                                              _state["act_cls"]):
-            continue
-        plan[site] = (layer, q)
+    live = [s for s in sites if s not in _state["disabled"]]
+    layers = {s: getattr(getattr(block, _SITE_LAYER[s][0], None), _SITE_LAYER[s][1], None) for s in live}
+    for site in live:
+        why = _blocker(site, layers[site], lora_types)
+        if why is not None:
+            return None, why
+    plan = {s: (layers[s], _quant_of(layers[s])) for s in live if not _passed_over(s, block)}
+    for layer, _ in plan.values():
         if not getattr(layer, "_h3b_quant_fuse_hook", False) and hasattr(layer, "register_forward_hook"):
             layer.register_forward_hook(_layer_post_hook)
             layer._h3b_quant_fuse_hook = True
@@ -298,45 +287,12 @@ def block_plan(block, sites, lora_types=()) -> tuple[dict | None, str]:  # noqa:
 
 
 def make_block_forward(orig_forward, sites, lora_types=()):  # noqa: ANN001,ANN201
-    """Wrap the DiT block's forward: plan the sites, run the block with the context set, materialise a stash left at
-    its end (h3_tp2/fp8_quant_fuse.py:646)."""
-    @functools.wraps(orig_forward)
-    def forward(self, *args, **kwargs):  # noqa: ANN001,ANN202
-        plan, _ = block_plan(self, sites, lora_types)
-        if plan is None:
-            return orig_forward(self, *args, **kwargs)
-        prev = getattr(_tls, "ctx", None)
-        ctx = _Ctx(self, plan)
-        _tls.ctx = ctx
-        ok = False
-        try:
-            out = orig_forward(self, *args, **kwargs)
-            ok = True
-            return out
-        finally:
-            _tls.ctx = prev
-            if ctx.pending is not None:
-                if ok:
-                    _materialize(ctx)
-                ctx.pending = None
-
-    forward._h3b_quant_fuse = True
-    return forward
+    """The DiT block's forward, run in a scope with this block's plan (h3_tp2/fp8_quant_fuse.py:646)."""
+    return _fw.wrap_block_forward(orig_forward, _scopes, lambda blk, *a, **kw: block_plan(blk, sites, lora_types),
+                                  lambda why: None, "_h3b_quant_fuse")
 
 
-def _take_site(site: str):  # noqa: ANN202
-    """The running block's context when ``site`` is planned there (a stash pending in front of it is materialised)."""
-    ctx = getattr(_tls, "ctx", None)
-    if ctx is None or site not in ctx.plan or site in _state["disabled"]:
-        return None
-    if ctx.pending is not None:
-        _materialize(ctx)
-    return ctx
-
-
-def _device_ok(*ts: torch.Tensor) -> bool:
-    dev = ts[0].device
-    return all(t.device == dev for t in ts) and dev.type in _state["device_types"]
+# ---- the four producer sites ---------------------------------------------------------------------------------------
 
 
 def _rows_ok(x: torch.Tensor, k: int, *others: torch.Tensor) -> bool:
@@ -350,140 +306,253 @@ def _k_of(layer) -> int:  # noqa: ANN001
     return int(w.shape[0]) if isinstance(w, torch.Tensor) and w.dim() == 2 else -1
 
 
+class _Site:
+    """One producer site.  ``call`` is the wrapped function's argument tuple.  ``keep_row``: the fused kernel also
+    stores the bf16 row (the RMS sites try without first; the other sites always produce it by other means)."""
+    name = ""
+    keep_row_modes: tuple | None = None      # None: one form only
+
+    def accepts(self, sc, layer, call) -> bool:  # noqa: ANN001
+        raise NotImplementedError
+
+    def rows(self, call) -> int:  # noqa: ANN001
+        raise NotImplementedError
+
+    def key(self, call) -> tuple:  # noqa: ANN001
+        raise NotImplementedError
+
+    def fused(self, call, r: int, keep_row) -> tuple:  # noqa: ANN001
+        raise NotImplementedError
+
+    def stock(self, call, r: int, keep_row, qobj) -> tuple:  # noqa: ANN001
+        raise NotImplementedError
+
+    def produce(self, call, keep_row, qobj, layer) -> tuple:  # noqa: ANN001
+        """(what the wrapped call returns, its Pending)."""
+        raise NotImplementedError
+
+
+def _serve(site: _Site, call: tuple):  # noqa: ANN202
+    """The wrapped producer's result when ``site`` is planned in the running block, accepts the call and passes (or has
+    passed) its first-call comparison; None sends the caller to the stock producer."""
+    sc = _scopes.current()
+    planned = None if sc is None else sc.plan.get(site.name)
+    if planned is None or _verdicts.off(site.name):
+        return None
+    _realize_outstanding(sc)           # a handoff nobody claimed before the next producer ran
+    layer, qobj = planned
+    if not site.accepts(sc, layer, call):
+        return None
+    r = min(_fw.CHECK_ROWS, site.rows(call))
+    if site.keep_row_modes is None:
+        if not _verdicts.judge(site.key(call), lambda: site.fused(call, r, None),
+                               lambda: site.stock(call, r, None, qobj)):
+            return None
+        mode = None
+    else:
+        mode = _verdicts.first_passing(site.key(call), _state["modes"], lambda m: site.fused(call, r, m),
+                                       lambda m: site.stock(call, r, m, qobj))
+        if mode is None:
+            return None
+    result, handoff = site.produce(call, mode, qobj, layer)
+    sc.handoffs[site.name] = handoff
+    _stats["fused_" + site.name] += 1
+    return result
+
+
+class _NormSite(_Site):
+    """qkv: ``rms_norm_indexed_scale_shift(x, weight, shift, scale, indices, eps)`` of norm1 (the qkv GEMM's input)."""
+    name, keep_row_modes = "qkv", (0, 1)
+
+    def __init__(self, orig):  # noqa: ANN001
+        self.orig = orig
+
+    def accepts(self, sc, layer, call) -> bool:  # noqa: ANN001
+        x, weight, shift, scale, indices, _ = call
+        return (weight is getattr(getattr(sc.block, "norm1", None), "weight", None)
+                and _rows_ok(x, _k_of(layer), shift, scale) and indices.dim() == 1 and indices.shape[0] == x.shape[0]
+                and _fw.same_device(_state["device_types"], x, weight, shift, scale, indices))
+
+    def rows(self, call) -> int:  # noqa: ANN001
+        return call[0].shape[0]
+
+    def key(self, call) -> tuple:  # noqa: ANN001
+        return ("qkv", call[0].shape[1], call[2].dtype, call[1].dtype)
+
+    def fused(self, call, r, keep_row) -> tuple:  # noqa: ANN001
+        x, weight, shift, scale, indices, eps = call
+        row = torch.empty_like(x[:r]) if keep_row else None
+        q, s = rms_quant(x[:r], weight, shift, scale, indices[:r], eps, self.orig, row)
+        return (q, s, row) if keep_row else (q, s)
+
+    def stock(self, call, r, keep_row, qobj) -> tuple:  # noqa: ANN001
+        x, weight, shift, scale, indices, eps = call
+        h = self.orig(x[:r], weight, shift, scale, indices[:r], eps)
+        return (*_stock_quant(qobj, h), h) if keep_row else _stock_quant(qobj, h)
+
+    def produce(self, call, keep_row, qobj, layer) -> tuple:  # noqa: ANN001
+        x = call[0]
+        ph = torch.empty_like(x)
+        q, s = rms_quant(*call, self.orig, ph if keep_row else None)
+        fill = (lambda t: None) if keep_row else (lambda t, c=call: t.copy_(self.orig(*c)))
+        return ph, Pending("qkv", ph, x.shape[1], q, s, qobj, layer, fill)
+
+
+class _GateNormSite(_Site):
+    """fc1: ``indexed_gate_rms_norm_scale_shift(residual, gate, branch, weight, shift, scale, indices, eps)`` of norm2,
+    whose modulated output feeds fc1 (the residual output is returned as stock's)."""
+    name, keep_row_modes = "fc1", (0, 1)
+
+    def __init__(self, orig):  # noqa: ANN001
+        self.orig = orig
+
+    def accepts(self, sc, layer, call) -> bool:  # noqa: ANN001
+        residual, gate, branch, weight, shift, scale, indices, _ = call
+        return (weight is getattr(getattr(sc.block, "norm2", None), "weight", None)
+                and _rows_ok(residual, _k_of(layer), gate, branch, shift, scale)
+                and branch.shape == residual.shape and branch.dtype == residual.dtype
+                and indices.dim() == 1 and indices.shape[0] == residual.shape[0]
+                and _fw.same_device(_state["device_types"], residual, gate, branch, weight, shift, scale, indices))
+
+    def rows(self, call) -> int:  # noqa: ANN001
+        return call[0].shape[0]
+
+    def key(self, call) -> tuple:  # noqa: ANN001
+        return ("fc1", call[0].shape[1], call[1].dtype, call[3].dtype)
+
+    def _first(self, call, r) -> tuple:  # noqa: ANN001
+        residual, gate, branch, weight, shift, scale, indices, eps = call
+        return residual[:r], gate, branch[:r], weight, shift, scale, indices[:r], eps
+
+    def fused(self, call, r, keep_row) -> tuple:  # noqa: ANN001
+        sub = self._first(call, r)
+        row = torch.empty_like(sub[0]) if keep_row else None
+        return tuple(gate_rms_quant(*sub, self.orig, row)) + ((row,) if keep_row else ())
+
+    def stock(self, call, r, keep_row, qobj) -> tuple:  # noqa: ANN001
+        res, mod = self.orig(*self._first(call, r))
+        return (res, *_stock_quant(qobj, mod)) + ((mod,) if keep_row else ())
+
+    def produce(self, call, keep_row, qobj, layer) -> tuple:  # noqa: ANN001
+        residual = call[0]
+        ph = torch.empty_like(residual)
+        res, q, s = gate_rms_quant(*call, self.orig, ph if keep_row else None)
+        fill = (lambda t: None) if keep_row else (lambda t, c=call: t.copy_(self.orig(*c)[1]))
+        return (res, ph), Pending("fc1", ph, residual.shape[1], q, s, qobj, layer, fill)
+
+
+class _UnpackSite(_Site):
+    """out: the reverse unpack of ``ulysses_exact.exchange_back`` (receive [P, M, hl, d] -> [1, M, H, d]): the quant
+    reads the receive buffer, the model gets a placeholder of the unpacked shape."""
+    name = "out"
+
+    def accepts(self, sc, layer, call) -> bool:  # noqa: ANN001
+        recv, heads = call
+        ws, m, hl, d = recv.shape
+        return (recv.dtype == torch.bfloat16 and recv.is_contiguous() and m > 0 and ws * hl == heads
+                and ws & (ws - 1) == 0 and heads * d == _k_of(layer) and _fw.same_device(_state["device_types"], recv))
+
+    def rows(self, call) -> int:  # noqa: ANN001
+        return call[0].shape[1]
+
+    def key(self, call) -> tuple:  # noqa: ANN001
+        ws, _, hl, d = call[0].shape
+        return ("out", ws, hl * d)
+
+    def fused(self, call, r, keep_row) -> tuple:  # noqa: ANN001
+        return unpack_quant(call[0][:, :r].contiguous())
+
+    def stock(self, call, r, keep_row, qobj) -> tuple:  # noqa: ANN001
+        recv, heads = call
+        return _stock_quant(qobj, unpack_stock(recv[:, :r], heads)[0].reshape(r, heads * recv.shape[3]))
+
+    def produce(self, call, keep_row, qobj, layer) -> tuple:  # noqa: ANN001
+        recv, heads = call
+        ws, m, hl, d = recv.shape
+        q, s = unpack_quant(recv)
+        ph = torch.empty((1, m, heads, d), dtype=recv.dtype, device=recv.device)
+        return ph, Pending("out", ph, heads * d, q, s, qobj, layer,
+                           lambda t: t[0].view(m, ws, hl, d).copy_(recv.transpose(0, 1)))
+
+
+class _ActSite(_Site):
+    """fc2: ``SiluAndMul.forward(self, x)`` of the MLP's activation on fc1's bf16 output."""
+    name = "fc2"
+
+    def __init__(self, orig):  # noqa: ANN001
+        self.orig = orig
+
+    def accepts(self, sc, layer, call) -> bool:  # noqa: ANN001
+        act, x = call
+        return (act is getattr(getattr(sc.block, "mlp", None), "act_fn", None) and isinstance(x, torch.Tensor)
+                and _rows_ok(x, 2 * _k_of(layer)) and _fw.same_device(_state["device_types"], x))
+
+    def rows(self, call) -> int:  # noqa: ANN001
+        return call[1].shape[0]
+
+    def key(self, call) -> tuple:  # noqa: ANN001
+        return ("fc2", call[1].shape[1])
+
+    def fused(self, call, r, keep_row) -> tuple:  # noqa: ANN001
+        return silu_mul_quant(call[1][:r])
+
+    def stock(self, call, r, keep_row, qobj) -> tuple:  # noqa: ANN001
+        return _stock_quant(qobj, self.orig(call[0], call[1][:r]))
+
+    def produce(self, call, keep_row, qobj, layer) -> tuple:  # noqa: ANN001
+        act, x = call
+        q, s = silu_mul_quant(x)
+        ph = torch.empty((x.shape[0], x.shape[1] // 2), dtype=x.dtype, device=x.device)
+        return ph, Pending("fc2", ph, x.shape[1] // 2, q, s, qobj, layer, lambda t: t.copy_(self.orig(act, x)))
+
+
 def make_rms_wrapper(orig):  # noqa: ANN001,ANN201
-    """``rms_norm_indexed_scale_shift(x, weight, shift, scale, indices, eps)`` of the block's norm1: the qkv site
-    (h3_tp2/fp8_quant_fuse.py:704)."""
+    """``rms_norm_indexed_scale_shift`` with the qkv site (h3_tp2/fp8_quant_fuse.py:704)."""
+    site = _NormSite(orig)
+
     def rms_norm_indexed_scale_shift(x, weight, shift, scale, indices, eps):  # noqa: ANN001,ANN202
-        ctx = _take_site("qkv")
-        if ctx is not None:
-            layer, qobj = ctx.plan["qkv"]
-            if (weight is getattr(getattr(ctx.block, "norm1", None), "weight", None)
-                    and _rows_ok(x, _k_of(layer), shift, scale) and indices.dim() == 1
-                    and indices.shape[0] == x.shape[0] and _device_ok(x, weight, shift, scale, indices)):
-                r = min(_SELFCHECK_ROWS, x.shape[0])
-
-                def fused_rows(mode):  # noqa: ANN001,ANN202
-                    ph_r = torch.empty_like(x[:r]) if mode else None
-                    q_r, s_r = rms_quant(x[:r], weight, shift, scale, indices[:r], eps, orig, ph_r)
-                    return (q_r, s_r) + ((ph_r,) if mode else ())
-
-                def stock_rows():  # noqa: ANN202
-                    h = orig(x[:r], weight, shift, scale, indices[:r], eps)
-                    return (*_stock_quant(qobj, h), h)
-
-                mode = _pick_mode(("qkv", x.shape[1], shift.dtype, weight.dtype), fused_rows, stock_rows)
-                if mode is not None:
-                    ph = torch.empty_like(x)
-                    q, sc = rms_quant(x, weight, shift, scale, indices, eps, orig, ph if mode else None)
-
-                    def fill(t, _a=(x, weight, shift, scale, indices, eps)):  # noqa: ANN001,ANN202
-                        t.copy_(orig(*_a))
-                    ctx.pending = Pending("qkv", ph, x.shape[1], q, sc, qobj, layer, (lambda t: None) if mode else fill)
-                    _stats["fused_qkv"] += 1
-                    return ph
-        return orig(x, weight, shift, scale, indices, eps)
+        out = _serve(site, (x, weight, shift, scale, indices, eps))
+        return orig(x, weight, shift, scale, indices, eps) if out is None else out
 
     rms_norm_indexed_scale_shift._h3b_quant_fuse = True
     return rms_norm_indexed_scale_shift
 
 
 def make_gate_rms_wrapper(orig):  # noqa: ANN001,ANN201
-    """``indexed_gate_rms_norm_scale_shift(residual, gate, branch, weight, shift, scale, indices, eps)`` of the block's
-    norm2: the fc1 site (its modulated output feeds fc1; h3_tp2/fp8_quant_fuse.py:744)."""
+    """``indexed_gate_rms_norm_scale_shift`` with the fc1 site (h3_tp2/fp8_quant_fuse.py:744)."""
+    site = _GateNormSite(orig)
+
     def indexed_gate_rms_norm_scale_shift(residual, gate, branch, weight, shift, scale, indices, eps):  # noqa: ANN001,ANN202
-        ctx = _take_site("fc1")
-        if ctx is not None:
-            layer, qobj = ctx.plan["fc1"]
-            if (weight is getattr(getattr(ctx.block, "norm2", None), "weight", None)
-                    and _rows_ok(residual, _k_of(layer), gate, branch, shift, scale)
-                    and branch.shape == residual.shape and branch.dtype == residual.dtype
-                    and indices.dim() == 1 and indices.shape[0] == residual.shape[0]
-                    and _device_ok(residual, gate, branch, weight, shift, scale, indices)):
-                r = min(_SELFCHECK_ROWS, residual.shape[0])
-
-                def fused_rows(mode):  # noqa: ANN001,ANN202
-                    ph_r = torch.empty_like(residual[:r]) if mode else None
-                    out = gate_rms_quant(residual[:r], gate, branch[:r], weight, shift, scale, indices[:r], eps, orig,
-                                         ph_r)
-                    return tuple(out) + ((ph_r,) if mode else ())
-
-                def stock_rows():  # noqa: ANN202
-                    res, mod = orig(residual[:r], gate, branch[:r], weight, shift, scale, indices[:r], eps)
-                    return (res, *_stock_quant(qobj, mod), mod)
-
-                mode = _pick_mode(("fc1", residual.shape[1], gate.dtype, weight.dtype), fused_rows, stock_rows)
-                if mode is not None:
-                    ph = torch.empty_like(residual)
-                    res, q, sc = gate_rms_quant(residual, gate, branch, weight, shift, scale, indices, eps, orig,
-                                                ph if mode else None)
-
-                    def fill(t, _a=(residual, gate, branch, weight, shift, scale, indices, eps)):  # noqa: ANN001,ANN202
-                        t.copy_(orig(*_a)[1])
-                    ctx.pending = Pending("fc1", ph, residual.shape[1], q, sc, qobj, layer,
-                                          (lambda t: None) if mode else fill)
-                    _stats["fused_fc1"] += 1
-                    return res, ph
-        return orig(residual, gate, branch, weight, shift, scale, indices, eps)
+        call = (residual, gate, branch, weight, shift, scale, indices, eps)
+        out = _serve(site, call)
+        return orig(*call) if out is None else out
 
     indexed_gate_rms_norm_scale_shift._h3b_quant_fuse = True
     return indexed_gate_rms_norm_scale_shift
 
 
-def unpack_hook(recv: torch.Tensor, heads: int) -> torch.Tensor | None:
-    """The reverse unpack of ``ulysses_exact.exchange_back`` (the out site, h3_tp2/fp8_quant_fuse.py:785): a placeholder
-    [1, M, H, d] with the quant of the unpacked rows stashed, or None for the stock unpack."""
-    ctx = _take_site("out")
-    if ctx is None:
-        return None
-    layer, qobj = ctx.plan["out"]
-    ws, m, hl, d = recv.shape
-    if (recv.dtype != torch.bfloat16 or not recv.is_contiguous() or m == 0 or ws * hl != heads or ws & (ws - 1)
-            or heads * d != _k_of(layer) or not _device_ok(recv)):
-        return None
-    r = min(_SELFCHECK_ROWS, m)
-    if not _selfcheck(("out", ws, hl * d), lambda: unpack_quant(recv[:, :r].contiguous()),
-                      lambda: _stock_quant(qobj, unpack_stock(recv[:, :r], heads)[0].reshape(r, heads * d))):
-        return None
-    q, sc = unpack_quant(recv)
-    ph = torch.empty((1, m, heads, d), dtype=recv.dtype, device=recv.device)
+_UNPACK = _UnpackSite()
 
-    def fill(t, _recv=recv):  # noqa: ANN001,ANN202
-        t[0].view(m, ws, hl, d).copy_(_recv.transpose(0, 1))
-    ctx.pending = Pending("out", ph, heads * d, q, sc, qobj, layer, fill)
-    _stats["fused_out"] += 1
-    return ph
+
+def unpack_hook(recv: torch.Tensor, heads: int) -> torch.Tensor | None:
+    """``ulysses_exact.exchange_back``'s reverse unpack with the out site (h3_tp2/fp8_quant_fuse.py:785): the
+    placeholder [1, M, H, d], or None for the stock unpack."""
+    return _serve(_UNPACK, (recv, heads))
 
 
 def make_act_forward(orig):  # noqa: ANN001,ANN201
-    """``SiluAndMul.forward`` (the MLP's act_fn on fc1's bf16 output): the fc2 site (h3_tp2/fp8_quant_fuse.py:810)."""
-    def forward(self, x):  # noqa: ANN001,ANN202
-        ctx = _take_site("fc2")
-        if ctx is not None and self is getattr(getattr(ctx.block, "mlp", None), "act_fn", None):
-            layer, qobj = ctx.plan["fc2"]
-            if isinstance(x, torch.Tensor) and _rows_ok(x, 2 * _k_of(layer)) and _device_ok(x):
-                r = min(_SELFCHECK_ROWS, x.shape[0])
-                if _selfcheck(("fc2", x.shape[1]), lambda: silu_mul_quant(x[:r]),
-                              lambda: _stock_quant(qobj, orig(self, x[:r]))):
-                    q, sc = silu_mul_quant(x)
-                    ph = torch.empty((x.shape[0], x.shape[1] // 2), dtype=x.dtype, device=x.device)
+    """``SiluAndMul.forward`` with the fc2 site (h3_tp2/fp8_quant_fuse.py:810)."""
+    site = _ActSite(orig)
 
-                    def fill(t, _x=x, _m=self):  # noqa: ANN001,ANN202
-                        t.copy_(orig(_m, _x))
-                    ctx.pending = Pending("fc2", ph, x.shape[1] // 2, q, sc, qobj, layer, fill)
-                    _stats["fused_fc2"] += 1
-                    return ph
-        return orig(self, x)
+    def forward(self, x):  # noqa: ANN001,ANN202
+        out = _serve(site, (self, x))
+        return orig(self, x) if out is None else out
 
     forward._h3b_quant_fuse = True
     return forward
 
 
-def _lora_types() -> tuple:
-    try:
-        from vllm.lora.layers import BaseLayerWithLoRA  # noqa: PLC0415
-        return (BaseLayerWithLoRA,)
-    except ImportError:
-        return ()
+_lora_types = _fw.lora_types
 
 
 def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=None, check_source: bool = True,  # noqa: ANN001
@@ -556,10 +625,12 @@ def install(sites: tuple[str, ...] = SITES, tr=None, *, quant_cls=None, act_cls=
     if not getattr(quant_cls.forward, "_h3b_quant_fuse", False):
         _state["orig_quant"] = quant_cls.forward
         quant_cls.forward = make_quant_forward(quant_cls.forward)
-    if "qkv" in sites:
-        tr.rms_norm_indexed_scale_shift = make_rms_wrapper(tr.rms_norm_indexed_scale_shift)
-    if "fc1" in sites:
-        tr.indexed_gate_rms_norm_scale_shift = make_gate_rms_wrapper(tr.indexed_gate_rms_norm_scale_shift)
+    # the transformer-module producers of the qkv and fc1 sites, the activation class of fc2; the out site is a hook
+    # of the exact exchange's reverse unpack
+    for site, name, wrap in (("qkv", "rms_norm_indexed_scale_shift", make_rms_wrapper),
+                             ("fc1", "indexed_gate_rms_norm_scale_shift", make_gate_rms_wrapper)):
+        if site in sites:
+            setattr(tr, name, wrap(getattr(tr, name)))
     if "fc2" in sites and not getattr(act_cls.forward, "_h3b_quant_fuse", False):
         act_cls.forward = make_act_forward(act_cls.forward)
     if "out" in sites:

@@ -27,28 +27,30 @@ def stats() -> dict[str, int]:
 
 
 def _a2a(out: torch.Tensor, inp: torch.Tensor, group=None) -> None:  # noqa: ANN001
+    """The collective, looked up at call time (the a2a timing wrapper patches ``dist.all_to_all_single``)."""
     dist.all_to_all_single(out, inp, group=group)
 
 
 def send_shape(s_loc: int, heads: int, d: int, ws: int, groups: int) -> tuple[int, ...]:
+    """[G, P, M, 3, hl, d]: per head group and destination rank, each token's q, k and v side by side (:74)."""
     return (groups, ws, s_loc, 3, heads // (groups * ws), d)
 
 
-def _by_dest(x: torch.Tensor, ws: int, groups: int) -> torch.Tensor:
-    """[M, H, d] (any strides) -> view [G, P, M, hl, d]; head h = g*hg + p*hl + j."""
-    m, h, d = x.shape
-    return x.unflatten(1, (groups, ws, h // (groups * ws))).permute(1, 2, 0, 3, 4)
-
-
-def pack_qkv(send: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ws: int, groups: int) -> None:
-    """Fallback producer: q, k, v [M, H, d] -> send [G, P, M, 3, hl, d] in one stack (:84)."""
-    ops._need_cuda(send, q, k, v)
-    torch.stack((_by_dest(q, ws, groups), _by_dest(k, ws, groups), _by_dest(v, ws, groups)), dim=3, out=send)
+def dest_view(x: torch.Tensor, ws: int, groups: int) -> torch.Tensor:
+    """[M, H, d] (any strides) seen as [G, P, M, hl, d]: head h = (g * P + p) * hl + j goes to rank p in group g."""
+    return x.unflatten(1, (groups, ws, x.shape[1] // (groups * ws))).movedim(0, 2)
 
 
 def fill_slot(send: torch.Tensor, x: torch.Tensor, slot: int, ws: int, groups: int) -> None:
+    """Slot ``slot`` (0 q, 1 k, 2 v) of the combined send buffer from x [M, H, d]."""
     ops._need_cuda(send, x)
-    send[:, :, :, slot].copy_(_by_dest(x, ws, groups))
+    send.select(3, slot).copy_(dest_view(x, ws, groups))
+
+
+def pack_qkv(send: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ws: int, groups: int) -> None:
+    """The producer for q, k, v that come from elsewhere: all three slots of send [G, P, M, 3, hl, d] (:84)."""
+    for slot, x in enumerate((q, k, v)):
+        fill_slot(send, x, slot, ws, groups)
 
 
 def _kernel_launch(x_block, weight, rope_table, eps, out) -> None:  # noqa: ANN001
@@ -98,61 +100,80 @@ def local_attention(q, k, v, attn_metadata=None):  # noqa: ANN001,ANN201
     return torch.ops.h3b.flash_attn(q, k, v, None, valid)
 
 
+class _GroupExchange:
+    """The buffers of one combined-exchange forward and its three steps per head group g: ``arrive(g)`` (the forward
+    exchange of send[g]), ``attend(g)`` (the local attention on the strided q/k/v views of recv[g]) and ``depart(g, o)``
+    (the reverse exchange of its output into the result's head columns)."""
+
+    def __init__(self, send: torch.Tensor, result_shape: tuple, run_attn, ws: int, pg, a2a, v_f16: bool):  # noqa: ANN001
+        self.send, self.ws, self.pg, self.a2a, self.v_f16, self.run_attn = send, ws, pg, a2a, v_f16, run_attn
+        groups, _, s_loc, _, hl, d = send.shape
+        self.recv = torch.empty_like(send)
+        self.recv_b = torch.empty((groups, ws, s_loc, hl, d), dtype=send.dtype, device=send.device)
+        self.result = torch.empty(result_shape, dtype=send.dtype, device=send.device)
+
+    def arrive(self, g: int) -> None:
+        self.a2a(self.recv[g], self.send[g], group=self.pg)
+
+    def attend(self, g: int) -> torch.Tensor:
+        return self.run_attn(*qkv_views(self.recv[g], self.v_f16))
+
+    def depart(self, g: int, o: torch.Tensor) -> None:
+        back_into(o, self.recv_b[g], self.result, g, self.ws, self.a2a, self.pg)
+
+
+def _event_after(stream, work, after=None) -> torch.cuda.Event:  # noqa: ANN001
+    """Enqueue ``work()`` on ``stream`` (behind the event ``after`` when given); the event marks its end."""
+    with torch.cuda.stream(stream):
+        if after is not None:
+            stream.wait_event(after)
+        work()
+        done = torch.cuda.Event()
+        done.record(stream)
+    return done
+
+
 def nocopy_forward(query, key, value, run_attn, *, ws, groups, pg=None, a2a=None, send_box=None, comm=None,  # noqa: ANN001,ANN201
                    v_f16=False, v_in_box=False):
     """Strict Ulysses for batch 1 with one combined exchange per head group (:124).  ``send_box`` may hold a send
-    buffer a producer already filled with q and k (v is then packed from ``value`` here), or with all three
+    buffer a producer already filled with q and k (v is then written here from ``value``), or with all three
     (``v_in_box``: the qkv GEMM's interleaved epilogue, ``fp8_gemm_qkv_send(..., interleaved=True)``, whose v slots
-    hold f16 bits with ``v_f16``); ``comm``: a stream on which the exchanges overlap the attention of earlier groups.
-    Returns [1, M, H, d] contiguous."""
-    a2a = a2a or _a2a
+    hold f16 bits with ``v_f16``).  Without ``comm`` every step runs on the current stream, group after group, and the
+    send buffer is released once the forward exchanges are enqueued.  With a ``comm`` stream all forward exchanges are
+    queued there at once, group g's attention starts when its exchange has landed, and its reverse exchange goes back
+    on ``comm`` while the next group's attention runs; every buffer was allocated on the current stream and stays
+    referenced until the current stream has waited for the last reverse exchange.  Returns [1, M, H, d] contiguous."""
     _, s_loc, heads, d = query.shape
-    dt, dev = query.dtype, query.device
     if send_box:
         send = send_box.pop()
         if not v_in_box:
             fill_slot(send, value[0], 2, ws, groups)
     else:
-        send = torch.empty(send_shape(s_loc, heads, d, ws, groups), dtype=dt, device=dev)
+        send = torch.empty(send_shape(s_loc, heads, d, ws, groups), dtype=query.dtype, device=query.device)
         pack_qkv(send, query[0], key[0], value[0], ws, groups)
-    hl = send.shape[4]
-    recv = torch.empty_like(send)
-    recv_b = torch.empty((groups, ws, s_loc, hl, d), dtype=dt, device=dev)
-    result = torch.empty((1, s_loc, heads, d), dtype=dt, device=dev)
+    xch = _GroupExchange(send, (1, s_loc, heads, d), run_attn, ws, pg, a2a or _a2a, v_f16)
+    del send
     if comm is None:
         for g in range(groups):
-            a2a(recv[g], send[g], group=pg)
-        del send
+            xch.arrive(g)
+        xch.send = None
         for g in range(groups):
-            o = run_attn(*qkv_views(recv[g], v_f16))
-            back_into(o, recv_b[g], result, g, ws, a2a, pg)
-        return result
+            xch.depart(g, xch.attend(g))
+        return xch.result
     cur = torch.cuda.current_stream()
     comm.wait_stream(cur)
     try:
-        ready = []
-        with torch.cuda.stream(comm):
-            for g in range(groups):
-                a2a(recv[g], send[g], group=pg)
-                ev = torch.cuda.Event()
-                ev.record(comm)
-                ready.append(ev)
-        outs, back_ev = [], []
+        landed = [_event_after(comm, lambda g=g: xch.arrive(g)) for g in range(groups)]
+        outs, returned = [], []
         for g in range(groups):
-            cur.wait_event(ready[g])
-            o = run_attn(*qkv_views(recv[g], v_f16))
-            outs.append(o)
-            done = torch.cuda.Event()
-            done.record(cur)
-            with torch.cuda.stream(comm):
-                comm.wait_event(done)
-                back_into(o, recv_b[g], result, g, ws, a2a, pg)
-                ev = torch.cuda.Event()
-                ev.record(comm)
-            back_ev.append(ev)
-        for ev in back_ev:
+            cur.wait_event(landed[g])
+            outs.append(xch.attend(g))          # read on comm below: referenced until the join
+            computed = torch.cuda.Event()
+            computed.record(cur)
+            returned.append(_event_after(comm, lambda g=g: xch.depart(g, outs[g]), after=computed))
+        for ev in returned:
             cur.wait_event(ev)
-        return result
+        return xch.result
     except Exception:
         cur.wait_stream(comm)
         raise
@@ -279,16 +300,25 @@ def make_rope(orig, groups: int, strategy_info, launch=None, supported=None):  #
     return fused_qk_norm_rope
 
 
+class _Armed:
+    """While a model attention's forward runs, the rope wrapper redirects q/k for that attention (``_tls.armed``).  On
+    leaving, the previous owner comes back and a send buffer the forward made but did not use is dropped."""
+
+    def __init__(self, owner):  # noqa: ANN001
+        self.owner, self.prev = owner, None
+
+    def __enter__(self) -> None:
+        self.prev, _tls.armed = getattr(_tls, "armed", None), self.owner
+
+    def __exit__(self, *exc) -> None:  # noqa: ANN002
+        _tls.armed, _tls.pending = self.prev, None
+
+
 def make_armed_forward(orig_fwd):  # noqa: ANN001,ANN201
-    """Wrap the model attention's ``forward`` so the rope wrapper knows which attention its q/k feed (:316)."""
+    """The model attention's ``forward`` with its redirect armed (:316)."""
     def forward(self, *a, **kw):  # noqa: ANN001,ANN202
-        prev = getattr(_tls, "armed", None)
-        _tls.armed = self
-        try:
+        with _Armed(self):
             return orig_fwd(self, *a, **kw)
-        finally:
-            _tls.armed = prev
-            _tls.pending = None     # a send buffer never outlives the forward that made it
 
     forward._h3b_nocopy_armed = True
     return forward

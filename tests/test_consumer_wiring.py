@@ -282,16 +282,15 @@ def test_foreign_site_stash_and_calls_outside_a_block():
     a8, sa = oq.quant(torch.randn(t, C).to(BF16))
     w8, sb = og.quant_weight(torch.randn(C, C))
     ph = torch.empty(t, C, dtype=BF16)
-    ctx = fc._Ctx({})
-    ctx.pending["out"] = fc.Stash(a8, w8, sa.reshape(-1), sb, None, ph)
-    fc._tls.ctx = ctx
     x, gate = torch.randn(t, C).to(BF16), (0.1 * torch.randn(1, C)).to(BF16)
     idx = torch.zeros(t, dtype=torch.int64)
-    out = fc.make_gate_wrapper(og.indexed_gate)(x, gate, ph, idx)                  # fc2's consumer, out's stash
-    branch = og.scaled_mm(a8, w8, sa.reshape(-1), sb)
-    assert torch.equal(out, og.indexed_gate(x, gate, branch, idx)) and torch.equal(ph, branch)
-    assert fc.stats()["materialize"] == 1 and not ctx.pending and fc.stats()["fused_fc2"] == 0
-    fc._tls.ctx = None
+    with fc.scope(None, {}) as sc:
+        sc.handoffs["out"] = fc.Stash(a8, w8, sa.reshape(-1), sb, None, ph)
+        out = fc.make_gate_wrapper(og.indexed_gate)(x, gate, ph, idx)              # fc2's consumer, out's stash
+        branch = og.scaled_mm(a8, w8, sa.reshape(-1), sb)
+        assert torch.equal(out, og.indexed_gate(x, gate, branch, idx)) and torch.equal(ph, branch)
+        assert fc.stats()["materialize"] == 1 and not sc.handoffs and fc.stats()["fused_fc2"] == 0
+    assert fc._tls.ctx is None
     layer = _layer(C, C, 5)
     _install(_module())
     y = _linear(layer, x)                                                          # a GEMM outside any block
@@ -301,12 +300,11 @@ def test_foreign_site_stash_and_calls_outside_a_block():
 def test_stash_hook_takes_only_the_planned_weights_once():
     mine, other = _layer(64, C, 6), _layer(64, C, 7)
     a8, sa = oq.quant(torch.randn(4, C).to(BF16))
-    ctx = fc._Ctx({(mine.weight.data_ptr(), tuple(mine.weight.shape)): "fc2"})
-    fc._tls.ctx = ctx
+    sc = fc.scope(None, {(mine.weight.data_ptr(), tuple(mine.weight.shape)): "fc2"}).__enter__()
     assert fc.stash_hook(a8, other.weight, sa, other.weight_scale, BF16, None) is None
     assert fc.stash_hook(a8, mine.weight, sa, mine.weight_scale, torch.float16, None) is None   # bf16 outputs only
     ph = fc.stash_hook(a8, mine.weight, sa, mine.weight_scale, BF16, None)
-    assert ph.shape == (4, 64) and ph.dtype == BF16 and set(ctx.pending) == {"fc2"}
-    st = ctx.pending["fc2"]
+    assert ph.shape == (4, 64) and ph.dtype == BF16 and set(sc.handoffs) == {"fc2"}
+    st = sc.handoffs["fc2"]
     assert st.a is a8 and st.w.shape == (64, C) and st.w.data_ptr() == mine.weight.data_ptr() and st.sa.shape == (4,)
     assert fc.stash_hook(a8, mine.weight, sa, mine.weight_scale, BF16, None) is None             # once per block

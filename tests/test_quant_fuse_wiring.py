@@ -147,17 +147,14 @@ def test_stash_met_by_another_quant_is_materialised(fuse):
     blk = tr.MiniMaxH3DiTBlock()
     fq.install(("qkv",), tr, quant_cls=Quant, act_cls=Act, lora_types=(), **_AS_REVIEWED)
     x, shift, scale, gate, idx = _inputs(80, 1)
-    ctx = fq._Ctx(blk, fq.block_plan(blk, ("qkv",))[0])
-    fq._tls.ctx = ctx
-    try:
+    with fq.scope(blk, fq.block_plan(blk, ("qkv",))[0]) as sc:
         ph = tr.rms_norm_indexed_scale_shift(x, blk.norm1.weight, shift, scale, idx, 1e-6)
         assert fq.pending_placeholder(ph)
         Quant()(torch.zeros(3, C).to(BF16))                      # another tensor's quant first
-        assert ctx.pending is None and fq.stats()["materialize"] == 1
+        assert not sc.handoffs and fq.stats()["materialize"] == 1
         ref = orms.rms_norm_scale_shift(x, blk.norm1.weight, shift, scale, idx, 1e-6)
         assert torch.equal(ph.view(torch.int16), ref.view(torch.int16))
-    finally:
-        fq._tls.ctx = None
+    assert fq._tls.ctx is None
 
 
 def test_a_fused_producer_that_differs_disables_its_site(fuse, monkeypatch):
