@@ -466,6 +466,394 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 
+// ------------------------------------------------------------------------------------------------------------------
+// The CTA-pair kernel.  A cluster of two CTAs on two SMs computes 256 query rows of one head: CTA r holds rows
+// [128 r, 128 r + 128) of Q, keys [64 r, 64 r + 64) of each 128-key K tile and columns [64 r, 64 r + 64) of each V tile
+// in its shared memory (every tile is loaded once for the pair, no multicast), and its 128 rows of S, O and P in its
+// TMEM.  The even CTA's single MMA thread issues 2-SM MMAs (tcgen05.mma.cta_group::2, M = 256): S = Q K^T (N = 128
+// keys) and O += P V (N = 128 = d, P from TMEM).  Per CTA, TMEM columns: S0 | S1 | O | P0 | P1 (128, 128, 128, 64,
+// 64).  S is double buffered and P has columns of its own, so the MMA for S(j+1) runs while the softmax of step j
+// does; each step the tensor pipe does S(j+2) and P(j) V(j).
+//   warps 0-7 : softmax + epilogue.  Warp w serves TMEM lanes [32 (w % 4), +32) (query rows) and the key / O column
+//               half w / 4: every thread reads its row's 128 scores (the row maximum needs all of them) and
+//               exponentiates its 64, so the two halves never wait for each other during the key loop.  Their
+//               partial row sums are added once, at the end.
+//   warp 8    : TMA producer of this CTA's tiles; every load completes on the even CTA's barrier, armed with the
+//               pair's bytes by the even CTA's producer
+//   warp 9    : TMEM allocator of the pair; in the even CTA the MMA issuer, whose commits arrive on both CTAs'
+//               barriers (one multicast commit per event)
+// The handoffs into the even CTA's barriers from the odd CTA's softmax warps are relaxed cluster arrivals (tensor
+// memory is ordered by tcgen05.wait and the tcgen05 fences): a release at cluster scope stalls a warp ~1,000 cycles.
+// Every wait is bounded; the two CTAs leave together (cluster barrier) after all MMAs completed.
+namespace pair {
+constexpr int QROWS = 128;                     // query rows per CTA
+constexpr int KH = 64;                         // keys of each 128-key tile per CTA
+constexpr int Q_BYTES = QROWS * D * 2;         // 32 KB
+constexpr int Q_HALF = Q_BYTES / 2;            // 64 of the 128 dims of the 128 rows (one 128-byte swizzle column)
+constexpr int K_BYTES = KH * D * 2;            // 16 KB
+constexpr int K_HALF = K_BYTES / 2;
+constexpr int V_BYTES = BKV * 64 * 2;          // 16 KB: 128 keys x this CTA's 64 columns
+constexpr int STAGE_BYTES = K_BYTES + V_BYTES; // stage n: K tile n and V tile n - 2 (what the MMAs of step n read)
+constexpr int STAGES = 5;
+constexpr int THREADS = 320;
+constexpr int STAGE_AREA = Q_BYTES + STAGES * STAGE_BYTES;
+constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 2 + 2;   // q, full/empty per stage, s_full, p_full, pv_done,
+                                                            // s_free, done + l_ready
+constexpr int SMEM_BYTES = STAGE_AREA + 1024 + 256 + 2 * QROWS * 4;
+constexpr uint32_t S_COL0 = 0, O_COL = 256, P_COL0 = 384;  // S buffer b at 128 b, P buffer b at 384 + 64 b
+static_assert(8 * (NBARS + 1) <= 256, "barrier area");
+static_assert(SMEM_BYTES <= 232448, "shared memory");
+}  // namespace pair
+
+// exp2(s * c - m) of the 64 scores s[OFF, OFF + 64) as 32 packed 16-bit pairs, their sum added into l8
+template <bool F16, int POLY, int OFF>
+__device__ __forceinline__ void exp_half(const uint32_t (&s)[128], float c, float neg_m, float (&l8)[8],
+                                         uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x0, x1, e0, e1;
+    ffma2(x0, x1, __uint_as_float(s[OFF + 2 * i]), __uint_as_float(s[OFF + 2 * i + 1]), c, c, neg_m, neg_m);
+    if ((i & 7) >= 8 - POLY) {
+      ex2_poly2(x0, x1, e0, e1);
+    } else {
+      e0 = ex2(x0);
+      e1 = ex2(x1);
+    }
+    const int a = (2 * i) & 7;
+    fadd2(l8[a], l8[a + 1], l8[a], l8[a + 1], e0, e1);
+    pk[i] = pack_p<F16>(e0, e1);
+  }
+}
+
+template <bool F16, int POLY = 0>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
+    flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ Params p) {
+  using namespace pair;
+  constexpr uint32_t IDESC_QK = idesc_make(FMT_BF16, FMT_BF16, 0, 2 * QROWS, BKV);
+  constexpr uint32_t IDESC_PV = idesc_make(F16 ? FMT_F16 : FMT_BF16, F16 ? FMT_F16 : FMT_BF16, 1, 2 * QROWS, D);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sS = sQ + Q_BYTES;  // stage n % STAGES: K half (K_BYTES), then V half (V_BYTES)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGE_AREA);
+  const uint32_t b0 = smem_u32(bars);
+  // q_full | full[STAGES] | empty[STAGES] | s_full[2] | p_full[2] | pv_done[2] | s_free[2] | done | l_ready
+  const uint32_t q_full = b0;
+  auto st_full = [&](int s) { return b0 + 8u * (1 + s); };
+  auto st_empty = [&](int s) { return b0 + 8u * (1 + STAGES + s); };
+  auto s_full = [&](int b) { return b0 + 8u * (1 + 2 * STAGES + b); };
+  auto p_full = [&](int b) { return b0 + 8u * (3 + 2 * STAGES + b); };
+  auto pv_done = [&](int b) { return b0 + 8u * (5 + 2 * STAGES + b); };
+  auto s_free = [&](int b) { return b0 + 8u * (7 + 2 * STAGES + b); };
+  const uint32_t done_bar = b0 + 8u * (9 + 2 * STAGES);
+  const uint32_t l_ready = b0 + 8u * (10 + 2 * STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  float* lred = reinterpret_cast<float*>(smem + STAGE_AREA + 256);  // [2][QROWS] partial row sums of the two halves
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();  // 0: the pair's leader (issues the MMAs)
+  const int head = blockIdx.y;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x >> 1) * 2 * QROWS + crank * QROWS;  // this CTA's first row
+  // the range flag comes from an earlier launch: every CTA of the grid reads the same value and leaves together
+  if (p.range_flag != nullptr) {
+    const bool raised = *reinterpret_cast<const volatile int32_t*>(p.range_flag) != 0;
+    if (p.range_mode == 0 && raised) {
+      if (threadIdx.x == 0) record_status(p.wc, H3B_ERANGE);
+      return;
+    }
+    if ((p.range_mode == 1 && raised) || (p.range_mode == 2 && !raised)) return;
+  }
+  const bool aborted_at_entry = status_bad(p.wc);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(st_full(s), 1);
+      mbar_init(st_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(p_full(b), 16);  // one arrival per softmax warp of both CTAs (counted on the leader's)
+      mbar_init(s_free(b), 16);  // likewise, once the warp has read its scores
+      mbar_init(pv_done(b), 1);
+    }
+    mbar_init(done_bar, 1);
+    mbar_init(l_ready, 8);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nkv = p.nkv;
+  const int nsteps = nkv + 2;  // stage n carries K(n) (n < nkv) and V(n - 2) (n >= 2)
+
+  if (!aborted_at_entry) {
+    if (warp == 8) {
+      if (lane == 0) {
+        // ---------------- TMA producer ----------------
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        const uint32_t lead_b0 = mapa_shared(b0, 0);
+        auto lead = [&](uint32_t bar) { return bar - b0 + lead_b0; };
+        if (crank == 0) mbar_arrive_expect_tx(q_full, 2 * Q_BYTES);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_3d_pair(sQ + hf * Q_HALF, &tmQ, lead(q_full), hf * 64, static_cast<int32_t>(q0), head);
+        int issued[STAGES];
+        for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+        for (int n = 0; n < nsteps; ++n) {
+          const int st = n % STAGES;
+          if (!mbar_wait(st_empty(st), (static_cast<uint32_t>(n / STAGES) & 1u) ^ 1u, p.wc)) break;
+          const bool k_now = n < nkv, v_now = n >= 2;
+          if (crank == 0) mbar_arrive_expect_tx(st_full(st), 2u * ((k_now ? K_BYTES : 0) + (v_now ? V_BYTES : 0)));
+          const uint32_t base = sS + st * STAGE_BYTES;
+          if (k_now)
+            for (int hf = 0; hf < 2; ++hf)
+              tma_load_3d_pair(base + hf * K_HALF, &tmK, lead(st_full(st)), hf * 64,
+                               n * BKV + static_cast<int>(crank) * KH, head);
+          if (v_now)
+            tma_load_3d_pair(base + K_BYTES, &tmV, lead(st_full(st)), static_cast<int>(crank) * 64, (n - 2) * BKV,
+                             head);
+          issued[st]++;
+        }
+        // drain: no TMA write may be in flight into shared memory the CTA is about to release.  The leader sees the
+        // pair's bytes on its full barriers; the partner's loads of a stage have landed once the MMAs that read
+        // them completed (its empty barriers), and its Q once the first S MMA did (stage 0's empty barrier)
+        const uint64_t t0 = globaltimer();
+        if (crank == 0)
+          while (!mbar_try_wait(q_full, 0) && globaltimer() - t0 < p.wc.timeout) {
+          }
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s] > 0) {
+            const uint32_t bar = crank == 0 ? st_full(s) : st_empty(s);
+            while (!mbar_try_wait(bar, static_cast<uint32_t>(issued[s] - 1) & 1u) && globaltimer() - t0 < p.wc.timeout) {
+            }
+          }
+      }
+    } else if (warp == 9) {
+      if (lane == 0 && crank == 0) {
+        // ---------------- MMA issuer (the leader only) ----------------
+        // Step n: S(n) = Q K(n)^T into S buffer n & 1 (once every softmax warp has read S(n - 2) out of it), then
+        // O += P(n - 2) V(n - 2) (once the softmax of step n - 2 wrote P).  So S(n) is computed while the softmax of
+        // step n - 1 runs.  Each completion event is one multicast commit that arrives on the barrier of both CTAs.
+        constexpr uint16_t kBoth = 3;
+        bool ok = mbar_wait(q_full, 0, p.wc);
+        tc_fence_after();
+        for (int n = 0; n < nsteps && ok; ++n) {
+          const int st = n % STAGES;
+          const uint32_t base = sS + st * STAGE_BYTES;
+          if (!mbar_wait(st_full(st), static_cast<uint32_t>(n / STAGES) & 1u, p.wc)) {
+            ok = false;
+            break;
+          }
+          if (n < nkv) {
+            if (n >= 2 && !mbar_wait(s_free(n & 1), static_cast<uint32_t>((n - 2) >> 1) & 1u, p.wc)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + S_COL0 + 128u * static_cast<uint32_t>(n & 1);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t cq = (kk >> 2) * Q_HALF + (kk & 3) * 32, ck = (kk >> 2) * K_HALF + (kk & 3) * 32;
+              umma_f16_ss_pair(d, sdesc_sw128(sQ + cq, 16, 1024), sdesc_sw128(base + ck, 16, 1024), IDESC_QK, kk != 0);
+            }
+            umma_commit_pair_mc(s_full(n & 1), kBoth);
+          }
+          if (n >= 2) {
+            const int j = n - 2;
+            if (!mbar_wait(p_full(j & 1), static_cast<uint32_t>(j >> 1) & 1u, p.wc)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a = tmem + P_COL0 + 64u * static_cast<uint32_t>(j & 1);
+#pragma unroll
+            for (int kk = 0; kk < BKV / 16; ++kk)
+              umma_f16_ts_pair(tmem + O_COL, a + 8u * kk, sdesc_sw128(base + K_BYTES + kk * 2048, V_BYTES, 1024),
+                               IDESC_PV, j > 0 || kk != 0);
+            umma_commit_pair_mc(pv_done(j & 1), kBoth);
+          }
+          umma_commit_pair_mc(st_empty(st), kBoth);  // K(n) and V(n - 2) are read once these MMAs complete
+        }
+        // every issued MMA completes before the pair's TMEM is released
+        umma_commit_pair(done_bar);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(done_bar, 0) && globaltimer() - t0 < p.wc.timeout) {
+        }
+      }
+    } else {
+      // ---------------- softmax + epilogue (warps 0-7) ----------------
+      const int g = warp >> 2;    // key / O column half
+      const int sub = warp & 3;   // TMEM lanes [32 sub, 32 sub + 32)
+      const int row = sub * 32 + lane;
+      const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
+      const uint32_t o_tmem = tmem + lane_addr + O_COL + 64u * static_cast<uint32_t>(g);
+      const uint32_t lead_b0 = mapa_shared(b0, 0);
+      const float c = p.scale_log2;
+      float m_run = -INFINITY, l_run = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(s_full(b), static_cast<uint32_t>(j >> 1) & 1u, p.wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t s[128];
+        const uint32_t s_tmem = tmem + lane_addr + S_COL0 + 128u * static_cast<uint32_t>(b);
+        tmem_ld32_at<0>(s_tmem + 0, s);
+        tmem_ld32_at<32>(s_tmem + 32, s);
+        tmem_ld32_at<64>(s_tmem + 64, s);
+        tmem_ld32_at<96>(s_tmem + 96, s);
+        tmem_ld_wait();
+        reg_fence(s);
+        // the scores are in registers: S buffer b may take S(j + 2)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(s_free(b) - b0 + lead_b0);
+        const int64_t kv_left = p.valid_kv - static_cast<int64_t>(j) * BKV;
+        if (kv_left < BKV) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= kv_left) s[i] = __float_as_uint(-INFINITY);
+        }
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
+#pragma unroll
+        for (int i = 16; i < 128; i += 2)
+          m8[(i >> 1) & 7] = fmax3(m8[(i >> 1) & 7], __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        const float m_new = fmaxf(m_run, mx * c);
+        const bool need = j > 0 && (m_new - m_run > RESCALE_THRESHOLD);
+        if (j == 0) {
+          m_run = m_new;
+        } else if (__any_sync(0xffffffffu, need)) {
+          // O holds P(j-1) V(j-1) once that MMA completed; rescale this warp's rows of this half
+          if (!mbar_wait(pv_done((j - 1) & 1), static_cast<uint32_t>((j - 1) >> 1) & 1u, p.wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float alpha = need ? ex2(m_run - m_new) : 1.0f;
+          if (need) {
+            l_run *= alpha;
+            m_run = m_new;
+          }
+#pragma unroll 1
+          for (int cc = 0; cc < 64; cc += 8) {
+            uint32_t o[8];
+            tmem_ld8(o_tmem + cc, o);
+            tmem_ld_wait();
+            asm volatile("" : "+r"(o[0]), "+r"(o[1]), "+r"(o[2]), "+r"(o[3]), "+r"(o[4]), "+r"(o[5]), "+r"(o[6]), "+r"(o[7]));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st8(o_tmem + cc, o);
+          }
+          tmem_st_wait();
+        }
+        // P buffer b is free again once P(j-2) V(j-2) completed
+        if (j >= 2) {
+          if (!mbar_wait(pv_done(b), static_cast<uint32_t>((j - 2) >> 1) & 1u, p.wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[32];
+        if (g == 0)   // the half is warp-uniform; the register indices stay compile-time constants
+          exp_half<F16, POLY, 0>(s, c, -m_run, l8, pk);
+        else
+          exp_half<F16, POLY, 64>(s, c, -m_run, l8, pk);
+        // keys [64 g, 64 g + 64) of the tile as 16-bit pairs: P columns [32 g, 32 g + 32)
+        tmem_st32(tmem + lane_addr + P_COL0 + 64u * static_cast<uint32_t>(b) + 32u * static_cast<uint32_t>(g), pk);
+        l_run += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(p_full(b) - b0 + lead_b0);
+      }
+      const int jl = nkv - 1;
+      if (ok && mbar_wait(pv_done(jl & 1), static_cast<uint32_t>(jl >> 1) & 1u, p.wc)) {
+        tc_fence_after();
+        // the row's sum: the two halves' partial sums, added in the same order by both
+        lred[g * QROWS + row] = l_run;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(l_ready);
+        if (mbar_wait(l_ready, 0, p.wc)) {
+          const float inv_l = 1.0f / (lred[row] + lred[QROWS + row]);
+          const int64_t t = q0 + row;
+          uint16_t* orow = p.o + t * p.o_tok + static_cast<int64_t>(head) * p.o_head + 64 * g;
+          // peer stores: the warp's 32 rows x 128 B are staged in the stage area (every load was consumed by MMAs
+          // that completed before the last pv_done) and leave as 4 rows per store instruction
+          uint4* stg = reinterpret_cast<uint4*>(smem + Q_BYTES) + warp * 32 * 8;
+#pragma unroll
+          for (int cc = 0; cc < 64; cc += 32) {
+            uint32_t o[32];
+            tmem_ld32(o_tmem + cc, o);
+            tmem_ld_wait();
+            reg_fence(o);
+            float f[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = inv_l;
+            if (p.colmax != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                f[i] = inv_l * __int_as_float((127 + colscale_exp(__ldg(p.colmax + head * D + 64 * g + cc + i))) << 23);
+            }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = 8 * v + 2 * e;
+                __nv_bfloat162 bb = __floats2bfloat162_rn(__uint_as_float(o[i]) * f[i], __uint_as_float(o[i + 1]) * f[i + 1]);
+                w[e] = *reinterpret_cast<uint32_t*>(&bb);
+              }
+              const uint4 val = make_uint4(w[0], w[1], w[2], w[3]);
+              const int gi = (cc >> 3) + v;  // 16-byte granule of the row's 128 bytes
+              if (p.m_rows > 0)
+                stg[lane * 8 + (gi ^ (lane & 7))] = val;
+              else if (t < p.s_q)
+                *reinterpret_cast<uint4*>(orow + 8 * gi) = val;
+            }
+          }
+          if (p.m_rows > 0) {  // Ulysses reverse exchange: row t goes to rank t / m_rows, slot `rank` there
+            __syncwarp();
+            const int64_t r0 = q0 + sub * 32;
+#pragma unroll 4
+            for (int it = 0; it < 8; ++it) {
+              const int idx = it * 32 + lane, r = idx >> 3, part = idx & 7;
+              const int64_t tt = r0 + r;
+              if (tt < p.s_q) {
+                const int64_t owner = tt / p.m_rows;
+                uint16_t* dst = p.peer_o[owner < H3B_MAX_RANKS ? owner : 0] +
+                                (p.rank * p.m_rows + (tt - owner * p.m_rows)) * p.o_tok +
+                                static_cast<int64_t>(head) * p.o_head + 64 * g + part * 8;
+                *reinterpret_cast<uint4*>(dst) = stg[r * 8 + (part ^ (r & 7))];
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves (or frees the pair's TMEM) while the other may still signal it
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc_pair(tmem, 512);
+}
+
 }  // namespace attn
 }  // namespace h3b
 
@@ -496,6 +884,16 @@ static cudaError_t set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Which attention kernel runs: the one-CTA kernel (default) or the CTA-pair kernel (H3B_ATTN_PAIR=1; both compute
+// the same softmax within the kernels' tolerance)
+static bool use_pair() {
+  static const bool on = [] {
+    const char* v = getenv("H3B_ATTN_PAIR");
+    return v != nullptr && v[0] != '\0' && atoi(v) != 0;
+  }();
+  return on;
+}
+
 // once per device: the shared-memory opt-in of every kernel variant (first calls from several threads serialise
 // on the mutex; a device is marked done only after every attribute was set)
 static int attn_attrs() {
@@ -513,6 +911,11 @@ static int attn_attrs() {
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<true, 3>, SMEM_BYTES);
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<true, 4>, SMEM_BYTES);
   if (e == cudaSuccess) e = set_smem(flash_attn_kernel<false, kDefaultPoly>, SMEM_BYTES);
+  if (e == cudaSuccess) e = set_smem(flash_attn_pair_kernel<true, 0>, pair::SMEM_BYTES);
+  if (e == cudaSuccess) e = set_smem(flash_attn_pair_kernel<true, 2>, pair::SMEM_BYTES);
+  if (e == cudaSuccess) e = set_smem(flash_attn_pair_kernel<true, 3>, pair::SMEM_BYTES);
+  if (e == cudaSuccess) e = set_smem(flash_attn_pair_kernel<true, 4>, pair::SMEM_BYTES);
+  if (e == cudaSuccess) e = set_smem(flash_attn_pair_kernel<false, kDefaultPoly>, pair::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "flash_attn: smem attribute");
   done[dev] = true;
   return H3B_OK;
@@ -529,12 +932,30 @@ static int launch_attention(const void* q, int64_t q_tok, int64_t q_head, const 
   // K and V maps end at valid_kv: the last key tile's rows beyond it come from the TMA's zero fill, never from
   // memory (padding rows may hold anything, even values whose product with a zero P would not be zero)
   rc = make_qkv_map(&tq, q, p.s_q, p.heads, q_tok, q_head, BQ);
-  if (!rc) rc = make_qkv_map(&tk, k, p.valid_kv, p.heads, k_tok, k_head, BKV);
+  const bool pr = use_pair();
+  if (!rc) rc = make_qkv_map(&tk, k, p.valid_kv, p.heads, k_tok, k_head, pr ? pair::KH : BKV);
   if (!rc) rc = make_qkv_map(&tv, v, p.valid_kv, p.heads, v_tok, v_head, BKV);
   if (rc) return rc;
   p.nkv = static_cast<int>((p.valid_kv + BKV - 1) / BKV);
-  dim3 grid(static_cast<unsigned>((p.s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(p.heads));
   const int poly = poly_pairs();
+  if (pr) {  // clusters of two CTAs over 256-row query tiles
+    dim3 grid(2 * static_cast<unsigned>((p.s_q + 2 * pair::QROWS - 1) / (2 * pair::QROWS)),
+              static_cast<unsigned>(p.heads));
+    const int sm = pair::SMEM_BYTES;
+    if (!v_f16)
+      flash_attn_pair_kernel<false, kDefaultPoly><<<grid, pair::THREADS, sm, st>>>(tq, tk, tv, p);
+    else if (poly == 0)
+      flash_attn_pair_kernel<true, 0><<<grid, pair::THREADS, sm, st>>>(tq, tk, tv, p);
+    else if (poly == 2)
+      flash_attn_pair_kernel<true, 2><<<grid, pair::THREADS, sm, st>>>(tq, tk, tv, p);
+    else if (poly == 3)
+      flash_attn_pair_kernel<true, 3><<<grid, pair::THREADS, sm, st>>>(tq, tk, tv, p);
+    else
+      flash_attn_pair_kernel<true, 4><<<grid, pair::THREADS, sm, st>>>(tq, tk, tv, p);
+    H3B_CHECK_LAUNCH("flash_attn launch");
+    return H3B_OK;
+  }
+  dim3 grid(static_cast<unsigned>((p.s_q + 2 * BQ - 1) / (2 * BQ)), static_cast<unsigned>(p.heads));
   if (!v_f16)
     flash_attn_kernel<false, kDefaultPoly><<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
   else if (poly == 0)

@@ -187,6 +187,47 @@ __device__ __forceinline__ void umma_f8_ss_pair(uint32_t d, uint64_t a, uint64_t
       "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
+// the 3-D form of tma_load_2d_pair (no multicast)
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* m, uint32_t bar, int32_t c0,
+                                                 int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// kind::f16 pair MMAs (bf16 or f16 operands, f32 accumulator), issued by one thread of the even CTA: D rows
+// [128 r, 128 r + 128) in CTA r's TMEM, A rows likewise from CTA r (shared memory, or TMEM for the _ts form), B
+// columns [N/2 r, N/2 r + N/2) from CTA r's shared memory
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                                 uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// one arrival on the mbarrier at shared::cta offset `bar` in each CTA of `cta_mask` (a bit per CTA rank of the cluster)
+// when the pair MMAs issued so far by this thread complete (one instruction for the barriers of both CTAs)
+__device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+// arrive on an mbarrier of any CTA of the cluster without release ordering of this thread's memory operations: for
+// handing over tensor-memory contents, whose ordering comes from tcgen05.wait::ld / ::st and
+// tcgen05.fence::before_thread_sync before the arrival (a release at cluster scope stalls the warp ~1,000 cycles)
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 // arrive (once) on the mbarrier at shared::cluster address `bar` (either CTA of the pair) when the pair MMAs issued
 // so far by this thread complete
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
