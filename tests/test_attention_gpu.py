@@ -150,3 +150,41 @@ def test_poly_exp2_variants_in_a_fresh_process(dev, poly):
     assert out.returncode == 0, out.stderr
     rel, mabs, status = out.stdout.split()
     assert float(rel) <= 2e-3 and float(mabs) <= 2e-2 and int(status) == 0
+
+
+def test_pair_kernel_in_a_fresh_process(dev):
+    """H3B_ATTN_PAIR=1 selects the CTA-pair kernel (2-SM MMAs): within the attention tolerance of fp32 SDPA on odd
+    lengths, valid_kv, the scaled pass for a v beyond f16, and the peer-store epilogue equal to the local output."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys, torch\n"
+        f"sys.path[:0] = [{str(root / 'minimax-h3-2x-dgx-spark-tp2_b200')!r}, {str(root)!r}, {str(root / 'tests')!r}]\n"
+        "from h3b import ops\n"
+        "from oracle import attention as oa\n"
+        "from _util import rel_l2\n"
+        "worst = 0.0\n"
+        "for s, h, vk, big in [(1000, 2, None, None), (300, 3, 129, None), (777, 2, 600, 90000.0), (4096, 1, None, None)]:\n"
+        "    g = torch.Generator().manual_seed(s)\n"
+        "    q, k, v = (torch.randn(s, h, 128, generator=g).to(torch.bfloat16) for _ in range(3))\n"
+        "    if big: v[5, 0, 3] = big\n"
+        "    o = ops.flash_attn(q.cuda(), k.cuda(), v.cuda(), valid_kv=vk).float().cpu()\n"
+        "    ref = oa.sdpa(q, k, v, valid_kv=vk)\n"
+        "    worst = max(worst, rel_l2(o, ref))\n"
+        "ws, m = 2, 192\n"
+        "g = torch.Generator().manual_seed(3)\n"
+        "q, k, v = (torch.randn(ws * m, 2, 128, generator=g).to(torch.bfloat16).cuda() for _ in range(3))\n"
+        "back = [torch.full((ws, m, 2, 128), -1.0, dtype=torch.bfloat16, device='cuda') for _ in range(ws)]\n"
+        "ops.flash_attn_p2p(q, k, v, back, 1)\n"
+        "o = ops.flash_attn(q, k, v)\n"
+        "same = all(torch.equal(back[t][1].view(torch.int16), o[t * m:(t + 1) * m].view(torch.int16)) for t in range(ws))\n"
+        "print(worst, int(same), ops.device_status())\n")
+    env = dict(os.environ, H3B_ATTN_PAIR="1")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    worst, same, status = out.stdout.split()
+    assert float(worst) <= 2e-3 and same == "1" and int(status) == 0
