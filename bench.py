@@ -12,7 +12,9 @@ group), so no explicit flush is needed.  Rank 0 prints one JSON line.
 After the timed regions every rank checks its part of one more forward against the CPU oracle on 64 sampled rows
 (``parity`` in the JSON line, the worst over ranks): the qkv projection rows it received from every rank, the
 attention of its heads for those rows against the device's K/V, the reverse exchange, and the whole block's output
-rows through the oracle's attention, quant and out projection.
+rows through the oracle's attention, quant and out projection.  Then the ``ffn`` section times BASELINE configs[4],
+the block's FFN over the same M = 124,992 / SP rows per rank (RMSNorm + quant, fc1 with the SwiGLU epilogue, quant,
+fc2; no communication), with its own sampled-row parity.
 
 ``--impl reference`` times the reference's CPU path for the same workload on the host cores (the oracle port of
 h3_tp2's eager arithmetic: per-token quant, FP8 GEMM epilogue, fp32 SDPA) on a bounded per-head sample, as the
@@ -379,6 +381,119 @@ def block_parity(blk, keep: dict, rank: int, world: int, m: int, dev, pg, rows: 
 # ---------------------------------------------------------------------------------------------------------------
 
 
+FFN = 13_824   # hidden 5120 -> gate/up 2 x 13,824 -> 5120
+
+
+def ffn_flops(m: int) -> float:
+    return 2.0 * m * HIDDEN * 2 * FFN + 2.0 * m * FFN * HIDDEN
+
+
+def ffn_weights(dev):
+    """The cfg4 FFN's weights (seed 2): W1 [2F, C] (gate rows, then up rows) and W2 [C, F] ~ N(0, 0.02), quantised per
+    output channel to e4m3, and the RMSNorm weight (bf16, around 1)."""
+    from h3b.block import quant_weight  # noqa: PLC0415
+    g = torch.Generator(device=dev).manual_seed(2)
+    w1 = torch.randn(2 * FFN, HIDDEN, device=dev, generator=g) * 0.02
+    w2 = torch.randn(HIDDEN, FFN, device=dev, generator=g) * 0.02
+    norm_w = (1.0 + 0.1 * torch.randn(HIDDEN, device=dev, generator=g)).to(torch.bfloat16)
+    return (norm_w, *quant_weight(w1), *quant_weight(w2))
+
+
+FFN_STAGES = ("rms_quant", "fc1_swiglu", "quant_h", "fc2")
+
+
+def ffn_forward(x, norm_w, w1, s1, w2, s2, marks=None, keep=None):
+    """RMSNorm (eps 1e-6) + per-token quant -> fc1 with the SwiGLU epilogue -> per-token quant -> fc2 (the torch ops
+    the plugin's MLP path calls); ``marks`` gets a CUDA event before and after each stage."""
+    def mark():
+        if marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append(ev)
+    mark()
+    q, sq = torch.ops.h3b.rms_quant(x, norm_w, None, None, None, 1e-6, None)
+    mark()
+    h = torch.ops.h3b.fp8_gemm_swiglu(q, w1, sq, s1, None)
+    mark()
+    hq, sh = torch.ops.h3b.quant(h)
+    mark()
+    y = torch.ops.h3b.fp8_gemm(hq, w2, sh, s2, None, torch.bfloat16)
+    mark()
+    if keep is not None:
+        keep.update(h=h, y=y)
+    return y
+
+
+def ffn_parity(x, weights, keep, rows: int = 64) -> dict:
+    """The FFN's sampled rows against the CPU oracle: the SwiGLU output h (the fc1 GEMM with its epilogue; CUDA's expf
+    against torch's exp) and the FFN output y.  Threshold rel-L2 <= 1e-2 (the FP8 GEMM contract) for both."""
+    from oracle import gemm as og  # noqa: PLC0415
+    from oracle import quant as oq  # noqa: PLC0415
+    from oracle import rms as orms  # noqa: PLC0415
+    norm_w, w1, s1, w2, s2 = (t.cpu() for t in weights)
+    idx = torch.linspace(0, x.shape[0] - 1, rows).round().long()
+    xr = x[idx.to(x.device)].cpu()
+    q, sq = orms.rms_quant(xr, norm_w, eps=1e-6)
+    h = og.swiglu_epilogue(og.accumulate(q, w1), sq, s1, None)
+    hq, sh = oq.quant(h)
+    y = og.scaled_mm(hq, w2, sh, s2)
+
+    def rel(a, b):
+        a, b = a.double(), b.double()
+        return float((a - b).norm() / b.norm().clamp_min(1e-300))
+    r_h = rel(keep["h"][idx.to(x.device)].float().cpu(), h.float())
+    r_y = rel(keep["y"][idx.to(x.device)].float().cpu(), y.float())
+    return {"rows": rows, "rel_l2": {"swiglu_h": r_h, "ffn_y": r_y}, "tolerance": 1e-2,
+            "ok": bool(r_h <= 1e-2 and r_y <= 1e-2)}
+
+
+def run_ffn(args, rank: int, world: int, dev, pg, m: int) -> dict:
+    """BASELINE configs[4] at this SP: the FFN over this rank's M = 124,992 / SP rows (replicas: the FFN is row-local,
+    no communication), device-timed over --steps steps after --warmup, the worst rank's time."""
+    from h3b import ops  # noqa: PLC0415
+    weights = ffn_weights(dev)
+    x = make_x(rank, m, dev)
+    for _ in range(args.warmup):
+        ffn_forward(x, *weights)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(group=pg, device_ids=[dev.index])
+    marks_all = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        marks = []
+        ffn_forward(x, *weights, marks=marks)
+        marks_all.append(marks)
+    end.record()
+    torch.cuda.synchronize(dev)
+    vals = [start.elapsed_time(end) / args.steps] + [
+        statistics.mean(mk[i].elapsed_time(mk[i + 1]) for mk in marks_all) for i in range(len(FFN_STAGES))]
+    if world > 1:
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+        vals = t.tolist()
+    ms = vals[0]
+    keep = {}
+    ffn_forward(x, *weights, keep=keep)
+    torch.cuda.synchronize(dev)
+    status = ops.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} in the FFN")
+    par = ffn_parity(x, weights, keep)
+    if world > 1:
+        t = torch.tensor([par["rel_l2"]["swiglu_h"], par["rel_l2"]["ffn_y"]], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+        par["rel_l2"] = {"swiglu_h": t[0].item(), "ffn_y": t[1].item()}
+        par["ok"] = bool(t.max().item() <= 1e-2)
+    fl = ffn_flops(m)
+    return {"workload": f"cfg4 FFN: M = {m} rows per rank (124,992 / SP), hidden {HIDDEN} -> 2 x {FFN} -> {HIDDEN}, "
+                        "RMSNorm eps 1e-6 + per-token e4m3 quant, fc1 with the SwiGLU epilogue, quant, fc2",
+            "rows_per_rank": m, "ms_per_step": ms, "tflops": world * fl / (ms * 1e-3) / 1e12,
+            "tflops_per_gpu": fl / (ms * 1e-3) / 1e12, "ms_per_stage": dict(zip(FFN_STAGES, vals[1:])),
+            "scaling": "weak (replicas: no communication)", "parity": par}
+
+
 def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
     import h3b  # noqa: PLC0415
     from h3b.block import AttentionBlock  # noqa: PLC0415
@@ -511,6 +626,7 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
         torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
     parity = block_parity(blk, keep, rank, world, m, dev, pg)
     del keep
+    ffn = None if args.no_ffn else run_ffn(args, rank, world, dev, pg, m)
 
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -535,6 +651,8 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
         "clocks": clocks.summary(),
         "parity": parity,
     }
+    if ffn is not None:
+        line["ffn"] = ffn
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1
         cpu_sample(tokens, q_rows=256, threads=cores)            # warm-up (thread pool, page faults)
@@ -565,6 +683,7 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0, help="override the token count (tests / small runs)")
     ap.add_argument("--ref-rows", type=int, default=1024, help="query rows of the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ffn", action="store_true", help="skip the cfg4 FFN section of the JSON line")
     ap.add_argument("--groups", type=int, default=0,
                     help="Ulysses head groups overlapped with attention (NCCL exchange; 0: the measured default)")
     ap.add_argument("--exchange", choices=("nccl", "nocopy", "p2p"), default="p2p",

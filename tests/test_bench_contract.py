@@ -98,3 +98,27 @@ def test_block_parity_passes_on_oracle_data_and_catches_a_planted_error():
     blk, keep = _fake_block_run(m, plant=plant_y)
     par = bench.block_parity(blk, keep, 0, 1, m, torch.device("cpu"), None, rows=16)
     assert not par["ok"] and par["rel_l2"]["out"] > 1e-2
+
+
+def test_ffn_parity_passes_on_oracle_data_and_catches_a_planted_error():
+    """The FFN section's parity check, fed the oracle's own h and y (built on the CPU), passes; one changed output row
+    fails it."""
+    import bench
+    from oracle import gemm as og
+    from oracle import quant as oq
+    from oracle import rms as orms
+    m = 96
+    g = torch.Generator().manual_seed(5)
+    norm_w = (1.0 + 0.1 * torch.randn(bench.HIDDEN, generator=g)).to(torch.bfloat16)
+    w1, s1 = og.quant_weight(torch.randn(2 * 256, bench.HIDDEN, generator=g) * 0.02)
+    w2, s2 = og.quant_weight(torch.randn(bench.HIDDEN, 256, generator=g) * 0.02)
+    x = torch.randn(m, bench.HIDDEN, generator=g).to(torch.bfloat16)
+    q, sq = orms.rms_quant(x, norm_w, eps=1e-6)
+    h = og.swiglu_epilogue(og.accumulate(q, w1), sq, s1, None)
+    hq, sh = oq.quant(h)
+    y = og.scaled_mm(hq, w2, sh, s2)
+    par = bench.ffn_parity(x, (norm_w, w1, s1, w2, s2), {"h": h, "y": y}, rows=16)
+    assert par["ok"] and par["rel_l2"]["ffn_y"] < 5e-3     # CPU matmuls of a row subset may round differently
+    y2 = y.clone()
+    y2[0] *= 2
+    assert not bench.ffn_parity(x, (norm_w, w1, s1, w2, s2), {"h": h, "y": y2}, rows=16)["ok"]
