@@ -376,18 +376,23 @@ __global__ void __launch_bounds__(THREADS, 1)
               e0 = ex2(x0);
               e1 = ex2(x1);
             }
-            const int a = (2 * i) & 7;
-            fadd2(l8[a], l8[a + 1], l8[a], l8[a + 1], e0, e1);
+            s[32 * cc + 2 * i] = __float_as_uint(e0);  // kept for the row sum, taken after P is handed over
+            s[32 * cc + 2 * i + 1] = __float_as_uint(e1);
             pk[i] = pack_p<F16>(e0, e1);
           }
           tmem_st16(s_tmem + 16 * cc, pk);
         }
-        const float lsum = ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-        l_run += lsum;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full(q));
+        // the row sum is off the MMA warp's critical path: same pairs, same order as summing during the exponentials
+#pragma unroll
+        for (int i = 0; i < 128; i += 2) {
+          const int a = i & 7;
+          fadd2(l8[a], l8[a + 1], l8[a], l8[a + 1], __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+        }
+        l_run += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
       }
       if (ok && mbar_wait(o_full(q), 0, p.wc)) {
         tc_fence_after();
