@@ -315,12 +315,14 @@ def block_parity(blk, keep: dict, rank: int, world: int, m: int, dev, pg, rows: 
     oracle (oracle.quant / oracle.gemm / oracle.attention):
       qkv       the q/k/v rows this rank received from every rank (its head group's columns) against the oracle's
                 quant + FP8 projection of those ranks' inputs (regenerated from their seeds);
-      attention every rank's oracle attention for its head group at those query rows (the oracle's q against the
-                device's K/V of all tokens), exchanged back, against this rank's reverse receive buffer;
+      attention every rank's oracle attention for its head group at those query rows (the device's q rows against
+                the device's K/V of all tokens, so that this stage measures the attention alone), exchanged back,
+                against this rank's reverse receive buffer;
       out       the device's y rows against the oracle's quant + out projection of the device's reverse buffer rows;
       block     the device's y rows against the oracle's quant + out projection of the oracle's attention rows.
     Thresholds: GEMM-based stages rel-L2 <= 1e-2 (the FP8 GEMM contract); attention rel-L2 <= 2e-3 and max-abs <=
-    2e-2 (the attention contract); block rel-L2 <= 1e-2."""
+    2e-2 after dividing each column by max(1, its largest |ref|), as the attention tests measure it (the raw max-abs
+    is reported beside it); block rel-L2 <= 1e-2."""
     from oracle import attention as oa  # noqa: PLC0415
     from oracle import gemm as og  # noqa: PLC0415
     from oracle import quant as oq  # noqa: PLC0415
@@ -346,7 +348,7 @@ def block_parity(blk, keep: dict, rank: int, world: int, m: int, dev, pg, rows: 
     for h in range(hl):
         kh = keep["k"][:, h:h + 1].contiguous().cpu()
         vh = keep["v"][:, h:h + 1].contiguous().cpu()
-        o_or[:, h:h + 1] = oa.sdpa(qkv[:, 0, h:h + 1], kh, vh, chunk=world * rows)
+        o_or[:, h:h + 1] = oa.sdpa(got[:, 0, h:h + 1].to(torch.bfloat16), kh, vh, chunk=world * rows)
     o_or = o_or.reshape(world, rows, hl, d)                                              # [dest rank, R, hl, d]
     if world > 1:
         recv = torch.empty_like(o_or, device=dev)
@@ -356,22 +358,31 @@ def block_parity(blk, keep: dict, rank: int, world: int, m: int, dev, pg, rows: 
         attn_or = o_or
     back = keep["back"][:, idx_d].float().cpu()                                          # [head group, R, hl, d]
     r_attn = rel(back, attn_or)
-    a_attn = float((back - attn_or).abs().max())
+    err = (back - attn_or).abs()
+    a_attn = float(err.max())
+    worst = int(err.argmax())
+    # the attention tests' max-abs measure: each column's error over max(1, that column's largest |ref|)
+    colscale = attn_or.abs().amax(dim=1, keepdim=True).clamp_min(1.0)
+    s_attn = float((err / colscale).max())
+    w_ref, w_got = float(attn_or.reshape(-1)[worst]), float(back.reshape(-1)[worst])
     wo8, so_w = blk.wo8.cpu(), blk.so.cpu()
     y = keep["y"][idx_d].float().cpu()
     ob8, obs = oq.quant(back.permute(1, 0, 2, 3).reshape(rows, H * d).to(torch.bfloat16))
     r_out = rel(y, og.scaled_mm(ob8, wo8, obs, so_w).float())
     oa8, oas = oq.quant(attn_or.permute(1, 0, 2, 3).reshape(rows, H * d).to(torch.bfloat16))
     r_block = rel(y, og.scaled_mm(oa8, wo8, oas, so_w).float())
-    vals = [r_qkv, r_attn, a_attn, r_out, r_block]
+    print(f"[rank {rank}] attention parity: worst |err| {a_attn:.4g} at ref {w_ref:.4g} (got {w_got:.4g}), "
+          f"column-scaled {s_attn:.4g}", file=sys.stderr, flush=True)
+    vals = [r_qkv, r_attn, a_attn, r_out, r_block, s_attn]
     if world > 1:
         t = torch.tensor(vals, dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
         vals = t.tolist()
-    r_qkv, r_attn, a_attn, r_out, r_block = vals
-    ok = r_qkv <= 1e-2 and r_attn <= 2e-3 and a_attn <= 2e-2 and r_out <= 1e-2 and r_block <= 1e-2
+    r_qkv, r_attn, a_attn, r_out, r_block, s_attn = vals
+    ok = r_qkv <= 1e-2 and r_attn <= 2e-3 and s_attn <= 2e-2 and r_out <= 1e-2 and r_block <= 1e-2
     return {"rows": rows, "tokens_checked": rows * world, "rel_l2": {"qkv": r_qkv, "attention": r_attn,
             "out": r_out, "block": r_block}, "max_abs": {"attention": a_attn},
+            "max_abs_colscaled": {"attention": s_attn},
             "tolerance": {"qkv": 1e-2, "attention": [2e-3, 2e-2], "out": 1e-2, "block": 1e-2},
             "oracle": "oracle.quant + oracle.gemm + oracle.attention (fp32 SDPA) on the CPU", "ok": bool(ok)}
 

@@ -21,6 +21,9 @@
 //                 4 of them from the other CTA).
 //   The accumulator is double buffered in TMEM (2 x 256 of the 512 columns) so the epilogue of tile i overlaps the
 //   main loop of tile i+1.  Every wait is bounded (common.cuh).  No TMA multicast.
+#include <stdlib.h>
+#include <string.h>
+
 #include "common.cuh"
 
 namespace h3b {
@@ -35,8 +38,9 @@ constexpr int GROUP_M = 8;   // pair row blocks (256 rows each) sharing one colu
 constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
 // epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows)
 constexpr int STAGING_BYTES = 4 * 32 * 256;
-// ring, alignment slack, barriers, staging (230,656 B of the 232,448 a CTA may have)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + STAGING_BYTES;
+// ring, alignment slack, barriers (1 KB, so that the staging starts 1024-byte aligned as the 128-byte swizzle of the
+// TMA stores needs), staging: 231,424 B of the 232,448 a CTA may have
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING_BYTES;
 constexpr uint32_t IDESC = idesc_make(FMT_E4M3, FMT_E4M3, 0, 2 * BM, BN);
 
 struct Params {
@@ -70,6 +74,7 @@ struct Params {
   int64_t ldg, gate_rows;
   const int64_t* gidx;
   int p2p;                               // QKV_SEND into the peers' receive buffers
+  int tma_out;                           // 1: staged blocks leave through TMA stores (tmY, below)
   int rank;
   void* peer[H3B_MAX_RANKS][3];
   int32_t* peer_rf[H3B_MAX_RANKS];
@@ -127,13 +132,14 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
 // With Params::p2p the QKV_SEND epilogue stores into the other GPUs' receive buffers (send_slab).
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ Params p) {
+                    const __grid_constant__ CUtensorMap tmY0, const __grid_constant__ CUtensorMap tmY1,
+                    const __grid_constant__ CUtensorMap tmY2, const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
-  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256);
+  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 1024);
   const uint32_t smem0 = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -276,7 +282,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int row_in_tile = sub * 32 + lane;
       const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
       uint4* stg = staging + sub * 32 * 16;
-      auto stage = [&](int g, uint4 val) { stg[lane * 16 + (g ^ (lane & 15))] = val; };
+      // With TMA stores the block is staged as the two 64-column boxes the stores read: 32 rows x 128 B each, in
+      // the 128-byte swizzle (granule c of row r at r * 8 + (c ^ (r & 7))); otherwise as 32 rows x 256 B.
+      const bool tma = p.tma_out != 0;
+      auto stage = [&](int g, uint4 val) {
+        if (tma)
+          stg[(g >> 3) * 256 + lane * 8 + ((g & 7) ^ (lane & 7))] = val;
+        else
+          stg[lane * 16 + (g ^ (lane & 15))] = val;
+      };
+      // before the block's values are staged: the previous TMA stores of this warp have read the staging
+      auto staging_free = [&]() {
+        if (tma) {
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+        }
+      };
+      // the staged block leaves as two TMA stores (box 64 columns x 32 rows); rows at or beyond M and columns at or
+      // beyond the map's extent are clipped by the TMA unit
+      auto store_tma = [&](const CUtensorMap* map, int rank, int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t src = smem_u32(stg);
+          if (rank == 2) {
+            tma_store_2d(map, src, c0, c1);
+            tma_store_2d(map, src + 4096, c0 + 64, c1);
+          } else {
+            tma_store_4d(map, src, c0, c1, c2, c3);
+            tma_store_4d(map, src + 4096, c0 + 64, c1, c2, c3);
+          }
+          bulk_commit();
+        }
+      };
       // the warp's rows m0 + r (r < 32) of one 128-column block: row r to base + (m0 + r) * rstride, granules
       // below `granules`
       auto store_rows = [&](uint16_t* base, int64_t rstride, int64_t m0, int granules) {
@@ -311,6 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
         const uint32_t tacc = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN);
         if (p.epi == H3B_EPI_SWIGLU) {
+          staging_free();
           for (int c0 = 0; c0 < 128; c0 += 32) {
             uint32_t g[32], u[32];
             tmem_ld32(tacc + c0, g);
@@ -346,7 +385,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             for (int v = 0; v < 4; ++v) stage(c0 / 8 + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
           }
           release_acc();
-          store_rows(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(nb) * 128, p.ldy, m0, 16);
+          if (tma)
+            store_tma(&tmY0, 2, nb * 128, static_cast<int32_t>(m0), 0, 0);
+          else
+            store_rows(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(nb) * 128, p.ldy, m0, 16);
         } else {
           for (int b0 = 0; b0 < BN; b0 += 128) {
             const int64_t nbk = static_cast<int64_t>(nb) * BN + b0;  // first column of the block
@@ -368,9 +410,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               qstride = static_cast<int64_t>(p.rsh) * 128;
             }
             if (p.epi == H3B_EPI_QKV_SEND && p.norm_w[0] != nullptr && which < 2) {
-              // q or k head with RMSNorm + partial RoPE, stored row by row: its arithmetic, not its stores, bounds
-              // this epilogue (staging measured 3 % slower here)
+              // q or k head with RMSNorm + partial RoPE: with TMA stores the head is staged and leaves as whole lines
+              // like the other blocks; without them each thread stores its row's values (staging for plain stores
+              // measured 3 % slower here)
               const __nv_bfloat16* wn = p.norm_w[which];
+              staging_free();
               uint16_t* dst = qbase + m * qstride;
               const uint32_t hbase = tacc + b0;
               // pass 1: the bf16 head values (the GEMM output the reference normalises) and their sum of squares
@@ -445,7 +489,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                       ob[i] = __fadd_rn(__fmul_rn(nb2[i], c4[e]), __fmul_rn(na[i], s4[e]));
                     }
                   }
-                  if (row_ok) {
+                  if (tma) {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                      stage((e0 >> 3) + q, make_uint4(pack2(oa[8 * q], oa[8 * q + 1], 0), pack2(oa[8 * q + 2], oa[8 * q + 3], 0),
+                                                      pack2(oa[8 * q + 4], oa[8 * q + 5], 0), pack2(oa[8 * q + 6], oa[8 * q + 7], 0)));
+                      stage(((e0 + half) >> 3) + q,
+                            make_uint4(pack2(ob[8 * q], ob[8 * q + 1], 0), pack2(ob[8 * q + 2], ob[8 * q + 3], 0),
+                                       pack2(ob[8 * q + 4], ob[8 * q + 5], 0), pack2(ob[8 * q + 6], ob[8 * q + 7], 0)));
+                    }
+                  } else if (row_ok) {
                     uint4* da = reinterpret_cast<uint4*>(dst + e0);
                     uint4* db = reinterpret_cast<uint4*>(dst + e0 + half);
 #pragma unroll
@@ -456,6 +509,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                          pack2(ob[8 * q + 4], ob[8 * q + 5], 0), pack2(ob[8 * q + 6], ob[8 * q + 7], 0));
                     }
                   }
+                } else if (tma) {
+#pragma unroll
+                  for (int q = 0; q < 2; ++q)
+                    stage((e0 >> 3) + q, make_uint4(pack2(na[8 * q], na[8 * q + 1], 0), pack2(na[8 * q + 2], na[8 * q + 3], 0),
+                                                    pack2(na[8 * q + 4], na[8 * q + 5], 0), pack2(na[8 * q + 6], na[8 * q + 7], 0)));
                 } else if (row_ok) {
                   uint4* da = reinterpret_cast<uint4*>(dst + e0);
 #pragma unroll
@@ -465,9 +523,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 }
               }
               if (last_block) release_acc();
+              if (tma) {
+                const int h = static_cast<int>(nbk - static_cast<int64_t>(which) * p.hd) >> 7;
+                store_tma(which == 0 ? &tmY0 : &tmY1, 4, 0, j, static_cast<int32_t>(m0), (h / p.hg) * p.ws + dst_rank);
+              }
               continue;
             }
             // scaled accumulator of the block, 32 columns at a time, staged as the output's 16-bit values
+            staging_free();
             const bool as_f16 = p.epi == H3B_EPI_QKV_SEND && which == 2 && p.v_f16;
             int32_t* rf = p.epi == H3B_EPI_QKV_SEND ? (p.p2p ? p.peer_rf[dst_rank] : p.range_flag) : nullptr;
             for (int c = 0; c < 128; c += 32) {
@@ -518,7 +581,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
             if (last_block) release_acc();
             const int granules = p.N - nbk >= 128 ? 16 : static_cast<int>((p.N - nbk) / 8);
-            if (p.epi == H3B_EPI_QKV_SEND) {
+            if (p.epi == H3B_EPI_QKV_SEND && tma) {
+              // map of q, k or v: (d, head in the send row, token, group-major slab), box (64, 1, 32, 1)
+              const int h = static_cast<int>(nbk - static_cast<int64_t>(which) * p.hd) >> 7;
+              const int g = h / p.hg;
+              store_tma(which == 0 ? &tmY0 : (which == 1 ? &tmY1 : &tmY2), 4, 0, j, static_cast<int32_t>(m0),
+                        g * p.ws + dst_rank);
+            } else if (p.epi == H3B_EPI_QKV_SEND) {
               store_rows(qbase, qstride, m0, 16);  // with p2p: the destination rank's receive buffer
             } else if (p.epi == EPI_GATE) {
               // y = x + gate[idx[m]] * o with o the staged bf16 output: fp32, product and sum rounded separately
@@ -556,6 +625,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + mr * p.ldy + col) = make_uint4(w[0], w[1], w[2], w[3]);
               }
               __syncwarp();
+            } else if (tma) {
+              store_tma(&tmY0, 2, static_cast<int32_t>(nbk), static_cast<int32_t>(m0), 0, 0);
             } else {
               store_rows(static_cast<uint16_t*>(p.y) + nbk, p.ldy, m0, granules);
             }
@@ -566,6 +637,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           acc_phase ^= 1u;
         }
       }
+      if (tma && lane == 0) bulk_wait_all0();  // this warp's TMA stores are complete before the CTA leaves
     }
   }
   __syncwarp();
@@ -721,6 +793,41 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
     int rc = encode_tmap(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
+  // output maps of the TMA-store epilogue: plain and SwiGLU outputs, and the local (not peer) q/k/v send buffers;
+  // H3B_GEMM_TMA_STORE=0 keeps the staged blocks on plain stores (a tuning switch: both write the same bytes)
+  CUtensorMap tmY[3];
+  memset(tmY, 0, sizeof(tmY));
+  static const bool tma_store_on = [] {
+    const char* v = getenv("H3B_GEMM_TMA_STORE");
+    return v == nullptr || v[0] == '\0' || atoi(v) != 0;
+  }();
+  if (tma_store_on) {
+    if (epilogue == H3B_EPI_PLAIN || (epilogue == H3B_EPI_SWIGLU && (reinterpret_cast<uintptr_t>(y) & 15u) == 0)) {
+      const uint64_t cols = static_cast<uint64_t>(epilogue == H3B_EPI_SWIGLU ? p.half : N);
+      const uint64_t dims[2] = {cols, static_cast<uint64_t>(M)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(ldy) * 2};
+      const uint32_t box[2] = {64, 32};
+      int rc = encode_tmap(&tmY[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, y, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      p.tma_out = 1;
+    } else if (epilogue == H3B_EPI_QKV_SEND && !p.p2p) {
+      const int groups = send->groups > 1 ? send->groups : 1;
+      const uint64_t row = static_cast<uint64_t>(p.rsh) * 256;  // bytes between a slab's token rows
+      const uint64_t dims[4] = {128, static_cast<uint64_t>(p.hl), static_cast<uint64_t>(M),
+                                static_cast<uint64_t>(groups) * static_cast<uint64_t>(p.ws)};
+      const uint64_t strides[3] = {256, row, row * static_cast<uint64_t>(M)};
+      const uint32_t box[4] = {64, 1, 32, 1};
+      for (int i = 0; i < 3; ++i) {
+        const void* base = p.qkv_step ? static_cast<const void*>(static_cast<const uint16_t*>(p.send[0]) + i * p.qkv_step)
+                                      : p.send[i];
+        int rc = encode_tmap(&tmY[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, base, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+      }
+      p.tma_out = 1;
+    }
+  }
   // per device: the shared-memory limit and how many CTA pairs fit at once (a pair needs two SMs of one GPC; the
   // grid is that many pairs, or fewer when there are fewer tiles)
   static int pairs_fit[64] = {};
@@ -743,7 +850,8 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
   }
   const int tiles = p.num_mb * p.num_nb;
   const int grid = 2 * (tiles < pairs_fit[dev] ? tiles : pairs_fit[dev]);
-  fp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
+  fp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
+                                                                                            tmY[2], p);
   H3B_CHECK_LAUNCH("fp8_gemm launch");
   return H3B_OK;
 }

@@ -323,3 +323,57 @@ def test_consumers_against_the_reference_mirrors(dev, golden):
     assert int(ud.max()) <= 1 and (ud == 0).float().mean().item() > 0.99
     _check_modulated(mod.cpu(), t16(g["gr_mod_out"]))
     assert ops.device_status() == 0
+
+
+def test_tma_store_epilogue_equals_plain_stores(dev, tmp_path):
+    """The staged output blocks leave through TMA stores by default; H3B_GEMM_TMA_STORE=0 keeps them on plain stores.
+    Both write the same bytes: plain and f16 outputs, the SwiGLU output, and the q/k/v send layouts (head groups,
+    interleaved, q/k RMSNorm + RoPE) on shapes with partial row and column tiles, each computed in a fresh process
+    per setting."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys, torch\n"
+        f"sys.path[:0] = [{str(root / 'minimax-h3-2x-dgx-spark-tp2_b200')!r}, {str(root)!r}]\n"
+        "from h3b import ops\n"
+        "E4M3 = torch.float8_e4m3fn\n"
+        "def inputs(M, N, K, seed):\n"
+        "    g = torch.Generator(device='cuda').manual_seed(seed)\n"
+        "    a = torch.randint(-4, 5, (M, K), device='cuda', generator=g).to(E4M3)\n"
+        "    w = torch.randint(-2, 3, (N, K), device='cuda', generator=g).to(E4M3)\n"
+        "    sa = torch.rand(M, device='cuda', generator=g) * 0.05 + 1e-3\n"
+        "    sb = torch.rand(N, device='cuda', generator=g) * 0.05 + 1e-3\n"
+        "    return a, w, sa, sb\n"
+        "out = {}\n"
+        "a, w, sa, sb = inputs(333, 400, 256, 1)\n"
+        "out['plain'] = ops.fp8_gemm(a, w, sa, sb)\n"
+        "out['f16'] = ops.fp8_gemm(a, w, sa, sb, out_dtype=torch.float16)\n"
+        "a, w, sa, sb = inputs(300, 768, 512, 2)\n"
+        "out['swiglu'] = ops.fp8_gemm_swiglu(a, w, sa, sb)\n"
+        "a, w, sa, sb = inputs(150, 3 * 8 * 128, 256, 3)\n"
+        "for i, t in enumerate(ops.fp8_gemm_qkv_send(a, w, sa, sb, 8, 2, groups=2, v_f16=True)):\n"
+        "    out[f'grouped{i}'] = t\n"
+        "out['inter'] = ops.fp8_gemm_qkv_send(a, w, sa, sb, 8, 2, interleaved=True)\n"
+        "g = torch.Generator(device='cuda').manual_seed(4)\n"
+        "qw, kw = (torch.rand(128, device='cuda', generator=g) + 0.5).to(torch.bfloat16), (torch.rand(128, device='cuda', generator=g) + 0.5).to(torch.bfloat16)\n"
+        "tab = torch.rand(150, 96, device='cuda', generator=g) * 2 - 1\n"
+        "for i, t in enumerate(ops.fp8_gemm_qkv_send(a, w, sa, sb, 8, 2, qk_norm=(qw, kw, tab, 1e-6))):\n"
+        "    out[f'norm{i}'] = t\n"
+        "torch.cuda.synchronize()\n"
+        "assert ops.device_status() == 0\n"
+        "torch.save({k: v.cpu() for k, v in out.items()}, sys.argv[1])\n")
+    res = {}
+    for setting in ("0", "1"):
+        path = tmp_path / f"out{setting}.pt"
+        env = dict(os.environ, H3B_GEMM_TMA_STORE=setting)
+        run = subprocess.run([sys.executable, "-c", code, str(path)], env=env, capture_output=True, text=True,
+                             timeout=300)
+        assert run.returncode == 0, run.stderr[-3000:]
+        res[setting] = torch.load(path)
+    assert res["0"].keys() == res["1"].keys()
+    for key in res["0"]:
+        assert same_bits(res["0"][key], res["1"][key]), key
