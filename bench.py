@@ -505,6 +505,51 @@ def run_ffn(args, rank: int, world: int, dev, pg, m: int) -> dict:
             "scaling": "weak (replicas: no communication)", "parity": par}
 
 
+OTHER_CONFIGS = (("cfg1", 66_960, "31x36x60"), ("cfg3", 366_912, "91x48x84"))
+
+
+def run_configs(args, blk, rank: int, world: int, dev, pg) -> list:
+    """BASELINE configs[1] and configs[3] through the same block at this SP: device-timed ms per block over 3 steps
+    after 2 warm-up forwards (the worst rank's time), and the sampled-row parity of one more forward against the CPU
+    oracle (32 rows per rank)."""
+    from h3b import ops  # noqa: PLC0415
+    out = []
+    for name, tokens, grid in OTHER_CONFIGS:
+        if tokens % world:
+            continue
+        m = tokens // world
+        x = make_x(rank, m, dev)
+        for _ in range(2):
+            blk(x)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(group=pg, device_ids=[dev.index])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            blk(x)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / 3
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+            ms = t.item()
+        keep = {}
+        blk.forward(x, keep=keep)
+        torch.cuda.synchronize(dev)
+        status = ops.device_status()
+        if status != 0:
+            raise RuntimeError(f"device status {status} in {name}")
+        par = block_parity(blk, keep, rank, world, m, dev, pg, rows=32)
+        del keep, x
+        fl = sum(block_flops(tokens).values())
+        out.append({"config": f"{name}: {tokens} tokens ({grid}), SP={world}", "tokens": tokens, "rows_per_rank": m,
+                    "ms_per_block": ms, "tflops": fl / (ms * 1e-3) / 1e12, "steps": 3, "warmup": 2,
+                    "parity_ok": par["ok"], "parity_rel_l2": par["rel_l2"]})
+    return out
+
+
 def run_h3b(args, rank: int, world: int, local_rank: int, pg) -> None:
     import h3b  # noqa: PLC0415
     from h3b.block import AttentionBlock  # noqa: PLC0415
@@ -637,6 +682,7 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
         torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
     parity = block_parity(blk, keep, rank, world, m, dev, pg)
     del keep
+    configs = None if args.no_configs else run_configs(args, blk, rank, world, dev, pg)
     ffn = None if args.no_ffn else run_ffn(args, rank, world, dev, pg, m)
 
     line = {
@@ -662,6 +708,8 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
         "clocks": clocks.summary(),
         "parity": parity,
     }
+    if configs is not None:
+        line["other_configs"] = configs
     if ffn is not None:
         line["ffn"] = ffn
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -695,6 +743,8 @@ def main() -> None:
     ap.add_argument("--ref-rows", type=int, default=1024, help="query rows of the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ffn", action="store_true", help="skip the cfg4 FFN section of the JSON line")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the cfg1 / cfg3 block timings (other_configs) of the JSON line")
     ap.add_argument("--groups", type=int, default=0,
                     help="Ulysses head groups overlapped with attention (NCCL exchange; 0: the measured default)")
     ap.add_argument("--exchange", choices=("nccl", "nocopy", "p2p"), default="p2p",
