@@ -279,132 +279,6 @@ __global__ void __launch_bounds__(THREADS) rms_quant_kernel(RmsArgs a) {
   }
 }
 
-// The same arithmetic (same element-to-thread map, same reduction order: bit-identical results) with the rows
-// streamed into shared memory: a persistent CTA keeps NS rows in flight through untiled bulk copies (x, and for K8
-// the branch row), holds the norm weight in shared memory, and issues each row's modulation / gate loads before its
-// reductions, so a row's DRAM latency overlaps the previous rows' reductions instead of following them.  Launched
-// for K8 (GATED); the launcher keeps the per-row kernel for K7.
-template <int THREADS, int VPT, bool GATED>
-__global__ void __launch_bounds__(THREADS) rms_quant_staged_kernel(RmsArgs a, WaitCtl wc) {
-  constexpr int NS = 3;
-  extern __shared__ __align__(16) uint8_t dsm[];
-  __shared__ float red[33];
-  __shared__ uint32_t redu[33];
-  const int64_t nvec = a.hidden / 8;
-  const uint32_t rowbytes = static_cast<uint32_t>(a.hidden * 2);
-  const uint32_t stage_bytes = rowbytes * (GATED ? 2u : 1u);
-  uint4* wsm = reinterpret_cast<uint4*>(dsm);
-  uint8_t* stages = dsm + rowbytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + NS * stage_bytes);
-  const uint32_t bar0 = smem_u32(bars);
-  if (threadIdx.x == 0) {
-    for (int st = 0; st < NS; ++st) mbar_init(bar0 + 8u * st, 1);
-    fence_mbar_init();
-  }
-  for (int64_t i = threadIdx.x; i < nvec; i += THREADS) wsm[i] = __ldg(reinterpret_cast<const uint4*>(a.weight) + i);
-  __syncthreads();
-  uint32_t issued[NS] = {};
-  auto issue = [&](int64_t row, int st) {
-    const uint32_t dst = smem_u32(stages + st * stage_bytes);
-    mbar_arrive_expect_tx(bar0 + 8u * st, stage_bytes);
-    bulk_load(dst, a.x + row * a.stride_x, rowbytes, bar0 + 8u * st);
-    if (GATED) bulk_load(dst + rowbytes, a.branch + row * a.stride_branch, rowbytes, bar0 + 8u * st);
-    issued[st]++;
-  };
-  if (threadIdx.x == 0)
-    for (int st = 0; st < NS; ++st) {
-      const int64_t row = blockIdx.x + static_cast<int64_t>(st) * gridDim.x;
-      if (row < a.rows) issue(row, st);
-    }
-  int it = 0;
-  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x, ++it) {
-    const int st = it % NS;
-    const int64_t idx = a.indices != nullptr ? a.indices[row] : 0;
-    uint4 shv[VPT], scv[VPT], gv[VPT];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
-      shv[k] = scv[k] = gv[k] = make_uint4(0, 0, 0, 0);
-      if (i < nvec) {
-        if (a.shift != nullptr) {
-          shv[k] = __ldg(reinterpret_cast<const uint4*>(a.shift + idx * a.stride_shift) + i);
-          scv[k] = __ldg(reinterpret_cast<const uint4*>(a.scale + idx * a.stride_scale) + i);
-        }
-        if (GATED) gv[k] = __ldg(reinterpret_cast<const uint4*>(a.gate + idx * a.stride_gate) + i);
-      }
-    }
-    const bool ok = mbar_wait(bar0 + 8u * st, static_cast<uint32_t>(it / NS) & 1u, wc);
-    if (__syncthreads_or(!ok)) break;
-    const uint4* xs = reinterpret_cast<const uint4*>(stages + st * stage_bytes);
-    uint4 xv[VPT];
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
-      xv[k] = make_uint4(0, 0, 0, 0);
-      if (i < nvec) {
-        float x[8];
-        unpack8(xs[i], x);
-        if (GATED) {
-          float g[8], b[8];
-          unpack8(gv[k], g);
-          unpack8(xs[nvec + i], b);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = fmaf(g[e], b[e], x[e]);
-          xv[k] = pack8(x);  // the bf16 residual value
-          *reinterpret_cast<uint4*>(a.residual_out + row * a.hidden + i * 8) = xv[k];
-          unpack8(xv[k], x);
-        } else {
-          xv[k] = xs[i];
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
-      }
-    }
-    const float var = __fdiv_rn(block_sum<THREADS>(ss, red), static_cast<float>(a.hidden));
-    // every thread has read stage st (block_sum synchronised): refill it with the row NS rounds ahead
-    if (threadIdx.x == 0) {
-      const int64_t next = row + static_cast<int64_t>(NS) * gridDim.x;
-      if (next < a.rows) {
-        fence_proxy_async_smem();
-        issue(next, st);
-      }
-    }
-    const float rstd = rsqrtf(var + a.eps);
-    uint32_t m2 = 0;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int64_t i = threadIdx.x + static_cast<int64_t>(k) * THREADS;
-      if (i < nvec) {
-        float x[8], w[8];
-        unpack8(xv[k], x);
-        unpack8(wsm[i], w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = x[e] * rstd * w[e];
-        if (a.shift != nullptr) {
-          float sh[8], sc[8];
-          unpack8(shv[k], sh);
-          unpack8(scv[k], sc);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = fmaf(x[e], 1.0f + sc[e], sh[e]);
-        }
-        xv[k] = pack8(x);
-        if (a.ph != nullptr) *reinterpret_cast<uint4*>(a.ph + row * a.hidden + i * 8) = xv[k];
-        m2 = absmax8(xv[k], m2);
-      }
-    }
-    quant_tail<THREADS, VPT>(xv, m2, nvec, a.q + row * a.hidden, a.s + row, a.div_mode, redu);
-  }
-  // copies still in flight (after an early exit) complete before the CTA's shared memory goes away
-  if (threadIdx.x == 0) {
-    const uint64_t t0 = globaltimer();
-    for (int st = 0; st < NS; ++st)
-      if (issued[st] > 0)
-        while (!mbar_try_wait(bar0 + 8u * st, (issued[st] - 1) & 1u) && globaltimer() - t0 < wc.timeout) {
-        }
-  }
-}
-
 // ---------------------------------------------------------------------------------------------------------------
 // K11: SiLU-mul + quant (fp8_quant_fuse._silu_mul_quant_kernel; vLLM act_and_mul arithmetic)
 // K5 : SwiGLU scale pass (+ quant) over the fp32 fc1 product (fp8_swiglu._scale_swiglu / _scale_swiglu_quant)
@@ -753,6 +627,22 @@ static inline int grid_elems(int64_t n, int threads) {
 }
 
 // VPT choices for 256-thread CTAs: widths up to 256 * 8 * 16 = 32768 elements
+// the same for CTAs of 128 threads, with every VPT up to 6 and 10 (a row of 5120 is 128 x 5 vectors exactly)
+#define H3B_VPT128_DISPATCH(NVEC, LAUNCH)     \
+  do {                                        \
+    const int64_t per_ = ((NVEC) + 127) / 128; \
+    if (per_ <= 1) { LAUNCH(1); }             \
+    else if (per_ <= 2) { LAUNCH(2); }        \
+    else if (per_ <= 3) { LAUNCH(3); }        \
+    else if (per_ <= 4) { LAUNCH(4); }        \
+    else if (per_ <= 5) { LAUNCH(5); }        \
+    else if (per_ <= 6) { LAUNCH(6); }        \
+    else if (per_ <= 8) { LAUNCH(8); }        \
+    else if (per_ <= 10) { LAUNCH(10); }      \
+    else if (per_ <= 12) { LAUNCH(12); }      \
+    else { LAUNCH(16); }                      \
+  } while (0)
+
 #define H3B_VPT_DISPATCH(NVEC, LAUNCH)        \
   do {                                        \
     const int64_t per_ = ((NVEC) + 255) / 256; \
@@ -817,34 +707,21 @@ static int rms_common(RmsArgs& a, bool gated, cudaStream_t st) {
     return fail(H3B_EALIGN, "rms_quant: rows, strides and pointers must be 16-byte granular");
   const int64_t nvec = a.hidden / 8;
   if (nvec > 256 * 16) return fail(H3B_EUNSUPPORTED, "rms_quant: hidden %lld above 32768", (long long)a.hidden);
-  if (gated && a.hidden <= 8192) {
-    // K8 reads two rows per token: streamed through shared memory (weight + 3 stages of residual and branch),
-    // persistent grid (0.479 against 0.543 ms at 62,496 x 5120).  K7 keeps a CTA per row: with one row per token the
-    // persistent form holds fewer rows in flight than the resident CTAs do (0.350 against 0.304 ms).
-    const size_t smem = static_cast<size_t>(a.hidden) * 2 * (1 + 3 * (gated ? 2 : 1)) + 3 * 8;
-    WaitCtl wc{device_status_word(), wait_timeout_ns()};
-    if (wc.status == nullptr) return fail(H3B_ECUDA, "rms_quant: device status word");
-    cudaError_t e = cudaSuccess;
-    int per_sm = 0;
-#define L(V)                                                                                                      \
-  do {                                                                                                            \
-    auto kern = rms_quant_staged_kernel<256, V, GATED_>;                                                          \
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));        \
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem);           \
-    if (e == cudaSuccess) {                                                                                       \
-      int64_t blocks = static_cast<int64_t>(num_sms()) * (per_sm > 0 ? per_sm : 1);                               \
-      if (blocks > a.rows) blocks = a.rows;                                                                       \
-      kern<<<static_cast<int>(blocks), 256, smem, st>>>(a, wc);                                                  \
-    }                                                                                                             \
-  } while (0)
-    constexpr bool GATED_ = true;
-    H3B_VPT_DISPATCH(nvec, L);
+  // A CTA of 128 threads per row (rows up to 16,384 wide): measured against 256 threads at 62,496 x 5120, 0.240 against
+  // 0.304 ms (K7) and 0.407 against 0.473 ms (K8, then a persistent kernel streaming rows through shared memory); 512
+  // threads and one warp per row were slower.  More, smaller CTAs keep more rows in flight per SM and shorten each
+  // row's two block reductions.
+  if (nvec <= 128 * 16) {
+    if (gated) {
+#define L(V) rms_quant_kernel<128, V, true><<<grid_rows(a.rows), 128, 0, st>>>(a)
+      H3B_VPT128_DISPATCH(nvec, L);
 #undef L
-    if (e != cudaSuccess) return cuda_fail(e, "rms_quant: staged kernel setup");
-    H3B_CHECK_LAUNCH("rms_quant launch");
-    return H3B_OK;
-  }
-  if (gated) {
+    } else {
+#define L(V) rms_quant_kernel<128, V, false><<<grid_rows(a.rows), 128, 0, st>>>(a)
+      H3B_VPT128_DISPATCH(nvec, L);
+#undef L
+    }
+  } else if (gated) {
 #define L(V) rms_quant_kernel<256, V, true><<<grid_rows(a.rows), 256, 0, st>>>(a)
     H3B_VPT_DISPATCH(nvec, L);
 #undef L
@@ -920,9 +797,15 @@ int h3b_silu_mul_quant_e4m3(const void* x, int64_t rows, int64_t d, int64_t stri
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* qq = static_cast<uint8_t*>(q);
+  if (nvec == 288 * 6) {
+    // the DiT FFN width (13,824): 288 threads x 6 vectors cover the row exactly (0.288 against 0.308 ms with 256 x 8
+    // at 15,624 rows; 192 x 9 and 576 x 3 were slower)
+    silu_mul_quant_kernel<288, 6><<<grid_rows(rows), 288, 0, st>>>(xb, rows, d, stride_x, qq, s, div_mode);
+  } else {
 #define L(V) silu_mul_quant_kernel<256, V><<<grid_rows(rows), 256, 0, st>>>(xb, rows, d, stride_x, qq, s, div_mode)
-  H3B_VPT_DISPATCH(nvec, L);
+    H3B_VPT_DISPATCH(nvec, L);
 #undef L
+  }
   H3B_CHECK_LAUNCH("silu_mul_quant launch");
   return H3B_OK;
 }
@@ -979,9 +862,13 @@ int h3b_scale_swiglu_quant(const float* x, const float* sa, const float* sb, con
   const auto* bb = static_cast<const __nv_bfloat16*>(bias);
   auto* qq = static_cast<uint8_t*>(q);
   if (al16(sb) && (bias == nullptr || al16(bias))) {
+    if (nvec == 288 * 6) {  // the DiT FFN width: 288 x 6 covers it exactly (0.560 against 0.594 ms)
+      scale_swiglu_quant_kernel<288, 6, true><<<grid_rows(M), 288, 0, st>>>(x, sa, sb, bb, M, half, qq, s, div_mode);
+    } else {
 #define L(V) scale_swiglu_quant_kernel<256, V, true><<<grid_rows(M), 256, 0, st>>>(x, sa, sb, bb, M, half, qq, s, div_mode)
-    H3B_VPT_DISPATCH(nvec, L);
+      H3B_VPT_DISPATCH(nvec, L);
 #undef L
+    }
   } else {
 #define L(V) scale_swiglu_quant_kernel<256, V, false><<<grid_rows(M), 256, 0, st>>>(x, sa, sb, bb, M, half, qq, s, div_mode)
     H3B_VPT_DISPATCH(nvec, L);
