@@ -159,3 +159,20 @@ def test_ulysses_ranks_with_v_outside_f16(dev, ws, groups):
     y = torch.cat(ou.run_ranks(body, ws), dim=0)
     assert torch.equal(y.view(torch.int16), full.view(torch.int16))
     assert ops.device_status() == 0
+
+
+def test_kernel_launches_per_forward_match_the_bench_claim(dev):
+    """bench.py reports AttentionBlock.KERNELS_PER_FORWARD launches of this library's kernels per forward: count them
+    in a CUDA activity trace of one forward (the library's kernels live in the h3b, attn and gemm namespaces)."""
+    from torch.profiler import ProfilerActivity, profile
+    n, hidden, heads = 1024, 512, 4
+    blk = AttentionBlock(hidden, heads, device=dev, weights=ob.make_weights(hidden, heads, seed=1))
+    x = torch.randn(n, hidden, generator=torch.Generator().manual_seed(0)).to(BF16).to(dev)
+    blk(x)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        blk(x)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    ours = [s for s in names if any(ns in s for ns in ("h3b::", "attn::", "gemm::"))]
+    assert len(ours) == AttentionBlock.KERNELS_PER_FORWARD, ours
