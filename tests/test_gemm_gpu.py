@@ -377,3 +377,20 @@ def test_tma_store_epilogue_equals_plain_stores(dev, tmp_path):
     assert res["0"].keys() == res["1"].keys()
     for key in res["0"]:
         assert same_bits(res["0"][key], res["1"][key]), key
+
+
+def test_strided_output_rows_keep_their_gaps(dev):
+    """An output view with a row stride above N (the caller's wider buffer): every row gets its N values and the
+    columns between rows stay untouched (the TMA stores clip at N; partial row and column tiles included)."""
+    M, N, K = 333, 400, 256
+    g = torch.Generator(device=dev).manual_seed(11)
+    a = torch.randint(-4, 5, (M, K), device=dev, generator=g).to(E4M3)
+    w = torch.randint(-2, 3, (N, K), device=dev, generator=g).to(E4M3)
+    sa = torch.rand(M, device=dev, generator=g) * 0.05 + 1e-3
+    sb = torch.rand(N, device=dev, generator=g) * 0.05 + 1e-3
+    buf = torch.full((M, N + 72), 7.0, dtype=BF16, device=dev)
+    y = ops.fp8_gemm(a, w, sa, sb, out=buf[:, :N])
+    ref = ops.fp8_gemm(a, w, sa, sb)
+    assert same_bits(y.cpu(), ref.cpu())
+    assert bool((buf[:, N:] == 7.0).all())
+    assert ops.device_status() == 0
