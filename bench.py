@@ -11,8 +11,10 @@ group), so no explicit flush is needed.  Rank 0 prints one JSON line.
 
 After the timed regions every rank checks its part of one more forward against the CPU oracle on 64 sampled rows
 (``parity`` in the JSON line, the worst over ranks): the qkv projection rows it received from every rank, the
-attention of its heads for those rows against the device's K/V, the reverse exchange, and the whole block's output
-rows through the oracle's attention, quant and out projection.  Then the ``ffn`` section times BASELINE configs[4],
+attention of its heads for those rows (the device's q against the device's K/V), the reverse exchange, and the whole block's output
+rows through the oracle's attention, quant and out projection.  ``other_configs`` then runs BASELINE configs[1]
+(66,960 tokens) and configs[3] (366,912 tokens) through the same block at this SP (3 timed steps each, 32 sampled
+rows of parity per rank; ``--no-configs`` skips them).  Then the ``ffn`` section times BASELINE configs[4],
 the block's FFN over the same M = 124,992 / SP rows per rank (RMSNorm + quant, fc1 with the SwiGLU epilogue, quant,
 fc2; no communication), with its own sampled-row parity.
 
