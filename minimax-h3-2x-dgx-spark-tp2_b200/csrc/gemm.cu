@@ -33,7 +33,7 @@ constexpr int BM = 128, BN = 256, BK = 128, STAGES = 6;  // BM: rows per CTA (th
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int B_BYTES = 128 * BK;  // 16 KB: this CTA's half of the 256 B rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;
+constexpr int THREADS = 192;  // producer, MMA issuer, 4 epilogue warps (the SwiGLU form: 8, THREADS + 128)
 constexpr int GROUP_M = 8;   // pair row blocks (256 rows each) sharing one column block's W tile in L2
 constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
 // epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows)
@@ -130,7 +130,11 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
 }
 
 // With Params::p2p the QKV_SEND epilogue stores into the other GPUs' receive buffers (send_slab).
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+// EW: epilogue warps.  4 for every epilogue; 8 for the SwiGLU one (with TMA stores), whose per-element arithmetic
+// (silu with expf and an IEEE division, three bf16 roundings) makes four warps a bottleneck: each of the 8 takes 64
+// of a tile's 128 output columns for its 32 rows and stores them as one TMA box.
+template <int EW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmY0, const __grid_constant__ CUtensorMap tmY1,
                     const __grid_constant__ CUtensorMap tmY2, const __grid_constant__ Params p) {
@@ -159,7 +163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 8);  // one arrival per epilogue warp of both CTAs (counted on the leader's)
+      mbar_init(tempty_bar(a), 2 * EW);  // one arrival per epilogue warp of both CTAs (counted on the leader's)
     }
     mbar_init(done_bar, 1);
     fence_mbar_init();
@@ -279,9 +283,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       // instruction then writes two whole 256-byte rows (four full lines) instead of 16 bytes of 32 different rows,
       // which keeps the load/store path free for the TMA fills of the main loop.
       const int sub = warp & 3;
+      const int hw = (warp - 2) >> 2;  // EW = 8: which 64 of the block's 128 output columns
       const int row_in_tile = sub * 32 + lane;
       const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-      uint4* stg = staging + sub * 32 * 16;
+      uint4* stg = EW == 4 ? staging + sub * 32 * 16 : staging + (warp - 2) * 32 * 8;
       // With TMA stores the block is staged as the two 64-column boxes the stores read: 32 rows x 128 B each, in
       // the 128-byte swizzle (granule c of row r at r * 8 + (c ^ (r & 7))); otherwise as 32 rows x 256 B.
       const bool tma = p.tma_out != 0;
@@ -348,9 +353,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const bool row_ok = m < p.M;
         const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
         const uint32_t tacc = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN);
-        if (p.epi == H3B_EPI_SWIGLU) {
+        if (EW == 8 || p.epi == H3B_EPI_SWIGLU) {
           staging_free();
-          for (int c0 = 0; c0 < 128; c0 += 32) {
+          for (int c0 = EW == 8 ? 64 * hw : 0; c0 < (EW == 8 ? 64 * hw + 64 : 128); c0 += 32) {
             uint32_t g[32], u[32];
             tmem_ld32(tacc + c0, g);
             tmem_ld32(tacc + 128 + c0, u);
@@ -382,14 +387,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               o[i / 2] = pack2(silu_mul_bf16(gv[0], uv[0]), silu_mul_bf16(gv[1], uv[1]), 0);
             }
 #pragma unroll
-            for (int v = 0; v < 4; ++v) stage(c0 / 8 + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
+            for (int v = 0; v < 4; ++v) {
+              const uint4 val = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              if (EW == 8) {
+                const int g = (c0 - 64 * hw) / 8 + v;  // granule of the warp's own 64-column box
+                stg[lane * 8 + (g ^ (lane & 7))] = val;
+              } else {
+                stage(c0 / 8 + v, val);
+              }
+            }
           }
           release_acc();
-          if (tma)
+          if (EW == 8) {  // one box: the warp's 32 rows x its 64 columns
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmY0, smem_u32(stg), nb * 128 + 64 * hw, static_cast<int32_t>(m0));
+              bulk_commit();
+            }
+          } else if (tma) {
             store_tma(&tmY0, 2, nb * 128, static_cast<int32_t>(m0), 0, 0);
-          else
+          } else {
             store_rows(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(nb) * 128, p.ldy, m0, 16);
-        } else {
+          }
+        } else if constexpr (EW == 4) {
           for (int b0 = 0; b0 < BN; b0 += 128) {
             const int64_t nbk = static_cast<int64_t>(nb) * BN + b0;  // first column of the block
             const bool last_block = b0 + 128 >= BN || nbk + 128 >= p.N;
@@ -828,30 +849,43 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
       p.tma_out = 1;
     }
   }
-  // per device: the shared-memory limit and how many CTA pairs fit at once (a pair needs two SMs of one GPC; the
-  // grid is that many pairs, or fewer when there are fewer tiles)
-  static int pairs_fit[64] = {};
+  // per device and kernel form: the shared-memory limit and how many CTA pairs fit at once (a pair needs two SMs of
+  // one GPC; the grid is that many pairs, or fewer when there are fewer tiles).  The SwiGLU epilogue with TMA stores
+  // runs the 8-epilogue-warp form (H3B_GEMM_SWIGLU_WARPS=4, a tuning switch, keeps 4: both write the same bytes).
+  static const bool swiglu8_on = [] {
+    const char* v = getenv("H3B_GEMM_SWIGLU_WARPS");
+    return v == nullptr || v[0] == '\0' || atoi(v) != 4;
+  }();
+  const bool ew8 = swiglu8_on && epilogue == H3B_EPI_SWIGLU && p.tma_out;
+  static int pairs_fit[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(H3B_EUNSUPPORTED, "fp8_gemm: device ordinal %d", dev);
-  if (pairs_fit[dev] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  const int threads = ew8 ? THREADS + 128 : THREADS;
+  int& fit_dev = pairs_fit[ew8 ? 1 : 0][dev];
+  if (fit_dev == 0) {
+    auto kern = ew8 ? fp8_gemm_kernel<8> : fp8_gemm_kernel<4>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     int fit = 0;
     if (e == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(static_cast<unsigned>(num_sms() & ~1), 1, 1);
-      cfg.blockDim = dim3(THREADS, 1, 1);
+      cfg.blockDim = dim3(threads, 1, 1);
       cfg.dynamicSmemBytes = SMEM_BYTES;
-      e = cudaOccupancyMaxActiveClusters(&fit, fp8_gemm_kernel, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
     }
     if (e != cudaSuccess) return cuda_fail(e, "fp8_gemm: smem attribute / cluster occupancy");
     if (fit < 1) return fail(H3B_EUNSUPPORTED, "fp8_gemm: no CTA pair fits on this device");
-    pairs_fit[dev] = fit;
+    fit_dev = fit;
   }
   const int tiles = p.num_mb * p.num_nb;
-  const int grid = 2 * (tiles < pairs_fit[dev] ? tiles : pairs_fit[dev]);
-  fp8_gemm_kernel<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
-                                                                                            tmY[2], p);
+  const int grid = 2 * (tiles < fit_dev ? tiles : fit_dev);
+  if (ew8)
+    fp8_gemm_kernel<8><<<grid, threads, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
+                                                                                               tmY[2], p);
+  else
+    fp8_gemm_kernel<4><<<grid, threads, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
+                                                                                               tmY[2], p);
   H3B_CHECK_LAUNCH("fp8_gemm launch");
   return H3B_OK;
 }
