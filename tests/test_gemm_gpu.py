@@ -329,7 +329,8 @@ def test_tma_store_epilogue_equals_plain_stores(dev, tmp_path):
     """The staged output blocks leave through TMA stores by default; H3B_GEMM_TMA_STORE=0 keeps them on plain stores.
     Both write the same bytes: plain and f16 outputs, the SwiGLU output, and the q/k/v send layouts (head groups,
     interleaved, q/k RMSNorm + RoPE) on shapes with partial row and column tiles, each computed in a fresh process
-    per setting."""
+    per setting.  (With TMA stores the SwiGLU epilogue runs its 8-warp form, without them the 4-warp one, so this also
+    compares the two.)"""
     import os
     import subprocess
     import sys
