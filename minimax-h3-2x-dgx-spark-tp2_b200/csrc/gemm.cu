@@ -24,6 +24,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace h3b {
@@ -862,6 +864,8 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(H3B_EUNSUPPORTED, "fp8_gemm: device ordinal %d", dev);
   const int threads = ew8 ? THREADS + 128 : THREADS;
+  static std::mutex fit_mu;  // first calls from several threads compute the entry once
+  std::unique_lock<std::mutex> fit_lock(fit_mu);
   int& fit_dev = pairs_fit[ew8 ? 1 : 0][dev];
   if (fit_dev == 0) {
     auto kern = ew8 ? fp8_gemm_kernel<8> : fp8_gemm_kernel<4>;
@@ -878,8 +882,10 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
     if (fit < 1) return fail(H3B_EUNSUPPORTED, "fp8_gemm: no CTA pair fits on this device");
     fit_dev = fit;
   }
+  const int fit_now = fit_dev;
+  fit_lock.unlock();
   const int tiles = p.num_mb * p.num_nb;
-  const int grid = 2 * (tiles < fit_dev ? tiles : fit_dev);
+  const int grid = 2 * (tiles < fit_now ? tiles : fit_now);
   if (ew8)
     fp8_gemm_kernel<8><<<grid, threads, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
                                                                                                tmY[2], p);
