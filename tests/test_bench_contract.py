@@ -122,3 +122,12 @@ def test_ffn_parity_passes_on_oracle_data_and_catches_a_planted_error():
     y2 = y.clone()
     y2[0] *= 2
     assert not bench.ffn_parity(x, (norm_w, w1, s1, w2, s2), {"h": h, "y": y2}, rows=16)["ok"]
+
+
+def test_other_configs_shard_at_every_driver_n():
+    """The cfg1 / cfg3 token counts of the JSON line's other_configs split evenly over 1, 2, 4 and 8 ranks, as the
+    heads do, so the driver's scaling runs carry them at every N."""
+    import bench
+    for _, tokens, _grid in bench.OTHER_CONFIGS:
+        for n in (1, 2, 4, 8):
+            assert tokens % n == 0 and bench.HEADS % n == 0
