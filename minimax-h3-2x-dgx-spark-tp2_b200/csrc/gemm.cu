@@ -38,11 +38,19 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;  // producer, MMA issuer, 4 epilogue warps (the SwiGLU form: 8, THREADS + 128)
 constexpr int GROUP_M = 8;   // pair row blocks (256 rows each) sharing one column block's W tile in L2
 constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
-// epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows)
+// epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows); 64 KB for the 8-warp q/k/v
+// form, which holds one block per warp and runs a 5-stage ring to make room
 constexpr int STAGING_BYTES = 4 * 32 * 256;
+// epilogue forms: 0 four warps (every epilogue), 1 eight warps for SwiGLU, 2 eight warps for the q/k/v send layout
+constexpr int MODE_STD = 0, MODE_SWIGLU8 = 1, MODE_QKV8 = 2;
+__host__ __device__ constexpr int mode_stages(int mode) { return mode == MODE_QKV8 ? 5 : STAGES; }
+__host__ __device__ constexpr int mode_staging(int mode) { return mode == MODE_QKV8 ? 2 * STAGING_BYTES : STAGING_BYTES; }
 // ring, alignment slack, barriers (1 KB, so that the staging starts 1024-byte aligned as the 128-byte swizzle of the
-// TMA stores needs), staging: 231,424 B of the 232,448 a CTA may have
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING_BYTES;
+// TMA stores needs), staging: 231,424 B of the 232,448 a CTA may have in every form
+__host__ __device__ constexpr int mode_smem(int mode) {
+  return mode_stages(mode) * (16384 + 16384) + 1024 + 1024 + mode_staging(mode);
+}
+static_assert(mode_smem(MODE_STD) <= 232448 && mode_smem(MODE_QKV8) <= 232448, "shared memory");
 constexpr uint32_t IDESC = idesc_make(FMT_E4M3, FMT_E4M3, 0, 2 * BM, BN);
 
 struct Params {
@@ -132,34 +140,39 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
 }
 
 // With Params::p2p the QKV_SEND epilogue stores into the other GPUs' receive buffers (send_slab).
-// EW: epilogue warps.  4 for every epilogue; 8 for the SwiGLU one (with TMA stores), whose per-element arithmetic
-// (silu with expf and an IEEE division, three bf16 roundings) makes four warps a bottleneck: each of the 8 takes 64
-// of a tile's 128 output columns for its 32 rows and stores them as one TMA box.
-template <int EW>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
+// MODE: the epilogue form.  MODE_STD: 4 epilogue warps, every epilogue.  MODE_SWIGLU8: 8 warps for the SwiGLU
+// epilogue (with TMA stores), whose per-element arithmetic (silu with expf and an IEEE division, three bf16 roundings)
+// makes four warps a bottleneck: each of the 8 takes 64 of a tile's 128 output columns for its 32 rows and stores
+// them as one TMA box.  MODE_QKV8: 8 warps for the local q/k/v send epilogue with the qk-norm (and TMA stores),
+// each taking one of the tile's two 128-column head blocks for its 32 rows (the qk-norm needs a head's 128 columns
+// in one thread), with 64 KB of staging and a 5-stage ring.
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(MODE == MODE_STD ? THREADS : THREADS + 128, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmY0, const __grid_constant__ CUtensorMap tmY1,
                     const __grid_constant__ CUtensorMap tmY2, const __grid_constant__ Params p) {
+  constexpr int EW = MODE == MODE_STD ? 4 : 8;
+  constexpr int NST = mode_stages(MODE);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
-  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 1024);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NST * STAGE_BYTES);
+  // bars: full[NST], empty[NST], tfull[2], tempty[2], done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NST + 5);
+  uint4* staging = reinterpret_cast<uint4*>(smem + NST * STAGE_BYTES + 1024);
   const uint32_t smem0 = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
-  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
-  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-  const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
+  auto empty_bar = [&](int s) { return bar0 + 8u * (NST + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * NST + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * NST + 2 + a); };
+  const uint32_t done_bar = bar0 + 8u * (2 * NST + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = cluster_ctarank();  // 0: the pair's leader (issues the MMAs), 1: its partner
   const uint32_t peer = crank ^ 1u;
   const bool aborted_at_entry = status_bad(p.wc);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
@@ -191,8 +204,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
         const uint32_t lead_full0 = mapa_shared(full_bar(0), 0);
         int stage = 0;
         uint32_t phase = 0;
-        int issued[STAGES];
-        for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+        int issued[NST];
+        for (int s = 0; s < NST; ++s) issued[s] = 0;
         bool ok = true;
         for (int t = first_tile; t < num_tiles && ok; t += tile_step) {
           int mb, nb;
@@ -213,7 +226,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
             tma_load_2d_pair(sA, &tmA, fb, kb * BK, arow);
             tma_load_2d_pair(sB, &tmB, fb, kb * BK, brow);
             issued[stage]++;
-            if (++stage == STAGES) {
+            if (++stage == NST) {
               stage = 0;
               phase ^= 1u;
             }
@@ -222,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
         // drain: never leave a TMA write in flight into shared memory the CTA is about to release.  The leader
         // sees both CTAs' bytes on its full barriers; the partner's last load of a stage has landed once the
         // leader's MMAs consumed it (its empty barrier).
-        for (int s = 0; s < STAGES; ++s)
+        for (int s = 0; s < NST; ++s)
           if (issued[s] > 0) {
             const uint32_t par = static_cast<uint32_t>(issued[s] - 1) & 1u;
             const uint32_t bar = crank == 0 ? full_bar(s) : empty_bar(s);
@@ -258,15 +271,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
             for (int kk = 0; kk < BK / 32; ++kk)
               umma_f8_ss_pair(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | kk) != 0);
             umma_commit_pair(empty_bar(stage));
-            umma_commit_pair(peer_bar0 + 8u * (STAGES + stage));
-            if (++stage == STAGES) {
+            umma_commit_pair(peer_bar0 + 8u * (NST + stage));
+            if (++stage == NST) {
               stage = 0;
               phase ^= 1u;
             }
           }
           if (!ok) break;
           umma_commit_pair(tfull_bar(acc));
-          umma_commit_pair(peer_bar0 + 8u * (2 * STAGES + acc));
+          umma_commit_pair(peer_bar0 + 8u * (2 * NST + acc));
           if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
@@ -288,7 +301,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
       const int hw = (warp - 2) >> 2;  // EW = 8: which 64 of the block's 128 output columns
       const int row_in_tile = sub * 32 + lane;
       const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-      uint4* stg = EW == 4 ? staging + sub * 32 * 16 : staging + (warp - 2) * 32 * 8;
+      uint4* stg = MODE == MODE_STD ? staging + sub * 32 * 16
+                   : (MODE == MODE_SWIGLU8 ? staging + (warp - 2) * 32 * 8 : staging + (warp - 2) * 32 * 16);
       // With TMA stores the block is staged as the two 64-column boxes the stores read: 32 rows x 128 B each, in
       // the 128-byte swizzle (granule c of row r at r * 8 + (c ^ (r & 7))); otherwise as 32 rows x 256 B.
       const bool tma = p.tma_out != 0;
@@ -355,9 +369,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
         const bool row_ok = m < p.M;
         const float sam = row_ok ? __ldg(p.sa + m) : 0.0f;
         const uint32_t tacc = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN);
-        if (EW == 8 || p.epi == H3B_EPI_SWIGLU) {
+        if (MODE == MODE_SWIGLU8 || (MODE == MODE_STD && p.epi == H3B_EPI_SWIGLU)) {
           staging_free();
-          for (int c0 = EW == 8 ? 64 * hw : 0; c0 < (EW == 8 ? 64 * hw + 64 : 128); c0 += 32) {
+          for (int c0 = MODE == MODE_SWIGLU8 ? 64 * hw : 0; c0 < (MODE == MODE_SWIGLU8 ? 64 * hw + 64 : 128); c0 += 32) {
             uint32_t g[32], u[32];
             tmem_ld32(tacc + c0, g);
             tmem_ld32(tacc + 128 + c0, u);
@@ -391,7 +405,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const uint4 val = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
-              if (EW == 8) {
+              if (MODE == MODE_SWIGLU8) {
                 const int g = (c0 - 64 * hw) / 8 + v;  // granule of the warp's own 64-column box
                 stg[lane * 8 + (g ^ (lane & 7))] = val;
               } else {
@@ -400,7 +414,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
             }
           }
           release_acc();
-          if (EW == 8) {  // one box: the warp's 32 rows x its 64 columns
+          if (MODE == MODE_SWIGLU8) {  // one box: the warp's 32 rows x its 64 columns
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -412,11 +426,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
           } else {
             store_rows(static_cast<uint16_t*>(p.y) + static_cast<int64_t>(nb) * 128, p.ldy, m0, 16);
           }
-        } else if constexpr (EW == 4) {
-          for (int b0 = 0; b0 < BN; b0 += 128) {
+        } else if constexpr (MODE != MODE_SWIGLU8) {
+          // MODE_QKV8: this warp's one block (hw); every warp still releases the accumulator once per tile
+          for (int b0 = MODE == MODE_QKV8 ? 128 * hw : 0; b0 < (MODE == MODE_QKV8 ? 128 * hw + 128 : BN); b0 += 128) {
             const int64_t nbk = static_cast<int64_t>(nb) * BN + b0;  // first column of the block
-            const bool last_block = b0 + 128 >= BN || nbk + 128 >= p.N;
-            if (nbk >= p.N) break;  // warp-uniform
+            const bool last_block = MODE == MODE_QKV8 || b0 + 128 >= BN || nbk + 128 >= p.N;
+            if (nbk >= p.N) {  // warp-uniform
+              if (MODE == MODE_QKV8) release_acc();
+              break;
+            }
             // QKV_SEND: the block is one head of q, k or v; its destination rows are 256 B apart from the slab base
             int which = 0, dst_rank = 0, j = 0;
             uint16_t* qbase = nullptr;
@@ -853,29 +871,40 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
   }
   // per device and kernel form: the shared-memory limit and how many CTA pairs fit at once (a pair needs two SMs of
   // one GPC; the grid is that many pairs, or fewer when there are fewer tiles).  The SwiGLU epilogue with TMA stores
-  // runs the 8-epilogue-warp form (H3B_GEMM_SWIGLU_WARPS=4, a tuning switch, keeps 4: both write the same bytes).
+  // runs the 8-epilogue-warp form (H3B_GEMM_SWIGLU_WARPS=4, a tuning switch, keeps 4: both write the same bytes);
   static const bool swiglu8_on = [] {
     const char* v = getenv("H3B_GEMM_SWIGLU_WARPS");
     return v == nullptr || v[0] == '\0' || atoi(v) != 4;
   }();
-  const bool ew8 = swiglu8_on && epilogue == H3B_EPI_SWIGLU && p.tma_out;
-  static int pairs_fit[2][64] = {};
+  // the local q/k/v send epilogue with the qk-norm + RoPE and TMA stores runs the 8-warp form (4.90 against 5.01-5.14
+  // ms at 62,496 rows; without the norm the 5-stage ring costs more than the extra warps give back: 4.11-4.17 against
+  // 4.08-4.13, so that one keeps 4).  H3B_GEMM_QKV_WARPS=4 keeps 4 for the norm form too (same bytes).
+  static const bool qkv8_on = [] {
+    const char* v = getenv("H3B_GEMM_QKV_WARPS");
+    return v == nullptr || v[0] == '\0' || atoi(v) != 4;
+  }();
+  int mode = MODE_STD;
+  if (swiglu8_on && epilogue == H3B_EPI_SWIGLU && p.tma_out) mode = MODE_SWIGLU8;
+  if (qkv8_on && epilogue == H3B_EPI_QKV_SEND && p.tma_out && p.norm_w[0] != nullptr) mode = MODE_QKV8;
+  static int pairs_fit[3][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fail(H3B_EUNSUPPORTED, "fp8_gemm: device ordinal %d", dev);
-  const int threads = ew8 ? THREADS + 128 : THREADS;
+  const int threads = mode == MODE_STD ? THREADS : THREADS + 128;
+  const int smem = mode_smem(mode);
   static std::mutex fit_mu;  // first calls from several threads compute the entry once
   std::unique_lock<std::mutex> fit_lock(fit_mu);
-  int& fit_dev = pairs_fit[ew8 ? 1 : 0][dev];
+  int& fit_dev = pairs_fit[mode][dev];
   if (fit_dev == 0) {
-    auto kern = ew8 ? fp8_gemm_kernel<8> : fp8_gemm_kernel<4>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    auto kern = mode == MODE_SWIGLU8 ? fp8_gemm_kernel<MODE_SWIGLU8>
+                                     : (mode == MODE_QKV8 ? fp8_gemm_kernel<MODE_QKV8> : fp8_gemm_kernel<MODE_STD>);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     int fit = 0;
     if (e == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(static_cast<unsigned>(num_sms() & ~1), 1, 1);
       cfg.blockDim = dim3(threads, 1, 1);
-      cfg.dynamicSmemBytes = SMEM_BYTES;
+      cfg.dynamicSmemBytes = smem;
       e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
     }
     if (e != cudaSuccess) return cuda_fail(e, "fp8_gemm: smem attribute / cluster occupancy");
@@ -886,12 +915,13 @@ int fp8_gemm_impl(const void* a, int64_t lda, const void* w, int64_t ldw, const 
   fit_lock.unlock();
   const int tiles = p.num_mb * p.num_nb;
   const int grid = 2 * (tiles < fit_now ? tiles : fit_now);
-  if (ew8)
-    fp8_gemm_kernel<8><<<grid, threads, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
-                                                                                               tmY[2], p);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (mode == MODE_SWIGLU8)
+    fp8_gemm_kernel<MODE_SWIGLU8><<<grid, threads, smem, st>>>(tmA, tmB, tmY[0], tmY[1], tmY[2], p);
+  else if (mode == MODE_QKV8)
+    fp8_gemm_kernel<MODE_QKV8><<<grid, threads, smem, st>>>(tmA, tmB, tmY[0], tmY[1], tmY[2], p);
   else
-    fp8_gemm_kernel<4><<<grid, threads, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, tmY[0], tmY[1],
-                                                                                               tmY[2], p);
+    fp8_gemm_kernel<MODE_STD><<<grid, threads, smem, st>>>(tmA, tmB, tmY[0], tmY[1], tmY[2], p);
   H3B_CHECK_LAUNCH("fp8_gemm launch");
   return H3B_OK;
 }
