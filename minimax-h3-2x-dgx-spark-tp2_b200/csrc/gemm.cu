@@ -16,9 +16,13 @@
 //   warps 2..5  : epilogue; thread t of the 128 owns accumulator row t of its CTA (TMEM lane), reads 32-column
 //                 slices with tcgen05.ld, applies the scales (and SwiGLU to the gate/up halves, or the gated
 //                 residual), stages each 128-column block of its warp's 32 rows in shared memory and stores it as two
-//                 whole rows per instruction (into y, or scattered into the Ulysses send layout); each warp arrives on
-//                 the leader's accumulator-empty barrier once its TMEM reads of a tile are done (8 arrivals per tile,
-//                 4 of them from the other CTA).
+//                 whole rows per instruction or as TMA boxes (into y, or scattered into the Ulysses send layout); each
+//                 warp arrives on the leader's accumulator-empty barrier once its TMEM reads of a tile are done (8
+//                 arrivals per tile, 4 of them from the other CTA).
+//   Two epilogue forms run 8 warps (2..9; the template MODE): SwiGLU (MODE_SWIGLU8, each warp 64 of a tile's 128
+//   output columns of its 32 rows) and the q/k/v send layout with qk RMSNorm + RoPE (MODE_QKV8, each warp one of the
+//   tile's two 128-column heads, with 64 KB of staging and a 5-stage ring); the accumulator-empty barrier then counts
+//   16 arrivals.
 //   The accumulator is double buffered in TMEM (2 x 256 of the 512 columns) so the epilogue of tile i overlaps the
 //   main loop of tile i+1.  Every wait is bounded (common.cuh).  No TMA multicast.
 #include <stdlib.h>
@@ -35,7 +39,7 @@ constexpr int BM = 128, BN = 256, BK = 128, STAGES = 6;  // BM: rows per CTA (th
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int B_BYTES = 128 * BK;  // 16 KB: this CTA's half of the 256 B rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;  // producer, MMA issuer, 4 epilogue warps (the SwiGLU form: 8, THREADS + 128)
+constexpr int THREADS = 192;  // producer, MMA issuer, 4 epilogue warps (the 8-warp forms: THREADS + 128)
 constexpr int GROUP_M = 8;   // pair row blocks (256 rows each) sharing one column block's W tile in L2
 constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
 // epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows); 64 KB for the 8-warp q/k/v
