@@ -67,9 +67,10 @@ def fused_config() -> tuple[int, int, int, int, int]:
     return 256, 256, 128, 6, 6
 
 
-def tile_coords(pid: int, M: int, N: int, block_m: int = 256, block_n: int = 256, group_m: int = 8) -> tuple[int, int]:
+def tile_coords(pid: int, M: int, N: int, block_m: int = 256, block_n: int = 256, group_m: int = 16) -> tuple[int, int]:
     """Grouped raster of the persistent kernel: pair tile ``pid`` -> (row block, column block); GROUP_M row blocks
-    share each column block's W tile in L2 (h3_tp2/fp8_gemm.py:188 is the same raster)."""
+    share each column block's W tile in L2 (h3_tp2/fp8_gemm.py:188 is the same raster; the defaults are this
+    kernel's: 256 x 256 pair tiles in groups of 16 row blocks)."""
     num_mb, num_nb = -(-M // block_m), -(-N // block_n)
     in_group = group_m * num_nb
     group = pid // in_group

@@ -284,7 +284,7 @@ def test_gemm_tile_raster_covers_every_tile_once(M, N):
     num_mb, num_nb = -(-M // bm), -(-N // bn)
     seen = [fp8_gemm.tile_coords(t, M, N) for t in range(num_mb * num_nb)]
     assert sorted(seen) == [(i, j) for i in range(num_mb) for j in range(num_nb)]
-    # within a group of 8 row blocks, consecutive tiles walk down the rows of one column block first
+    # within a group of GROUP_M row blocks, consecutive tiles walk down the rows of one column block first
     if num_mb >= 2 and num_nb >= 2:
         assert seen[1] == (1, 0)
 
