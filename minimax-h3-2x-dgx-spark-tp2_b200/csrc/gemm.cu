@@ -41,7 +41,7 @@ constexpr int B_BYTES = 128 * BK;  // 16 KB: this CTA's half of the 256 B rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;  // producer, MMA issuer, 4 epilogue warps (the 8-warp forms: THREADS + 128)
 // pair row blocks (256 rows each) sharing one column block's W tile in L2: 16 measured 2-4 % faster than 8 on the
-// qkv GEMM and the FFN at 15,624-124,992 rows (interleaved runs on one GPU), 32 slower
+// qkv GEMM and the FFN at 15,624-124,992 rows (interleaved runs on one GPU), 12, 24 and 32 slower
 constexpr int GROUP_M = 16;
 constexpr int EPI_GATE = 3;  // internal epilogue kind of h3b_fp8_gemm_gate
 // epilogue staging: per epilogue warp 32 rows x 256 B (one 128-column block of its rows); 64 KB for the 8-warp q/k/v
