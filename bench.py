@@ -60,10 +60,22 @@ def measured_peaks() -> dict:
         try:
             d = json.loads(p.read_text())
             return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
-                    "source": "measured"}
+                    "sustained_sm_mhz": (d.get("clocks_under_load") or {}).get("sm_mhz_median"), "source": "measured"}
         except Exception:  # noqa: BLE001
             pass
-    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "sustained_sm_mhz": 1300.0,
+            "source": "fallback"}
+
+
+def clock_normalised(achieved: float, peak: float, peak_mhz, run_mhz) -> dict:
+    """The roofline fraction with the peak moved to the kernel's own SM clock.  The sustained peak was measured at the
+    median SM clock ``peak_mhz`` (a cuBLAS loop under the power cap) and tensor throughput scales with the clock, so
+    against ``run_mhz`` (the median sampled over the timed region) the attainable rate is peak * run_mhz / peak_mhz."""
+    if not peak_mhz or not run_mhz:
+        return {"frac_at_run_clock": None, "peak_sm_mhz": peak_mhz, "run_sm_mhz": run_mhz}
+    at_clock = peak * float(run_mhz) / float(peak_mhz)
+    return {"frac_at_run_clock": achieved / at_clock, "peak_at_run_clock": at_clock, "peak_sm_mhz": peak_mhz,
+            "run_sm_mhz": run_mhz}
 
 
 class ClockSampler:
@@ -673,6 +685,7 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
     attn_fl_per_launch = fl["attention"] / world
     achieved = attn_fl_per_launch / (attn_ms * 1e-3) / 1e12
     peak = peaks["bf16_sustained"]
+    clk = clocks.summary()
     # ---- parity: one more forward, its sampled rows against the CPU oracle on every rank (outside the timings) ----
     keep = {}
     blk.forward(x, keep=keep)
@@ -703,11 +716,12 @@ def _timed(args, blk, rank, world, local_rank, pg, dev, tokens, m, p2p) -> None:
                      "peak_source": f"{peaks['source']} bf16 dense, sustained (kernel timed inside a long step)",
                      "traffic": None,
                      "traffic_source": "not measured by this run (DRAM bytes need an ncu capture; the committed "
-                                       "profiles hold them)"},
+                                       "profiles hold them)",
+                     **clock_normalised(achieved, peak, peaks.get("sustained_sm_mhz"), clk.get("sm_mhz"))},
         "e2e": {"value": total_fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": m * HIDDEN * 2, "d2h_bytes_per_step": m * HIDDEN * 2},
         "gpu_launches": (blk.KERNELS_PER_FORWARD + (blk.P2P_BARRIERS if p2p else 0)) * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clk,
         "parity": parity,
     }
     if configs is not None:

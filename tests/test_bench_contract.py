@@ -131,3 +131,18 @@ def test_other_configs_shard_at_every_driver_n():
     for _, tokens, _grid in bench.OTHER_CONFIGS:
         for n in (1, 2, 4, 8):
             assert tokens % n == 0 and bench.HEADS % n == 0
+
+
+def test_roofline_fraction_at_the_kernels_own_clock():
+    """The clock-normalised roofline: the sustained peak, measured at one median SM clock, is moved to the clock the
+    timed region ran at before the kernel's rate is divided by it; missing clocks give no fraction, not a guess."""
+    import bench
+
+    r = bench.clock_normalised(1100.0, 1363.1, 1312.0, 1560.0)
+    assert abs(r["peak_at_run_clock"] - 1363.1 * 1560.0 / 1312.0) < 1e-9
+    assert abs(r["frac_at_run_clock"] - 1100.0 / (1363.1 * 1560.0 / 1312.0)) < 1e-12
+    assert r["peak_sm_mhz"] == 1312.0 and r["run_sm_mhz"] == 1560.0
+    assert bench.clock_normalised(1100.0, 1363.1, None, 1560.0)["frac_at_run_clock"] is None
+    assert bench.clock_normalised(1100.0, 1363.1, 1312.0, None)["frac_at_run_clock"] is None
+    peaks = bench.measured_peaks()
+    assert "sustained_sm_mhz" in peaks
